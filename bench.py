@@ -1,0 +1,376 @@
+"""Benchmark: voxels/s of full-volume 8x-mirrored 3-D U-Net sliding-window inference on B200.
+
+One step = one full pass of the inference hot path over the benchmark volume
+(1 x 101 x 768 x 768 synthetic CT, PlainConvUNet 32..320,
+patch 128^3, step 0.5, 8 mirrored views, 1 fold; 121 tiles, 968 forwards):
+mirrored tile gather -> U-Net forward of the 8 views as one batch -> fused seg
+head + flip-back + Gaussian accumulation, for every tile; then normalise +
+argmax into float32 logits and uint8 labels on the device.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+``value``: whole-job voxels/s with the preprocessed volume resident in HBM
+(CUDA events on the compute stream, max over ranks).  ``e2e``: the same
+metric through the public API with the volume in pinned host memory and the
+float32 logits copied back each step.  ``--impl reference`` times the CPU
+restatement of the reference path (oracle port; the reference itself needs
+MLX on Apple silicon) on the host cores and extrapolates per forward.
+Multi-GPU: launched with torchrun, one rank per GPU; (tile, fold) units are
+sharded and the accumulators merged once with an NCCL reduce-scatter.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "voxels/sec full-volume 3D U-Net inference (8x mirror TTA)"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--config", type=int, default=2, help="BASELINE config number (2, 3, 4 or 5)")
+    p.add_argument("--precision", choices=["fp32", "tf32"], default="fp32")
+    p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "source": "measured"}
+    return {**FALLBACK_PEAKS, "source": "fallback"}
+
+
+def forward_flops(spec, patch) -> float:
+    """Algorithmic FLOPs (2 x MAC) of one network forward at ``patch`` (convs, transposed convs, seg head)."""
+    from nnunet_mlx_b200.model.topology import ResidualEncoderUNetSpec
+
+    flops = 0.0
+    shape = list(patch)
+
+    def conv(cin, cout, k, vox):
+        return 2.0 * vox * cout * cin * math.prod(k)
+
+    sizes = []
+    if isinstance(spec, ResidualEncoderUNetSpec):
+        stem = spec.effective_stem_channels
+        vox = math.prod(shape)
+        flops += conv(spec.input_channels, stem, spec.kernel_sizes[0], vox)
+        cin = stem
+        for s, f in enumerate(spec.features):
+            shape = [a // b for a, b in zip(shape, spec.strides[s])]
+            vox = math.prod(shape)
+            sizes.append(list(shape))
+            for b in range(spec.encoder_blocks[s]):
+                bin_ = cin if b == 0 else f
+                flops += conv(bin_, f, spec.kernel_sizes[s], vox) + conv(f, f, spec.kernel_sizes[s], vox)
+                if b == 0 and bin_ != f:
+                    flops += conv(bin_, f, (1, 1, 1), vox)
+            cin = f
+    else:
+        cin = spec.input_channels
+        for s, f in enumerate(spec.features):
+            shape = [a // b for a, b in zip(shape, spec.strides[s])]
+            vox = math.prod(shape)
+            sizes.append(list(shape))
+            for b in range(spec.encoder_convs[s]):
+                flops += conv(cin if b == 0 else f, f, spec.kernel_sizes[s], vox)
+            cin = f
+    stages = len(spec.features)
+    for d in range(stages - 1):
+        src = stages - 1 - d
+        below, skip = spec.features[src], spec.features[src - 1]
+        vin = math.prod(sizes[src])
+        vout = math.prod(sizes[src - 1])
+        flops += 2.0 * vin * below * skip * math.prod(spec.strides[src])
+        for b in range(spec.decoder_convs[d]):
+            flops += conv(2 * skip if b == 0 else skip, skip, spec.kernel_sizes[src - 1], vout)
+    flops += 2.0 * math.prod(sizes[0]) * spec.features[0] * spec.num_classes
+    return flops
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(spec, weights, patch, forwards: int, voxels: int):
+    """Oracle (PyTorch-CPU float32 port of the reference forward) on the host cores, one 128^3 forward."""
+    import numpy as np
+    import torch
+
+    from oracle import network as onet
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    x = np.random.default_rng(0).standard_normal((1, *patch, spec.input_channels)).astype(np.float32)
+    onet.forward(x[:, :32, :32, :32], weights, spec) if min(patch) >= 32 else None  # warm the thread pool
+    t0 = time.perf_counter()
+    onet.forward(x, weights, spec)
+    seconds = time.perf_counter() - t0
+    value = voxels / (seconds * forwards)
+    return {"value": value, "unit": "voxels/s", "cores": cores, "kind": "port",
+            "sample": f"1 forward of one {patch[0]}^3 tile ({seconds:.2f} s) on {cores} threads, "
+                      f"extrapolated x{forwards} forwards (oracle/network.py, torch {torch.__version__} CPU)"}
+
+
+def setup_distributed(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the CPU restatement of the reference path on the host cores."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    from nnunet_mlx_b200.prediction.sliding_window import volume_work
+    from nnunet_mlx_b200.synthetic import CONFIGS, config_spec, seeded_weights
+
+    spec = config_spec(args.config)
+    weights = seeded_weights(spec, CONFIGS[args.config]["seeds"][0])
+    shape = {2: (101, 768, 768), 3: (155, 240, 240), 4: (284, 400, 400), 5: (101, 768, 768)}[args.config]
+    work = volume_work(shape, (128,) * 3, 0.5, 8, len(CONFIGS[args.config]["seeds"]))
+    times = []
+    for i in range(args.warmup + args.steps):
+        sample = cpu_baseline(spec, weights, (128, 128, 128), work["forwards"], work["voxels"])
+        if i >= args.warmup:
+            times.append(sample)
+    value = statistics.median(s["value"] for s in times)
+    seconds_per_volume = work["voxels"] / value
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": seconds_per_volume * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "config": {"workload": f"config{args.config}", "volume": list(shape),
+                                        "patch": [128, 128, 128], "tiles": work["tiles"],
+                                        "forwards": work["forwards"], "extrapolated": True},
+        "cpu_baseline": {**times[-1], "value": value},
+        "e2e": {"value": value, "unit": "voxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    del np
+
+
+def main():
+    args = parse_args()
+    world, rank, local = setup_distributed(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from nnunet_mlx_b200 import _native, build, kernels
+    from nnunet_mlx_b200.distributed import predict_volume_sharded
+    from nnunet_mlx_b200.model.network import build_network
+    from nnunet_mlx_b200.prediction.inference import ArrayPredictor
+    from nnunet_mlx_b200.prediction.sliding_window import volume_work
+    from nnunet_mlx_b200.synthetic import CONFIGS, config_spec, config_volume, seeded_weights
+
+    build.build_extension()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    cfg = CONFIGS[args.config]
+    spec = config_spec(args.config)
+    patch = (128, 128, 128)
+    weights = [seeded_weights(spec, seed) for seed in cfg["seeds"]]
+    models = [build_network(spec, precision=args.precision, device=device).load_weights(w) for w in weights]
+    host = config_volume(args.config)
+    shape = host.shape[1:]
+    axes = cfg["mirror"]
+    views = 2 ** len(axes)
+    work = volume_work(shape, patch, 0.5, views, len(models))
+    volume = torch.from_numpy(host).to(device)
+
+    def step():
+        return predict_volume_sharded(models, volume, patch_size=patch, num_classes=spec.num_classes,
+                                      mirroring_axes=axes, step_fraction=0.5)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    kernels.PROFILE.reset()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kernels.PROFILE.enable(True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    kernels.PROFILE.enable(False)
+    barrier()
+    elapsed = start.elapsed_time(end) / 1e3
+    if world > 1:
+        t = torch.tensor([elapsed], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    status, where = _native.device_status(reset=True)
+    if status != 0:
+        raise SystemExit(f"device status {status} at wait site {where}")
+    value = work["voxels"] * args.steps / elapsed
+    prof = kernels.PROFILE.summary()
+
+    # end to end through the public API: pinned host volume in, host logits out
+    e2e = None
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(1, min(args.steps, 2))
+    if world == 1:
+        predictor = ArrayPredictor(models, patch_size=patch, num_outputs=spec.num_classes, mirroring_axes=axes)
+        pinned = torch.from_numpy(host).pin_memory()
+        predictor.predict_logits_from_preprocessed_data(pinned)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            out = predictor.predict_logits_from_preprocessed_data(pinned)
+        e2e_seconds = (time.perf_counter() - t0) / e2e_steps
+        e2e = {"value": work["voxels"] / e2e_seconds, "unit": "voxels/s",
+               "h2d_bytes_per_step": int(host.nbytes), "d2h_bytes_per_step": int(out.nbytes),
+               "api": "ArrayPredictor.predict_logits_from_preprocessed_data", "steps": e2e_steps}
+    else:
+        pinned = torch.from_numpy(host).pin_memory()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            vol = pinned.to(device, non_blocking=True)
+            z0, z1, logits, labels, invalid = predict_volume_sharded(
+                models, vol, patch_size=patch, num_classes=spec.num_classes, mirroring_axes=axes)
+            d2h = 0
+            if logits is not None:
+                d2h = logits.cpu().nbytes + labels.cpu().nbytes
+        torch.cuda.synchronize()
+        e2e_seconds = (time.perf_counter() - t0) / e2e_steps
+        t = torch.tensor([e2e_seconds], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_seconds = float(t.item())
+        e2e = {"value": work["voxels"] / e2e_seconds, "unit": "voxels/s",
+               "h2d_bytes_per_step": int(host.nbytes) * world, "d2h_bytes_per_step": int(d2h) * world,
+               "api": "distributed.predict_volume_sharded (pinned host volume per rank)", "steps": e2e_steps}
+
+    if rank == 0:
+        pk = peaks()
+        fwd = forward_flops(spec, patch)
+        conv = prof.get("conv3d_tc", {})
+        achieved = conv.get("flops", 0.0) / conv["seconds"] / 1e12 if conv.get("seconds") else 0.0
+        line = {
+            "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (split-TF32 tensor cores)"
+            if args.precision == "fp32" else "tf32",
+            "data": "synthetic",
+            "config": {"workload": f"config{args.config}", "volume": list(shape), "patch": list(patch),
+                       "step_fraction": 0.5, "mirror_views": views, "folds": len(models), "tiles": work["tiles"],
+                       "forwards": work["forwards"], "gflop_per_forward": fwd / 1e9,
+                       "l2": "inputs larger than L2 (activations >= 2 GB per layer)",
+                       "parallelism": f"tiles x folds sharded over {world} GPU(s)"},
+            "conv_tflops_effective": work["forwards"] * fwd * args.steps / elapsed / 1e12 / world,
+            "roofline": {"bound": "tensor", "kernel": "conv3d_tc_kernel", "achieved": achieved,
+                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / pk["bf16_tflops"] if achieved else None,
+                         "traffic": None, "peak_source": f"{pk['source']} dense bf16",
+                         "note": "achieved = algorithmic conv FLOPs / summed CUDA-event time of the tensor-core "
+                                 "conv launches; fp32 mode issues 3 TF32 MMAs per product and TF32 runs at half "
+                                 "the bf16 rate, so this mode's arithmetic ceiling is peak/6"},
+            "kernels": prof,
+            "clocks": clocks.summary(),
+            "gpu_launches": kernels.PROFILE.launches,
+            "e2e": e2e,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(spec, weights[0], patch, work["forwards"], work["voxels"])
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,189 @@
+/*
+ * nnb.h -- C ABI of the B200 (sm_100a) inference path for nnU-Net 3-D U-Nets.
+ *
+ * The reference (MedMLX/nnunet-mlx v0.9.0) runs this path through MLX ops and
+ * Metal kernels held in Python strings; its "FFI" is `mx.fast.metal_kernel`
+ * plus MLX's built-in `mx.conv3d` / `mx.matmul`.  Each entry point below
+ * replaces one of those call sites; the citation names the reference file and
+ * lines (paths relative to the reference project root).
+ *
+ * Conventions
+ *  - All pointers are device pointers owned by the caller (PyTorch tensors in
+ *    the Python host).  The library allocates no memory.
+ *  - `stream` is a `cudaStream_t` passed as `void*`; every call is
+ *    asynchronous on that stream.
+ *  - Every function returns 0 on success or a negative NNB_E* code;
+ *    nnb_last_error() returns a message for the calling thread's last error.
+ *  - Activations are channels-last float32 (B, D, H, W, C).  An activation
+ *    read by a convolution may be "lazy": the raw output of the previous
+ *    convolution plus per-(sample, channel) `scale`/`shift` from its instance
+ *    norm and a LeakyReLU flag.  Consumers apply y = act(x * scale + shift)
+ *    while loading and load 0 for zero-padding taps, so normalised
+ *    activations never make an extra round trip through HBM.
+ */
+#ifndef NNB_H
+#define NNB_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NNB_ABI_VERSION 1
+
+enum nnb_status {
+  NNB_OK = 0,
+  NNB_E_INVALID = -1,     /* bad argument (shape, pointer, alignment) */
+  NNB_E_UNSUPPORTED = -2, /* valid request outside the implemented envelope */
+  NNB_E_CUDA = -3,        /* a CUDA runtime call failed */
+  NNB_E_DEVICE = -4,      /* a device-side check failed (bounded wait expired, bad index) */
+  NNB_E_NONFINITE = -5    /* non-finite or non-positive normaliser found */
+};
+
+/* Arithmetic of the convolution contractions. */
+enum nnb_precision {
+  NNB_PREC_FP32 = 0,   /* split-TF32 (hi/lo, 3 products): float32-level accuracy */
+  NNB_PREC_TF32 = 1,   /* single-pass TF32 tensor cores (fast, looser bound)     */
+  NNB_PREC_SIMT = 2    /* plain float32 FMA on CUDA cores (any shape)            */
+};
+
+/* One channel segment of a convolution input (two segments = decoder concat). */
+typedef struct nnb_segment {
+  const float* data;   /* (B, D, H, W, channels) float32 */
+  const float* scale;  /* (B, channels) or NULL for identity */
+  const float* shift;  /* (B, channels), required when scale != NULL */
+  int32_t channels;
+  int32_t leaky;       /* 1: LeakyReLU(slope) after the affine */
+} nnb_segment;
+
+typedef struct nnb_conv3d_args {
+  int32_t batch;
+  int32_t in_dims[3];   /* D, H, W of every segment */
+  int32_t out_dims[3];
+  int32_t kernel[3];
+  int32_t stride[3];
+  int32_t pad[3];
+  int32_t num_segments; /* 1 or 2 */
+  nnb_segment seg[2];
+  float slope;          /* LeakyReLU negative slope used by lazy segments */
+  int32_t cout;
+  const float* weight;  /* converted layout (cout, kD, kH, kW, cin_total) */
+  const void* packed;   /* tensor-core weight image from nnb_conv3d_pack, or NULL */
+  const float* bias;    /* (cout) added to the output, or NULL */
+  float* out;           /* (B, oD, oH, oW, cout) */
+  float* partials;      /* (B, ceil(oD*oH*oW/128), cout, 2) per-tile (sum, M2), or NULL */
+  int32_t precision;    /* enum nnb_precision */
+} nnb_conv3d_args;
+
+/* Library identity. */
+int32_t nnb_abi_version(void);
+const char* nnb_last_error(void);
+
+/*
+ * First device-side error recorded by a kernel since the last reset (0 when
+ * none), e.g. a bounded mbarrier wait that expired; `where` receives the wait
+ * site.  Synchronises with the device.  No reference counterpart: the
+ * reference's Metal kernels have no device-side waits.
+ */
+int32_t nnb_device_status(int32_t* where, int32_t reset);
+
+/*
+ * 3-D convolution with padding, stride and up to two concatenated input
+ * segments, optional lazy instance-norm + LeakyReLU per segment, optional
+ * bias, and per-128-voxel-tile instance-norm partial statistics of the
+ * output.  Replaces `ConvNorm._conv_norm` -> `_unbiased_convolution`
+ * (`mx.conv3d`, and the split-K decoder concat) in
+ * src/nnunet_mlx/model/network.py:214-269,305-322 and the single-channel
+ * Metal kernel src/nnunet_mlx/kernels/metal_single_channel_conv.py:32-97.
+ */
+int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
+
+/* Bytes of the tensor-core weight image for (cout, kvol, cin_total, precision). */
+int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision);
+
+/*
+ * Build the tensor-core weight image (per N-tile, per K-step, hi/lo split,
+ * 128-byte swizzled K-major rows) from converted-layout weights.  Replaces the
+ * weight layout work MLX does inside `mx.conv3d` for
+ * src/nnunet_mlx/model/network.py:261-269.
+ */
+int32_t nnb_conv3d_pack(const float* weight, int32_t cout, int32_t kvol, int32_t cin_total,
+                        int32_t precision, void* packed, void* stream);
+
+/*
+ * Instance-norm statistics from per-tile (sum, M2) partials (Chan's parallel
+ * combination in float64) -> per-(sample, channel) scale = gamma*rsqrt(var+eps)
+ * and shift = beta - mean*scale.  Replaces the reduction passes of
+ * src/nnunet_mlx/kernels/metal_native_norm.py:32-60,92-153 (the affine pass
+ * 62-70,155-168 is applied lazily by consumers).
+ */
+int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t voxels,
+                                   int32_t channels, const float* gamma, const float* beta,
+                                   float eps, float* scale, float* shift, void* stream);
+
+/*
+ * Non-overlapping transposed convolution (kernel == stride) with lazy input
+ * segment and bias.  Replaces `NonOverlappingConvTranspose3d`
+ * src/nnunet_mlx/model/network.py:101-174.  weight: (cout, kD, kH, kW, cin).
+ */
+int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
+                             const int32_t kernel[3], float slope, const float* weight,
+                             const float* bias, int32_t cout, float* out, void* stream);
+
+/*
+ * Residual join of `ResidualBlock` / `BottleneckResidualBlock`:
+ * out = LeakyReLU(act(branch) + act(skip)) over (rows, channels), where act
+ * applies the segment's lazy affine.  Replaces
+ * src/nnunet_mlx/model/network.py:511-516,568-573.
+ */
+int32_t nnb_residual_join(const nnb_segment* branch, const nnb_segment* skip, int32_t batch,
+                          int64_t voxels, float slope, float* out, void* stream);
+
+/*
+ * Gather one tile of a channel-first (cin, Z, Y, X) volume at `offset` into a
+ * channels-last batch of `views` mirrored copies (B = views): view v is
+ * flipped along the axes whose bits are set in flip_masks[v].  Replaces the
+ * tile slicing and `mx.flip` + `mx.contiguous` of
+ * src/nnunet_mlx/prediction/sliding_window.py:408-411,517-518.
+ */
+int32_t nnb_gather_views(const float* volume, int32_t cin, const int32_t vol_dims[3],
+                         const int32_t offset[3], const int32_t patch[3], int32_t views,
+                         const int32_t* flip_masks, float* out, void* stream);
+
+/*
+ * Fused segmentation head + mirror flip-back + view average + Gaussian-weighted
+ * accumulation of one tile: for each tile voxel, logits_v = W . act(x_v[flip_v(p)]) + b
+ * for every view in order, pred = (sum_v logits_v) / views, and
+ * acc[offset + p] += pred * g[p]; normalizer[offset + p] += g[p] when
+ * add_normalizer != 0.  Replaces the seg head (network.py:875-876),
+ * `mirrored_prediction` (sliding_window.py:489-527) and the scatter-add of
+ * `_accumulate_logits` (sliding_window.py:435-436).
+ */
+int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                            const int32_t patch[3], float slope, const float* seg_weight,
+                            const float* seg_bias, int32_t classes, const float* gaussian,
+                            float* acc, float* normalizer, const int32_t acc_dims[3],
+                            const int32_t offset[3], int32_t add_normalizer, void* stream);
+
+/*
+ * Normalise accumulated logits and reduce them to labels over the crop
+ * window: q = (acc / normalizer) / fold_divisor; label = first argmax of q;
+ * writes channel-first float32 logits (classes, cD, cH, cW) when `logits` is
+ * non-NULL and labels (uint8 when label_bytes == 1, uint16 when 2) when
+ * `labels` is non-NULL.  A non-finite or non-positive normaliser or a
+ * non-finite quotient stores the invalid label (all ones) and sets
+ * *invalid_count.  Replaces src/nnunet_mlx/kernels/metal_normalized_labels.py:19-98
+ * and the finalize divide of sliding_window.py:169-176.
+ */
+int32_t nnb_normalize_labels(const float* acc, const float* normalizer, int32_t classes,
+                             const int32_t acc_dims[3], const int32_t crop_lo[3],
+                             const int32_t crop_dims[3], float fold_divisor, float* logits,
+                             void* labels, int32_t label_bytes, int32_t* invalid_count,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NNB_H */

@@ -1,0 +1,112 @@
+"""ctypes binding of the C ABI in ``include/nnb.h`` (library ``_nnb.so``).
+
+The shared library is built in-tree by ``nnunet_mlx_b200.build.build_extension``
+(``nvcc -gencode arch=compute_100a,code=sm_100a``).  There is no fallback: if
+the library is missing or the GPU is not an sm_100 device, every compute call
+raises ``ContractError``.  Nonzero C status codes become ``ContractError``
+carrying ``nnb_last_error()``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+from nnunet_mlx_b200.errors import ContractError
+
+LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
+ABI_VERSION = 1
+
+PREC_FP32 = 0   # split-TF32 hi/lo tensor cores, float32-level accuracy
+PREC_TF32 = 1   # single-pass TF32 tensor cores
+PREC_SIMT = 2   # CUDA-core float32
+
+STATUS = {0: "ok", -1: "invalid argument", -2: "unsupported", -3: "CUDA error", -4: "device check failed",
+          -5: "non-finite"}
+
+I32x3 = ctypes.c_int32 * 3
+
+
+class Segment(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("shift", ctypes.c_void_p),
+                ("channels", ctypes.c_int32), ("leaky", ctypes.c_int32)]
+
+
+class Conv3dArgs(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("in_dims", I32x3), ("out_dims", I32x3), ("kernel", I32x3),
+                ("stride", I32x3), ("pad", I32x3), ("num_segments", ctypes.c_int32), ("seg", Segment * 2),
+                ("slope", ctypes.c_float), ("cout", ctypes.c_int32), ("weight", ctypes.c_void_p),
+                ("packed", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),
+                ("partials", ctypes.c_void_p), ("precision", ctypes.c_int32)]
+
+
+SYMBOLS = {
+    "nnb_abi_version": (ctypes.c_int32, []),
+    "nnb_last_error": (ctypes.c_char_p, []),
+    "nnb_device_status": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
+    "nnb_conv3d": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs), ctypes.c_void_p]),
+    "nnb_conv3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
+    "nnb_conv3d_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_instance_norm_finalize": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                                    ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                                    ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
+                                                    ctypes.c_void_p]),
+    "nnb_conv_transpose3d": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, I32x3, I32x3,
+                                              ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                              ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_residual_join": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.POINTER(Segment), ctypes.c_int32,
+                                           ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_gather_views": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, I32x3, ctypes.c_int32,
+                                          ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_accumulate_tile": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32,
+                                             ctypes.POINTER(ctypes.c_int32), I32x3, ctypes.c_float,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_void_p, I32x3, I32x3, ctypes.c_int32,
+                                             ctypes.c_void_p]),
+    "nnb_normalize_labels": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3,
+                                              I32x3, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load ``_nnb.so`` once; raise ``ContractError`` if it is missing or mismatched."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("NNB_LIBRARY", LIB_PATH))
+    if not path.is_file():
+        raise ContractError(f"CUDA extension not built: {path} is missing "
+                            "(run nnunet_mlx_b200.build.build_extension())")
+    lib = ctypes.CDLL(str(path))
+    for name, (restype, argtypes) in SYMBOLS.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    if lib.nnb_abi_version() != ABI_VERSION:
+        raise ContractError("CUDA extension ABI version mismatch")
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        message = load().nnb_last_error().decode(errors="replace")
+        raise ContractError(f"{what} failed ({STATUS.get(status, status)}): {message}")
+
+
+def device_status(reset: bool = True) -> tuple[int, int]:
+    where = ctypes.c_int32(0)
+    status = load().nnb_device_status(ctypes.byref(where), 1 if reset else 0)
+    return int(status), int(where.value)
+
+
+def dims3(values) -> ctypes.Array:
+    values = tuple(int(v) for v in values)
+    if len(values) != 3:
+        raise ContractError(f"expected three spatial sizes, got {values}")
+    return I32x3(*values)

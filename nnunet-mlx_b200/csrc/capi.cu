@@ -1,0 +1,177 @@
+// extern "C" entry points declared in include/nnb.h: argument validation,
+// per-thread error messages and dispatch to the kernels.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace nnb {
+
+static thread_local char g_error[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+}
+
+// kernels implemented in the other translation units
+int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream);
+bool conv3d_tc_supported(const nnb_conv3d_args& a);
+int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream);
+int64_t conv3d_tc_packed_bytes(int cout, int kvol, int cin_total, int precision);
+int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int precision, void* packed,
+                       cudaStream_t stream);
+int launch_norm_finalize(const float* partials, int batch, int voxels, int channels, const float* gamma,
+                         const float* beta, float eps, float* scale, float* shift, cudaStream_t stream);
+int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
+                               float slope, const float* weight, const float* bias, int cout, float* out,
+                               cudaStream_t stream);
+int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch, int64_t voxels, float slope,
+                         float* out, cudaStream_t stream);
+int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const int32_t off[3],
+                        const int32_t patch[3], int views, const int32_t* masks, float* out, cudaStream_t stream);
+int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
+                           float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
+                           float* acc, float* normalizer, const int32_t ad[3], const int32_t off[3],
+                           int add_normalizer, cudaStream_t stream);
+int launch_normalize_labels(const float* acc, const float* normalizer, int classes, const int32_t ad[3],
+                            const int32_t lo[3], const int32_t cd[3], float fold_divisor, float* logits,
+                            void* labels, int label_bytes, int32_t* invalid_count, cudaStream_t stream);
+
+static int check_segment(const nnb_segment& s, const char* what) {
+  NNB_REQUIRE(s.data != nullptr, "%s: null data", what);
+  NNB_REQUIRE(s.channels >= 1, "%s: channels must be positive", what);
+  NNB_REQUIRE(s.scale == nullptr || s.shift != nullptr, "%s: scale without shift", what);
+  return NNB_OK;
+}
+
+static bool positive3(const int32_t d[3]) { return d[0] > 0 && d[1] > 0 && d[2] > 0; }
+
+}  // namespace nnb
+
+using namespace nnb;
+
+extern "C" {
+
+int32_t nnb_abi_version(void) { return NNB_ABI_VERSION; }
+
+const char* nnb_last_error(void) { return g_error; }
+
+int32_t nnb_conv3d(const nnb_conv3d_args* a, void* stream) {
+  NNB_REQUIRE(a != nullptr, "conv3d: null args");
+  NNB_REQUIRE(a->batch >= 1, "conv3d: batch must be positive");
+  NNB_REQUIRE(positive3(a->in_dims) && positive3(a->out_dims) && positive3(a->kernel) && positive3(a->stride),
+              "conv3d: dims, kernel and stride must be positive");
+  NNB_REQUIRE(a->num_segments == 1 || a->num_segments == 2, "conv3d: 1 or 2 input segments");
+  for (int s = 0; s < a->num_segments; ++s) {
+    int rc = check_segment(a->seg[s], "conv3d segment");
+    if (rc) return rc;
+  }
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(a->pad[i] >= 0, "conv3d: negative padding");
+    const int expect = (a->in_dims[i] + 2 * a->pad[i] - a->kernel[i]) / a->stride[i] + 1;
+    NNB_REQUIRE(a->out_dims[i] == expect, "conv3d: out_dims[%d]=%d, expected %d", i, a->out_dims[i], expect);
+  }
+  NNB_REQUIRE(a->cout >= 1 && a->weight != nullptr && a->out != nullptr, "conv3d: missing weight/output");
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (a->precision == NNB_PREC_SIMT) return launch_conv3d_simt(*a, st);
+  NNB_REQUIRE(a->precision == NNB_PREC_FP32 || a->precision == NNB_PREC_TF32, "conv3d: unknown precision %d",
+              a->precision);
+  if (a->packed != nullptr && conv3d_tc_supported(*a)) return launch_conv3d_tc(*a, st);
+  // Outside the tensor-core envelope (few input channels, odd channel counts)
+  // the CUDA-core kernel computes in plain float32, which also satisfies the
+  // requested accuracy.
+  return launch_conv3d_simt(*a, st);
+}
+
+int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision) {
+  return conv3d_tc_packed_bytes(cout, kvol, cin_total, precision);
+}
+
+int32_t nnb_conv3d_pack(const float* weight, int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision,
+                        void* packed, void* stream) {
+  NNB_REQUIRE(weight != nullptr && packed != nullptr, "conv3d_pack: null pointer");
+  NNB_REQUIRE(cout >= 1 && kvol >= 1 && cin_total >= 1, "conv3d_pack: bad shape");
+  return launch_conv3d_pack(weight, cout, kvol, cin_total, precision, packed, (cudaStream_t)stream);
+}
+
+int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t voxels, int32_t channels,
+                                   const float* gamma, const float* beta, float eps, float* scale, float* shift,
+                                   void* stream) {
+  NNB_REQUIRE(partials && scale && shift, "instance_norm_finalize: null pointer");
+  NNB_REQUIRE(batch >= 1 && voxels >= 1 && channels >= 1, "instance_norm_finalize: bad shape");
+  NNB_REQUIRE(eps > 0.f, "instance_norm_finalize: eps must be positive");
+  return launch_norm_finalize(partials, batch, voxels, channels, gamma, beta, eps, scale, shift,
+                              (cudaStream_t)stream);
+}
+
+int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
+                             const int32_t kernel[3], float slope, const float* weight, const float* bias,
+                             int32_t cout, float* out, void* stream) {
+  NNB_REQUIRE(input != nullptr, "conv_transpose3d: null input");
+  int rc = check_segment(*input, "conv_transpose3d input");
+  if (rc) return rc;
+  NNB_REQUIRE(batch >= 1 && positive3(in_dims) && positive3(kernel), "conv_transpose3d: bad shape");
+  NNB_REQUIRE(weight && out && cout >= 1, "conv_transpose3d: missing weight/output");
+  return launch_conv_transpose_simt(*input, batch, in_dims, kernel, slope, weight, bias, cout, out,
+                                    (cudaStream_t)stream);
+}
+
+int32_t nnb_residual_join(const nnb_segment* branch, const nnb_segment* skip, int32_t batch, int64_t voxels,
+                          float slope, float* out, void* stream) {
+  NNB_REQUIRE(branch && skip && out, "residual_join: null pointer");
+  int rc = check_segment(*branch, "residual branch");
+  if (rc) return rc;
+  rc = check_segment(*skip, "residual skip");
+  if (rc) return rc;
+  NNB_REQUIRE(branch->channels == skip->channels, "residual_join: channel mismatch");
+  NNB_REQUIRE(batch >= 1 && voxels >= 1, "residual_join: bad shape");
+  return launch_residual_join(*branch, *skip, batch, voxels, slope, out, (cudaStream_t)stream);
+}
+
+int32_t nnb_gather_views(const float* volume, int32_t cin, const int32_t vol_dims[3], const int32_t offset[3],
+                         const int32_t patch[3], int32_t views, const int32_t* flip_masks, float* out,
+                         void* stream) {
+  NNB_REQUIRE(volume && out && flip_masks && cin >= 1, "gather_views: bad arguments");
+  for (int i = 0; i < 3; ++i)
+    NNB_REQUIRE(offset[i] >= 0 && patch[i] >= 1 && offset[i] + patch[i] <= vol_dims[i],
+                "gather_views: tile [%d, %d) outside axis %d of size %d", offset[i], offset[i] + patch[i], i,
+                vol_dims[i]);
+  return launch_gather_views(volume, cin, vol_dims, offset, patch, views, flip_masks, out, (cudaStream_t)stream);
+}
+
+int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                            const int32_t patch[3], float slope, const float* seg_weight, const float* seg_bias,
+                            int32_t classes, const float* gaussian, float* acc, float* normalizer,
+                            const int32_t acc_dims[3], const int32_t offset[3], int32_t add_normalizer,
+                            void* stream) {
+  NNB_REQUIRE(features && flip_masks && seg_weight && seg_bias && gaussian && acc, "accumulate_tile: null pointer");
+  int rc = check_segment(*features, "accumulate features");
+  if (rc) return rc;
+  NNB_REQUIRE(classes >= 1, "accumulate_tile: classes must be positive");
+  NNB_REQUIRE(!add_normalizer || normalizer != nullptr, "accumulate_tile: missing normalizer");
+  for (int i = 0; i < 3; ++i)
+    NNB_REQUIRE(offset[i] >= 0 && patch[i] >= 1 && offset[i] + patch[i] <= acc_dims[i],
+                "accumulate_tile: tile outside accumulator on axis %d", i);
+  return launch_accumulate_tile(*features, views, flip_masks, patch, slope, seg_weight, seg_bias, classes, gaussian,
+                                acc, normalizer, acc_dims, offset, add_normalizer, (cudaStream_t)stream);
+}
+
+int32_t nnb_normalize_labels(const float* acc, const float* normalizer, int32_t classes, const int32_t acc_dims[3],
+                             const int32_t crop_lo[3], const int32_t crop_dims[3], float fold_divisor,
+                             float* logits, void* labels, int32_t label_bytes, int32_t* invalid_count,
+                             void* stream) {
+  NNB_REQUIRE(acc && normalizer && invalid_count && classes >= 1, "normalize_labels: bad arguments");
+  NNB_REQUIRE(fold_divisor > 0.f, "normalize_labels: fold_divisor must be positive");
+  for (int i = 0; i < 3; ++i)
+    NNB_REQUIRE(crop_lo[i] >= 0 && crop_dims[i] >= 1 && crop_lo[i] + crop_dims[i] <= acc_dims[i],
+                "normalize_labels: crop outside accumulator on axis %d", i);
+  return launch_normalize_labels(acc, normalizer, classes, acc_dims, crop_lo, crop_dims, fold_divisor, logits,
+                                 labels, label_bytes, invalid_count, (cudaStream_t)stream);
+}
+
+}  // extern "C"

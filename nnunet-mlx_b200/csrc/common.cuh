@@ -1,0 +1,76 @@
+// Shared helpers for the nnb CUDA sources: error reporting, lazy-activation
+// loads and the per-tile instance-norm partial statistics format.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/nnb.h"
+
+namespace nnb {
+
+// Rows (output voxels) per statistics tile.  Tiles never straddle samples:
+// tile t of sample b covers sample-local voxels [128 t, 128 t + 128).
+constexpr int kTileRows = 128;
+
+void set_error(const char* fmt, ...);
+
+#define NNB_REQUIRE(cond, ...)                 \
+  do {                                         \
+    if (!(cond)) {                             \
+      ::nnb::set_error(__VA_ARGS__);           \
+      return NNB_E_INVALID;                    \
+    }                                          \
+  } while (0)
+
+#define NNB_CUDA_CHECK(expr)                                                        \
+  do {                                                                              \
+    cudaError_t nnb_err_ = (expr);                                                  \
+    if (nnb_err_ != cudaSuccess) {                                                  \
+      ::nnb::set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(nnb_err_), \
+                       __FILE__, __LINE__);                                         \
+      return NNB_E_CUDA;                                                            \
+    }                                                                               \
+  } while (0)
+
+#define NNB_LAUNCH_CHECK()                                                          \
+  do {                                                                              \
+    cudaError_t nnb_err_ = cudaGetLastError();                                      \
+    if (nnb_err_ != cudaSuccess) {                                                  \
+      ::nnb::set_error("kernel launch failed: %s (%s:%d)", cudaGetErrorString(nnb_err_), \
+                       __FILE__, __LINE__);                                         \
+      return NNB_E_CUDA;                                                            \
+    }                                                                               \
+  } while (0)
+
+inline int tiles_per_sample(int64_t voxels) { return (int)((voxels + kTileRows - 1) / kTileRows); }
+
+__device__ __forceinline__ float leaky(float v, float slope) { return v >= 0.f ? v : v * slope; }
+
+// Apply a segment's lazy affine + activation to one raw value.
+__device__ __forceinline__ float activate(float raw, const float* scale, const float* shift,
+                                          int leaky_flag, float slope, int idx) {
+  if (scale == nullptr) return raw;
+  float v = fmaf(raw, __ldg(scale + idx), __ldg(shift + idx));
+  return leaky_flag ? leaky(v, slope) : v;
+}
+
+// Combine (count, mean, M2) triples (Chan et al. parallel variance).
+struct Moments {
+  double n, mean, m2;
+};
+
+__device__ __forceinline__ Moments merge(Moments a, Moments b) {
+  if (b.n == 0) return a;
+  if (a.n == 0) return b;
+  double n = a.n + b.n;
+  double delta = b.mean - a.mean;
+  Moments r;
+  r.n = n;
+  r.mean = a.mean + delta * (b.n / n);
+  r.m2 = a.m2 + b.m2 + delta * delta * (a.n * b.n / n);
+  return r;
+}
+
+}  // namespace nnb

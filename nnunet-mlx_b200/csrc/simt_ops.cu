@@ -1,0 +1,249 @@
+// CUDA-core kernels of the path: the any-shape float32 convolution (used for
+// the few-channel first layer and for shapes outside the tensor-core
+// envelope), the transposed convolution, instance-norm finalisation and the
+// residual join.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace nnb {
+
+// ---------------------------------------------------------------------------
+// Direct convolution: one thread per output voxel, CO output channels per
+// block column; lazy input activation; per-tile (sum, M2) of the output.
+// Reference semantics: `_unbiased_convolution` (network.py:240-269) with the
+// tap order of the single-channel kernel (metal_single_channel_conv.py:32-59).
+// ---------------------------------------------------------------------------
+template <int CO>
+__global__ void __launch_bounds__(kTileRows) conv3d_simt_kernel(nnb_conv3d_args a, int tps) {
+  __shared__ float red[kTileRows][CO + 1];
+  const int t = blockIdx.x % tps;
+  const int b = blockIdx.x / tps;
+  const int co0 = blockIdx.y * CO;
+  const int nco = min(CO, a.cout - co0);
+  const int r = threadIdx.x;
+  const int OD = a.out_dims[0], OH = a.out_dims[1], OW = a.out_dims[2];
+  const int ID = a.in_dims[0], IH = a.in_dims[1], IW = a.in_dims[2];
+  const int64_t ovox = (int64_t)OD * OH * OW;
+  const int64_t m = (int64_t)t * kTileRows + r;
+  const bool valid = m < ovox;
+  const int ox = (int)(m % OW), oy = (int)((m / OW) % OH), oz = (int)(m / ((int64_t)OW * OH));
+  const int kvol = a.kernel[0] * a.kernel[1] * a.kernel[2];
+  int cin_total = 0;
+  for (int s = 0; s < a.num_segments; ++s) cin_total += a.seg[s].channels;
+  const int64_t wstride = (int64_t)kvol * cin_total;  // distance between output channels
+
+  float acc[CO];
+#pragma unroll
+  for (int j = 0; j < CO; ++j) acc[j] = 0.f;
+
+  if (valid) {
+    int tap = 0;
+    for (int kz = 0; kz < a.kernel[0]; ++kz) {
+      const int iz = oz * a.stride[0] - a.pad[0] + kz;
+      for (int ky = 0; ky < a.kernel[1]; ++ky) {
+        const int iy = oy * a.stride[1] - a.pad[1] + ky;
+        for (int kx = 0; kx < a.kernel[2]; ++kx, ++tap) {
+          const int ix = ox * a.stride[2] - a.pad[2] + kx;
+          if (iz < 0 || iz >= ID || iy < 0 || iy >= IH || ix < 0 || ix >= IW) continue;
+          int cbase = 0;
+          for (int s = 0; s < a.num_segments; ++s) {
+            const nnb_segment seg = a.seg[s];
+            const float* src = seg.data + ((((int64_t)b * ID + iz) * IH + iy) * IW + ix) * seg.channels;
+            const float* wp = a.weight + (int64_t)co0 * wstride + (int64_t)tap * cin_total + cbase;
+            for (int ci = 0; ci < seg.channels; ++ci) {
+              const float v = activate(__ldg(src + ci), seg.scale, seg.shift, seg.leaky, a.slope,
+                                       b * seg.channels + ci);
+#pragma unroll
+              for (int j = 0; j < CO; ++j)
+                if (j < nco) acc[j] = fmaf(v, __ldg(wp + j * wstride + ci), acc[j]);
+            }
+            cbase += seg.channels;
+          }
+        }
+      }
+    }
+  }
+  if (a.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < CO; ++j)
+      if (j < nco) acc[j] += __ldg(a.bias + co0 + j);
+  }
+  if (valid) {
+    float* dst = a.out + ((int64_t)b * ovox + m) * a.cout + co0;
+#pragma unroll
+    for (int j = 0; j < CO; ++j)
+      if (j < nco) dst[j] = acc[j];
+  }
+  if (a.partials == nullptr) return;
+#pragma unroll
+  for (int j = 0; j < CO; ++j) red[r][j] = valid ? acc[j] : 0.f;
+  __syncthreads();
+  if (r < nco) {
+    const int rows = (int)min((int64_t)kTileRows, ovox - (int64_t)t * kTileRows);
+    float sum = 0.f;
+    for (int i = 0; i < rows; ++i) sum += red[i][r];
+    const float mean = sum / rows;
+    float m2 = 0.f;
+    for (int i = 0; i < rows; ++i) {
+      const float d = red[i][r] - mean;
+      m2 = fmaf(d, d, m2);
+    }
+    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 2;
+    p[0] = sum;
+    p[1] = m2;
+  }
+}
+
+int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
+  const int64_t ovox = (int64_t)a.out_dims[0] * a.out_dims[1] * a.out_dims[2];
+  const int tps = tiles_per_sample(ovox);
+  constexpr int CO = 16;
+  dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + CO - 1) / CO));
+  NNB_REQUIRE((int64_t)tps * a.batch < (1LL << 31), "conv3d: too many tiles");
+  conv3d_simt_kernel<CO><<<grid, kTileRows, 0, stream>>>(a, tps);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Instance-norm finalisation: one block per (channel, sample); each thread
+// merges its tiles' (n, mean, M2) in float64, then a tree merge.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restrict__ partials,
+                                                            int voxels, int channels, int tps,
+                                                            const float* __restrict__ gamma,
+                                                            const float* __restrict__ beta, float eps,
+                                                            float* __restrict__ scale,
+                                                            float* __restrict__ shift) {
+  __shared__ Moments sm[256];
+  const int c = blockIdx.x;
+  const int b = blockIdx.y;
+  Moments acc{0.0, 0.0, 0.0};
+  for (int t = threadIdx.x; t < tps; t += blockDim.x) {
+    const int n = min(kTileRows, voxels - t * kTileRows);
+    const float* p = partials + (((int64_t)b * tps + t) * channels + c) * 2;
+    Moments tile{(double)n, (double)p[0] / n, (double)p[1]};
+    acc = merge(acc, tile);
+  }
+  sm[threadIdx.x] = acc;
+  __syncthreads();
+  for (int stride = blockDim.x / 2; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride) sm[threadIdx.x] = merge(sm[threadIdx.x], sm[threadIdx.x + stride]);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const Moments tot = sm[0];
+    double var = tot.m2 / tot.n;
+    if (var < 0) var = 0;
+    const double inv = 1.0 / sqrt(var + (double)eps);
+    const double sc = gamma != nullptr ? (double)gamma[c] * inv : inv;
+    const double sh = (beta != nullptr ? (double)beta[c] : 0.0) - tot.mean * sc;
+    scale[(int64_t)b * channels + c] = (float)sc;
+    shift[(int64_t)b * channels + c] = (float)sh;
+  }
+}
+
+int launch_norm_finalize(const float* partials, int batch, int voxels, int channels, const float* gamma,
+                         const float* beta, float eps, float* scale, float* shift, cudaStream_t stream) {
+  const int tps = tiles_per_sample(voxels);
+  dim3 grid((unsigned)channels, (unsigned)batch);
+  norm_finalize_kernel<<<grid, 256, 0, stream>>>(partials, voxels, channels, tps, gamma, beta, eps, scale,
+                                                 shift);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Transposed convolution with kernel == stride (non-overlapping blocks):
+// one thread per output voxel and 32-channel output group.
+// Reference: NonOverlappingConvTranspose3d (network.py:139-174).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) conv_transpose_simt_kernel(nnb_segment in, int batch, int ID, int IH,
+                                                                  int IW, int KD, int KH, int KW, float slope,
+                                                                  const float* __restrict__ weight,
+                                                                  const float* __restrict__ bias, int cout,
+                                                                  float* __restrict__ out) {
+  const int OD = ID * KD, OH = IH * KH, OW = IW * KW;
+  const int64_t total = (int64_t)batch * OD * OH * OW;
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= total) return;
+  const int ox = (int)(o % OW), oy = (int)((o / OW) % OH), oz = (int)((o / ((int64_t)OW * OH)) % OD);
+  const int b = (int)(o / ((int64_t)OW * OH * OD));
+  const int ix = ox / KW, iy = oy / KH, iz = oz / KD;
+  const int tap = ((oz % KD) * KH + (oy % KH)) * KW + (ox % KW);
+  const int kvol = KD * KH * KW;
+  const int cin = in.channels;
+  const float* src = in.data + ((((int64_t)b * ID + iz) * IH + iy) * IW + ix) * cin;
+  const int co0 = blockIdx.y * 32;
+  const int nco = min(32, cout - co0);
+  float acc[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+  for (int ci = 0; ci < cin; ++ci) {
+    const float v = activate(__ldg(src + ci), in.scale, in.shift, in.leaky, slope, b * cin + ci);
+    const float* wp = weight + ((int64_t)co0 * kvol + tap) * cin + ci;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nco) acc[j] = fmaf(v, __ldg(wp + (int64_t)j * kvol * cin), acc[j]);
+  }
+  float* dst = out + o * cout + co0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nco) dst[j] = acc[j] + (bias != nullptr ? __ldg(bias + co0 + j) : 0.f);
+}
+
+int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
+                               float slope, const float* weight, const float* bias, int cout, float* out,
+                               cudaStream_t stream) {
+  const int64_t total = (int64_t)batch * in_dims[0] * k[0] * in_dims[1] * k[1] * in_dims[2] * k[2];
+  dim3 grid((unsigned)((total + 127) / 128), (unsigned)((cout + 31) / 32));
+  NNB_REQUIRE((total + 127) / 128 < (1LL << 31), "conv_transpose3d: output too large");
+  conv_transpose_simt_kernel<<<grid, 128, 0, stream>>>(in, batch, in_dims[0], in_dims[1], in_dims[2], k[0], k[1],
+                                                       k[2], slope, weight, bias, cout, out);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Residual join: out = LeakyReLU(act(branch) + act(skip)), float4 vectorised.
+// ---------------------------------------------------------------------------
+__global__ void residual_join_kernel(nnb_segment br, nnb_segment sk, int64_t per_sample, int channels,
+                                     int64_t total4, float slope, float* __restrict__ out) {
+  for (int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4;
+       i4 += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = i4 * 4;
+    const float4 x = __ldg(reinterpret_cast<const float4*>(br.data) + i4);
+    const float4 y = __ldg(reinterpret_cast<const float4*>(sk.data) + i4);
+    const float xs[4] = {x.x, x.y, x.z, x.w};
+    const float ys[4] = {y.x, y.y, y.z, y.w};
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t idx = i + e;
+      const int c = (int)(idx % channels);
+      const int b = (int)(idx / per_sample);
+      const float u = activate(xs[e], br.scale, br.shift, br.leaky, slope, b * channels + c);
+      const float w = activate(ys[e], sk.scale, sk.shift, sk.leaky, slope, b * channels + c);
+      r[e] = leaky(u + w, slope);
+    }
+    reinterpret_cast<float4*>(out)[i4] = make_float4(r[0], r[1], r[2], r[3]);
+  }
+}
+
+int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch, int64_t voxels, float slope,
+                         float* out, cudaStream_t stream) {
+  const int64_t per_sample = voxels * br.channels;
+  const int64_t total = per_sample * batch;
+  NNB_REQUIRE(total % 4 == 0, "residual_join: element count must be a multiple of 4");
+  const int64_t total4 = total / 4;
+  const int blocks = (int)std::min<int64_t>((total4 + 255) / 256, 148 * 16);
+  residual_join_kernel<<<blocks, 256, 0, stream>>>(br, sk, per_sample, br.channels, total4, slope, out);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+}  // namespace nnb

@@ -1,0 +1,198 @@
+// Sliding-window kernels: mirrored tile gather, fused segmentation head +
+// flip-back + Gaussian accumulation, and normalise + label reduction.
+// All three are HBM-bound streaming kernels.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace nnb {
+
+struct Dims3 {
+  int d[3];
+};
+
+// ---------------------------------------------------------------------------
+// (cin, Z, Y, X) volume tile at `off` -> (views, P0, P1, P2, cin) channels-last,
+// view v flipped along axis a when bit a of mask[v] is set.
+// Reference: tile slice + mx.flip (sliding_window.py:408-411,517-518).
+// ---------------------------------------------------------------------------
+// Up to 8 views (every subset of 3 mirroring axes); masks carried by value.
+struct ViewMasks {
+  int m[8];
+};
+
+__global__ void gather_views8_kernel(const float* __restrict__ vol, int cin, Dims3 vd, Dims3 off, Dims3 patch,
+                                     int views, ViewMasks masks, float* __restrict__ out) {
+  const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
+  const int64_t total = pvox * views;
+  const int64_t vstride = (int64_t)vd.d[0] * vd.d[1] * vd.d[2];
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int v = (int)(o / pvox);
+    const int64_t p = o - (int64_t)v * pvox;
+    const int k = (int)(p % patch.d[2]);
+    const int j = (int)((p / patch.d[2]) % patch.d[1]);
+    const int i = (int)(p / ((int64_t)patch.d[2] * patch.d[1]));
+    const int mask = masks.m[v];
+    const int si = (mask & 1) ? patch.d[0] - 1 - i : i;
+    const int sj = (mask & 2) ? patch.d[1] - 1 - j : j;
+    const int sk = (mask & 4) ? patch.d[2] - 1 - k : k;
+    const int64_t src = ((int64_t)(off.d[0] + si) * vd.d[1] + (off.d[1] + sj)) * vd.d[2] + (off.d[2] + sk);
+    float* dst = out + o * cin;
+    for (int c = 0; c < cin; ++c) dst[c] = __ldg(vol + (int64_t)c * vstride + src);
+  }
+}
+
+int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const int32_t off[3],
+                        const int32_t patch[3], int views, const int32_t* masks, float* out, cudaStream_t stream) {
+  NNB_REQUIRE(views >= 1 && views <= 8, "gather_views: 1..8 views supported, got %d", views);
+  ViewMasks vm{};
+  for (int v = 0; v < views; ++v) {
+    NNB_REQUIRE(masks[v] >= 0 && masks[v] < 8, "gather_views: bad flip mask");
+    vm.m[v] = masks[v];
+  }
+  Dims3 dvd{{vd[0], vd[1], vd[2]}}, doff{{off[0], off[1], off[2]}}, dp{{patch[0], patch[1], patch[2]}};
+  const int64_t total = (int64_t)patch[0] * patch[1] * patch[2] * views;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  gather_views8_kernel<<<blocks, 256, 0, stream>>>(vol, cin, dvd, doff, dp, views, vm, out);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Fused seg head + flip-back + view mean + Gaussian accumulation (one tile).
+// features: (views, P0, P1, P2, F) lazy; seg_w: (C, F); acc: (AD, AH, AW, C).
+// Per voxel and class chunk of CC classes, views are added in order.
+// ---------------------------------------------------------------------------
+template <int CC>
+__global__ void __launch_bounds__(256) accumulate_tile_kernel(
+    nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
+    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, float* __restrict__ acc,
+    float* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+  const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
+  const int F = feat.channels;
+  const float inv_views = 1.0f / (float)views;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pvox;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(p % patch.d[2]);
+    const int j = (int)((p / patch.d[2]) % patch.d[1]);
+    const int i = (int)(p / ((int64_t)patch.d[2] * patch.d[1]));
+    const float g = __ldg(gauss + p);
+    const int64_t dst = ((int64_t)(off.d[0] + i) * ad.d[1] + (off.d[1] + j)) * ad.d[2] + (off.d[2] + k);
+    for (int c0 = 0; c0 < classes; c0 += CC) {
+      float pred[CC];
+#pragma unroll
+      for (int c = 0; c < CC; ++c) pred[c] = 0.f;
+      for (int v = 0; v < views; ++v) {
+        const int mask = masks.m[v];
+        const int si = (mask & 1) ? patch.d[0] - 1 - i : i;
+        const int sj = (mask & 2) ? patch.d[1] - 1 - j : j;
+        const int sk = (mask & 4) ? patch.d[2] - 1 - k : k;
+        const int64_t q = (((int64_t)v * patch.d[0] + si) * patch.d[1] + sj) * patch.d[2] + sk;
+        const float* src = feat.data + q * F;
+        float logit[CC];
+#pragma unroll
+        for (int c = 0; c < CC; ++c) logit[c] = 0.f;
+        for (int f = 0; f < F; ++f) {
+          const float z = activate(__ldg(src + f), feat.scale, feat.shift, feat.leaky, slope, v * F + f);
+#pragma unroll
+          for (int c = 0; c < CC; ++c)
+            if (c0 + c < classes) logit[c] = fmaf(z, __ldg(seg_w + (int64_t)(c0 + c) * F + f), logit[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < CC; ++c)
+          if (c0 + c < classes) pred[c] += logit[c] + __ldg(seg_b + c0 + c);
+      }
+#pragma unroll
+      for (int c = 0; c < CC; ++c)
+        if (c0 + c < classes) {
+          float* a = acc + dst * classes + c0 + c;
+          *a += (pred[c] * inv_views) * g;
+        }
+    }
+    if (add_normalizer) normalizer[dst] += g;
+  }
+}
+
+int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
+                           float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
+                           float* acc, float* normalizer, const int32_t ad[3], const int32_t off[3],
+                           int add_normalizer, cudaStream_t stream) {
+  NNB_REQUIRE(views >= 1 && views <= 8, "accumulate_tile: 1..8 views supported");
+  ViewMasks vm{};
+  for (int v = 0; v < views; ++v) vm.m[v] = masks[v];
+  Dims3 dp{{patch[0], patch[1], patch[2]}}, dad{{ad[0], ad[1], ad[2]}}, doff{{off[0], off[1], off[2]}};
+  const int64_t pvox = (int64_t)patch[0] * patch[1] * patch[2];
+  const int blocks = (int)std::min<int64_t>((pvox + 255) / 256, 148 * 16);
+  accumulate_tile_kernel<4><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss,
+                                                        acc, normalizer, dad, doff, add_normalizer);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Normalise + first-argmax labels + channel-first logits over the crop.
+// Reference: metal_normalized_labels.py:19-40 (first max, invalid flag).
+// ---------------------------------------------------------------------------
+template <typename LabelT>
+__global__ void normalize_labels_kernel(const float* __restrict__ acc, const float* __restrict__ normalizer,
+                                        int classes, Dims3 ad, Dims3 lo, Dims3 cd, float fold_divisor,
+                                        float* __restrict__ logits, LabelT* __restrict__ labels,
+                                        int* __restrict__ invalid_count, LabelT invalid_label) {
+  const int64_t total = (int64_t)cd.d[0] * cd.d[1] * cd.d[2];
+  int local_invalid = 0;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int x = (int)(o % cd.d[2]);
+    const int y = (int)((o / cd.d[2]) % cd.d[1]);
+    const int z = (int)(o / ((int64_t)cd.d[2] * cd.d[1]));
+    const int64_t src = ((int64_t)(lo.d[0] + z) * ad.d[1] + (lo.d[1] + y)) * ad.d[2] + (lo.d[2] + x);
+    const float den = __ldg(normalizer + src);
+    bool invalid = !isfinite(den) || den <= 0.f;
+    float best = -INFINITY;
+    int winner = 0;
+    bool have = false;
+    for (int c = 0; c < classes; ++c) {
+      float q = __ldg(acc + src * classes + c) / den;
+      if (fold_divisor != 1.0f) q = q / fold_divisor;
+      invalid |= !isfinite(q);
+      if (logits != nullptr) logits[(int64_t)c * total + o] = q;
+      if (!have || q > best) {
+        best = q;
+        winner = c;
+        have = true;
+      }
+    }
+    if (labels != nullptr) labels[o] = invalid ? invalid_label : (LabelT)winner;
+    local_invalid += invalid ? 1 : 0;
+  }
+  if (local_invalid) atomicAdd(invalid_count, local_invalid);
+}
+
+int launch_normalize_labels(const float* acc, const float* normalizer, int classes, const int32_t ad[3],
+                            const int32_t lo[3], const int32_t cd[3], float fold_divisor, float* logits,
+                            void* labels, int label_bytes, int32_t* invalid_count, cudaStream_t stream) {
+  Dims3 dad{{ad[0], ad[1], ad[2]}}, dlo{{lo[0], lo[1], lo[2]}}, dcd{{cd[0], cd[1], cd[2]}};
+  const int64_t total = (int64_t)cd[0] * cd[1] * cd[2];
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  NNB_CUDA_CHECK(cudaMemsetAsync(invalid_count, 0, sizeof(int32_t), stream));
+  if (label_bytes == 1) {
+    NNB_REQUIRE(classes <= 255, "normalize_labels: uint8 labels need <= 255 classes");
+    normalize_labels_kernel<uint8_t><<<blocks, 256, 0, stream>>>(acc, normalizer, classes, dad, dlo, dcd,
+                                                                 fold_divisor, logits, (uint8_t*)labels,
+                                                                 invalid_count, (uint8_t)0xFF);
+  } else {
+    NNB_REQUIRE(label_bytes == 2, "normalize_labels: label_bytes must be 1 or 2");
+    NNB_REQUIRE(classes <= 65535, "normalize_labels: too many classes for uint16 labels");
+    normalize_labels_kernel<uint16_t><<<blocks, 256, 0, stream>>>(acc, normalizer, classes, dad, dlo, dcd,
+                                                                  fold_divisor, logits, (uint16_t*)labels,
+                                                                  invalid_count, (uint16_t)0xFFFF);
+  }
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+}  // namespace nnb

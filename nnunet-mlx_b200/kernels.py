@@ -1,0 +1,307 @@
+"""Torch-tensor wrappers around the C ABI: the device operations of the inference path.
+
+PyTorch only owns device memory and provides the current stream; every
+operation here is one call into ``_nnb.so``.  Tensors must be contiguous
+float32 CUDA tensors (channels-last activations ``(B, D, H, W, C)``).
+
+Reference counterparts: ``instance_norm`` (reference
+``kernels/metal_native_norm.py:92-168``), ``single_channel_conv3d``
+(``kernels/metal_single_channel_conv.py:75-97``) and ``normalized_labels``
+(``kernels/metal_normalized_labels.py:57-98``), plus the MLX ``conv3d`` /
+``matmul`` calls of ``model/network.py``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from nnunet_mlx_b200 import _native
+from nnunet_mlx_b200.errors import ContractError
+
+TILE_ROWS = 128
+
+
+class _Profile:
+    """Optional CUDA-event timing of every device call (used by ``bench.py`` over its timed region).
+
+    When enabled, each wrapper records an event pair on the current stream and
+    the algorithmic FLOPs / bytes of the call; ``launches`` counts kernel
+    launches of this library.
+    """
+
+    def __init__(self) -> None:
+        self.active = False
+        self.reset()
+
+    def reset(self) -> None:
+        self.records = []
+        self.launches = 0
+
+    def enable(self, on: bool) -> None:
+        self.active = on
+
+    def start(self, name: str, flops: float = 0.0, nbytes: float = 0.0, launches: int = 1):
+        if not self.active:
+            return None
+        event = torch.cuda.Event(enable_timing=True)
+        event.record()
+        return name, event, flops, nbytes, launches
+
+    def stop(self, token) -> None:
+        if token is None:
+            return
+        event = torch.cuda.Event(enable_timing=True)
+        event.record()
+        self.records.append((token, event))
+        self.launches += token[4]
+
+    def summary(self) -> dict:
+        out: dict[str, dict] = {}
+        for (name, e0, flops, nbytes, _), e1 in self.records:
+            item = out.setdefault(name, {"calls": 0, "seconds": 0.0, "flops": 0.0, "bytes": 0.0})
+            item["calls"] += 1
+            item["seconds"] += e0.elapsed_time(e1) / 1e3
+            item["flops"] += flops
+            item["bytes"] += nbytes
+        total = sum(v["seconds"] for v in out.values()) or 1.0
+        for item in out.values():
+            item["share"] = item["seconds"] / total
+        return out
+
+
+PROFILE = _Profile()
+
+
+@dataclass(frozen=True)
+class Lazy:
+    """An activation as stored: raw values plus the pending instance-norm affine.
+
+    ``value = act(raw * scale[b, c] + shift[b, c])`` where ``act`` is LeakyReLU
+    when ``leaky`` is set; ``scale is None`` means the raw tensor is final.
+    """
+
+    raw: torch.Tensor
+    scale: torch.Tensor | None = None
+    shift: torch.Tensor | None = None
+    leaky: bool = False
+
+    @property
+    def channels(self) -> int:
+        return int(self.raw.shape[-1])
+
+    @property
+    def spatial(self) -> tuple[int, int, int]:
+        return tuple(int(s) for s in self.raw.shape[1:4])
+
+    def segment(self) -> _native.Segment:
+        _check_tensor(self.raw, "activation")
+        if self.scale is not None:
+            _check_tensor(self.scale, "scale")
+            _check_tensor(self.shift, "shift")
+        return _native.Segment(self.raw.data_ptr(),
+                               0 if self.scale is None else self.scale.data_ptr(),
+                               0 if self.shift is None else self.shift.data_ptr(),
+                               self.channels, 1 if self.leaky else 0)
+
+
+def _check_tensor(t: torch.Tensor | None, name: str) -> None:
+    if t is None or not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+        raise ContractError(f"{name} must be a contiguous float32 CUDA tensor")
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def tiles_per_sample(voxels: int) -> int:
+    return (voxels + TILE_ROWS - 1) // TILE_ROWS
+
+
+def packed_bytes(cout: int, kvol: int, cin: int, precision: int) -> int:
+    return int(_native.load().nnb_conv3d_packed_bytes(cout, kvol, cin, precision))
+
+
+def pack_weights(weight: torch.Tensor, precision: int) -> torch.Tensor | None:
+    """Tensor-core weight image of a converted-layout ``(C_out, kD, kH, kW, C_in)`` weight.
+
+    Returns ``None`` when the layer is outside the tensor-core envelope (it
+    then runs on the CUDA-core kernel).
+    """
+    if precision not in (_native.PREC_FP32, _native.PREC_TF32):
+        return None
+    _check_tensor(weight, "weight")
+    cout, cin = int(weight.shape[0]), int(weight.shape[-1])
+    kvol = int(math.prod(weight.shape[1:-1]))
+    nbytes = packed_bytes(cout, kvol, cin, precision)
+    if nbytes <= 0 or cout % 16 != 0:
+        return None
+    # over-allocate so the image can start on a 1024-byte boundary
+    storage = torch.empty(nbytes + 1024, dtype=torch.uint8, device=weight.device)
+    offset = (-storage.data_ptr()) % 1024
+    image = storage[offset:offset + nbytes]
+    _native.check(_native.load().nnb_conv3d_pack(weight.data_ptr(), cout, kvol, cin, precision,
+                                                 image.data_ptr(), _stream()), "conv3d_pack")
+    return image
+
+
+def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cout: int,
+           packed: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+           precision: int = _native.PREC_FP32, slope: float = 0.01, stats: bool = True):
+    """Convolution of the channel concatenation of ``inputs``; returns ``(out, partials)``."""
+    if not 1 <= len(inputs) <= 2:
+        raise ContractError("conv3d takes one or two input segments")
+    first = inputs[0]
+    batch = int(first.raw.shape[0])
+    in_dims = first.spatial
+    for item in inputs[1:]:
+        if item.spatial != in_dims or int(item.raw.shape[0]) != batch:
+            raise ContractError("concatenated convolution inputs must share batch and spatial shape")
+    out_dims = tuple((i + 2 * p - k) // s + 1 for i, p, k, s in zip(in_dims, pad, kernel, stride))
+    if min(out_dims) < 1:
+        raise ContractError(f"convolution output would be empty for input {in_dims}")
+    device = first.raw.device
+    out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=device)
+    partials = None
+    if stats:
+        tps = tiles_per_sample(math.prod(out_dims))
+        partials = torch.empty((batch, tps, cout, 2), dtype=torch.float32, device=device)
+    args = _native.Conv3dArgs()
+    args.batch = batch
+    args.in_dims = _native.dims3(in_dims)
+    args.out_dims = _native.dims3(out_dims)
+    args.kernel = _native.dims3(kernel)
+    args.stride = _native.dims3(stride)
+    args.pad = _native.dims3(pad)
+    args.num_segments = len(inputs)
+    for index, item in enumerate(inputs):
+        args.seg[index] = item.segment()
+    args.slope = float(slope)
+    args.cout = int(cout)
+    _check_tensor(weight, "weight")
+    args.weight = weight.data_ptr()
+    args.packed = _ptr(packed)
+    args.bias = _ptr(bias)
+    args.out = out.data_ptr()
+    args.partials = _ptr(partials)
+    args.precision = int(precision)
+    cin = sum(item.channels for item in inputs)
+    tensor_cores = (packed is not None and precision in (_native.PREC_FP32, _native.PREC_TF32)
+                    and all(item.channels % 32 == 0 for item in inputs) and cout % 16 == 0)
+    flops = 2.0 * batch * math.prod(out_dims) * cout * cin * math.prod(kernel)
+    token = PROFILE.start("conv3d_tc" if tensor_cores else "conv3d_simt", flops,
+                          4.0 * (out.numel() + sum(item.raw.numel() for item in inputs)))
+    _native.check(_native.load().nnb_conv3d(ctypes.byref(args), _stream()), "conv3d")
+    PROFILE.stop(token)
+    return out, partials
+
+
+def instance_norm_finalize(partials: torch.Tensor, voxels: int, gamma: torch.Tensor | None,
+                           beta: torch.Tensor | None, eps: float):
+    batch, _, channels, _ = partials.shape
+    scale = torch.empty((batch, channels), dtype=torch.float32, device=partials.device)
+    shift = torch.empty_like(scale)
+    token = PROFILE.start("instance_norm_finalize", 0.0, partials.numel() * 4.0)
+    _native.check(_native.load().nnb_instance_norm_finalize(
+        partials.data_ptr(), batch, voxels, channels, _ptr(gamma), _ptr(beta), float(eps),
+        scale.data_ptr(), shift.data_ptr(), _stream()), "instance_norm_finalize")
+    PROFILE.stop(token)
+    return scale, shift
+
+
+def conv_transpose3d(x: Lazy, weight: torch.Tensor, bias: torch.Tensor | None, kernel,
+                     slope: float = 0.01) -> torch.Tensor:
+    batch = int(x.raw.shape[0])
+    cout = int(weight.shape[0])
+    out_dims = tuple(s * k for s, k in zip(x.spatial, kernel))
+    out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=x.raw.device)
+    seg = x.segment()
+    _check_tensor(weight, "weight")
+    token = PROFILE.start("conv_transpose3d", 2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()))
+    _native.check(_native.load().nnb_conv_transpose3d(
+        ctypes.byref(seg), batch, _native.dims3(x.spatial), _native.dims3(kernel), float(slope),
+        weight.data_ptr(), _ptr(bias), cout, out.data_ptr(), _stream()), "conv_transpose3d")
+    PROFILE.stop(token)
+    return out
+
+
+def residual_join(branch: Lazy, skip: Lazy, slope: float) -> torch.Tensor:
+    if branch.raw.shape != skip.raw.shape:
+        raise ContractError(f"residual shapes differ: {tuple(branch.raw.shape)} vs {tuple(skip.raw.shape)}")
+    out = torch.empty_like(branch.raw)
+    b, s = branch.segment(), skip.segment()
+    voxels = math.prod(branch.spatial)
+    token = PROFILE.start("residual_join", 0.0, 12.0 * out.numel())
+    _native.check(_native.load().nnb_residual_join(ctypes.byref(b), ctypes.byref(s), int(branch.raw.shape[0]),
+                                                   voxels, float(slope), out.data_ptr(), _stream()),
+                  "residual_join")
+    PROFILE.stop(token)
+    return out
+
+
+def gather_views(volume: torch.Tensor, offset, patch, masks: list[int], out: torch.Tensor | None = None):
+    """(C, Z, Y, X) volume -> (views, *patch, C) mirrored channels-last tile batch."""
+    _check_tensor(volume, "volume")
+    cin = int(volume.shape[0])
+    if out is None:
+        out = torch.empty((len(masks), *patch, cin), dtype=torch.float32, device=volume.device)
+    mask_arr = (ctypes.c_int32 * len(masks))(*masks)
+    token = PROFILE.start("gather_views", 0.0, 8.0 * out.numel())
+    _native.check(_native.load().nnb_gather_views(
+        volume.data_ptr(), cin, _native.dims3(volume.shape[1:]), _native.dims3(offset), _native.dims3(patch),
+        len(masks), mask_arr, out.data_ptr(), _stream()), "gather_views")
+    PROFILE.stop(token)
+    return out
+
+
+def accumulate_tile(features: Lazy, masks: list[int], seg_weight: torch.Tensor, seg_bias: torch.Tensor,
+                    gaussian: torch.Tensor, acc: torch.Tensor, normalizer: torch.Tensor, offset,
+                    add_normalizer: bool, slope: float) -> None:
+    seg = features.segment()
+    mask_arr = (ctypes.c_int32 * len(masks))(*masks)
+    _check_tensor(acc, "accumulator")
+    classes = int(seg_weight.shape[0])
+    pvox = math.prod(features.spatial)
+    token = PROFILE.start("accumulate_tile", 2.0 * features.raw.numel() * classes,
+                          4.0 * (features.raw.numel() + pvox * (2 * classes + 3)))
+    _native.check(_native.load().nnb_accumulate_tile(
+        ctypes.byref(seg), len(masks), mask_arr, _native.dims3(features.spatial), float(slope),
+        seg_weight.data_ptr(), seg_bias.data_ptr(), int(seg_weight.shape[0]), gaussian.data_ptr(),
+        acc.data_ptr(), normalizer.data_ptr(), _native.dims3(acc.shape[:3]), _native.dims3(offset),
+        1 if add_normalizer else 0, _stream()), "accumulate_tile")
+    PROFILE.stop(token)
+
+
+def normalize_labels(acc: torch.Tensor, normalizer: torch.Tensor, crop_lo, crop_dims, *, fold_divisor: float = 1.0,
+                     want_logits: bool = True, label_dtype: torch.dtype | None = torch.uint8):
+    """Normalised channel-first logits ``(C, *crop)`` and labels ``(*crop)``; invalid count tensor."""
+    classes = int(acc.shape[-1])
+    device = acc.device
+    logits = torch.empty((classes, *crop_dims), dtype=torch.float32, device=device) if want_logits else None
+    labels = None
+    label_bytes = 1
+    if label_dtype is not None:
+        if label_dtype == torch.uint8:
+            label_bytes = 1
+        elif label_dtype in (torch.uint16, torch.int16):
+            label_bytes = 2
+        else:
+            raise ContractError("labels must be uint8 or uint16")
+        labels = torch.empty(tuple(crop_dims), dtype=label_dtype, device=device)
+    invalid = torch.zeros((1,), dtype=torch.int32, device=device)
+    voxels = math.prod(crop_dims)
+    token = PROFILE.start("normalize_labels", 0.0, 4.0 * voxels * (2 * classes + 1) + voxels * label_bytes,
+                          launches=2)
+    _native.check(_native.load().nnb_normalize_labels(
+        acc.data_ptr(), normalizer.data_ptr(), classes, _native.dims3(acc.shape[:3]), _native.dims3(crop_lo),
+        _native.dims3(crop_dims), float(fold_divisor), _ptr(logits), _ptr(labels), label_bytes,
+        invalid.data_ptr(), _stream()), "normalize_labels")
+    PROFILE.stop(token)
+    return logits, labels, invalid

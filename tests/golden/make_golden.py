@@ -1,0 +1,207 @@
+"""Generate the golden vectors under ``tests/golden`` from the reference's own code.
+
+Run in a container where the reference checkout is available::
+
+    python tests/golden/make_golden.py /path/to/nnunet-mlx
+
+It imports only the reference's pure-host helpers, which run without MLX:
+
+* ``nnunet_mlx.prediction.sliding_window.compute_steps`` (reference 32-67),
+  ``gaussian_importance`` (70-93) and ``nnunet_fp16_gaussian`` (96-113);
+* ``nnunet_mlx.storage.weights.map_key_and_layout`` / ``convert_state_dict``
+  (reference 48-182) applied to upstream-style state-dict keys;
+* ``nnunet_mlx.prediction.inference.logits_to_probabilities`` /
+  ``probabilities_to_segmentation`` (reference 210-269).
+
+It also copies the reference's recorded upstream vectors from
+``tests/fixtures/darwin-arm64/upstream_runner.npz`` (head conversion arrays and
+float16 fold-rounding probes).  Outputs: ``geometry.json``, ``gaussian.npz``,
+``weights_map.json``, ``upstream_runner_subset.npz``.  Nothing at test time
+reads the reference checkout.
+"""
+
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+# Geometry cases: the BASELINE volumes (z padded to the patch where smaller),
+# the reference tests' small shapes and odd edge cases.
+STEP_CASES = [
+    ((128, 128, 128), (128, 128, 128), 0.5),
+    ((128, 768, 768), (128, 128, 128), 0.5),
+    ((155, 240, 240), (128, 128, 128), 0.5),
+    ((284, 400, 400), (128, 128, 128), 0.5),
+    ((17, 33, 49), (16, 32, 32), 0.5),
+    ((4, 4, 4), (4, 4, 4), 0.5),
+    ((5, 6, 7), (4, 4, 4), 0.5),
+    ((9, 10, 11), (4, 4, 4), 0.5),
+    ((200, 123, 77), (64, 48, 32), 0.33),
+    ((300, 300, 300), (96, 160, 160), 1.0),
+    ((129, 130, 131), (128, 64, 32), 0.25),
+    ((101, 257), (80, 96), 0.5),
+]
+
+GAUSSIAN_FULL = [(4, 4, 4), (5, 6, 7), (16, 32, 32), (4, 5), (7, 9)]
+GAUSSIAN_SUMMARY = [(128, 128, 128), (96, 160, 160), (80, 192, 160)]
+FP16_GAUSSIAN = [(4, 4, 4), (16, 32, 32), (8, 8, 8)]
+
+
+def _upstream_plain_keys(stages: int, enc_convs, dec_convs, cin, feats, classes, k=3):
+    """Upstream dynamic-network-architectures PlainConvUNet state-dict shapes."""
+    shapes: dict[str, tuple[int, ...]] = {}
+    ch = cin
+    for s in range(stages):
+        for c in range(enc_convs[s]):
+            ci = ch if c == 0 else feats[s]
+            p = f"encoder.stages.{s}.0.convs.{c}"
+            shapes[f"{p}.conv.weight"] = (feats[s], ci, k, k, k)
+            shapes[f"{p}.conv.bias"] = (feats[s],)
+            shapes[f"{p}.norm.weight"] = (feats[s],)
+            shapes[f"{p}.norm.bias"] = (feats[s],)
+            shapes[f"{p}.all_modules.0.weight"] = (feats[s], ci, k, k, k)
+        ch = feats[s]
+    for d in range(stages - 1):
+        below, skip = feats[stages - 1 - d], feats[stages - 2 - d]
+        shapes[f"decoder.transpconvs.{d}.weight"] = (below, skip, 2, 2, 2)
+        shapes[f"decoder.transpconvs.{d}.bias"] = (skip,)
+        for c in range(dec_convs[d]):
+            ci = 2 * skip if c == 0 else skip
+            p = f"decoder.stages.{d}.convs.{c}"
+            shapes[f"{p}.conv.weight"] = (skip, ci, k, k, k)
+            shapes[f"{p}.conv.bias"] = (skip,)
+            shapes[f"{p}.norm.weight"] = (skip,)
+            shapes[f"{p}.norm.bias"] = (skip,)
+        shapes[f"decoder.seg_layers.{d}.weight"] = (classes, skip, 1, 1, 1)
+        shapes[f"decoder.seg_layers.{d}.bias"] = (classes,)
+        shapes[f"decoder.encoder.stages.0.0.convs.0.conv.weight"] = (feats[0], cin, k, k, k)
+    return shapes
+
+
+def _upstream_residual_keys(cin, feats, blocks, classes, k=3):
+    shapes: dict[str, tuple[int, ...]] = {}
+    stem = feats[0]
+    shapes["encoder.stem.convs.0.conv.weight"] = (stem, cin, k, k, k)
+    shapes["encoder.stem.convs.0.conv.bias"] = (stem,)
+    shapes["encoder.stem.convs.0.norm.weight"] = (stem,)
+    shapes["encoder.stem.convs.0.norm.bias"] = (stem,)
+    ch = stem
+    for s, f in enumerate(feats):
+        for b in range(blocks[s]):
+            ci = ch if b == 0 else f
+            p = f"encoder.stages.{s}.blocks.{b}"
+            shapes[f"{p}.conv1.conv.weight"] = (f, ci, k, k, k)
+            shapes[f"{p}.conv1.conv.bias"] = (f,)
+            shapes[f"{p}.conv1.norm.weight"] = (f,)
+            shapes[f"{p}.conv1.norm.bias"] = (f,)
+            shapes[f"{p}.conv2.conv.weight"] = (f, f, k, k, k)
+            shapes[f"{p}.conv2.conv.bias"] = (f,)
+            shapes[f"{p}.conv2.norm.weight"] = (f,)
+            shapes[f"{p}.conv2.norm.bias"] = (f,)
+            if b == 0 and ci != f:
+                shapes[f"{p}.skip.1.conv.weight"] = (f, ci, 1, 1, 1)
+                shapes[f"{p}.skip.1.norm.weight"] = (f,)
+                shapes[f"{p}.skip.1.norm.bias"] = (f,)
+        ch = f
+    for d in range(len(feats) - 1):
+        below, skip = feats[len(feats) - 1 - d], feats[len(feats) - 2 - d]
+        shapes[f"decoder.transpconvs.{d}.weight"] = (below, skip, 2, 2, 2)
+        shapes[f"decoder.transpconvs.{d}.bias"] = (skip,)
+        p = f"decoder.stages.{d}.convs.0"
+        shapes[f"{p}.conv.weight"] = (skip, 2 * skip, k, k, k)
+        shapes[f"{p}.conv.bias"] = (skip,)
+        shapes[f"{p}.norm.weight"] = (skip,)
+        shapes[f"{p}.norm.bias"] = (skip,)
+        shapes[f"decoder.seg_layers.{d}.weight"] = (classes, skip, 1, 1, 1)
+        shapes[f"decoder.seg_layers.{d}.bias"] = (classes,)
+    return shapes
+
+
+class _Tensor:
+    """Minimal object with the ``detach().cpu().numpy()`` chain the converter expects."""
+
+    def __init__(self, array: np.ndarray) -> None:
+        self.array = array
+
+    def detach(self):
+        return self
+
+    def cpu(self):
+        return self
+
+    def numpy(self):
+        return self.array
+
+
+def main(reference: Path) -> None:
+    sys.path.insert(0, str(reference / "src"))
+    from nnunet_mlx.prediction import inference
+    from nnunet_mlx.prediction.sliding_window import (
+        compute_steps,
+        gaussian_importance,
+        nnunet_fp16_gaussian,
+    )
+    from nnunet_mlx.storage.weights import convert_state_dict, map_key_and_layout
+
+    geometry = [
+        {"image": list(i), "patch": list(p), "step": s,
+         "steps": [list(a) for a in compute_steps(i, p, step_fraction=s)]}
+        for i, p, s in STEP_CASES
+    ]
+    (HERE / "geometry.json").write_text(json.dumps(geometry, indent=1) + "\n")
+
+    arrays: dict[str, np.ndarray] = {}
+    for patch in GAUSSIAN_FULL:
+        arrays["full_" + "x".join(map(str, patch))] = gaussian_importance(patch)
+    for patch in GAUSSIAN_SUMMARY:
+        g = gaussian_importance(patch)
+        name = "x".join(map(str, patch))
+        c = tuple(s // 2 for s in patch)
+        arrays[f"line0_{name}"] = g[:, c[1], c[2]].copy()
+        arrays[f"line1_{name}"] = g[c[0], :, c[2]].copy()
+        arrays[f"line2_{name}"] = g[c[0], c[1], :].copy()
+        arrays[f"stats_{name}"] = np.array(
+            [g.max(), g.min(), g.astype(np.float64).sum()], dtype=np.float64)
+    for patch in FP16_GAUSSIAN:
+        arrays["fp16_" + "x".join(map(str, patch))] = nnunet_fp16_gaussian(patch)
+    np.savez_compressed(HERE / "gaussian.npz", **arrays)
+
+    rng = np.random.default_rng(7)
+    cases = {
+        "plain": _upstream_plain_keys(3, (2, 2, 2), (2, 2), 2, (4, 8, 16), 3),
+        "residual": _upstream_residual_keys(1, (4, 8, 16), (1, 2, 2), 3),
+    }
+    wmap = {}
+    layouts: dict[str, np.ndarray] = {}
+    for name, shapes in cases.items():
+        state = {k: _Tensor(rng.standard_normal(s).astype(np.float32)) for k, s in shapes.items()}
+        converted = convert_state_dict(state)
+        entries = {}
+        for key, tensor in state.items():
+            mapped = map_key_and_layout(key, tensor.array)
+            entries[key] = None if mapped is None else mapped[0]
+            if mapped is not None and key.endswith(("transpconvs.0.weight", "stages.0.0.convs.0.conv.weight",
+                                                    "blocks.0.skip.1.conv.weight", "seg_layers.0.weight")):
+                layouts[f"{name}|{key}|source"] = tensor.array
+                layouts[f"{name}|{key}|converted"] = np.ascontiguousarray(mapped[1])
+        wmap[name] = {"entries": entries, "dropped": list(converted.dropped_keys),
+                      "converted_keys": sorted(converted.weights),
+                      "source_shapes": {k: list(v) for k, v in shapes.items()}}
+    (HERE / "weights_map.json").write_text(json.dumps(wmap, indent=1, sort_keys=True) + "\n")
+    np.savez_compressed(HERE / "weights_layout.npz", **layouts)
+
+    recorded = np.load(reference / "tests" / "fixtures" / "darwin-arm64" / "upstream_runner.npz")
+    subset = {k: recorded[k] for k in recorded.files if k.startswith(("head_", "rounding_"))}
+    # the reference's own host conversion of the recorded logits, as a cross-check
+    subset["reference_probabilities_class"] = inference.logits_to_probabilities(
+        recorded["head_logits_class"], has_regions=False)
+    np.savez_compressed(HERE / "upstream_runner_subset.npz", **subset)
+
+
+if __name__ == "__main__":
+    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
