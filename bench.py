@@ -171,7 +171,7 @@ def cpu_baseline(spec, weights, patch, forwards: int, voxels: int):
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     x = np.random.default_rng(0).standard_normal((1, *patch, spec.input_channels)).astype(np.float32)
-    onet.forward(x[:, :32, :32, :32], weights, spec) if min(patch) >= 32 else None  # warm the thread pool
+    onet.forward(x[:, :64, :64, :64], weights, spec)  # warm the thread pool (64^3 keeps the 6th stage at 2^3)
     t0 = time.perf_counter()
     onet.forward(x, weights, spec)
     seconds = time.perf_counter() - t0

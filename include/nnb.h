@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 1
+#define NNB_ABI_VERSION 3
 
 enum nnb_status {
   NNB_OK = 0,
@@ -74,6 +74,9 @@ typedef struct nnb_conv3d_args {
   float* out;           /* (B, oD, oH, oW, cout) */
   float* partials;      /* (B, ceil(oD*oH*oW/128), cout, 2) per-tile (sum, M2), or NULL */
   int32_t precision;    /* enum nnb_precision */
+  int32_t operand_format; /* 0: raw float32 segments (lazy affine allowed; CUDA-core kernel);
+                             1: segments prepared by nnb_prepare_operand for `precision`
+                             (tensor-core kernel; scale/shift must be NULL) */
 } nnb_conv3d_args;
 
 /* Library identity. */
@@ -98,6 +101,18 @@ int32_t nnb_device_status(int32_t* where, int32_t reset);
  * Metal kernel src/nnunet_mlx/kernels/metal_single_channel_conv.py:32-97.
  */
 int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
+
+/*
+ * Tensor-core operand preparation: apply a lazy activation's affine +
+ * LeakyReLU once per element and write the TF32 form the tensor-core
+ * convolution gathers -- split (NNB_PREC_FP32): per voxel [hi(C) | lo(C)],
+ * hi = x with the 13 low mantissa bits cleared, lo = x - hi; NNB_PREC_TF32:
+ * x rounded to TF32.  out holds batch * voxels * C * (2 or 1) floats.  Replaces
+ * the affine pass of src/nnunet_mlx/kernels/metal_native_norm.py:62-70,155-168
+ * (there the normalised activation is materialised in float32).
+ */
+int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t voxels, float slope,
+                            int32_t precision, float* out, void* stream);
 
 /* Bytes of the tensor-core weight image for (cout, kvol, cin_total, precision). */
 int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision);
@@ -125,11 +140,25 @@ int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t
 /*
  * Non-overlapping transposed convolution (kernel == stride) with lazy input
  * segment and bias.  Replaces `NonOverlappingConvTranspose3d`
- * src/nnunet_mlx/model/network.py:101-174.  weight: (cout, kD, kH, kW, cin).
+ * src/nnunet_mlx/model/network.py:101-174 (matmul + interleave + bias).
+ * weight: (cout, kD, kH, kW, cin).  With `packed` (from
+ * nnb_conv_transpose3d_pack) and 32-multiple channel counts it runs as a
+ * tensor-core GEMM whose epilogue scatters every (tap, channel) block to its
+ * up-sampled voxel, and `input` must then be an operand prepared by
+ * nnb_prepare_operand for `precision`; otherwise it runs on CUDA cores over
+ * the raw (lazy) input.
  */
 int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
                              const int32_t kernel[3], float slope, const float* weight,
-                             const float* bias, int32_t cout, float* out, void* stream);
+                             const float* bias, int32_t cout, const void* packed, int32_t precision,
+                             float* out, void* stream);
+
+/* Bytes of the tensor-core image of a transposed-convolution weight (0: not eligible). */
+int64_t nnb_conv_transpose3d_packed_bytes(int32_t cout, int32_t ktaps, int32_t cin, int32_t precision);
+
+/* Build that image (rows = tap * cout + channel) from a (cout, kD, kH, kW, cin) weight. */
+int32_t nnb_conv_transpose3d_pack(const float* weight, int32_t cout, int32_t ktaps, int32_t cin,
+                                  int32_t precision, void* packed, void* stream);
 
 /*
  * Residual join of `ResidualBlock` / `BottleneckResidualBlock`:

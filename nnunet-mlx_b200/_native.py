@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 1
+ABI_VERSION = 3
 
 PREC_FP32 = 0   # split-TF32 hi/lo tensor cores, float32-level accuracy
 PREC_TF32 = 1   # single-pass TF32 tensor cores
@@ -38,7 +38,8 @@ class Conv3dArgs(ctypes.Structure):
                 ("stride", I32x3), ("pad", I32x3), ("num_segments", ctypes.c_int32), ("seg", Segment * 2),
                 ("slope", ctypes.c_float), ("cout", ctypes.c_int32), ("weight", ctypes.c_void_p),
                 ("packed", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),
-                ("partials", ctypes.c_void_p), ("precision", ctypes.c_int32)]
+                ("partials", ctypes.c_void_p), ("precision", ctypes.c_int32),
+                ("operand_format", ctypes.c_int32)]
 
 
 SYMBOLS = {
@@ -47,6 +48,8 @@ SYMBOLS = {
     "nnb_device_status": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "nnb_conv3d": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs), ctypes.c_void_p]),
     "nnb_conv3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
+    "nnb_prepare_operand": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
+                                             ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_conv3d_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_instance_norm_finalize": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
@@ -55,7 +58,10 @@ SYMBOLS = {
                                                     ctypes.c_void_p]),
     "nnb_conv_transpose3d": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, I32x3, I32x3,
                                               ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
-                                              ctypes.c_void_p, ctypes.c_void_p]),
+                                              ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_conv_transpose3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
+    "nnb_conv_transpose3d_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                   ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_residual_join": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.POINTER(Segment), ctypes.c_int32,
                                            ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_gather_views": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, I32x3, ctypes.c_int32,

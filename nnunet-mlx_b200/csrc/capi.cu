@@ -30,6 +30,13 @@ int launch_norm_finalize(const float* partials, int batch, int voxels, int chann
 int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
                                float slope, const float* weight, const float* bias, int cout, float* out,
                                cudaStream_t stream);
+int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
+                             float slope, const float* bias, int cout, const void* packed, int precision, float* out,
+                             cudaStream_t stream);
+int launch_conv3d_pack_rows(const float* w, int rows, int kvol, int cin_total, int precision, int row_taps,
+                            int up_cout, void* packed, cudaStream_t stream);
+int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int split, float* out,
+                           cudaStream_t stream);
 int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch, int64_t voxels, float slope,
                          float* out, cudaStream_t stream);
 int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const int32_t off[3],
@@ -78,14 +85,32 @@ int32_t nnb_conv3d(const nnb_conv3d_args* a, void* stream) {
   }
   NNB_REQUIRE(a->cout >= 1 && a->weight != nullptr && a->out != nullptr, "conv3d: missing weight/output");
   const cudaStream_t st = (cudaStream_t)stream;
-  if (a->precision == NNB_PREC_SIMT) return launch_conv3d_simt(*a, st);
-  NNB_REQUIRE(a->precision == NNB_PREC_FP32 || a->precision == NNB_PREC_TF32, "conv3d: unknown precision %d",
-              a->precision);
-  if (a->packed != nullptr && conv3d_tc_supported(*a)) return launch_conv3d_tc(*a, st);
-  // Outside the tensor-core envelope (few input channels, odd channel counts)
-  // the CUDA-core kernel computes in plain float32, which also satisfies the
-  // requested accuracy.
+  NNB_REQUIRE(a->precision == NNB_PREC_FP32 || a->precision == NNB_PREC_TF32 || a->precision == NNB_PREC_SIMT,
+              "conv3d: unknown precision %d", a->precision);
+  if (a->operand_format == 1) {
+    NNB_REQUIRE(a->precision != NNB_PREC_SIMT && a->packed != nullptr, "conv3d: prepared operands need a packed "
+                "weight image and a tensor-core precision");
+    for (int s = 0; s < a->num_segments; ++s)
+      NNB_REQUIRE(a->seg[s].scale == nullptr, "conv3d: prepared operands carry no lazy affine");
+    NNB_REQUIRE(conv3d_tc_supported(*a), "conv3d: shape outside the tensor-core envelope");
+    return launch_conv3d_tc(*a, st);
+  }
+  NNB_REQUIRE(a->operand_format == 0, "conv3d: unknown operand_format %d", a->operand_format);
+  // Raw float32 operands run on the CUDA-core kernel in plain float32 (used for
+  // the few-channel first layer and shapes outside the tensor-core envelope),
+  // which also satisfies the requested accuracy.
   return launch_conv3d_simt(*a, st);
+}
+
+int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t voxels, float slope, int32_t precision,
+                            float* out, void* stream) {
+  NNB_REQUIRE(input != nullptr && out != nullptr, "prepare_operand: null pointer");
+  int rc = check_segment(*input, "prepare_operand input");
+  if (rc) return rc;
+  NNB_REQUIRE(batch >= 1 && voxels >= 1, "prepare_operand: bad shape");
+  NNB_REQUIRE(precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32, "prepare_operand: precision");
+  return launch_prepare_operand(*input, batch, voxels, slope, precision == NNB_PREC_FP32 ? 1 : 0, out,
+                                (cudaStream_t)stream);
 }
 
 int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision) {
@@ -111,14 +136,30 @@ int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t
 
 int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
                              const int32_t kernel[3], float slope, const float* weight, const float* bias,
-                             int32_t cout, float* out, void* stream) {
+                             int32_t cout, const void* packed, int32_t precision, float* out, void* stream) {
   NNB_REQUIRE(input != nullptr, "conv_transpose3d: null input");
   int rc = check_segment(*input, "conv_transpose3d input");
   if (rc) return rc;
   NNB_REQUIRE(batch >= 1 && positive3(in_dims) && positive3(kernel), "conv_transpose3d: bad shape");
   NNB_REQUIRE(weight && out && cout >= 1, "conv_transpose3d: missing weight/output");
+  if (packed != nullptr && (precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32) && input->channels % 32 == 0 &&
+      cout % 32 == 0)
+    return launch_conv_transpose_tc(*input, batch, in_dims, kernel, slope, bias, cout, packed, precision, out,
+                                    (cudaStream_t)stream);
   return launch_conv_transpose_simt(*input, batch, in_dims, kernel, slope, weight, bias, cout, out,
                                     (cudaStream_t)stream);
+}
+
+int64_t nnb_conv_transpose3d_packed_bytes(int32_t cout, int32_t ktaps, int32_t cin, int32_t precision) {
+  if (cout % 32 != 0) return 0;
+  return conv3d_tc_packed_bytes(cout * ktaps, 1, cin, precision);
+}
+
+int32_t nnb_conv_transpose3d_pack(const float* weight, int32_t cout, int32_t ktaps, int32_t cin, int32_t precision,
+                                  void* packed, void* stream) {
+  NNB_REQUIRE(weight != nullptr && packed != nullptr, "conv_transpose3d_pack: null pointer");
+  NNB_REQUIRE(cout % 32 == 0 && ktaps >= 1 && cin >= 1, "conv_transpose3d_pack: bad shape");
+  return launch_conv3d_pack_rows(weight, cout * ktaps, 1, cin, precision, ktaps, cout, packed, (cudaStream_t)stream);
 }
 
 int32_t nnb_residual_join(const nnb_segment* branch, const nnb_segment* skip, int32_t batch, int64_t voxels,

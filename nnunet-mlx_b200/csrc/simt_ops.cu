@@ -98,9 +98,111 @@ __global__ void __launch_bounds__(kTileRows) conv3d_simt_kernel(nnb_conv3d_args 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Few-input-channel convolution (the first layer: 1..8 input channels):
+// memory-bound on its output, so one thread per output voxel computes a
+// 32-channel group from weights held in shared memory (broadcast reads), the
+// 128 x 32 output tile is staged in shared memory and written with coalesced
+// 16-byte stores, and the tile's (sum, M2) partials come from the same stage.
+// Tap order (kd, kh, kw) and zero padding as the reference's single-channel
+// kernel (metal_single_channel_conv.py:32-59).
+// ---------------------------------------------------------------------------
+constexpr int kSmallCin = 8;
+constexpr int kSmallMaxTaps = 27;
+
+__global__ void __launch_bounds__(kTileRows) conv3d_small_cin_kernel(nnb_conv3d_args a, int tps) {
+  __shared__ float w_s[kSmallMaxTaps * kSmallCin * 32];  // [tap][ci][co]
+  __shared__ float out_s[kTileRows][33];
+  const int t = blockIdx.x % tps;
+  const int b = blockIdx.x / tps;
+  const int co0 = blockIdx.y * 32;
+  const int r = threadIdx.x;
+  const int cin = a.seg[0].channels;
+  const int kvol = a.kernel[0] * a.kernel[1] * a.kernel[2];
+  for (int i = threadIdx.x; i < kvol * cin * 32; i += blockDim.x) {
+    const int co = i % 32, ci = (i / 32) % cin, tap = i / (32 * cin);
+    w_s[i] = co0 + co < a.cout ? a.weight[((int64_t)(co0 + co) * kvol + tap) * cin + ci] : 0.f;
+  }
+  __syncthreads();
+  const int OD = a.out_dims[0], OH = a.out_dims[1], OW = a.out_dims[2];
+  const int ID = a.in_dims[0], IH = a.in_dims[1], IW = a.in_dims[2];
+  const int64_t ovox = (int64_t)OD * OH * OW;
+  const int64_t m = (int64_t)t * kTileRows + r;
+  const bool valid = m < ovox;
+  const int ox = (int)(m % OW), oy = (int)((m / OW) % OH), oz = (int)(m / ((int64_t)OW * OH));
+  const nnb_segment seg = a.seg[0];
+  float acc[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+  if (valid) {
+    int tap = 0;
+    for (int kz = 0; kz < a.kernel[0]; ++kz) {
+      const int iz = oz * a.stride[0] - a.pad[0] + kz;
+      for (int ky = 0; ky < a.kernel[1]; ++ky) {
+        const int iy = oy * a.stride[1] - a.pad[1] + ky;
+        for (int kx = 0; kx < a.kernel[2]; ++kx, ++tap) {
+          const int ix = ox * a.stride[2] - a.pad[2] + kx;
+          if (iz < 0 || iz >= ID || iy < 0 || iy >= IH || ix < 0 || ix >= IW) continue;
+          const float* src = seg.data + ((((int64_t)b * ID + iz) * IH + iy) * IW + ix) * cin;
+          for (int ci = 0; ci < cin; ++ci) {
+            const float v = activate(__ldg(src + ci), seg.scale, seg.shift, seg.leaky, a.slope, b * cin + ci);
+            const float* wp = w_s + (tap * cin + ci) * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = fmaf(v, wp[j], acc[j]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (a.bias != nullptr && co0 + j < a.cout) acc[j] += __ldg(a.bias + co0 + j);
+    out_s[r][j] = valid ? acc[j] : 0.f;
+  }
+  __syncthreads();
+  // coalesced store of the valid rows: 8 threads per row, 16 bytes each
+  const int rows = (int)min((int64_t)kTileRows, ovox - (int64_t)t * kTileRows);
+  const int ncols = min(32, a.cout - co0);
+  float* base = a.out + ((int64_t)b * ovox + (int64_t)t * kTileRows) * a.cout + co0;
+  if (ncols == 32 && (a.cout % 4) == 0) {
+    for (int i = threadIdx.x; i < rows * 8; i += blockDim.x) {
+      const int row = i >> 3, c4 = (i & 7) * 4;
+      *reinterpret_cast<float4*>(base + (int64_t)row * a.cout + c4) =
+          make_float4(out_s[row][c4], out_s[row][c4 + 1], out_s[row][c4 + 2], out_s[row][c4 + 3]);
+    }
+  } else {
+    for (int i = threadIdx.x; i < rows * 32; i += blockDim.x) {
+      const int row = i >> 5, c = i & 31;
+      if (c < ncols) base[(int64_t)row * a.cout + c] = out_s[row][c];
+    }
+  }
+  if (a.partials == nullptr) return;
+  if (r < ncols) {
+    float sum = 0.f;
+    for (int i = 0; i < rows; ++i) sum += out_s[i][r];
+    const float mean = sum / rows;
+    float m2 = 0.f;
+    for (int i = 0; i < rows; ++i) {
+      const float d = out_s[i][r] - mean;
+      m2 = fmaf(d, d, m2);
+    }
+    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 2;
+    p[0] = sum;
+    p[1] = m2;
+  }
+}
+
 int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
   const int64_t ovox = (int64_t)a.out_dims[0] * a.out_dims[1] * a.out_dims[2];
   const int tps = tiles_per_sample(ovox);
+  if (a.num_segments == 1 && a.seg[0].channels <= kSmallCin &&
+      a.kernel[0] * a.kernel[1] * a.kernel[2] <= kSmallMaxTaps) {
+    dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + 31) / 32));
+    NNB_REQUIRE((int64_t)tps * a.batch < (1LL << 31), "conv3d: too many tiles");
+    conv3d_small_cin_kernel<<<grid, kTileRows, 0, stream>>>(a, tps);
+    NNB_LAUNCH_CHECK();
+    return NNB_OK;
+  }
   constexpr int CO = 16;
   dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + CO - 1) / CO));
   NNB_REQUIRE((int64_t)tps * a.batch < (1LL << 31), "conv3d: too many tiles");
@@ -242,6 +344,67 @@ int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch
   const int64_t total4 = total / 4;
   const int blocks = (int)std::min<int64_t>((total4 + 255) / 256, 148 * 16);
   residual_join_kernel<<<blocks, 256, 0, stream>>>(br, sk, per_sample, br.channels, total4, slope, out);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+}  // namespace nnb
+
+namespace nnb {
+
+// ---------------------------------------------------------------------------
+// Operand preparation for the tensor-core convolution: one pass over a lazy
+// activation that applies its instance-norm affine + LeakyReLU once per
+// element (instead of once per tap inside the convolution) and writes the
+// TF32 form the MMA consumes.  split != 0: per voxel [hi(C) | lo(C)] with
+// hi = x with the 13 low mantissa bits cleared and lo = x - hi (both exact);
+// split == 0: x rounded to TF32 (nearest).  HBM-bound: 4 bytes read and 8
+// (split) or 4 bytes written per element.
+// ---------------------------------------------------------------------------
+__global__ void prepare_operand_kernel(nnb_segment in, int64_t voxels_total, int64_t per_sample_vox, float slope,
+                                       int split, float* __restrict__ out) {
+  const int C = in.channels;
+  const int c4n = C / 4;
+  const int64_t total = voxels_total * c4n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t vox = i / c4n;
+    const int c4 = (int)(i - vox * c4n) * 4;
+    const int b = (int)(vox / per_sample_vox);
+    const float4 x = __ldg(reinterpret_cast<const float4*>(in.data) + i);
+    float v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = activate(v[e], in.scale, in.shift, in.leaky, slope, b * C + c4 + e);
+    if (split) {
+      float hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        hi[e] = __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u);
+        lo[e] = v[e] - hi[e];
+      }
+      float* dst = out + vox * 2 * C + c4;
+      *reinterpret_cast<float4*>(dst) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<float4*>(dst + C) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    } else {
+      float r[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint32_t t;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v[e]));
+        r[e] = __uint_as_float(t);
+      }
+      *reinterpret_cast<float4*>(out + vox * C + c4) = make_float4(r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
+int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int split, float* out,
+                           cudaStream_t stream) {
+  NNB_REQUIRE(in.channels % 4 == 0, "prepare_operand: channels must be a multiple of 4");
+  NNB_REQUIRE((reinterpret_cast<uintptr_t>(in.data) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+              "prepare_operand: 16-byte aligned tensors required");
+  const int64_t total = (int64_t)batch * voxels * (in.channels / 4);
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  prepare_operand_kernel<<<blocks, 256, 0, stream>>>(in, (int64_t)batch * voxels, voxels, slope, split, out);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }

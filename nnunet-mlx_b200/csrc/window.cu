@@ -65,8 +65,90 @@ int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const in
 // ---------------------------------------------------------------------------
 // Fused seg head + flip-back + view mean + Gaussian accumulation (one tile).
 // features: (views, P0, P1, P2, F) lazy; seg_w: (C, F); acc: (AD, AH, AW, C).
-// Per voxel and class chunk of CC classes, views are added in order.
+// One thread per tile voxel; per view it reads the F features of the
+// flipped source voxel with 16-byte loads, applies the view's lazy affine
+// (staged in shared memory with the head weights), computes the C logits and
+// adds them to the running view sum in view order.  HBM-bound on the feature
+// read (views * P^3 * F * 4 bytes per tile).
 // ---------------------------------------------------------------------------
+constexpr int kAccMaxC = 8;        // classes per pass
+
+template <int FV>  // FV = F / 4 (float4 chunks), compile-time for register arrays
+__global__ void __launch_bounds__(256) accumulate_tile_vec_kernel(
+    nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
+    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, float* __restrict__ acc,
+    float* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+  constexpr int F = FV * 4;
+  __shared__ float s_sc[8][F];
+  __shared__ float s_sh[8][F];
+  __shared__ float s_w[kAccMaxC][F];
+  __shared__ float s_b[kAccMaxC];
+  __shared__ int s_mask[8];
+  if (threadIdx.x < 8) s_mask[threadIdx.x] = masks.m[threadIdx.x];
+  for (int i = threadIdx.x; i < views * F; i += blockDim.x) {
+    const int v = i / F, f = i % F;
+    s_sc[v][f] = feat.scale ? feat.scale[v * F + f] : 1.f;
+    s_sh[v][f] = feat.scale ? feat.shift[v * F + f] : 0.f;
+  }
+  const bool lazy = feat.scale != nullptr;
+  const float inv_views = 1.0f / (float)views;
+  const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
+  for (int c0 = 0; c0 < classes; c0 += kAccMaxC) {
+    const int nc = min(kAccMaxC, classes - c0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kAccMaxC * F; i += blockDim.x) {
+      const int c = i / F, f = i % F;
+      s_w[c][f] = c < nc ? seg_w[(int64_t)(c0 + c) * F + f] : 0.f;
+    }
+    if (threadIdx.x < kAccMaxC) s_b[threadIdx.x] = threadIdx.x < nc ? seg_b[c0 + threadIdx.x] : 0.f;
+    __syncthreads();
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pvox;
+         p += (int64_t)gridDim.x * blockDim.x) {
+      const int k = (int)(p % patch.d[2]);
+      const int j = (int)((p / patch.d[2]) % patch.d[1]);
+      const int i = (int)(p / ((int64_t)patch.d[2] * patch.d[1]));
+      float pred[kAccMaxC];
+#pragma unroll
+      for (int c = 0; c < kAccMaxC; ++c) pred[c] = 0.f;
+      for (int v = 0; v < views; ++v) {
+        const int mask = s_mask[v];
+        const int si = (mask & 1) ? patch.d[0] - 1 - i : i;
+        const int sj = (mask & 2) ? patch.d[1] - 1 - j : j;
+        const int sk = (mask & 4) ? patch.d[2] - 1 - k : k;
+        const int64_t q = (((int64_t)v * patch.d[0] + si) * patch.d[1] + sj) * patch.d[2] + sk;
+        const float4* src = reinterpret_cast<const float4*>(feat.data + q * F);
+        float logit[kAccMaxC];
+#pragma unroll
+        for (int c = 0; c < kAccMaxC; ++c) logit[c] = 0.f;
+#pragma unroll
+        for (int f4 = 0; f4 < FV; ++f4) {
+          const float4 x = __ldg(src + f4);
+          float z[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int f = f4 * 4 + e;
+            if (lazy) {
+              const float y = fmaf(z[e], s_sc[v][f], s_sh[v][f]);
+              z[e] = feat.leaky ? leaky(y, slope) : y;
+            }
+#pragma unroll
+            for (int c = 0; c < kAccMaxC; ++c) logit[c] = fmaf(z[e], s_w[c][f], logit[c]);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < kAccMaxC; ++c) pred[c] += logit[c] + s_b[c];
+      }
+      const float g = __ldg(gauss + p);
+      const int64_t dst = ((int64_t)(off.d[0] + i) * ad.d[1] + (off.d[1] + j)) * ad.d[2] + (off.d[2] + k);
+      float* a = acc + dst * classes + c0;
+#pragma unroll
+      for (int c = 0; c < kAccMaxC; ++c)
+        if (c < nc) a[c] += (pred[c] * inv_views) * g;
+      if (add_normalizer && c0 == 0) normalizer[dst] += g;
+    }
+  }
+}
+
 template <int CC>
 __global__ void __launch_bounds__(256) accumulate_tile_kernel(
     nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
@@ -127,8 +209,14 @@ int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* ma
   Dims3 dp{{patch[0], patch[1], patch[2]}}, dad{{ad[0], ad[1], ad[2]}}, doff{{off[0], off[1], off[2]}};
   const int64_t pvox = (int64_t)patch[0] * patch[1] * patch[2];
   const int blocks = (int)std::min<int64_t>((pvox + 255) / 256, 148 * 16);
-  accumulate_tile_kernel<4><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss,
-                                                        acc, normalizer, dad, doff, add_normalizer);
+  const bool aligned = (reinterpret_cast<uintptr_t>(feat.data) & 15) == 0;
+  if (aligned && feat.channels == 32) {
+    accumulate_tile_vec_kernel<8><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes,
+                                                              gauss, acc, normalizer, dad, doff, add_normalizer);
+  } else {
+    accumulate_tile_kernel<4><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss,
+                                                          acc, normalizer, dad, doff, add_normalizer);
+  }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import ctypes
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 
@@ -88,6 +88,8 @@ class Lazy:
     scale: torch.Tensor | None = None
     shift: torch.Tensor | None = None
     leaky: bool = False
+    # tensor-core operands derived from this activation, by precision (see prepare_operand)
+    prepared: dict = field(default_factory=dict, compare=False, repr=False)
 
     @property
     def channels(self) -> int:
@@ -123,6 +125,41 @@ def _ptr(t: torch.Tensor | None) -> int:
 
 def tiles_per_sample(voxels: int) -> int:
     return (voxels + TILE_ROWS - 1) // TILE_ROWS
+
+
+def prepare_operand(x: Lazy, precision: int, slope: float) -> Lazy:
+    """The tensor-core operand of ``x`` (affine + LeakyReLU applied once, TF32 hi/lo or TF32).
+
+    Cached on ``x`` so an activation read by two convolutions (an encoder output
+    and its skip connection) is prepared once.
+    """
+    cached = x.prepared.get(precision)
+    if cached is not None:
+        return cached
+    halves = 2 if precision == _native.PREC_FP32 else 1
+    out = torch.empty((*x.raw.shape[:-1], halves * x.channels), dtype=torch.float32, device=x.raw.device)
+    seg = x.segment()
+    voxels = math.prod(x.spatial)
+    token = PROFILE.start("prepare_operand", 0.0, 4.0 * x.raw.numel() * (1 + halves))
+    _native.check(_native.load().nnb_prepare_operand(ctypes.byref(seg), int(x.raw.shape[0]), voxels, float(slope),
+                                                     int(precision), out.data_ptr(), _stream()), "prepare_operand")
+    PROFILE.stop(token)
+    # the prepared tensor's segment: channels are the logical channel count
+    operand = _Prepared(out, x.channels)
+    x.prepared[precision] = operand
+    return operand
+
+
+class _Prepared(Lazy):
+    """A prepared operand: ``raw`` holds ``halves * logical`` floats per voxel."""
+
+    def __init__(self, raw: torch.Tensor, logical_channels: int) -> None:
+        super().__init__(raw)
+        object.__setattr__(self, "logical_channels", logical_channels)
+
+    @property
+    def channels(self) -> int:
+        return self.logical_channels
 
 
 def packed_bytes(cout: int, kvol: int, cin: int, precision: int) -> int:
@@ -195,6 +232,12 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
     cin = sum(item.channels for item in inputs)
     tensor_cores = (packed is not None and precision in (_native.PREC_FP32, _native.PREC_TF32)
                     and all(item.channels % 32 == 0 for item in inputs) and cout % 16 == 0)
+    if tensor_cores:
+        for index, item in enumerate(inputs):
+            args.seg[index] = prepare_operand(item, precision, slope).segment()
+        args.operand_format = 1
+    else:
+        args.operand_format = 0
     flops = 2.0 * batch * math.prod(out_dims) * cout * cin * math.prod(kernel)
     token = PROFILE.start("conv3d_tc" if tensor_cores else "conv3d_simt", flops,
                           4.0 * (out.numel() + sum(item.raw.numel() for item in inputs)))
@@ -216,18 +259,42 @@ def instance_norm_finalize(partials: torch.Tensor, voxels: int, gamma: torch.Ten
     return scale, shift
 
 
+def pack_transposed_weights(weight: torch.Tensor, precision: int) -> torch.Tensor | None:
+    """Tensor-core image of a stride == kernel transposed-convolution weight ``(C_out, kD, kH, kW, C_in)``."""
+    if precision not in (_native.PREC_FP32, _native.PREC_TF32):
+        return None
+    _check_tensor(weight, "weight")
+    cout, cin = int(weight.shape[0]), int(weight.shape[-1])
+    ktaps = int(math.prod(weight.shape[1:-1]))
+    nbytes = int(_native.load().nnb_conv_transpose3d_packed_bytes(cout, ktaps, cin, precision))
+    if nbytes <= 0:
+        return None
+    storage = torch.empty(nbytes + 1024, dtype=torch.uint8, device=weight.device)
+    offset = (-storage.data_ptr()) % 1024
+    image = storage[offset:offset + nbytes]
+    _native.check(_native.load().nnb_conv_transpose3d_pack(weight.data_ptr(), cout, ktaps, cin, precision,
+                                                           image.data_ptr(), _stream()), "conv_transpose3d_pack")
+    return image
+
+
 def conv_transpose3d(x: Lazy, weight: torch.Tensor, bias: torch.Tensor | None, kernel,
-                     slope: float = 0.01) -> torch.Tensor:
+                     slope: float = 0.01, packed: torch.Tensor | None = None,
+                     precision: int = _native.PREC_SIMT) -> torch.Tensor:
     batch = int(x.raw.shape[0])
     cout = int(weight.shape[0])
     out_dims = tuple(s * k for s, k in zip(x.spatial, kernel))
     out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=x.raw.device)
-    seg = x.segment()
     _check_tensor(weight, "weight")
-    token = PROFILE.start("conv_transpose3d", 2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()))
+    tensor_cores = (packed is not None and x.channels % 32 == 0 and cout % 32 == 0
+                    and precision in (_native.PREC_FP32, _native.PREC_TF32))
+    seg = prepare_operand(x, precision, slope).segment() if tensor_cores else x.segment()
+    token = PROFILE.start("conv_transpose3d_tc" if tensor_cores else "conv_transpose3d_simt",
+                          2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()))
     _native.check(_native.load().nnb_conv_transpose3d(
         ctypes.byref(seg), batch, _native.dims3(x.spatial), _native.dims3(kernel), float(slope),
-        weight.data_ptr(), _ptr(bias), cout, out.data_ptr(), _stream()), "conv_transpose3d")
+        weight.data_ptr(), _ptr(bias), cout, _ptr(packed) if tensor_cores else 0, int(precision), out.data_ptr(),
+        _stream()),
+        "conv_transpose3d")
     PROFILE.stop(token)
     return out
 

@@ -81,7 +81,7 @@ class _UNetBase:
         self.device = torch.device(device)
         self.training = False
         self.layers: dict[str, ConvLayer] = {}
-        self.up: dict[int, tuple[torch.Tensor, torch.Tensor | None, tuple[int, int, int]]] = {}
+        self.up: dict[int, tuple[torch.Tensor, torch.Tensor | None, tuple[int, int, int], torch.Tensor | None]] = {}
         self.seg_weight: torch.Tensor | None = None
         self.seg_bias: torch.Tensor | None = None
         self._loaded = False
@@ -109,10 +109,10 @@ class _UNetBase:
         stages = len(spec.features)
         for d in range(stages - 1):
             src = stages - 1 - d
-            w = weights[f"up{d}.weight"]
+            w = self._tensor(weights[f"up{d}.weight"])
             b = weights.get(f"up{d}.bias")
-            self.up[d] = (self._tensor(w), None if b is None else self._tensor(b),
-                          tuple(int(k) for k in spec.strides[src]))
+            self.up[d] = (w, None if b is None else self._tensor(b), tuple(int(k) for k in spec.strides[src]),
+                          kernels.pack_transposed_weights(w, PRECISIONS[self.precision]))
             for blk in range(spec.decoder_convs[d]):
                 self._conv_layer(weights, f"dec{d}.block{blk}", _unit(spec), conv_bias=spec.conv_bias)
         last = stages - 2
@@ -147,9 +147,10 @@ class _UNetBase:
         spec = self.spec
         hidden = skips.pop()
         for d in range(len(spec.features) - 1):
-            weight, bias, kernel = self.up[d]
+            weight, bias, kernel, packed = self.up[d]
             skip = skips.pop()
-            up = Lazy(kernels.conv_transpose3d(hidden, weight, bias, kernel, spec.leaky_slope))
+            up = Lazy(kernels.conv_transpose3d(hidden, weight, bias, kernel, spec.leaky_slope, packed=packed,
+                                               precision=PRECISIONS[self.precision]))
             up = _match_spatial(up, skip)
             hidden = self._conv_norm(f"dec{d}.block0", [up, skip], act=True)
             for blk in range(1, spec.decoder_convs[d]):

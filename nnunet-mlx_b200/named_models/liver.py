@@ -1,0 +1,7 @@
+"""``liver`` runner (reference ``src/nnunet_mlx/named_models/liver.py``): ``run`` and ``load_model``."""
+
+from nnunet_mlx_b200.named_models import make
+
+run, load_model = make("liver")
+
+__all__ = ["load_model", "run"]

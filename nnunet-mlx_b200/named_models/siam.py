@@ -1,0 +1,7 @@
+"""``siam`` runner (reference ``src/nnunet_mlx/named_models/siam.py``): ``run`` and ``load_model``."""
+
+from nnunet_mlx_b200.named_models import make
+
+run, load_model = make("siam")
+
+__all__ = ["load_model", "run"]

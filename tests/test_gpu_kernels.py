@@ -115,18 +115,32 @@ def test_instance_norm_finalize_with_affine_matches_torch(cuda_device):
     np.testing.assert_allclose(normed.numpy(), ref.numpy(), rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("kernel", [(2, 2, 2), (1, 2, 2)])
-def test_conv_transpose_matches_torch(cuda_device, kernel):
-    from nnunet_mlx_b200 import kernels
+@pytest.mark.parametrize("kernel,cin,cout,precision", [
+    ((2, 2, 2), 16, 8, "simt"),
+    ((1, 2, 2), 16, 8, "simt"),
+    ((2, 2, 2), 64, 32, "fp32"),
+    ((2, 2, 2), 320, 320, "fp32"),
+    ((1, 2, 2), 32, 64, "fp32"),
+    ((2, 2, 2), 128, 64, "tf32"),
+])
+def test_conv_transpose_matches_torch(cuda_device, kernel, cin, cout, precision):
+    from nnunet_mlx_b200 import _native, kernels
 
     rng = np.random.default_rng(5)
-    lz, raw, sc, sh = _make_segment(rng, 2, (3, 4, 5), 16, True, cuda_device)
-    w = torch.from_numpy(rng.standard_normal((8, *kernel, 16)).astype(np.float32))  # (cout, k, cin)
-    b = torch.from_numpy(rng.standard_normal(8).astype(np.float32))
-    out = kernels.conv_transpose3d(lz, w.to(cuda_device), b.to(cuda_device), kernel)
+    lz, raw, sc, sh = _make_segment(rng, 2, (3, 4, 5), cin, True, cuda_device)
+    w = torch.from_numpy((rng.standard_normal((cout, *kernel, cin)) / np.sqrt(cin)).astype(np.float32))
+    b = torch.from_numpy(rng.standard_normal(cout).astype(np.float32))
+    prec = {"fp32": _native.PREC_FP32, "tf32": _native.PREC_TF32, "simt": _native.PREC_SIMT}[precision]
+    wd = w.to(cuda_device)
+    packed = kernels.pack_transposed_weights(wd, prec)
+    if precision != "simt":
+        assert packed is not None
+    out = kernels.conv_transpose3d(lz, wd, b.to(cuda_device), kernel, packed=packed, precision=prec)
     x = _lazy_ref(raw, sc, sh, True).permute(0, 4, 1, 2, 3)
-    ref = F.conv_transpose3d(x, w.permute(4, 0, 1, 2, 3), b, stride=kernel).permute(0, 2, 3, 4, 1)
-    np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), rtol=1e-5, atol=1e-5)
+    ref = F.conv_transpose3d(x.double(), w.permute(4, 0, 1, 2, 3).double(), b.double(),
+                             stride=kernel).permute(0, 2, 3, 4, 1).float()
+    tol = TF32_TOL if precision == "tf32" else dict(rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), **tol)
 
 
 def test_residual_join_matches_reference(cuda_device):
