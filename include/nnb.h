@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 3
+#define NNB_ABI_VERSION 4
 
 enum nnb_status {
   NNB_OK = 0,
@@ -43,7 +43,7 @@ enum nnb_status {
 
 /* Arithmetic of the convolution contractions. */
 enum nnb_precision {
-  NNB_PREC_FP32 = 0,   /* split-TF32 (hi/lo, 3 products): float32-level accuracy */
+  NNB_PREC_FP32 = 0,   /* split-TF32 (hi/lo products): float32-level accuracy   */
   NNB_PREC_TF32 = 1,   /* single-pass TF32 tensor cores (fast, looser bound)     */
   NNB_PREC_SIMT = 2    /* plain float32 FMA on CUDA cores (any shape)            */
 };
@@ -72,7 +72,8 @@ typedef struct nnb_conv3d_args {
   const void* packed;   /* tensor-core weight image from nnb_conv3d_pack, or NULL */
   const float* bias;    /* (cout) added to the output, or NULL */
   float* out;           /* (B, oD, oH, oW, cout) */
-  float* partials;      /* (B, ceil(oD*oH*oW/128), cout, 2) per-tile (sum, M2), or NULL */
+  float* partials;      /* (B, nnb_conv3d_partial_tiles(args), cout, 3) per-tile
+                           (sum, M2, n) of the output, or NULL */
   int32_t precision;    /* enum nnb_precision */
   int32_t operand_format; /* 0: raw float32 segments (lazy affine allowed; CUDA-core kernel);
                              1: segments prepared by nnb_prepare_operand for `precision`
@@ -94,8 +95,10 @@ int32_t nnb_device_status(int32_t* where, int32_t reset);
 /*
  * 3-D convolution with padding, stride and up to two concatenated input
  * segments, optional lazy instance-norm + LeakyReLU per segment, optional
- * bias, and per-128-voxel-tile instance-norm partial statistics of the
- * output.  Replaces `ConvNorm._conv_norm` -> `_unbiased_convolution`
+ * bias, and per-tile instance-norm partial statistics of the output.  The
+ * tensor-core path (operand_format 1) needs 32-multiple segment channels,
+ * 16-byte aligned segments, cout % 16 == 0, kernel <= 15 and stride <= 8 per
+ * axis, and at most 1024 K-steps (taps x cin_total / 32).  Replaces `ConvNorm._conv_norm` -> `_unbiased_convolution`
  * (`mx.conv3d`, and the split-K decoder concat) in
  * src/nnunet_mlx/model/network.py:214-269,305-322 and the single-channel
  * Metal kernel src/nnunet_mlx/kernels/metal_single_channel_conv.py:32-97.
@@ -114,12 +117,22 @@ int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
 int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t voxels, float slope,
                             int32_t precision, float* out, void* stream);
 
+/*
+ * Tiles per sample of the partials nnb_conv3d writes for `args` (only the
+ * shape fields, operand_format and num_segments are read): bricks of at most
+ * 128 output voxels on the tensor-core path, 128-voxel runs otherwise.
+ * Negative: an nnb_status error.  No reference counterpart (MLX reduces
+ * statistics in its own norm pass).
+ */
+int64_t nnb_conv3d_partial_tiles(const nnb_conv3d_args* args);
+
 /* Bytes of the tensor-core weight image for (cout, kvol, cin_total, precision). */
 int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision);
 
 /*
- * Build the tensor-core weight image (per N-tile, per K-step, hi/lo split,
- * 128-byte swizzled K-major rows) from converted-layout weights.  Replaces the
+ * Build the tensor-core weight image (per N-tile, per K-step, [W_hi; W_lo]
+ * stacked along N, 128-byte swizzled K-major rows) from converted-layout
+ * weights.  The image must start on a 1024-byte boundary.  Replaces the
  * weight layout work MLX does inside `mx.conv3d` for
  * src/nnunet_mlx/model/network.py:261-269.
  */
@@ -127,13 +140,13 @@ int32_t nnb_conv3d_pack(const float* weight, int32_t cout, int32_t kvol, int32_t
                         int32_t precision, void* packed, void* stream);
 
 /*
- * Instance-norm statistics from per-tile (sum, M2) partials (Chan's parallel
- * combination in float64) -> per-(sample, channel) scale = gamma*rsqrt(var+eps)
+ * Instance-norm statistics from `tiles` per-tile (sum, M2, n) partials per
+ * (sample, channel) (Chan's parallel combination in float64) -> per-(sample, channel) scale = gamma*rsqrt(var+eps)
  * and shift = beta - mean*scale.  Replaces the reduction passes of
  * src/nnunet_mlx/kernels/metal_native_norm.py:32-60,92-153 (the affine pass
  * 62-70,155-168 is applied lazily by consumers).
  */
-int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t voxels,
+int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t tiles,
                                    int32_t channels, const float* gamma, const float* beta,
                                    float eps, float* scale, float* shift, void* stream);
 

@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 PREC_FP32 = 0   # split-TF32 hi/lo tensor cores, float32-level accuracy
 PREC_TF32 = 1   # single-pass TF32 tensor cores
@@ -47,6 +47,7 @@ SYMBOLS = {
     "nnb_last_error": (ctypes.c_char_p, []),
     "nnb_device_status": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "nnb_conv3d": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs), ctypes.c_void_p]),
+    "nnb_conv3d_partial_tiles": (ctypes.c_int64, [ctypes.POINTER(Conv3dArgs)]),
     "nnb_conv3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
     "nnb_prepare_operand": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),

@@ -25,7 +25,8 @@ int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream);
 int64_t conv3d_tc_packed_bytes(int cout, int kvol, int cin_total, int precision);
 int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int precision, void* packed,
                        cudaStream_t stream);
-int launch_norm_finalize(const float* partials, int batch, int voxels, int channels, const float* gamma,
+int conv3d_tc_partial_tiles(const nnb_conv3d_args& a);
+int launch_norm_finalize(const float* partials, int batch, int tiles, int channels, const float* gamma,
                          const float* beta, float eps, float* scale, float* shift, cudaStream_t stream);
 int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
                                float slope, const float* weight, const float* bias, int cout, float* out,
@@ -124,13 +125,24 @@ int32_t nnb_conv3d_pack(const float* weight, int32_t cout, int32_t kvol, int32_t
   return launch_conv3d_pack(weight, cout, kvol, cin_total, precision, packed, (cudaStream_t)stream);
 }
 
-int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t voxels, int32_t channels,
+int64_t nnb_conv3d_partial_tiles(const nnb_conv3d_args* a) {
+  NNB_REQUIRE(a != nullptr, "conv3d_partial_tiles: null args");
+  NNB_REQUIRE(positive3(a->out_dims) && positive3(a->kernel) && positive3(a->stride),
+              "conv3d_partial_tiles: dims, kernel and stride must be positive");
+  if (a->operand_format == 1) {
+    NNB_REQUIRE(a->num_segments == 1 || a->num_segments == 2, "conv3d_partial_tiles: 1 or 2 input segments");
+    return conv3d_tc_partial_tiles(*a);
+  }
+  return tiles_per_sample((int64_t)a->out_dims[0] * a->out_dims[1] * a->out_dims[2]);
+}
+
+int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t tiles, int32_t channels,
                                    const float* gamma, const float* beta, float eps, float* scale, float* shift,
                                    void* stream) {
   NNB_REQUIRE(partials && scale && shift, "instance_norm_finalize: null pointer");
-  NNB_REQUIRE(batch >= 1 && voxels >= 1 && channels >= 1, "instance_norm_finalize: bad shape");
+  NNB_REQUIRE(batch >= 1 && tiles >= 1 && channels >= 1, "instance_norm_finalize: bad shape");
   NNB_REQUIRE(eps > 0.f, "instance_norm_finalize: eps must be positive");
-  return launch_norm_finalize(partials, batch, voxels, channels, gamma, beta, eps, scale, shift,
+  return launch_norm_finalize(partials, batch, tiles, channels, gamma, beta, eps, scale, shift,
                               (cudaStream_t)stream);
 }
 

@@ -92,9 +92,10 @@ __global__ void __launch_bounds__(kTileRows) conv3d_simt_kernel(nnb_conv3d_args 
       const float d = red[i][r] - mean;
       m2 = fmaf(d, d, m2);
     }
-    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 2;
+    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 3;
     p[0] = sum;
     p[1] = m2;
+    p[2] = (float)rows;
   }
 }
 
@@ -186,9 +187,10 @@ __global__ void __launch_bounds__(kTileRows) conv3d_small_cin_kernel(nnb_conv3d_
       const float d = out_s[i][r] - mean;
       m2 = fmaf(d, d, m2);
     }
-    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 2;
+    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 3;
     p[0] = sum;
     p[1] = m2;
+    p[2] = (float)rows;
   }
 }
 
@@ -213,10 +215,10 @@ int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
 
 // ---------------------------------------------------------------------------
 // Instance-norm finalisation: one block per (channel, sample); each thread
-// merges its tiles' (n, mean, M2) in float64, then a tree merge.
+// merges its tiles' (sum, M2, n) partials in float64, then a tree merge.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restrict__ partials,
-                                                            int voxels, int channels, int tps,
+                                                            int channels, int tps,
                                                             const float* __restrict__ gamma,
                                                             const float* __restrict__ beta, float eps,
                                                             float* __restrict__ scale,
@@ -226,9 +228,10 @@ __global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restr
   const int b = blockIdx.y;
   Moments acc{0.0, 0.0, 0.0};
   for (int t = threadIdx.x; t < tps; t += blockDim.x) {
-    const int n = min(kTileRows, voxels - t * kTileRows);
-    const float* p = partials + (((int64_t)b * tps + t) * channels + c) * 2;
-    Moments tile{(double)n, (double)p[0] / n, (double)p[1]};
+    const float* p = partials + (((int64_t)b * tps + t) * channels + c) * 3;
+    const double n = (double)p[2];
+    if (n <= 0.0) continue;
+    Moments tile{n, (double)p[0] / n, (double)p[1]};
     acc = merge(acc, tile);
   }
   sm[threadIdx.x] = acc;
@@ -239,7 +242,7 @@ __global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restr
   }
   if (threadIdx.x == 0) {
     const Moments tot = sm[0];
-    double var = tot.m2 / tot.n;
+    double var = tot.n > 0.0 ? tot.m2 / tot.n : 0.0;
     if (var < 0) var = 0;
     const double inv = 1.0 / sqrt(var + (double)eps);
     const double sc = gamma != nullptr ? (double)gamma[c] * inv : inv;
@@ -249,12 +252,10 @@ __global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restr
   }
 }
 
-int launch_norm_finalize(const float* partials, int batch, int voxels, int channels, const float* gamma,
+int launch_norm_finalize(const float* partials, int batch, int tiles, int channels, const float* gamma,
                          const float* beta, float eps, float* scale, float* shift, cudaStream_t stream) {
-  const int tps = tiles_per_sample(voxels);
   dim3 grid((unsigned)channels, (unsigned)batch);
-  norm_finalize_kernel<<<grid, 256, 0, stream>>>(partials, voxels, channels, tps, gamma, beta, eps, scale,
-                                                 shift);
+  norm_finalize_kernel<<<grid, 256, 0, stream>>>(partials, channels, tiles, gamma, beta, eps, scale, shift);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }

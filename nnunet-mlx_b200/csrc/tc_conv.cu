@@ -1,418 +1,179 @@
-// Tensor-core (tcgen05 / TMEM) implicit-GEMM 3-D convolution for sm_100a.
+// Tensor-core (tcgen05 / TMEM / TMA) implicit-GEMM 3-D convolution for sm_100a.
 //
-// GEMM view: M = output voxels of one sample (128-row tiles that never
-// straddle samples), N = output channels (BN-wide tiles), K = taps x input
-// channels, walked in K-steps of one tap x 32 channels.
+// GEMM view: M = output voxels of one sample, N = output channels, K = taps x
+// input channels, walked in K-steps of one tap x 32 channels.
 //
-// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
-// Warp roles (9 warps):
-//   warps 0-3   producers (one warp per TMEM lane quarter).  For each step a producer
-//               thread gathers its row (one output voxel, 32 input channels;
-//               zero for padding taps), applies the lazy instance-norm affine
-//               + LeakyReLU of the producing layer, splits it into TF32 hi/lo
-//               and writes both halves into a TMEM A stage with tcgen05.st.
-//               The gathers of the next two steps are in flight while the
-//               current step is transformed and stored.  The group's first thread also issues the bulk copy
-//               (cp.async.bulk) of the step's pre-swizzled weight tile into a
-//               128B-swizzled K-major shared-memory stage.
-//   warp 8      allocates TMEM and issues tcgen05.mma (A from TMEM, B from
-//               shared memory): per 8-channel sub-step A_hi*B_hi + A_hi*B_lo +
-//               A_lo*B_hi (float32-level accuracy) or A*B (single-pass TF32),
-//               into one of two TMEM accumulators; tcgen05.commit releases the
-//               stage and, after the tile's last step, the accumulator.
-//   warps 4-7   epilogue: tcgen05.ld of a finished accumulator (overlapping
-//               the next tile's main loop), output rows to global memory and
-//               per-tile (sum, M2) instance-norm partials, or -- for a
-//               stride == kernel transposed convolution -- the scatter of each
-//               (tap, channel) column block to its up-sampled voxel plus bias.
+// Row tiles are bricks.  The 128 GEMM rows of a tile are a brick of output
+// voxels (tw x th x td, w fastest) chosen per layer to cover the volume with
+// the fewest tiles.  The input voxels one tap reads for a brick form the same
+// brick shifted by the tap offset and, for a strided convolution, sampled
+// every stride voxels -- exactly what one tiled TMA box load
+// (cp.async.bulk.tensor, 5-D map (channels, W, H, D, batch), box 32 x tw x th
+// x td x 1 with the convolution strides as element strides, 128-byte swizzle,
+// zero fill outside the volume = the zero padding) writes into shared memory,
+// already in the K-major SW128 layout tcgen05.mma reads.  Operands are
+// prepared once per activation by nnb_prepare_operand (the producing layer's
+// instance-norm affine + LeakyReLU applied, split into TF32 hi/lo halves), so
+// no thread touches activations in the main loop.
+//
+// Weights: B stacks [W_hi ; W_lo] along N (N = 2 x the tile's output
+// channels), so per 8-channel sub-step two MMAs, A_hi x [W_hi;W_lo] and
+// A_lo x [W_hi;W_lo], form every hi/lo product in the two halves of the
+// accumulator; the epilogue adds the halves (float32-level accuracy).  A
+// tcgen05.mma costs at least ~46 cycles at M = 128 whatever N is, so stacking
+// halves the instruction count of the 32- and 64-channel layers.  Single-pass
+// TF32 mode uses B = W_tf32 and one MMA per sub-step.
+//
+// Persistent kernel, one CTA per SM walking tiles blockIdx.x, +gridDim.x, ...
+//   warp 0      one thread issues, per K-step, the TMA box load(s) of A and
+//               the bulk copy of the pre-swizzled B tile into a pipeline stage.
+//   warp 1      allocates TMEM; one thread issues tcgen05.mma into one of two
+//               TMEM accumulators and tcgen05.commit releases stages and
+//               finished accumulators.
+//   warps 2-5   epilogue: tcgen05.ld of a finished accumulator (overlapping the
+//               next tile's main loop), bias, output rows, per-tile
+//               (sum, M2, n) instance-norm partials -- or, for a stride ==
+//               kernel transposed convolution run as a 1x1x1 GEMM with
+//               N = taps x channels, the scatter of each (tap, channel) block
+//               to its up-sampled voxel.
 //
 // Every mbarrier wait is bounded by the global timer; on expiry the CTA
-// records NNB_E_DEVICE in a device status word and drains.
+// records NNB_E_DEVICE in a device status word, waits (bounded) for its
+// copies and MMAs in flight, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <stdint.h>
 
 #include "common.cuh"
 
 namespace nnb {
-
-__device__ int g_device_status = 0;      // first device-side error code (0 = ok)
+__device__ int g_device_status = 0;
 __device__ int g_device_status_where = 0;
+}  // namespace nnb
 
+#include "tc_common.cuh"
+
+namespace nnb {
 namespace tc {
 
-constexpr int BM = 128;
-constexpr int BK = 32;              // input channels per K-step (128 bytes of fp32)
-constexpr int kProducerWarps = 4;               // one warp per TMEM lane quarter
-constexpr int kCtrlWarp = kProducerWarps + 4;    // warps 4..7 epilogue, warp 8 MMA
-constexpr int kThreads = (kCtrlWarp + 1) * 32;
-constexpr int kTmemCols = 512;
-constexpr int kMaxSmem = 227 * 1024;
-constexpr int kMaxKsteps = 1024;                 // K-step table capacity (taps x 32-channel chunks)
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int kThreads = 6 * 32;
+constexpr int kMiscBytes = 1024;
 
-template <int BN, bool SPLIT>
-struct Cfg {
-  static constexpr int kHalves = SPLIT ? 2 : 1;
-  static constexpr int kAcols = BK * kHalves;                      // TMEM columns per A stage
-  static constexpr int kAccCols = (BN + 31) / 32 * 32;
-  static constexpr int kAccBufs = (2 * kAccCols + 4 * kAcols <= kTmemCols) ? 2 : 1;
-  static constexpr int kBBytes = BN * 128 * kHalves;               // smem bytes per B stage
-  static constexpr int kTmemStages = (kTmemCols - kAccBufs * kAccCols) / kAcols;
-  static constexpr int kSmemStages = (176 * 1024) / kBBytes;
-  static constexpr int kS0 = kTmemStages < kSmemStages ? kTmemStages : kSmemStages;
-  static constexpr int S = kS0 > 8 ? 8 : kS0;
-  // barriers (2S + 4 x 8 B), TMEM slot, abort/vote words, epilogue scratch
-  static constexpr int kMiscBytes = 1024;
-  static constexpr int kFixedSmem = S * kBBytes + 1024 /*alignment slack*/ + kMiscBytes + 8 * kMaxKsteps;
-  static_assert(S >= 2, "too few pipeline stages");
+struct Geometry {
+  int ID, IH, IW;        // input volume (tensor map extent)
+  int OD, OH, OW;        // GEMM row space: output voxels (input voxels for a transposed conv)
+  int KD, KH, KW, SD, SH, SW, PD, PH, PW;
+  int tw, th, td, rows;  // brick of one tile, rows = tw * th * td <= 128
+  int nw, nh, tps;       // bricks along w and h; bricks per sample
+  int n_tiles, total_tiles;
+  int nchunk, ksteps, c0len;
+  int up_cout, UKD, UKH, UKW;  // transposed convolution scatter (up_cout = 0 otherwise)
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+struct OperandMaps {
+  CUtensorMap seg[2];
+};
 
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+template <int BC, bool SPLIT>
+struct Cfg {
+  static constexpr int kHalves = SPLIT ? 2 : 1;
+  static constexpr int N = SPLIT ? 2 * BC : BC;  // MMA N: stacked [W_hi; W_lo] rows
+  static constexpr int kAccBufs = (2 * N <= kTmemCols) ? 2 : 1;
+  static constexpr int kABytes = kHalves * BM * 128;
+  static constexpr int kBBytes = N * 128;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kS0 = (200 * 1024) / kStageBytes;
+  static constexpr int S = kS0 > 8 ? 8 : kS0;
+  static constexpr int kSmem = S * kStageBytes + 1024 /*alignment slack*/ + kMiscBytes + 4 * kMaxKsteps;
+  static_assert(S >= 2, "too few pipeline stages");
+  static_assert(kSmem <= kMaxSmem, "shared memory budget");
+  static_assert(N % 16 == 0 && N <= 256, "MMA N");
+};
 
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-// try_wait with a suspend-time hint: a waiting thread sleeps in hardware until
-// the phase completes (or ~0.5 ms pass) instead of spinning on issue slots.
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            int c4, uint32_t bar) {
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(500000u)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: returns false if the CTA is aborting or the time limit expired.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int where,
-                                       bool honor_abort = true) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (honor_abort && *abort_flag) return false;
-    if (global_ns() - start > kWaitLimitNs) {
-      *abort_flag = 1;
-      if (atomicCAS(&g_device_status, 0, NNB_E_DEVICE) == 0) g_device_status_where = where;
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
       : "memory");
 }
 
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
-// 32 consecutive TMEM columns of this thread's lane <- v[0..31]
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
-
-// 16 TMEM lanes x 32 columns from a warp: register k of thread t goes to lane
-// taddr.lane + t/4 + 8*((k>>1)&1), column taddr.col + 8*(k>>2) + 2*(t%4) + (k&1).
-__device__ __forceinline__ void tmem_st16x256_x4(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15, %16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), Blackwell descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);         // start address   [0,14)
-  d |= (uint64_t)1 << 16;                          // LBO (unused for swizzled K-major) [16,30)
-  d |= (uint64_t)(1024 >> 4) << 32;                // SBO             [32,46)
-  d |= (uint64_t)1 << 46;                          // version = 1     [46,48)
-  d |= (uint64_t)2 << 61;                          // SWIZZLE_128B    [61,64)
-  return d;
-}
-
-// Instruction descriptor: D=f32, A=B=tf32, K-major both, N>>3, M>>4.
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-               : "memory");
-}
-
-// Transpose-reduce: lane j ends with sum over the warp's lanes of x[j].
-__device__ __forceinline__ float warp_column_sums(float (&x)[32]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int h = 16; h >= 1; h >>= 1) {
-    const bool up = (lane & h) != 0;
-#pragma unroll
-    for (int i = 0; i < h; ++i) {
-      const float send = up ? x[i] : x[i + h];
-      const float keep = up ? x[i + h] : x[i];
-      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
-    }
-  }
-  return x[0];
-}
-
-struct Geometry {
-  int ID, IH, IW, OD, OH, OW;
-  int KD, KH, KW, SD, SH, SW, PD, PH, PW;
-  int tps;          // tiles per sample
-  int nchunk;       // 32-channel chunks over all segments
-  int ksteps;       // taps * nchunk
-  int n_tiles;      // N tiles
-  int total_tiles;  // batch * tps * n_tiles
-  int cin_total;
-  // scatter epilogue (stride == kernel transposed convolution); up_cout == 0 for a convolution
-  int up_cout, UKD, UKH, UKW;
+struct TileOrigin {
+  int b, nt, t, d0, h0, w0;
 };
 
-// Per-thread row state of the tile currently being gathered (recomputed only
-// when the tile changes).  A producer thread owns rows t/4 + 8i (i = 0..3) of
-// its warp's lane quarter: for each, the linear index of the voxel that tap 0
-// reads ((b, z, y, x) of the window corner, possibly outside the volume) and a
-// bit mask of the taps that fall inside the input.
-struct RowState {
-  int it, nt;
-  int64_t corner[4];
-  uint32_t taps[4];
-};
-
-__device__ __forceinline__ void row_state_update(const Geometry& g, int it, int qrow0, RowState& rs) {
-  const int tile = blockIdx.x + it * gridDim.x;
+__device__ __forceinline__ TileOrigin tile_origin(const Geometry& g, int tile) {
+  TileOrigin o;
+  o.nt = tile % g.n_tiles;
   const int mt = tile / g.n_tiles;
-  const int t = mt % g.tps;
-  const int b = mt / g.tps;
-  const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
-  rs.it = it;
-  rs.nt = tile - mt * g.n_tiles;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t m = (int64_t)t * BM + qrow0 + 8 * i;
-    uint32_t mask = 0;
-    int64_t corner = 0;
-    if (m < ovox) {
-      const int ox = (int)(m % g.OW), oy = (int)((m / g.OW) % g.OH), oz = (int)(m / ((int64_t)g.OW * g.OH));
-      const int bz = oz * g.SD - g.PD, by = oy * g.SH - g.PH, bx = ox * g.SW - g.PW;
-      corner = (((int64_t)b * g.ID + bz) * g.IH + by) * g.IW + bx;
-      int tap = 0;
-      for (int kz = 0; kz < g.KD; ++kz) {
-        const bool okz = bz + kz >= 0 && bz + kz < g.ID;
-        for (int ky = 0; ky < g.KH; ++ky) {
-          const bool oky = okz && by + ky >= 0 && by + ky < g.IH;
-          for (int kx = 0; kx < g.KW; ++kx, ++tap) {
-            if (oky && bx + kx >= 0 && bx + kx < g.IW) mask |= 1u << tap;
-          }
-        }
-      }
-    }
-    rs.corner[i] = corner;
-    rs.taps[i] = mask;
-  }
+  o.b = mt / g.tps;
+  o.t = mt - o.b * g.tps;
+  const int plane = g.nh * g.nw;
+  const int tdi = o.t / plane;
+  const int rem = o.t - tdi * plane;
+  const int thi = rem / g.nw;
+  o.d0 = tdi * g.td;
+  o.h0 = thi * g.th;
+  o.w0 = (rem - thi * g.nw) * g.tw;
+  return o;
 }
 
-// One half-step of a thread: rows 2h and 2h+1, 8 channels each, hi (and lo).
-struct HalfInfo {
-  int it, ks, nt;
-};
-
-// K-step table entry: .x = tap | chunk << 8, .y = voxel offset of the tap from the window corner
-template <bool SPLIT>
-__device__ __forceinline__ void gather_half(const nnb_conv3d_args& a, const Geometry& g, int it, int ks, int half,
-                                            int qrow0, int cq, const int2* kstab, RowState& rs, HalfInfo& info,
-                                            float (&v)[32]) {
-  if (it != rs.it) row_state_update(g, it, qrow0, rs);
-  const int2 e = kstab[ks];
-  const int tap = e.x & 255;
-  const int cglob = (e.x >> 8) * BK;
-  const bool second = cglob >= a.seg[0].channels;
-  const float* sdata = second ? a.seg[1].data : a.seg[0].data;
-  const int schan = second ? a.seg[1].channels : a.seg[0].channels;
-  const int cl = cglob - (second ? a.seg[0].channels : 0) + 8 * cq;
-  const int64_t rstride = (int64_t)(SPLIT ? 2 : 1) * schan;  // floats per voxel of the prepared operand
-  info.it = it;
-  info.ks = ks;
-  info.nt = rs.nt;
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int i = 2 * half + j;
-    if ((rs.taps[i] >> tap) & 1u) {
-      const float* src = sdata + (rs.corner[i] + e.y) * rstride + cl;
-      const float4 h0 = __ldg(reinterpret_cast<const float4*>(src));
-      const float4 h1 = __ldg(reinterpret_cast<const float4*>(src) + 1);
-      v[16 * j + 0] = h0.x; v[16 * j + 1] = h0.y; v[16 * j + 2] = h0.z; v[16 * j + 3] = h0.w;
-      v[16 * j + 4] = h1.x; v[16 * j + 5] = h1.y; v[16 * j + 6] = h1.z; v[16 * j + 7] = h1.w;
-      if constexpr (SPLIT) {
-        const float4 l0 = __ldg(reinterpret_cast<const float4*>(src + schan));
-        const float4 l1 = __ldg(reinterpret_cast<const float4*>(src + schan) + 1);
-        v[16 * j + 8] = l0.x; v[16 * j + 9] = l0.y; v[16 * j + 10] = l0.z; v[16 * j + 11] = l0.w;
-        v[16 * j + 12] = l1.x; v[16 * j + 13] = l1.y; v[16 * j + 14] = l1.z; v[16 * j + 15] = l1.w;
-      }
-    } else {
-#pragma unroll
-      for (int f = 0; f < 16; ++f) v[16 * j + f] = 0.f;
-    }
-  }
-}
-
-// Registers of one 16x256b.x4 store from two rows' 8 values: register k -> lane
-// +8*((k>>1)&1), column 8*(k>>2) + 2*(t%4) + (k&1); TMEM column 8*rep + 2*(t%4) + e
-// holds channel 8*(t%4) + 2*rep + e (the weight image uses the same K order).
-__device__ __forceinline__ void st_rows(uint32_t taddr, const float (&v)[32], int off) {
-  uint32_t r[16];
-#pragma unroll
-  for (int rep = 0; rep < 4; ++rep) {
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      r[4 * rep + e] = __float_as_uint(v[off + 2 * rep + e]);
-      r[4 * rep + 2 + e] = __float_as_uint(v[16 + off + 2 * rep + e]);
-    }
-  }
-  tmem_st16x256_x4(taddr, r);
-}
-
-// Returns false when the CTA is aborting.
-template <int BN, bool SPLIT>
-__device__ __forceinline__ bool process_half(const nnb_conv3d_args& a, const Geometry& g, int G, int half,
-                                             const HalfInfo& info, const float (&v)[32], uint64_t* bars,
-                                             uint8_t* b_stages, uint32_t tmem_a0, uint32_t lane_base, bool leader,
-                                             volatile int* abort_flag, int& s) {
-  using C = Cfg<BN, SPLIT>;
-  constexpr int S = C::S;
-  if (half == 0) {
-    if (G >= S) {
-      const bool ok = mbar_wait(smem_u32(&bars[S + s]), ((G / S) - 1) & 1, abort_flag, 2);
-      if (!__all_sync(0xffffffffu, ok)) return false;  // warp-uniform exit before .sync.aligned ops
-      fence_after();  // order the TMEM overwrite after the MMAs that read this stage
-    }
-    if (leader) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.packed) +
-                           ((int64_t)info.nt * g.ksteps + info.ks) * C::kBBytes;
-      const uint32_t full = smem_u32(&bars[s]);
-      mbar_arrive_expect_tx(full, C::kBBytes);
-      bulk_g2s(smem_u32(b_stages + s * C::kBBytes), src, C::kBBytes, full);
-    }
-  }
-  __syncwarp();
-  const uint32_t a_stage = tmem_a0 + s * C::kAcols + lane_base + ((16u * half) << 16);
-  st_rows(a_stage, v, 0);
-  if constexpr (SPLIT) st_rows(a_stage + BK, v, 8);
-  if (half == 1) {
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    fence_before();
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(smem_u32(&bars[s]));
-    if (++s == S) s = 0;
-  }
-  return true;
-}
-
-template <int BN, bool SPLIT>
-__global__ void __launch_bounds__(kThreads, 1) conv3d_tc_kernel(nnb_conv3d_args a, Geometry g) {
-  using C = Cfg<BN, SPLIT>;
+template <int BC, bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3d_tc_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
+  using C = Cfg<BC, SPLIT>;
   constexpr int S = C::S;
   constexpr int NB = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* b_stages = smem;
-  uint8_t* misc = smem + S * C::kBBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);  // full[S], empty[S], accf[2], acce[2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * (2 * S + 4));
+  uint8_t* stages = smem;  // S x [A hi | A lo | B], each 1024-aligned
+  uint8_t* misc = smem + S * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);  // full[S], empty[S], accf[2], acce[2], drain
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * (2 * S + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* votes = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [4]
   float* red = reinterpret_cast<float*>(misc + 256);                      // [4][32]
   float* col_mean = red + 4 * 32;                                         // [32]
-  int2* kstab = reinterpret_cast<int2*>(misc + C::kMiscBytes);            // [ksteps <= kMaxKsteps]
+  int* kstab = reinterpret_cast<int*>(misc + kMiscBytes);                 // kx | ky<<4 | kz<<8 | chunk<<12
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int my_tiles = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
+  const uint32_t drain_bar = smem_u32(&bars[2 * S + 4]);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&bars[s]), 5);      // 4 producer warps + 1 expect_tx arrival
+      mbar_init(smem_u32(&bars[s]), 1);      // producer's arrive.expect_tx, then the copies' bytes
       mbar_init(smem_u32(&bars[S + s]), 1);  // tcgen05.commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&bars[2 * S + i]), 1);      // accumulator full: tcgen05.commit
       mbar_init(smem_u32(&bars[2 * S + 2 + i]), 4);  // accumulator empty: 4 epilogue warps
     }
+    mbar_init(drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   for (int ks = threadIdx.x; ks < g.ksteps; ks += blockDim.x) {
     const int tap = ks / g.nchunk, chunk = ks - tap * g.nchunk;
     const int kx = tap % g.KW, ky = (tap / g.KW) % g.KH, kz = tap / (g.KW * g.KH);
-    kstab[ks] = make_int2(tap | (chunk << 8), (kz * g.IH + ky) * g.IW + kx);
+    kstab[ks] = kx | (ky << 4) | (kz << 8) | (chunk << 12);
   }
-  if (warp == kCtrlWarp) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
                  : "memory");
@@ -422,100 +183,95 @@ __global__ void __launch_bounds__(kThreads, 1) conv3d_tc_kernel(nnb_conv3d_args 
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_a0 = tmem + NB * C::kAccCols;
 
-  if (warp == kCtrlWarp) {
-    // ------------------------------ MMA issuer ------------------------------
+  if (warp == 0) {
+    // ------------------------------ TMA producer -----------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM, BN);
+      const uint32_t tx = (uint32_t)(C::kHalves * g.rows * 128 + C::kBBytes);
+      int issued = 0;
+      bool alive = true;
+      for (int it = 0; it < my_tiles && alive; ++it) {
+        const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
+        const int wb = o.w0 * g.SW - g.PW, hb = o.h0 * g.SH - g.PH, db = o.d0 * g.SD - g.PD;
+        const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(a.packed) + (int64_t)o.nt * g.ksteps * C::kBBytes;
+        for (int ks = 0; ks < g.ksteps; ++ks) {
+          const int G = it * g.ksteps + ks;
+          const int s = G % S;
+          if (G >= S && !mbar_wait(smem_u32(&bars[S + s]), ((G / S) - 1) & 1, abort_flag, 12)) {
+            alive = false;
+            break;
+          }
+          const int e = kstab[ks];
+          const int cg = (e >> 12) * BK;
+          const bool second = cg >= g.c0len;
+          const int cl = second ? cg - g.c0len : cg;
+          const int cs = second ? a.seg[1].channels : g.c0len;
+          const CUtensorMap* map = &maps.seg[second ? 1 : 0];
+          const int w = wb + (e & 15), h = hb + ((e >> 4) & 15), d = db + ((e >> 8) & 15);
+          const uint32_t full = smem_u32(&bars[s]);
+          const uint32_t st = smem_u32(stages + s * C::kStageBytes);
+          mbar_arrive_expect_tx(full, tx);
+          tma_load_5d(st, map, cl, w, h, d, o.b, full);
+          if constexpr (SPLIT) tma_load_5d(st + BM * 128, map, cs + cl, w, h, d, o.b, full);
+          bulk_g2s(st + C::kABytes, bsrc + (int64_t)ks * C::kBBytes, C::kBBytes, full);
+          issued = G + 1;
+        }
+      }
+      if (*abort_flag) {
+        // wait (bounded) for the copies still in flight: the last S issued steps
+        for (int G = std::max(0, issued - S); G < issued; ++G)
+          mbar_wait(smem_u32(&bars[G % S]), (G / S) & 1, abort_flag, 15, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer -------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM, C::N);
       bool alive = true;
       for (int it = 0; it < my_tiles && alive; ++it) {
         const int ab = NB == 2 ? (it & 1) : 0;
         if (it >= NB) {
-          if (!mbar_wait(smem_u32(&bars[2 * S + 2 + ab]), ((it / NB) - 1) & 1, abort_flag, 4)) break;
+          if (!mbar_wait(smem_u32(&bars[2 * S + 2 + ab]), ((it / NB) - 1) & 1, abort_flag, 14)) break;
           fence_after();
         }
-        const uint32_t d = tmem + ab * C::kAccCols;
+        const uint32_t d = tmem + ab * C::N;
         for (int ks = 0; ks < g.ksteps; ++ks) {
           const int G = it * g.ksteps + ks;
           const int s = G % S;
-          if (!mbar_wait(smem_u32(&bars[s]), (G / S) & 1, abort_flag, 1)) {
+          if (!mbar_wait(smem_u32(&bars[s]), (G / S) & 1, abort_flag, 11)) {
             alive = false;
             break;
           }
           fence_after();
-          const uint32_t b_hi = smem_u32(b_stages + s * C::kBBytes);
-          const uint32_t a_hi = tmem_a0 + s * C::kAcols;
+          const uint32_t st = smem_u32(stages + s * C::kStageBytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t dh = sw128_desc(b_hi + kk * 32);
-            mma_tf32_ts(d, a_hi + kk * 8, dh, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-            if constexpr (SPLIT) {
-              const uint64_t dl = sw128_desc(b_hi + BN * 128 + kk * 32);
-              mma_tf32_ts(d, a_hi + kk * 8, dl, idesc, 1u);
-              mma_tf32_ts(d, a_hi + BK + kk * 8, dh, idesc, 1u);
-            }
+            const uint64_t bd = sw128_desc(st + C::kABytes + kk * 32);
+            mma_tf32_ss(d, sw128_desc(st + kk * 32), bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (SPLIT) mma_tf32_ss(d, sw128_desc(st + BM * 128 + kk * 32), bd, idesc, 1u);
           }
           mma_commit(smem_u32(&bars[S + s]));
         }
-        mma_commit(smem_u32(&bars[2 * S + ab]));
+        if (alive) mma_commit(smem_u32(&bars[2 * S + ab]));
+      }
+      if (*abort_flag) {
+        // wait (bounded) for every MMA this thread issued before TMEM is freed
+        mma_commit(drain_bar);
+        mbar_wait(drain_bar, 0, abort_flag, 16, false);
       }
     }
     __syncwarp();
-  } else if (warp < kProducerWarps) {
-    // ------------------------------ producers -------------------------------
-    const int q = warp & 3;
-    const int qrow0 = q * 32 + (lane >> 2);  // first of this thread's rows (then +8, +16, +24)
-    const int cq = lane & 3;                 // 8-channel group of this thread
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const bool leader = (q == 0 && lane == 0);
-    // Half-steps H = 2G + half: three register buffers keep the gathers of the
-    // next two half-steps in flight while the current one is stored to TMEM.
-    const int total = 2 * my_tiles * g.ksteps;
-    RowState rs;
-    rs.it = -1;
-    int pit = 0, pks = 0, phalf = 0;  // next half-step to gather
-    auto gather_next = [&](HalfInfo& info, float (&v)[32]) {
-      gather_half<SPLIT>(a, g, pit, pks, phalf, qrow0, cq, kstab, rs, info, v);
-      if (++phalf == 2) {
-        phalf = 0;
-        if (++pks == g.ksteps) {
-          pks = 0;
-          ++pit;
-        }
-      }
-    };
-    HalfInfo i0, i1, i2;
-    float v0[32], v1[32], v2[32];
-    int H = 0;
-    int stage = 0;
-    if (total > 0) gather_next(i0, v0);
-    if (total > 1) gather_next(i1, v1);
-    while (H < total) {
-      if (H + 2 < total) gather_next(i2, v2);
-      if (!process_half<BN, SPLIT>(a, g, H >> 1, H & 1, i0, v0, bars, b_stages, tmem_a0, lane_base, leader,
-                                   abort_flag, stage))
-        break;
-      if (++H >= total) break;
-      if (H + 2 < total) gather_next(i0, v0);
-      if (!process_half<BN, SPLIT>(a, g, H >> 1, H & 1, i1, v1, bars, b_stages, tmem_a0, lane_base, leader,
-                                   abort_flag, stage))
-        break;
-      if (++H >= total) break;
-      if (H + 2 < total) gather_next(i1, v1);
-      if (!process_half<BN, SPLIT>(a, g, H >> 1, H & 1, i2, v2, bars, b_stages, tmem_a0, lane_base, leader,
-                                   abort_flag, stage))
-        break;
-      ++H;
-    }
   } else {
     // ------------------------------ epilogue ---------------------------------
-    const int q = warp & 3;
+    const int q = warp & 3;  // warps 2..5 own TMEM lane quarters 2, 3, 0, 1
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const int row = q * 32 + lane;
+    const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
+    const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
     for (int it = 0; it < my_tiles; ++it) {
       const int ab = NB == 2 ? (it & 1) : 0;
-      const bool ok = mbar_wait(smem_u32(&bars[2 * S + ab]), (it / NB) & 1, abort_flag, 3);
+      const bool ok = mbar_wait(smem_u32(&bars[2 * S + ab]), (it / NB) & 1, abort_flag, 13);
       // consistent stop decision across the four epilogue warps
       if (lane == 0) votes[q] = (!ok || *abort_flag) ? 1 : 0;
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -523,34 +279,38 @@ __global__ void __launch_bounds__(kThreads, 1) conv3d_tc_kernel(nnb_conv3d_args 
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (stop) break;
       fence_after();
-      const int tile = blockIdx.x + it * gridDim.x;
-      const int nt = tile % g.n_tiles;
-      const int mt = tile / g.n_tiles;
-      const int t = mt % g.tps;
-      const int b = mt / g.tps;
-      const int64_t m = (int64_t)t * BM + row;
-      const bool valid = m < ovox;
-      const int rows = (int)min((int64_t)BM, ovox - (int64_t)t * BM);
-      const int n0 = nt * BN;
-      const uint32_t acc = tmem + ab * C::kAccCols + lane_base;
-      for (int cc = 0; cc < C::kAccCols / 32; ++cc) {
+      const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
+      const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
+      const bool valid = row < g.rows && z < g.OD && y < g.OH && x < g.OW;
+      const int64_t m = ((int64_t)z * g.OH + y) * g.OW + x;
+      const int nvalid = min(g.td, g.OD - o.d0) * min(g.th, g.OH - o.h0) * min(g.tw, g.OW - o.w0);
+      const uint32_t acc = tmem + ab * C::N + lane_base;
+#pragma unroll 1
+      for (int cc = 0; cc < BC / 32; ++cc) {
+        const int nbase = o.nt * BC + cc * 32;
+        if (nbase >= a.cout) break;  // uniform across the epilogue warps
         float v[32];
         tmem_ld32(acc + cc * 32, v);
-        const int nbase = n0 + cc * 32;
-        if (nbase >= a.cout) continue;  // uniform: whole chunk beyond N
+        if constexpr (SPLIT) {
+          float u[32];
+          tmem_ld32(acc + BC + cc * 32, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += u[i];
+        }
         if (g.up_cout > 0) {
-          // scatter: column n = tap * up_cout + co of input voxel m -> up-sampled voxel
+          // scatter: GEMM column n = tap * up_cout + channel of input voxel (z, y, x)
           const int tap = nbase / g.up_cout;
           const int co0 = nbase - tap * g.up_cout;
           if (valid) {
             const int ux = tap % g.UKW, uy = (tap / g.UKW) % g.UKH, uz = tap / (g.UKW * g.UKH);
-            const int ix = (int)(m % g.OW), iy = (int)((m / g.OW) % g.OH), iz = (int)(m / ((int64_t)g.OW * g.OH));
-            const int OD2 = g.OD * g.UKD, OH2 = g.OH * g.UKH, OW2 = g.OW * g.UKW;
-            float* dst = a.out + ((((int64_t)b * OD2 + iz * g.UKD + uz) * OH2 + iy * g.UKH + uy) * OW2 +
-                                  ix * g.UKW + ux) * g.up_cout + co0;
+            const int64_t OH2 = (int64_t)g.OH * g.UKH, OW2 = (int64_t)g.OW * g.UKW;
+            const int64_t OD2 = (int64_t)g.OD * g.UKD;
+            float* dst = a.out + ((((int64_t)o.b * OD2 + z * g.UKD + uz) * OH2 + y * g.UKH + uy) * OW2 +
+                                  x * g.UKW + ux) * g.up_cout + co0;
+            if (a.bias != nullptr) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (a.bias != nullptr) v[i] += __ldg(a.bias + co0 + i);
+              for (int i = 0; i < 32; ++i) v[i] += __ldg(a.bias + co0 + i);
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -559,13 +319,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv3d_tc_kernel(nnb_conv3d_args 
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int n = nbase + i;
-          if (a.bias != nullptr && n < a.cout) v[i] += __ldg(a.bias + n);
+          if (a.bias != nullptr && nbase + i < a.cout) v[i] += __ldg(a.bias + nbase + i);
           if (!valid) v[i] = 0.f;
         }
         if (valid) {
-          float* dst = a.out + ((int64_t)b * ovox + m) * a.cout + nbase;
-          if (nbase + 32 <= a.cout && (a.cout % 4) == 0) {
+          float* dst = a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase;
+          if (nbase + 32 <= a.cout && (a.cout & 3) == 0) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
@@ -576,29 +335,28 @@ __global__ void __launch_bounds__(kThreads, 1) conv3d_tc_kernel(nnb_conv3d_args 
           }
         }
         if (a.partials != nullptr) {
-          float x[32];
+          // per-tile (sum, M2, n) of each column over the brick's valid rows
+          float xs[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = v[i];
-          const float colsum = warp_column_sums(x);
-          red[q * 32 + lane] = colsum;
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (q == 0) col_mean[lane] = (red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane]) / rows;
+          for (int i = 0; i < 32; ++i) xs[i] = v[i];
+          red[q * 32 + lane] = warp_column_sums(xs);
           asm volatile("bar.sync 1, 128;" ::: "memory");
           const float total = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
+          if (q == 0) col_mean[lane] = total / (float)nvalid;
+          asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float d = valid ? v[i] - col_mean[i] : 0.f;
-            x[i] = d * d;
+            const float dv = valid ? v[i] - col_mean[i] : 0.f;
+            xs[i] = dv * dv;
           }
-          const float colm2 = warp_column_sums(x);
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          red[q * 32 + lane] = colm2;
+          const float colm2 = warp_column_sums(xs);
+          red[q * 32 + lane] = colm2;  // every warp read red before the barrier above
           asm volatile("bar.sync 1, 128;" ::: "memory");
           if (q == 0 && nbase + lane < a.cout) {
-            const float m2 = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-            float* p = a.partials + (((int64_t)b * g.tps + t) * a.cout + nbase + lane) * 2;
+            float* p = a.partials + (((int64_t)o.b * g.tps + o.t) * a.cout + nbase + lane) * 3;
             p[0] = total;
-            p[1] = m2;
+            p[1] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
+            p[2] = (float)nvalid;
           }
           asm volatile("bar.sync 1, 128;" ::: "memory");
         }
@@ -609,45 +367,44 @@ __global__ void __launch_bounds__(kThreads, 1) conv3d_tc_kernel(nnb_conv3d_args 
     }
   }
   __syncthreads();
-  if (warp == kCtrlWarp) {
+  if (warp == 1) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
 // ---------------------------------------------------------------------------
-// Weight image: [n_tile][kstep][half][BN rows][128 B, 16-byte chunks XOR-swizzled by row%8].
-// GEMM row n of a convolution is output channel n; for a transposed
-// convolution (row_taps > 1) row n is (tap = n / up_cout, channel = n % up_cout)
-// and the single K tap reads weight (channel, tap, ci).
+// Weight image: [n_tile][kstep][N rows][128 B], natural K order within the
+// 32-channel step, 16-byte chunks XOR-swizzled by row % 8 (the SW128 K-major
+// layout).  Rows [0, BC) hold W_hi of the tile's BC GEMM columns and rows
+// [BC, 2 BC) W_lo (float32 mode), or BC rows of TF32.  GEMM column n is output
+// channel n, or for a transposed convolution (row_taps > 1) the pair
+// (tap = n / up_cout, channel = n % up_cout) reading weight (channel, tap, ci).
 // ---------------------------------------------------------------------------
-__global__ void pack_kernel(const float* __restrict__ w, int rows_total, int kvol, int cin_total, int bn, int halves,
-                            int nchunk, int row_taps, int up_cout, int64_t total_words, uint32_t* __restrict__ out) {
+__global__ void pack_kernel(const float* __restrict__ w, int cols_total, int kvol, int cin_total, int bc,
+                            int halves, int nchunk, int row_taps, int up_cout, int64_t total_words,
+                            uint32_t* __restrict__ out) {
+  const int nrows = halves * bc;
   for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total_words;
        o += (int64_t)gridDim.x * blockDim.x) {
-    const int word = (int)(o % 32);  // 4-byte word within a 128-byte row (physical position)
+    const int word = (int)(o % 32);  // 4-byte word within the 128-byte row (physical position)
     int64_t r = o / 32;
-    const int n = (int)(r % bn);
-    r /= bn;
-    const int half = (int)(r % halves);
-    r /= halves;
+    const int n = (int)(r % nrows);
+    r /= nrows;
     const int ks = (int)(r % ((int64_t)kvol * nchunk));
     const int nt = (int)(r / ((int64_t)kvol * nchunk));
-    const int logical_chunk = (word >> 2) ^ (n & 7);
-    const int c = logical_chunk * 4 + (word & 3);  // K column within the 32-channel step
-    // K column 8*rep + 2*j + e holds channel 8*j + 2*rep + e (the A operand's TMEM order)
-    const int k = 8 * ((c & 7) >> 1) + 2 * (c >> 3) + (c & 1);
-    const int tap = ks / nchunk;
-    const int chunk = ks % nchunk;
-    const int row = nt * bn + n;
+    const int k = ((word >> 2) ^ (n & 7)) * 4 + (word & 3);
+    const int half = n / bc;
+    const int col = nt * bc + (n - half * bc);
+    const int tap = ks / nchunk, chunk = ks - tap * nchunk;
     const int ci = chunk * BK + k;
     float val = 0.f;
-    if (row < rows_total && ci < cin_total) {
+    if (col < cols_total && ci < cin_total) {
       if (row_taps > 1) {
-        const int co = row % up_cout, utap = row / up_cout;
+        const int co = col % up_cout, utap = col / up_cout;
         val = w[((int64_t)co * row_taps + utap) * cin_total + ci];
       } else {
-        val = w[((int64_t)row * kvol + tap) * cin_total + ci];
+        val = w[((int64_t)col * kvol + tap) * cin_total + ci];
       }
     }
     uint32_t res;
@@ -655,61 +412,44 @@ __global__ void pack_kernel(const float* __restrict__ w, int rows_total, int kvo
       const uint32_t hi = __float_as_uint(val) & 0xFFFFE000u;
       res = half == 0 ? hi : __float_as_uint(val - __uint_as_float(hi));
     } else {
-      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(res) : "f"(val));
+      res = to_tf32(val);
     }
     out[o] = res;
   }
 }
 
-inline int pick_bn(int n) {
-  if (n <= 32) return 32;
-  if (n <= 64) return 64;
-  if (n % 128 == 0 || n <= 128) return 128;
-  if (n % 160 == 0) return 160;
+inline int pick_bc(int cols) {
+  if (cols <= 32) return 32;
+  if (cols <= 64) return 64;
   return 128;
 }
 
-template <int BN, bool SPLIT>
-int launch_bn(const nnb_conv3d_args& a, Geometry g, cudaStream_t stream) {
-  using C = Cfg<BN, SPLIT>;
-  auto kern = conv3d_tc_kernel<BN, SPLIT>;
-  const int smem = C::kFixedSmem;
-  int dev = 0;
-  NNB_CUDA_CHECK(cudaGetDevice(&dev));
-  static int configured_max[64] = {0};  // largest dynamic smem set per device for this instantiation
-  if (dev < 64 && configured_max[dev] < smem) {
-    NNB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
-    configured_max[dev] = kMaxSmem;
-  }
-  int sms = 148;
-  NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int grid = std::min(g.total_tiles, sms);
-  kern<<<grid, kThreads, smem, stream>>>(a, g);
-  NNB_LAUNCH_CHECK();
-  return NNB_OK;
-}
-
-int dispatch(const nnb_conv3d_args& a, Geometry& g, cudaStream_t stream) {
-  const int bn = pick_bn(a.cout);
-  g.n_tiles = (a.cout + bn - 1) / bn;
-  const int64_t tiles = (int64_t)a.batch * g.tps * g.n_tiles;
-  NNB_REQUIRE(tiles < (1LL << 31), "conv3d: too many tiles");
-  g.total_tiles = (int)tiles;
-  NNB_REQUIRE((reinterpret_cast<uintptr_t>(a.packed) & 1023) == 0, "conv3d: packed weights must be 1024-aligned");
-  const bool split = a.precision == NNB_PREC_FP32;
-  switch (bn) {
-    case 32:
-      return split ? launch_bn<32, true>(a, g, stream) : launch_bn<32, false>(a, g, stream);
-    case 64:
-      return split ? launch_bn<64, true>(a, g, stream) : launch_bn<64, false>(a, g, stream);
-    case 128:
-      return split ? launch_bn<128, true>(a, g, stream) : launch_bn<128, false>(a, g, stream);
-    default:
-      return split ? launch_bn<160, true>(a, g, stream) : launch_bn<160, false>(a, g, stream);
+// Brick (tw, th, td) with tw*th*td <= 128 covering the row space with the
+// fewest tiles (ties: the widest rows); a strided box spans tw * stride <= 256.
+inline void choose_brick(const int od, const int oh, const int ow, const int sd, const int sh, const int sw,
+                         int& tw, int& th, int& td) {
+  int64_t best = INT64_MAX;
+  tw = th = td = 1;
+  const int mw = std::min({ow, BM, 256 / sw});
+  for (int w = mw; w >= 1; --w) {
+    const int mh = std::min({oh, BM / w, 256 / sh});
+    for (int h = mh; h >= 1; --h) {
+      const int d = std::min({od, BM / (w * h), 256 / sd});
+      const int64_t tiles = (int64_t)((ow + w - 1) / w) * ((oh + h - 1) / h) * ((od + d - 1) / d);
+      if (tiles < best) {
+        best = tiles;
+        tw = w;
+        th = h;
+        td = d;
+      }
+    }
   }
 }
 
-Geometry base_geometry(const nnb_conv3d_args& a) {
+// Row-space geometry shared by the launch, the weight image size and the
+// partials query.  `rows` are output voxels (in_dims/out_dims/kernel/stride/
+// pad of the convolution).
+inline Geometry make_geometry(const nnb_conv3d_args& a) {
   Geometry g{};
   g.ID = a.in_dims[0];
   g.IH = a.in_dims[1];
@@ -726,17 +466,103 @@ Geometry base_geometry(const nnb_conv3d_args& a) {
   g.PD = a.pad[0];
   g.PH = a.pad[1];
   g.PW = a.pad[2];
-  g.tps = tiles_per_sample((int64_t)g.OD * g.OH * g.OW);
-  g.cin_total = 0;
-  for (int s = 0; s < a.num_segments; ++s) g.cin_total += a.seg[s].channels;
-  g.nchunk = g.cin_total / BK;
+  choose_brick(g.OD, g.OH, g.OW, g.SD, g.SH, g.SW, g.tw, g.th, g.td);
+  g.rows = g.tw * g.th * g.td;
+  g.nw = (g.OW + g.tw - 1) / g.tw;
+  g.nh = (g.OH + g.th - 1) / g.th;
+  g.tps = g.nw * g.nh * ((g.OD + g.td - 1) / g.td);
+  int cin_total = 0;
+  for (int s = 0; s < a.num_segments; ++s) cin_total += a.seg[s].channels;
+  g.c0len = a.seg[0].channels;
+  g.nchunk = cin_total / BK;
   g.ksteps = g.KD * g.KH * g.KW * g.nchunk;
+  const int bc = pick_bc(a.cout);
+  g.n_tiles = (a.cout + bc - 1) / bc;
+  g.up_cout = 0;
   return g;
+}
+
+using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+inline EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 5-D map (halves x channels, W, H, D, batch) of one prepared operand; the box
+// is one tile's brick for one 32-channel chunk, sampled every stride voxels.
+inline int encode_operand(const nnb_segment& seg, int halves, int batch, const Geometry& g, CUtensorMap* map) {
+  const EncodeTiledFn fn = encode_tiled();
+  NNB_REQUIRE(fn != nullptr, "conv3d: cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t inner = (cuuint64_t)halves * seg.channels;
+  const cuuint64_t dims[5] = {inner, (cuuint64_t)g.IW, (cuuint64_t)g.IH, (cuuint64_t)g.ID, (cuuint64_t)batch};
+  const cuuint64_t row = inner * sizeof(float);
+  const cuuint64_t strides[4] = {row, row * g.IW, row * g.IW * g.IH, row * g.IW * g.IH * g.ID};
+  const cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)(g.tw * g.SW), (cuuint32_t)(g.th * g.SH),
+                             (cuuint32_t)(g.td * g.SD), 1u};
+  const cuuint32_t estr[5] = {1u, (cuuint32_t)g.SW, (cuuint32_t)g.SH, (cuuint32_t)g.SD, 1u};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(seg.data), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  NNB_REQUIRE(r == CUDA_SUCCESS, "conv3d: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return NNB_OK;
+}
+
+template <int BC, bool SPLIT>
+int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& maps, cudaStream_t stream) {
+  using C = Cfg<BC, SPLIT>;
+  auto kern = conv3d_tc_kernel<BC, SPLIT>;
+  int dev = 0;
+  NNB_CUDA_CHECK(cudaGetDevice(&dev));
+  static int configured[64] = {0};  // dynamic shared memory opt-in done, per device
+  if (dev >= 64 || !configured[dev]) {
+    NNB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    if (dev < 64) configured[dev] = 1;
+  }
+  int sms = 148;
+  NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = std::min(g.total_tiles, sms);
+  kern<<<grid, kThreads, C::kSmem, stream>>>(a, g, maps);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int dispatch(const nnb_conv3d_args& a, Geometry& g, cudaStream_t stream) {
+  const int64_t tiles = (int64_t)a.batch * g.tps * g.n_tiles;
+  NNB_REQUIRE(tiles < (1LL << 31), "conv3d: too many tiles");
+  g.total_tiles = (int)tiles;
+  NNB_REQUIRE((reinterpret_cast<uintptr_t>(a.packed) & 1023) == 0, "conv3d: packed weights must be 1024-aligned");
+  const bool split = a.precision == NNB_PREC_FP32;
+  const int halves = split ? 2 : 1;
+  OperandMaps maps;
+  for (int s = 0; s < a.num_segments; ++s) {
+    const int rc = encode_operand(a.seg[s], halves, a.batch, g, &maps.seg[s]);
+    if (rc) return rc;
+  }
+  if (a.num_segments == 1) maps.seg[1] = maps.seg[0];
+  switch (pick_bc(a.cout)) {
+    case 32:
+      return split ? launch_bc<32, true>(a, g, maps, stream) : launch_bc<32, false>(a, g, maps, stream);
+    case 64:
+      return split ? launch_bc<64, true>(a, g, maps, stream) : launch_bc<64, false>(a, g, maps, stream);
+    default:
+      return split ? launch_bc<128, true>(a, g, maps, stream) : launch_bc<128, false>(a, g, maps, stream);
+  }
 }
 
 }  // namespace tc
 
 bool conv3d_tc_supported(const nnb_conv3d_args& a) {
+  if (a.precision != NNB_PREC_FP32 && a.precision != NNB_PREC_TF32) return false;
   int cin_total = 0;
   for (int s = 0; s < a.num_segments; ++s) {
     if (a.seg[s].channels % tc::BK != 0) return false;
@@ -744,33 +570,35 @@ bool conv3d_tc_supported(const nnb_conv3d_args& a) {
     cin_total += a.seg[s].channels;
   }
   if (a.cout % 16 != 0) return false;
-  // K-step table: taps x chunks entries, tap offsets < 16 per axis, chunk index < 2^19
-  if ((int64_t)a.kernel[0] * a.kernel[1] * a.kernel[2] * (cin_total / tc::BK) > tc::kMaxKsteps) return false;
-  if (a.kernel[0] > 15 || a.kernel[1] > 15 || a.kernel[2] > 15) return false;
-  return a.precision == NNB_PREC_FP32 || a.precision == NNB_PREC_TF32;
+  for (int i = 0; i < 3; ++i) {
+    if (a.kernel[i] > 15 || a.stride[i] > 8) return false;  // 4-bit tap offsets; TMA element strides <= 8
+  }
+  // K-step table capacity (taps x 32-channel chunks)
+  return (int64_t)a.kernel[0] * a.kernel[1] * a.kernel[2] * (cin_total / tc::BK) <= tc::kMaxKsteps;
 }
 
-int64_t conv3d_tc_packed_bytes(int rows, int kvol, int cin_total, int precision) {
-  if (cin_total % tc::BK != 0) return 0;
-  const int bn = tc::pick_bn(rows);
-  const int n_tiles = (rows + bn - 1) / bn;
+int64_t conv3d_tc_packed_bytes(int cols, int kvol, int cin_total, int precision) {
+  if (cols < 1 || kvol < 1 || cin_total < 1 || cin_total % tc::BK != 0) return 0;
+  if (precision != NNB_PREC_FP32 && precision != NNB_PREC_TF32) return 0;
+  const int bc = tc::pick_bc(cols);
+  const int n_tiles = (cols + bc - 1) / bc;
   const int halves = precision == NNB_PREC_FP32 ? 2 : 1;
-  return (int64_t)n_tiles * kvol * (cin_total / tc::BK) * halves * bn * 128;
+  return (int64_t)n_tiles * kvol * (cin_total / tc::BK) * halves * bc * 128;
 }
 
-int launch_conv3d_pack_rows(const float* w, int rows, int kvol, int cin_total, int precision, int row_taps,
+int launch_conv3d_pack_rows(const float* w, int cols, int kvol, int cin_total, int precision, int row_taps,
                             int up_cout, void* packed, cudaStream_t stream) {
   NNB_REQUIRE(cin_total % tc::BK == 0, "pack: input channels must be a multiple of %d", tc::BK);
   NNB_REQUIRE(precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32, "pack: precision");
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(packed) & 1023) == 0, "pack: image must be 1024-byte aligned");
-  const int bn = tc::pick_bn(rows);
-  const int n_tiles = (rows + bn - 1) / bn;
+  const int bc = tc::pick_bc(cols);
+  const int n_tiles = (cols + bc - 1) / bc;
   const int halves = precision == NNB_PREC_FP32 ? 2 : 1;
   const int nchunk = cin_total / tc::BK;
-  const int64_t words = (int64_t)n_tiles * kvol * nchunk * halves * bn * 32;
+  const int64_t words = (int64_t)n_tiles * kvol * nchunk * halves * bc * 32;
   const int blocks = (int)std::min<int64_t>((words + 255) / 256, 148 * 32);
-  tc::pack_kernel<<<blocks, 256, 0, stream>>>(w, rows, kvol, cin_total, bn, halves, nchunk, row_taps, up_cout, words,
-                                              reinterpret_cast<uint32_t*>(packed));
+  tc::pack_kernel<<<blocks, 256, 0, stream>>>(w, cols, kvol, cin_total, bc, halves, nchunk, row_taps, up_cout,
+                                              words, reinterpret_cast<uint32_t*>(packed));
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }
@@ -780,9 +608,11 @@ int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int pr
   return launch_conv3d_pack_rows(w, cout, kvol, cin_total, precision, 1, cout, packed, stream);
 }
 
+// Tiles per sample of the partials a tensor-core convolution writes.
+int conv3d_tc_partial_tiles(const nnb_conv3d_args& a) { return tc::make_geometry(a).tps; }
+
 int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream) {
-  tc::Geometry g = tc::base_geometry(a);
-  g.up_cout = 0;
+  tc::Geometry g = tc::make_geometry(a);
   return tc::dispatch(a, g, stream);
 }
 
@@ -813,7 +643,7 @@ int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_
   a.operand_format = 1;
   NNB_REQUIRE(in.scale == nullptr, "conv_transpose3d: prepared operands carry no lazy affine");
   NNB_REQUIRE(conv3d_tc_supported(a) && cout % 32 == 0, "conv_transpose3d: outside the tensor-core envelope");
-  tc::Geometry g = tc::base_geometry(a);
+  tc::Geometry g = tc::make_geometry(a);
   g.up_cout = cout;
   g.UKD = k[0];
   g.UKH = k[1];

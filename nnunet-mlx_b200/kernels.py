@@ -22,9 +22,6 @@ import torch
 from nnunet_mlx_b200 import _native
 from nnunet_mlx_b200.errors import ContractError
 
-TILE_ROWS = 128
-
-
 class _Profile:
     """Optional CUDA-event timing of every device call (used by ``bench.py`` over its timed region).
 
@@ -123,10 +120,6 @@ def _ptr(t: torch.Tensor | None) -> int:
     return 0 if t is None else t.data_ptr()
 
 
-def tiles_per_sample(voxels: int) -> int:
-    return (voxels + TILE_ROWS - 1) // TILE_ROWS
-
-
 def prepare_operand(x: Lazy, precision: int, slope: float) -> Lazy:
     """The tensor-core operand of ``x`` (affine + LeakyReLU applied once, TF32 hi/lo or TF32).
 
@@ -206,10 +199,6 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
         raise ContractError(f"convolution output would be empty for input {in_dims}")
     device = first.raw.device
     out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=device)
-    partials = None
-    if stats:
-        tps = tiles_per_sample(math.prod(out_dims))
-        partials = torch.empty((batch, tps, cout, 2), dtype=torch.float32, device=device)
     args = _native.Conv3dArgs()
     args.batch = batch
     args.in_dims = _native.dims3(in_dims)
@@ -227,7 +216,6 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
     args.packed = _ptr(packed)
     args.bias = _ptr(bias)
     args.out = out.data_ptr()
-    args.partials = _ptr(partials)
     args.precision = int(precision)
     cin = sum(item.channels for item in inputs)
     tensor_cores = (packed is not None and precision in (_native.PREC_FP32, _native.PREC_TF32)
@@ -238,6 +226,13 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
         args.operand_format = 1
     else:
         args.operand_format = 0
+    partials = None
+    if stats:
+        tiles = int(_native.load().nnb_conv3d_partial_tiles(ctypes.byref(args)))
+        if tiles < 1:
+            _native.check(tiles or -1, "conv3d_partial_tiles")
+        partials = torch.empty((batch, tiles, cout, 3), dtype=torch.float32, device=device)
+        args.partials = partials.data_ptr()
     flops = 2.0 * batch * math.prod(out_dims) * cout * cin * math.prod(kernel)
     token = PROFILE.start("conv3d_tc" if tensor_cores else "conv3d_simt", flops,
                           4.0 * (out.numel() + sum(item.raw.numel() for item in inputs)))
@@ -246,14 +241,15 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
     return out, partials
 
 
-def instance_norm_finalize(partials: torch.Tensor, voxels: int, gamma: torch.Tensor | None,
-                           beta: torch.Tensor | None, eps: float):
-    batch, _, channels, _ = partials.shape
+def instance_norm_finalize(partials: torch.Tensor, gamma: torch.Tensor | None, beta: torch.Tensor | None,
+                           eps: float):
+    """Per-(sample, channel) ``(scale, shift)`` from ``(B, tiles, C, 3)`` (sum, M2, n) partials."""
+    batch, tiles, channels, _ = partials.shape
     scale = torch.empty((batch, channels), dtype=torch.float32, device=partials.device)
     shift = torch.empty_like(scale)
     token = PROFILE.start("instance_norm_finalize", 0.0, partials.numel() * 4.0)
     _native.check(_native.load().nnb_instance_norm_finalize(
-        partials.data_ptr(), batch, voxels, channels, _ptr(gamma), _ptr(beta), float(eps),
+        partials.data_ptr(), batch, tiles, channels, _ptr(gamma), _ptr(beta), float(eps),
         scale.data_ptr(), shift.data_ptr(), _stream()), "instance_norm_finalize")
     PROFILE.stop(token)
     return scale, shift

@@ -32,7 +32,6 @@ sliding-window predictor passes the mirrored views of a tile as the batch.
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import numpy as np
@@ -139,8 +138,7 @@ class _UNetBase:
         out, partials = kernels.conv3d(
             inputs, layer.weight, kernel=layer.kernel, stride=layer.stride, pad=layer.pad, cout=layer.cout,
             packed=layer.packed, precision=PRECISIONS[self.precision], slope=self.spec.leaky_slope)
-        voxels = math.prod(out.shape[1:4])
-        scale, shift = kernels.instance_norm_finalize(partials, voxels, layer.gamma, layer.beta, self.spec.norm_eps)
+        scale, shift = kernels.instance_norm_finalize(partials, layer.gamma, layer.beta, self.spec.norm_eps)
         return Lazy(out, scale, shift, leaky=act)
 
     def _decode(self, skips: list[Lazy]) -> Lazy:

@@ -56,6 +56,11 @@ CONV_CASES = [
     (2, (8, 8, 8), [(32, True)], 64, (2, 2, 2), (2, 2, 2), (0, 0, 0), "fp32"),
     (1, (12, 12, 12), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "tf32"),
     (1, (5, 6, 7), [(64, True)], 48, (1, 3, 3), (1, 2, 2), (0, 1, 1), "fp32"),
+    # brick tiling: rows wider than one tile, anisotropic strides, partial N tiles
+    (1, (20, 17, 130), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (2, (16, 40, 40), [(32, True)], 64, (3, 3, 3), (1, 2, 2), (1, 1, 1), "tf32"),
+    (1, (7, 9, 11), [(96, True)], 96, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (1, (9, 9, 9), [(32, True), (64, False)], 16, (3, 3, 3), (2, 1, 2), (1, 1, 1), "fp32"),
 ]
 
 
@@ -85,8 +90,7 @@ def test_conv3d_matches_float32_reference(cuda_device, case):
     scale = ref.abs().max().item()
     np.testing.assert_allclose(got.numpy(), ref.numpy(), rtol=tol["rtol"], atol=tol["atol"] * max(1.0, scale))
     # instance-norm statistics from the per-tile partials
-    voxels = int(np.prod(out.shape[1:4]))
-    sc, sh = kernels.instance_norm_finalize(partials, voxels, None, None, 1e-5)
+    sc, sh = kernels.instance_norm_finalize(partials, None, None, 1e-5)
     r = ref.double()
     mean = r.mean(dim=(1, 2, 3))
     var = r.var(dim=(1, 2, 3), unbiased=False)
@@ -108,7 +112,7 @@ def test_instance_norm_finalize_with_affine_matches_torch(cuda_device):
     beta = torch.from_numpy(rng.standard_normal(4).astype(np.float32))
     out, partials = kernels.conv3d([Lazy(x.to(cuda_device))], w.to(cuda_device), kernel=(1, 1, 1), stride=(1, 1, 1),
                                    pad=(0, 0, 0), cout=4, precision=_native.PREC_SIMT)
-    sc, sh = kernels.instance_norm_finalize(partials, 990, gamma.to(cuda_device), beta.to(cuda_device), 1e-5)
+    sc, sh = kernels.instance_norm_finalize(partials, gamma.to(cuda_device), beta.to(cuda_device), 1e-5)
     y = out.cpu()
     normed = y * sc.cpu()[:, None, None, None, :] + sh.cpu()[:, None, None, None, :]
     ref = F.instance_norm(y.permute(0, 4, 1, 2, 3), weight=gamma, bias=beta, eps=1e-5).permute(0, 2, 3, 4, 1)
