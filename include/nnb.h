@@ -151,6 +151,30 @@ int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t
                                    float eps, float* scale, float* shift, void* stream);
 
 /*
+ * No-allocation variant of nnb_conv3d + nnb_instance_norm_finalize (no
+ * counterpart in the reference): the per-tile partials live in a fixed
+ * device array of NNB_STATIC_PARTIALS_FLOATS floats (16 MiB) inside the
+ * library, so the call allocates no device memory.  For callers that cannot
+ * allocate between launches -- an FFI host with no device allocator of its
+ * own, or a service that reserves all device memory up front (cudaMalloc
+ * synchronises the device and can fail under memory pressure).
+ *  - args->partials must be NULL; writes args->out plus per-(sample, channel)
+ *    scale/shift exactly as nnb_conv3d followed by nnb_instance_norm_finalize.
+ *  - Requests needing batch x nnb_conv3d_partial_tiles(args) x cout x 3 floats
+ *    beyond the scratch are rejected with NNB_E_UNSUPPORTED (e.g. a batch-8
+ *    128^3 32-channel layer needs 12.6 M floats: use nnb_conv3d).
+ *  - Nothing needs to start at zero (every partial is written before read).
+ *  - One scratch per device: calls overlapping on one device (other streams
+ *    or threads) race on it; order them.
+ *  - The first call on a device looks the scratch address up
+ *    (cudaGetSymbolAddress, with that device current); make it before any
+ *    stream capture begins.
+ */
+#define NNB_STATIC_PARTIALS_FLOATS (4 * 1024 * 1024)
+int32_t nnb_conv3d_norm_static(const nnb_conv3d_args* args, const float* gamma, const float* beta,
+                               float eps, float* scale, float* shift, void* stream);
+
+/*
  * Non-overlapping transposed convolution (kernel == stride) with lazy input
  * segment and bias.  Replaces `NonOverlappingConvTranspose3d`
  * src/nnunet_mlx/model/network.py:101-174 (matmul + interleave + bias).

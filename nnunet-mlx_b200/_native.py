@@ -48,6 +48,8 @@ SYMBOLS = {
     "nnb_device_status": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]),
     "nnb_conv3d": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs), ctypes.c_void_p]),
     "nnb_conv3d_partial_tiles": (ctypes.c_int64, [ctypes.POINTER(Conv3dArgs)]),
+    "nnb_conv3d_norm_static": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs), ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_conv3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
     "nnb_prepare_operand": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),

@@ -255,6 +255,61 @@ def instance_norm_finalize(partials: torch.Tensor, gamma: torch.Tensor | None, b
     return scale, shift
 
 
+def conv3d_norm_static(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cout: int,
+                       gamma: torch.Tensor | None, beta: torch.Tensor | None, eps: float,
+                       packed: torch.Tensor | None = None, precision: int = _native.PREC_FP32,
+                       slope: float = 0.01):
+    """``conv3d`` + ``instance_norm_finalize`` through ``nnb_conv3d_norm_static``.
+
+    The native call allocates nothing: its partial statistics live in the
+    library's fixed device scratch (``NNB_STATIC_PARTIALS_FLOATS`` floats, one
+    per device, so calls on one device must not overlap).  Returns
+    ``(out, scale, shift)``; a layer whose partials exceed the scratch raises
+    ``ContractError``.  Outputs (and a prepared operand on the tensor-core
+    path) are allocated here by torch, outside the native call.
+    """
+    first = inputs[0]
+    batch = int(first.raw.shape[0])
+    in_dims = first.spatial
+    for item in inputs[1:]:
+        if item.spatial != in_dims or int(item.raw.shape[0]) != batch:
+            raise ContractError("concatenated convolution inputs must share batch and spatial shape")
+    out_dims = tuple((i + 2 * p - k) // s + 1 for i, p, k, s in zip(in_dims, pad, kernel, stride))
+    if min(out_dims) < 1:
+        raise ContractError(f"convolution output would be empty for input {in_dims}")
+    device = first.raw.device
+    _check_tensor(weight, "weight")
+    out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=device)
+    scale = torch.empty((batch, cout), dtype=torch.float32, device=device)
+    shift = torch.empty_like(scale)
+    tensor_cores = (packed is not None and precision in (_native.PREC_FP32, _native.PREC_TF32)
+                    and all(item.channels % 32 == 0 for item in inputs) and cout % 16 == 0)
+    args = _native.Conv3dArgs()
+    args.batch = batch
+    args.in_dims = _native.dims3(in_dims)
+    args.out_dims = _native.dims3(out_dims)
+    args.kernel = _native.dims3(kernel)
+    args.stride = _native.dims3(stride)
+    args.pad = _native.dims3(pad)
+    args.num_segments = len(inputs)
+    for index, item in enumerate(inputs):
+        seg_src = prepare_operand(item, precision, slope) if tensor_cores else item
+        args.seg[index] = seg_src.segment()
+    args.slope = float(slope)
+    args.cout = int(cout)
+    args.weight = weight.data_ptr()
+    args.packed = _ptr(packed) if tensor_cores else 0
+    args.bias = 0
+    args.out = out.data_ptr()
+    args.partials = 0
+    args.precision = int(precision)
+    args.operand_format = 1 if tensor_cores else 0
+    _native.check(_native.load().nnb_conv3d_norm_static(
+        ctypes.byref(args), _ptr(gamma), _ptr(beta), float(eps), scale.data_ptr(), shift.data_ptr(), _stream()),
+        "conv3d_norm_static")
+    return out, scale, shift
+
+
 def pack_transposed_weights(weight: torch.Tensor, precision: int) -> torch.Tensor | None:
     """Tensor-core image of a stride == kernel transposed-convolution weight ``(C_out, kD, kH, kW, C_in)``."""
     if precision not in (_native.PREC_FP32, _native.PREC_TF32):
