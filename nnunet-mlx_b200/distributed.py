@@ -47,6 +47,36 @@ def slab_bounds(depth: int, rank: int, world: int) -> tuple[int, int]:
     return min(depth, rank * per), min(depth, (rank + 1) * per)
 
 
+def exchange_slabs(acc: torch.Tensor, normalizer: torch.Tensor, group=None):
+    """Sum every rank's ``(Z, Y, X, C)`` accumulator and ``(Z, Y, X)`` normaliser; keep this rank's z-slab.
+
+    One ``reduce_scatter_tensor`` over the z-major ``(Z*Y*X, C+1)`` packing
+    (z padded to a multiple of the world size).  Returns
+    ``(z_lo, z_hi, acc_slab, normalizer_slab)`` with the slab tensors shaped
+    ``(z_hi - z_lo, Y, X, C)`` and ``(z_hi - z_lo, Y, X)``.  Works on any
+    backend that implements the collective (NCCL on GPUs, gloo on CPU).
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    depth, height, width, classes = (int(s) for s in acc.shape)
+    if tuple(normalizer.shape) != (depth, height, width):
+        raise ContractError(f"normalizer shape {tuple(normalizer.shape)} does not match "
+                            f"accumulator {tuple(acc.shape)}")
+    z_lo, z_hi = slab_bounds(depth, rank, world)
+    per = -(-depth // world)
+    plane = height * width
+    full = torch.zeros((world * per * plane, classes + 1), dtype=torch.float32, device=acc.device)
+    full[: depth * plane, :classes] = acc.reshape(-1, classes)
+    full[: depth * plane, classes] = normalizer.reshape(-1)
+    mine = torch.empty((per * plane, classes + 1), dtype=torch.float32, device=acc.device)
+    dist.reduce_scatter_tensor(mine, full, group=group)
+    del full
+    mine = mine[: (z_hi - z_lo) * plane]
+    acc_slab = mine[:, :classes].contiguous().reshape(z_hi - z_lo, height, width, classes)
+    norm_slab = mine[:, classes].contiguous().reshape(z_hi - z_lo, height, width)
+    return z_lo, z_hi, acc_slab, norm_slab
+
+
 def run_units(models, volume: torch.Tensor, accumulator: VolumeAccumulator, offsets, units, patch, masks) -> None:
     current_tile = None
     batch = None
@@ -87,23 +117,11 @@ def predict_volume_sharded(models, volume: torch.Tensor, *, patch_size, num_clas
     units = shard_units(len(offsets), len(models), rank, world)
     run_units(models, volume, accumulator, offsets, units, patch, masks)
 
-    depth = spatial[0]
-    z_lo, z_hi = slab_bounds(depth, rank, world)
     if world > 1:
-        per = -(-depth // world)
-        plane = spatial[1] * spatial[2]
-        # pad z to world * per planes so the reduce-scatter splits evenly
-        full = torch.zeros((world * per * plane, num_classes + 1), dtype=torch.float32, device=volume.device)
-        full[: depth * plane, :num_classes] = accumulator.acc.reshape(-1, num_classes)
-        full[: depth * plane, num_classes] = accumulator.normalizer.reshape(-1)
+        z_lo, z_hi, acc, normalizer = exchange_slabs(accumulator.acc, accumulator.normalizer, group)
         del accumulator
-        mine = torch.empty((per * plane, num_classes + 1), dtype=torch.float32, device=volume.device)
-        dist.reduce_scatter_tensor(mine, full, group=group)
-        del full
-        mine = mine[: (z_hi - z_lo) * plane]
-        acc = mine[:, :num_classes].contiguous().reshape(z_hi - z_lo, spatial[1], spatial[2], num_classes)
-        normalizer = mine[:, num_classes].contiguous().reshape(z_hi - z_lo, spatial[1], spatial[2])
     else:
+        z_lo, z_hi = 0, spatial[0]
         acc, normalizer = accumulator.acc, accumulator.normalizer
     # intersect the slab with the crop window
     c0, c1 = crop[0].start, crop[0].stop

@@ -1,0 +1,65 @@
+"""Host side of the multi-GPU path on CPU: unit sharding, slab bounds and the
+slab exchange collective run as world-size 2 and 3 gloo process groups."""
+
+from __future__ import annotations
+
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from nnunet_mlx_b200.distributed import exchange_slabs, shard_units, slab_bounds
+
+
+@pytest.mark.parametrize("tiles,folds,world", [(121, 1, 8), (18, 5, 8), (144, 5, 3), (3, 1, 8), (7, 2, 2)])
+def test_shard_units_cover_every_unit_once_in_order(tiles, folds, world):
+    shards = [shard_units(tiles, folds, r, world) for r in range(world)]
+    flat = [u for shard in shards for u in shard]
+    assert flat == [(t, f) for t in range(tiles) for f in range(folds)]
+    sizes = [len(s) for s in shards]
+    assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("depth,world", [(128, 8), (101, 8), (5, 2), (1, 2), (284, 3)])
+def test_slab_bounds_partition_the_depth(depth, world):
+    bounds = [slab_bounds(depth, r, world) for r in range(world)]
+    assert bounds[0][0] == 0 and bounds[-1][1] == depth
+    for (lo0, hi0), (lo1, hi1) in zip(bounds, bounds[1:]):
+        assert lo0 <= hi0 == lo1 <= hi1
+
+
+def _rank_accumulator(rank: int, shape, classes: int):
+    rng = np.random.default_rng(100 + rank)
+    acc = torch.from_numpy(rng.standard_normal((*shape, classes)).astype(np.float32))
+    norm = torch.from_numpy(rng.uniform(0.1, 1.0, shape).astype(np.float32))
+    return acc, norm
+
+
+def _exchange_worker(rank: int, world: int, port: int, shape, classes: int) -> None:
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        acc, norm = _rank_accumulator(rank, shape, classes)
+        z_lo, z_hi, acc_slab, norm_slab = exchange_slabs(acc, norm)
+        assert (z_lo, z_hi) == slab_bounds(shape[0], rank, world)
+        total_acc = sum(_rank_accumulator(r, shape, classes)[0] for r in range(world))
+        total_norm = sum(_rank_accumulator(r, shape, classes)[1] for r in range(world))
+        assert acc_slab.shape == (z_hi - z_lo, shape[1], shape[2], classes)
+        assert norm_slab.shape == (z_hi - z_lo, shape[1], shape[2])
+        torch.testing.assert_close(acc_slab, total_acc[z_lo:z_hi], rtol=1e-6, atol=1e-6)
+        torch.testing.assert_close(norm_slab, total_norm[z_lo:z_hi], rtol=1e-6, atol=1e-6)
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world,shape,classes", [(2, (5, 6, 7), 3), (2, (1, 4, 4), 2), (3, (8, 3, 5), 5)])
+def test_exchange_slabs_sums_ranks_and_keeps_the_own_slab(world, shape, classes):
+    mp.spawn(_exchange_worker, args=(world, _free_port(), shape, classes), nprocs=world, join=True)
