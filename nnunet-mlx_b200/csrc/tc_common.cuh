@@ -53,10 +53,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false if the CTA is aborting or the time limit expired.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int where,
-                                       bool honor_abort = true) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Bounded wait, slow path: returns false if the CTA is aborting or the time limit expired.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int where,
+                                            bool honor_abort) {
   const uint64_t start = global_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -67,6 +66,15 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile i
       return false;
     }
   }
+}
+
+// Bounded wait: one inline try_wait (the common, already-completed or soon-completed case) and the
+// out-of-line timed loop otherwise.  Keeping the fast path free of calls matters on the MMA-issuing
+// thread: a tcgen05.mma holds the issuing thread for its whole issue slot, so anything between two
+// K-steps' MMAs (calls, descriptor arithmetic) adds to every step.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int where,
+                                          bool honor_abort = true) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, where, honor_abort);
 }
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -124,12 +132,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), Blackwell descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// `sbo` bytes apart (a multiple of 128), Blackwell descriptor version 1, base
+// offset 0.  The swizzle is a function of the shared-memory address bits
+// (measured on B200: a start at any 128-byte row and any multiple-of-128 group
+// stride read exactly the rows a TMA box or a row%8-swizzled store wrote from
+// a 1024-byte aligned base), so an operand may start inside a swizzle atom.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t sbo = 1024) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFF) >> 4);         // start address   [0,14)
   d |= (uint64_t)1 << 16;                          // LBO (unused for swizzled K-major) [16,30)
-  d |= (uint64_t)(1024 >> 4) << 32;                // SBO             [32,46)
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;      // SBO             [32,46)
   d |= (uint64_t)1 << 46;                          // version = 1     [46,48)
   d |= (uint64_t)2 << 61;                          // SWIZZLE_128B    [61,64)
   return d;

@@ -1,20 +1,10 @@
 // Tensor-core (tcgen05 / TMEM / TMA) implicit-GEMM 3-D convolution for sm_100a.
 //
 // GEMM view: M = output voxels of one sample, N = output channels, K = taps x
-// input channels, walked in K-steps of one tap x 32 channels.
-//
-// Row tiles are bricks.  The 128 GEMM rows of a tile are a brick of output
-// voxels (tw x th x td, w fastest) chosen per layer to cover the volume with
-// the fewest tiles.  The input voxels one tap reads for a brick form the same
-// brick shifted by the tap offset and, for a strided convolution, sampled
-// every stride voxels -- exactly what one tiled TMA box load
-// (cp.async.bulk.tensor, 5-D map (channels, W, H, D, batch), box 32 x tw x th
-// x td x 1 with the convolution strides as element strides, 128-byte swizzle,
-// zero fill outside the volume = the zero padding) writes into shared memory,
-// already in the K-major SW128 layout tcgen05.mma reads.  Operands are
-// prepared once per activation by nnb_prepare_operand (the producing layer's
-// instance-norm affine + LeakyReLU applied, split into TF32 hi/lo halves), so
-// no thread touches activations in the main loop.
+// input channels, walked in steps of 32 channels (128 bytes of float32).
+// Operands are prepared once per activation by nnb_prepare_operand (the
+// producing layer's instance-norm affine + LeakyReLU applied, split into TF32
+// hi/lo halves), so no thread touches activations in the main loop.
 //
 // Weights: B stacks [W_hi ; W_lo] along N (N = 2 x the tile's output
 // channels), so per 8-channel sub-step two MMAs, A_hi x [W_hi;W_lo] and
@@ -24,9 +14,26 @@
 // halves the instruction count of the 32- and 64-channel layers.  Single-pass
 // TF32 mode uses B = W_tf32 and one MMA per sub-step.
 //
+// Two ways to feed A, both from tiled TMA box loads (5-D map (channels, W, H,
+// D, batch), 128-byte swizzle, zero fill outside the volume = the padding):
+//
+//  * halo mode (stride 1, taps > 1, <= 64 output channels per tile): a tile is
+//    an 8 (w) x 16 (h) brick of output voxels.  Per (32-channel chunk, kz) one
+//    box brings the (8+KW-1) x (16+KH-1) input plane the brick's taps of that
+//    kz read; the MMA of tap (kx, ky) reads it through a descriptor starting
+//    (ky * pw + kx) rows in with 8-row groups pw rows apart (pw = 8+KW-1).  The
+//    128B swizzle is a function of the shared-memory address, so such
+//    unaligned starts and strides read exactly the rows the box wrote.  A
+//    3x3x3 conv then loads 3 planes of 180 rows per chunk instead of 27 boxes
+//    of 128 rows.  B streams per tap through its own ring.
+//  * box mode (everything else: strided convs, 1x1x1 GEMMs, wide layers):
+//    the tile is a brick chosen to cover the volume with the fewest tiles and
+//    each K-step (one tap x 32 channels) loads one box per half, the brick
+//    shifted by the tap offset and sampled every stride voxels (element
+//    strides = conv strides), plus that step's B tile.
+//
 // Persistent kernel, one CTA per SM walking tiles blockIdx.x, +gridDim.x, ...
-//   warp 0      one thread issues, per K-step, the TMA box load(s) of A and
-//               the bulk copy of the pre-swizzled B tile into a pipeline stage.
+//   warp 0      one thread issues the TMA box loads and the B bulk copies.
 //   warp 1      allocates TMEM; one thread issues tcgen05.mma into one of two
 //               TMEM accumulators and tcgen05.commit releases stages and
 //               finished accumulators.
@@ -61,7 +68,11 @@ namespace nnb {
 namespace tc {
 
 constexpr int kThreads = 6 * 32;
-constexpr int kMiscBytes = 1024;
+constexpr int kMiscBytes = 2048;  // mbarriers, TMEM slot, flags, epilogue reduction scratch
+constexpr int kMaxBars = 48;
+constexpr int kStageBudget = kMaxSmem - 1024 /*alignment slack*/ - kMiscBytes - 4 * kMaxKsteps;
+constexpr int kHaloW = 8;   // halo-mode brick: 8 (w) x 16 (h) x 1 (d)
+constexpr int kHaloH = 16;
 
 struct Geometry {
   int ID, IH, IW;        // input volume (tensor map extent)
@@ -72,6 +83,10 @@ struct Geometry {
   int n_tiles, total_tiles;
   int nchunk, ksteps, c0len;
   int up_cout, UKD, UKH, UKW;  // transposed convolution scatter (up_cout = 0 otherwise)
+  int halo;                    // 1: halo mode
+  int box[3];                  // TMA box extent along w, h, d (elements, before element strides)
+  int pw, plane_rows, plane_bytes;  // halo plane: row pitch, rows, bytes per half (1024-aligned)
+  int sa, sb;                  // halo-mode ring depths (A planes, B taps)
 };
 
 struct OperandMaps {
@@ -86,11 +101,9 @@ struct Cfg {
   static constexpr int kABytes = kHalves * BM * 128;
   static constexpr int kBBytes = N * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kS0 = (200 * 1024) / kStageBytes;
+  static constexpr int kS0 = kStageBudget / kStageBytes;
   static constexpr int S = kS0 > 8 ? 8 : kS0;
-  static constexpr int kSmem = S * kStageBytes + 1024 /*alignment slack*/ + kMiscBytes + 4 * kMaxKsteps;
   static_assert(S >= 2, "too few pipeline stages");
-  static_assert(kSmem <= kMaxSmem, "shared memory budget");
   static_assert(N % 16 == 0 && N <= 256, "MMA N");
 };
 
@@ -132,6 +145,172 @@ __device__ __forceinline__ TileOrigin tile_origin(const Geometry& g, int tile) {
   return o;
 }
 
+// Channel chunk -> (tensor map, channel coordinate of hi, of lo) for the two segments.
+struct ChunkSource {
+  const CUtensorMap* map;
+  int c_hi, c_lo;
+};
+
+__device__ __forceinline__ ChunkSource chunk_source(const nnb_conv3d_args& a, const Geometry& g,
+                                                    const OperandMaps& maps, int chunk) {
+  const int cg = chunk * BK;
+  const bool second = cg >= g.c0len;
+  const int cl = second ? cg - g.c0len : cg;
+  const int cs = second ? a.seg[1].channels : g.c0len;
+  return ChunkSource{&maps.seg[second ? 1 : 0], cl, cs + cl};
+}
+
+struct SharedMisc {
+  uint64_t* bars;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+  volatile int* votes;  // [4]
+  float* red;           // [4][32]
+  float* col_mean;      // [32]
+};
+
+__device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
+  SharedMisc m;
+  m.bars = reinterpret_cast<uint64_t*>(misc);
+  m.tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * kMaxBars);
+  m.abort_flag = reinterpret_cast<volatile int*>(m.tmem_slot + 1);
+  m.votes = reinterpret_cast<volatile int*>(m.tmem_slot + 2);
+  m.red = reinterpret_cast<float*>(misc + 512);
+  m.col_mean = reinterpret_cast<float*>(misc + 1024);
+  return m;
+}
+
+// One finished accumulator -> outputs + partials (or the transposed-conv scatter).
+template <int BC, bool SPLIT>
+__device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Geometry& g, const TileOrigin& o,
+                                              uint32_t acc, int q, int lane, float* red, float* col_mean) {
+  const int row = q * 32 + lane;
+  const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
+  const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
+  const bool valid = row < g.rows && z < g.OD && y < g.OH && x < g.OW;
+  const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
+  const int64_t m = ((int64_t)z * g.OH + y) * g.OW + x;
+  const int nvalid = min(g.td, g.OD - o.d0) * min(g.th, g.OH - o.h0) * min(g.tw, g.OW - o.w0);
+#pragma unroll 1
+  for (int cc = 0; cc < BC / 32; ++cc) {
+    const int nbase = o.nt * BC + cc * 32;
+    if (nbase >= a.cout) break;  // uniform across the epilogue warps
+    float v[32];
+    tmem_ld32(acc + cc * 32, v);
+    if constexpr (SPLIT) {
+      float u[32];
+      tmem_ld32(acc + BC + cc * 32, u);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += u[i];
+    }
+    if (g.up_cout > 0) {
+      // scatter: GEMM column n = tap * up_cout + channel of input voxel (z, y, x)
+      const int tap = nbase / g.up_cout;
+      const int co0 = nbase - tap * g.up_cout;
+      if (valid) {
+        const int ux = tap % g.UKW, uy = (tap / g.UKW) % g.UKH, uz = tap / (g.UKW * g.UKH);
+        const int64_t OH2 = (int64_t)g.OH * g.UKH, OW2 = (int64_t)g.OW * g.UKW;
+        const int64_t OD2 = (int64_t)g.OD * g.UKD;
+        float* dst = a.out + ((((int64_t)o.b * OD2 + z * g.UKD + uz) * OH2 + y * g.UKH + uy) * OW2 +
+                              x * g.UKW + ux) * g.up_cout + co0;
+        if (a.bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] += __ldg(a.bias + co0 + i);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+      continue;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (a.bias != nullptr && nbase + i < a.cout) v[i] += __ldg(a.bias + nbase + i);
+      if (!valid) v[i] = 0.f;
+    }
+    if (valid) {
+      float* dst = a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase;
+      if (nbase + 32 <= a.cout && (a.cout & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (nbase + i < a.cout) dst[i] = v[i];
+      }
+    }
+    if (a.partials != nullptr) {
+      // per-tile (sum, M2, n) of each column over the brick's valid rows
+      float xs[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) xs[i] = v[i];
+      red[q * 32 + lane] = warp_column_sums(xs);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const float total = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
+      if (q == 0) col_mean[lane] = total / (float)nvalid;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float dv = valid ? v[i] - col_mean[i] : 0.f;
+        xs[i] = dv * dv;
+      }
+      const float colm2 = warp_column_sums(xs);
+      red[q * 32 + lane] = colm2;  // every warp read red before the barrier above
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (q == 0 && nbase + lane < a.cout) {
+        float* p = a.partials + (((int64_t)o.b * g.tps + o.t) * a.cout + nbase + lane) * 3;
+        p[0] = total;
+        p[1] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
+        p[2] = (float)nvalid;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+  }
+}
+
+// Epilogue warps' loop over this CTA's tiles (accumulator full/empty handshake).
+template <int BC, bool SPLIT>
+__device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Geometry& g, int my_tiles,
+                                              uint32_t tmem, const SharedMisc& sm, uint64_t* accf, uint64_t* acce,
+                                              int warp, int lane) {
+  using C = Cfg<BC, SPLIT>;
+  constexpr int NB = C::kAccBufs;
+  const int q = warp & 3;  // warps 2..5 own TMEM lane quarters 2, 3, 0, 1
+  const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+  for (int it = 0; it < my_tiles; ++it) {
+    const int ab = NB == 2 ? (it & 1) : 0;
+    const bool ok = mbar_wait(smem_u32(&accf[ab]), (it / NB) & 1, sm.abort_flag, 13);
+    // consistent stop decision across the four epilogue warps
+    if (lane == 0) sm.votes[q] = (!ok || *sm.abort_flag) ? 1 : 0;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const bool stop = sm.votes[0] | sm.votes[1] | sm.votes[2] | sm.votes[3];
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (stop) break;
+    fence_after();
+    const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
+    epilogue_tile<BC, SPLIT>(a, g, o, tmem + ab * C::N + lane_base, q, lane, sm.red, sm.col_mean);
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&acce[ab]));
+  }
+}
+
+__device__ __forceinline__ void tmem_alloc_all(uint32_t* slot) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(kTmemCols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_free_all(uint32_t tmem) {
+  fence_after();
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Box mode: one TMA box per half and one B tile per K-step (tap x 32 channels).
+// ---------------------------------------------------------------------------
 template <int BC, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_tc_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
@@ -141,31 +320,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;  // S x [A hi | A lo | B], each 1024-aligned
-  uint8_t* misc = smem + S * C::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);  // full[S], empty[S], accf[2], acce[2], drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * (2 * S + 5));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* votes = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [4]
-  float* red = reinterpret_cast<float*>(misc + 256);                      // [4][32]
-  float* col_mean = red + 4 * 32;                                         // [32]
-  int* kstab = reinterpret_cast<int*>(misc + kMiscBytes);                 // kx | ky<<4 | kz<<8 | chunk<<12
+  const SharedMisc sm = shared_misc(smem + S * C::kStageBytes);
+  int* kstab = reinterpret_cast<int*>(smem + S * C::kStageBytes + kMiscBytes);  // kx | ky<<4 | kz<<8 | chunk<<12
+  uint64_t* full = sm.bars;
+  uint64_t* empty = sm.bars + S;
+  uint64_t* accf = sm.bars + 2 * S;
+  uint64_t* acce = sm.bars + 2 * S + 2;
+  const uint32_t drain_bar = smem_u32(sm.bars + 2 * S + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int my_tiles = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  const uint32_t drain_bar = smem_u32(&bars[2 * S + 4]);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&bars[s]), 1);      // producer's arrive.expect_tx, then the copies' bytes
-      mbar_init(smem_u32(&bars[S + s]), 1);  // tcgen05.commit
+      mbar_init(smem_u32(&full[s]), 1);   // producer's arrive.expect_tx, then the copies' bytes
+      mbar_init(smem_u32(&empty[s]), 1);  // tcgen05.commit
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&bars[2 * S + i]), 1);      // accumulator full: tcgen05.commit
-      mbar_init(smem_u32(&bars[2 * S + 2 + i]), 4);  // accumulator empty: 4 epilogue warps
+      mbar_init(smem_u32(&accf[i]), 1);  // accumulator full: tcgen05.commit
+      mbar_init(smem_u32(&acce[i]), 4);  // accumulator empty: 4 epilogue warps
     }
     mbar_init(drain_bar, 1);
-    *abort_flag = 0;
+    *sm.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   for (int ks = threadIdx.x; ks < g.ksteps; ks += blockDim.x) {
@@ -173,16 +350,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kx = tap % g.KW, ky = (tap / g.KW) % g.KH, kz = tap / (g.KW * g.KH);
     kstab[ks] = kx | (ky << 4) | (kz << 8) | (chunk << 12);
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == 1) tmem_alloc_all(sm.tmem_slot);
   fence_before();
   __syncthreads();
   fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *sm.tmem_slot;
 
   if (warp == 0) {
     // ------------------------------ TMA producer -----------------------------
@@ -197,30 +369,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < g.ksteps; ++ks) {
           const int G = it * g.ksteps + ks;
           const int s = G % S;
-          if (G >= S && !mbar_wait(smem_u32(&bars[S + s]), ((G / S) - 1) & 1, abort_flag, 12)) {
+          if (G >= S && !mbar_wait(smem_u32(&empty[s]), ((G / S) - 1) & 1, sm.abort_flag, 12)) {
             alive = false;
             break;
           }
           const int e = kstab[ks];
-          const int cg = (e >> 12) * BK;
-          const bool second = cg >= g.c0len;
-          const int cl = second ? cg - g.c0len : cg;
-          const int cs = second ? a.seg[1].channels : g.c0len;
-          const CUtensorMap* map = &maps.seg[second ? 1 : 0];
+          const ChunkSource src = chunk_source(a, g, maps, e >> 12);
           const int w = wb + (e & 15), h = hb + ((e >> 4) & 15), d = db + ((e >> 8) & 15);
-          const uint32_t full = smem_u32(&bars[s]);
+          const uint32_t fb = smem_u32(&full[s]);
           const uint32_t st = smem_u32(stages + s * C::kStageBytes);
-          mbar_arrive_expect_tx(full, tx);
-          tma_load_5d(st, map, cl, w, h, d, o.b, full);
-          if constexpr (SPLIT) tma_load_5d(st + BM * 128, map, cs + cl, w, h, d, o.b, full);
-          bulk_g2s(st + C::kABytes, bsrc + (int64_t)ks * C::kBBytes, C::kBBytes, full);
+          mbar_arrive_expect_tx(fb, tx);
+          tma_load_5d(st, src.map, src.c_hi, w, h, d, o.b, fb);
+          if constexpr (SPLIT) tma_load_5d(st + BM * 128, src.map, src.c_lo, w, h, d, o.b, fb);
+          bulk_g2s(st + C::kABytes, bsrc + (int64_t)ks * C::kBBytes, C::kBBytes, fb);
           issued = G + 1;
         }
       }
-      if (*abort_flag) {
+      if (*sm.abort_flag) {
         // wait (bounded) for the copies still in flight: the last S issued steps
         for (int G = std::max(0, issued - S); G < issued; ++G)
-          mbar_wait(smem_u32(&bars[G % S]), (G / S) & 1, abort_flag, 15, false);
+          mbar_wait(smem_u32(&full[G % S]), (G / S) & 1, sm.abort_flag, 15, false);
       }
     }
     __syncwarp();
@@ -228,149 +396,224 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ MMA issuer -------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(BM, C::N);
+      // Descriptors are stage-0 bases plus constant offsets (start address in 16-byte units), so the
+      // 4-8 MMAs of a K-step issue back to back with only adds between them.
+      const uint64_t desc0 = sw128_desc(smem_u32(stages));
+      constexpr uint32_t kLo = (BM * 128) >> 4, kB = C::kABytes >> 4, kStage = C::kStageBytes >> 4;
       bool alive = true;
+      int s = 0;
+      uint32_t phase = 0;
       for (int it = 0; it < my_tiles && alive; ++it) {
         const int ab = NB == 2 ? (it & 1) : 0;
         if (it >= NB) {
-          if (!mbar_wait(smem_u32(&bars[2 * S + 2 + ab]), ((it / NB) - 1) & 1, abort_flag, 14)) break;
+          if (!mbar_wait(smem_u32(&acce[ab]), ((it / NB) - 1) & 1, sm.abort_flag, 14)) break;
           fence_after();
         }
         const uint32_t d = tmem + ab * C::N;
         for (int ks = 0; ks < g.ksteps; ++ks) {
-          const int G = it * g.ksteps + ks;
-          const int s = G % S;
-          if (!mbar_wait(smem_u32(&bars[s]), (G / S) & 1, abort_flag, 11)) {
+          const uint64_t ad = desc0 + (uint64_t)(s * kStage);
+          if (!mbar_wait(smem_u32(&full[s]), phase, sm.abort_flag, 11)) {
             alive = false;
             break;
           }
           fence_after();
-          const uint32_t st = smem_u32(stages + s * C::kStageBytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t bd = sw128_desc(st + C::kABytes + kk * 32);
-            mma_tf32_ss(d, sw128_desc(st + kk * 32), bd, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-            if constexpr (SPLIT) mma_tf32_ss(d, sw128_desc(st + BM * 128 + kk * 32), bd, idesc, 1u);
+            mma_tf32_ss(d, ad + 2 * kk, ad + kB + 2 * kk, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (SPLIT) mma_tf32_ss(d, ad + kLo + 2 * kk, ad + kB + 2 * kk, idesc, 1u);
           }
-          mma_commit(smem_u32(&bars[S + s]));
+          mma_commit(smem_u32(&empty[s]));
+          if (++s == S) {
+            s = 0;
+            phase ^= 1u;
+          }
         }
-        if (alive) mma_commit(smem_u32(&bars[2 * S + ab]));
+        if (alive) mma_commit(smem_u32(&accf[ab]));
       }
-      if (*abort_flag) {
+      if (*sm.abort_flag) {
         // wait (bounded) for every MMA this thread issued before TMEM is freed
         mma_commit(drain_bar);
-        mbar_wait(drain_bar, 0, abort_flag, 16, false);
+        mbar_wait(drain_bar, 0, sm.abort_flag, 16, false);
       }
     }
     __syncwarp();
   } else {
-    // ------------------------------ epilogue ---------------------------------
-    const int q = warp & 3;  // warps 2..5 own TMEM lane quarters 2, 3, 0, 1
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const int row = q * 32 + lane;
-    const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
-    const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
-    for (int it = 0; it < my_tiles; ++it) {
-      const int ab = NB == 2 ? (it & 1) : 0;
-      const bool ok = mbar_wait(smem_u32(&bars[2 * S + ab]), (it / NB) & 1, abort_flag, 13);
-      // consistent stop decision across the four epilogue warps
-      if (lane == 0) votes[q] = (!ok || *abort_flag) ? 1 : 0;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      const bool stop = votes[0] | votes[1] | votes[2] | votes[3];
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (stop) break;
-      fence_after();
-      const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
-      const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
-      const bool valid = row < g.rows && z < g.OD && y < g.OH && x < g.OW;
-      const int64_t m = ((int64_t)z * g.OH + y) * g.OW + x;
-      const int nvalid = min(g.td, g.OD - o.d0) * min(g.th, g.OH - o.h0) * min(g.tw, g.OW - o.w0);
-      const uint32_t acc = tmem + ab * C::N + lane_base;
-#pragma unroll 1
-      for (int cc = 0; cc < BC / 32; ++cc) {
-        const int nbase = o.nt * BC + cc * 32;
-        if (nbase >= a.cout) break;  // uniform across the epilogue warps
-        float v[32];
-        tmem_ld32(acc + cc * 32, v);
-        if constexpr (SPLIT) {
-          float u[32];
-          tmem_ld32(acc + BC + cc * 32, u);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += u[i];
-        }
-        if (g.up_cout > 0) {
-          // scatter: GEMM column n = tap * up_cout + channel of input voxel (z, y, x)
-          const int tap = nbase / g.up_cout;
-          const int co0 = nbase - tap * g.up_cout;
-          if (valid) {
-            const int ux = tap % g.UKW, uy = (tap / g.UKW) % g.UKH, uz = tap / (g.UKW * g.UKH);
-            const int64_t OH2 = (int64_t)g.OH * g.UKH, OW2 = (int64_t)g.OW * g.UKW;
-            const int64_t OD2 = (int64_t)g.OD * g.UKD;
-            float* dst = a.out + ((((int64_t)o.b * OD2 + z * g.UKD + uz) * OH2 + y * g.UKH + uy) * OW2 +
-                                  x * g.UKW + ux) * g.up_cout + co0;
-            if (a.bias != nullptr) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] += __ldg(a.bias + co0 + i);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          }
-          continue;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (a.bias != nullptr && nbase + i < a.cout) v[i] += __ldg(a.bias + nbase + i);
-          if (!valid) v[i] = 0.f;
-        }
-        if (valid) {
-          float* dst = a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase;
-          if (nbase + 32 <= a.cout && (a.cout & 3) == 0) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (nbase + i < a.cout) dst[i] = v[i];
-          }
-        }
-        if (a.partials != nullptr) {
-          // per-tile (sum, M2, n) of each column over the brick's valid rows
-          float xs[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) xs[i] = v[i];
-          red[q * 32 + lane] = warp_column_sums(xs);
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          const float total = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-          if (q == 0) col_mean[lane] = total / (float)nvalid;
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float dv = valid ? v[i] - col_mean[i] : 0.f;
-            xs[i] = dv * dv;
-          }
-          const float colm2 = warp_column_sums(xs);
-          red[q * 32 + lane] = colm2;  // every warp read red before the barrier above
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (q == 0 && nbase + lane < a.cout) {
-            float* p = a.partials + (((int64_t)o.b * g.tps + o.t) * a.cout + nbase + lane) * 3;
-            p[0] = total;
-            p[1] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-            p[2] = (float)nvalid;
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-        }
-      }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars[2 * S + 2 + ab]));
-    }
+    epilogue_role<BC, SPLIT>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
   }
   __syncthreads();
-  if (warp == 1) {
-    fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  if (warp == 1) tmem_free_all(tmem);
+}
+
+// ---------------------------------------------------------------------------
+// Halo mode: one TMA box per (chunk, kz plane, half) feeds every (kx, ky) tap.
+// ---------------------------------------------------------------------------
+template <int BC, bool SPLIT>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3d_halo_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
+  using C = Cfg<BC, SPLIT>;
+  constexpr int NB = C::kAccBufs;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int SA = g.sa, SB = g.sb;
+  const int a_stage = C::kHalves * g.plane_bytes;
+  uint8_t* a_ring = smem;                    // SA x [plane hi | plane lo], 1024-aligned
+  uint8_t* b_ring = smem + SA * a_stage;     // SB x B tile, 1024-aligned
+  const SharedMisc sm = shared_misc(b_ring + SB * C::kBBytes);
+  uint64_t* a_full = sm.bars;
+  uint64_t* a_empty = sm.bars + SA;
+  uint64_t* b_full = sm.bars + 2 * SA;
+  uint64_t* b_empty = sm.bars + 2 * SA + SB;
+  uint64_t* accf = sm.bars + 2 * SA + 2 * SB;
+  uint64_t* acce = accf + 2;
+  const uint32_t drain_bar = smem_u32(accf + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int my_tiles = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int taps2d = g.KH * g.KW;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(smem_u32(&a_full[s]), 1);
+      mbar_init(smem_u32(&a_empty[s]), 1);
+    }
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(smem_u32(&b_full[s]), 1);
+      mbar_init(smem_u32(&b_empty[s]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&accf[i]), 1);
+      mbar_init(smem_u32(&acce[i]), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *sm.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (warp == 1) tmem_alloc_all(sm.tmem_slot);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *sm.tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer -----------------------------
+    if (lane == 0) {
+      const uint32_t tx_a = (uint32_t)(C::kHalves * g.plane_rows * 128);
+      int P = 0, T = 0;
+      bool alive = true;
+      for (int it = 0; it < my_tiles && alive; ++it) {
+        const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
+        const int wb = o.w0 - g.PW, hb = o.h0 - g.PH, db = o.d0 - g.PD;
+        const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(a.packed) + (int64_t)o.nt * g.ksteps * C::kBBytes;
+        for (int c = 0; c < g.nchunk && alive; ++c) {
+          const ChunkSource src = chunk_source(a, g, maps, c);
+          for (int kz = 0; kz < g.KD && alive; ++kz) {
+            const int sa = P % SA;
+            if (P >= SA && !mbar_wait(smem_u32(&a_empty[sa]), ((P / SA) - 1) & 1, sm.abort_flag, 22)) {
+              alive = false;
+              break;
+            }
+            const uint32_t fa = smem_u32(&a_full[sa]);
+            const uint32_t dst = smem_u32(a_ring + sa * a_stage);
+            mbar_arrive_expect_tx(fa, tx_a);
+            tma_load_5d(dst, src.map, src.c_hi, wb, hb, db + kz, o.b, fa);
+            if constexpr (SPLIT) tma_load_5d(dst + g.plane_bytes, src.map, src.c_lo, wb, hb, db + kz, o.b, fa);
+            ++P;
+            for (int t2 = 0; t2 < taps2d; ++t2) {
+              const int sb = T % SB;
+              if (T >= SB && !mbar_wait(smem_u32(&b_empty[sb]), ((T / SB) - 1) & 1, sm.abort_flag, 23)) {
+                alive = false;
+                break;
+              }
+              const int tap = kz * taps2d + t2;
+              const uint32_t fb = smem_u32(&b_full[sb]);
+              mbar_arrive_expect_tx(fb, C::kBBytes);
+              bulk_g2s(smem_u32(b_ring + sb * C::kBBytes), bsrc + (int64_t)(tap * g.nchunk + c) * C::kBBytes,
+                       C::kBBytes, fb);
+              ++T;
+            }
+          }
+        }
+      }
+      if (*sm.abort_flag) {
+        for (int i = std::max(0, P - SA); i < P; ++i)
+          mbar_wait(smem_u32(&a_full[i % SA]), (i / SA) & 1, sm.abort_flag, 25, false);
+        for (int i = std::max(0, T - SB); i < T; ++i)
+          mbar_wait(smem_u32(&b_full[i % SB]), (i / SB) & 1, sm.abort_flag, 26, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer -------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM, C::N);
+      // Stage-0 descriptor bases plus constant offsets (16-byte units): A planes with 8-row groups
+      // pw rows apart, B tiles with the usual 1024-byte groups.
+      const uint64_t adesc0 = sw128_desc(smem_u32(a_ring), (uint32_t)g.pw * 128);
+      const uint64_t bdesc0 = sw128_desc(smem_u32(b_ring));
+      const uint32_t a_stage16 = (uint32_t)a_stage >> 4, lo16 = (uint32_t)g.plane_bytes >> 4;
+      constexpr uint32_t kB16 = C::kBBytes >> 4;
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pb = 0;
+      bool alive = true;
+      for (int it = 0; it < my_tiles && alive; ++it) {
+        const int ab = NB == 2 ? (it & 1) : 0;
+        if (it >= NB) {
+          if (!mbar_wait(smem_u32(&acce[ab]), ((it / NB) - 1) & 1, sm.abort_flag, 24)) break;
+          fence_after();
+        }
+        const uint32_t d = tmem + ab * C::N;
+        uint32_t accumulate = 0;
+        for (int c = 0; c < g.nchunk && alive; ++c) {
+          for (int kz = 0; kz < g.KD && alive; ++kz) {
+            const uint64_t ap = adesc0 + (uint64_t)(sa * a_stage16);
+            if (!mbar_wait(smem_u32(&a_full[sa]), pa, sm.abort_flag, 21)) {
+              alive = false;
+              break;
+            }
+            fence_after();
+            for (int ky = 0; ky < g.KH && alive; ++ky) {
+              for (int kx = 0; kx < g.KW; ++kx) {
+                const uint64_t ad = ap + (uint64_t)((ky * g.pw + kx) * 8);
+                const uint64_t bd = bdesc0 + (uint64_t)(sb * kB16);
+                if (!mbar_wait(smem_u32(&b_full[sb]), pb, sm.abort_flag, 27)) {
+                  alive = false;
+                  break;
+                }
+                fence_after();
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                  mma_tf32_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (accumulate | kk) ? 1u : 0u);
+                  if constexpr (SPLIT) mma_tf32_ss(d, ad + lo16 + 2 * kk, bd + 2 * kk, idesc, 1u);
+                }
+                accumulate = 1;
+                mma_commit(smem_u32(&b_empty[sb]));
+                if (++sb == SB) {
+                  sb = 0;
+                  pb ^= 1u;
+                }
+              }
+            }
+            mma_commit(smem_u32(&a_empty[sa]));
+            if (++sa == SA) {
+              sa = 0;
+              pa ^= 1u;
+            }
+          }
+        }
+        if (alive) mma_commit(smem_u32(&accf[ab]));
+      }
+      if (*sm.abort_flag) {
+        mma_commit(drain_bar);
+        mbar_wait(drain_bar, 0, sm.abort_flag, 16, false);
+      }
+    }
+    __syncwarp();
+  } else {
+    epilogue_role<BC, SPLIT>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
+  }
+  __syncthreads();
+  if (warp == 1) tmem_free_all(tmem);
 }
 
 // ---------------------------------------------------------------------------
@@ -446,9 +689,34 @@ inline void choose_brick(const int od, const int oh, const int ow, const int sd,
   }
 }
 
+// Halo mode when the layer is a unit-stride multi-tap conv over at least one
+// 8-wide brick row, <= 64 output channels per tile, and two A planes plus four
+// B tiles fit the shared-memory budget.
+inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bbytes) {
+  if (g.SD != 1 || g.SH != 1 || g.SW != 1) return false;
+  if (g.KD * g.KH * g.KW < 2 || g.OW < kHaloW || g.OH < kHaloH / 2) return false;
+  if (pick_bc(a.cout) > 64) return false;
+  g.pw = kHaloW + g.KW - 1;
+  const int ph = kHaloH + g.KH - 1;
+  if (g.pw > 256 || ph > 256) return false;
+  g.plane_rows = g.pw * ph;
+  g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
+  const int a_stage = halves * g.plane_bytes;
+  const int budget = kMaxSmem - 1024 - kMiscBytes;
+  g.sa = (3 * a_stage + 4 * bbytes <= budget) ? 3 : 2;
+  g.sb = std::min(16, (budget - g.sa * a_stage) / bbytes);
+  if (g.sb < 4 || 2 * g.sa + 2 * g.sb + 5 > kMaxBars) return false;
+  g.box[0] = g.pw;
+  g.box[1] = ph;
+  g.box[2] = 1;
+  g.tw = kHaloW;
+  g.th = kHaloH;
+  g.td = 1;
+  return true;
+}
+
 // Row-space geometry shared by the launch, the weight image size and the
-// partials query.  `rows` are output voxels (in_dims/out_dims/kernel/stride/
-// pad of the convolution).
+// partials query.
 inline Geometry make_geometry(const nnb_conv3d_args& a) {
   Geometry g{};
   g.ID = a.in_dims[0];
@@ -466,11 +734,6 @@ inline Geometry make_geometry(const nnb_conv3d_args& a) {
   g.PD = a.pad[0];
   g.PH = a.pad[1];
   g.PW = a.pad[2];
-  choose_brick(g.OD, g.OH, g.OW, g.SD, g.SH, g.SW, g.tw, g.th, g.td);
-  g.rows = g.tw * g.th * g.td;
-  g.nw = (g.OW + g.tw - 1) / g.tw;
-  g.nh = (g.OH + g.th - 1) / g.th;
-  g.tps = g.nw * g.nh * ((g.OD + g.td - 1) / g.td);
   int cin_total = 0;
   for (int s = 0; s < a.num_segments; ++s) cin_total += a.seg[s].channels;
   g.c0len = a.seg[0].channels;
@@ -479,6 +742,18 @@ inline Geometry make_geometry(const nnb_conv3d_args& a) {
   const int bc = pick_bc(a.cout);
   g.n_tiles = (a.cout + bc - 1) / bc;
   g.up_cout = 0;
+  const int halves = a.precision == NNB_PREC_FP32 ? 2 : 1;
+  g.halo = plan_halo(a, g, halves, halves * bc * 128) ? 1 : 0;
+  if (!g.halo) {
+    choose_brick(g.OD, g.OH, g.OW, g.SD, g.SH, g.SW, g.tw, g.th, g.td);
+    g.box[0] = g.tw * g.SW;
+    g.box[1] = g.th * g.SH;
+    g.box[2] = g.td * g.SD;
+  }
+  g.rows = g.tw * g.th * g.td;
+  g.nw = (g.OW + g.tw - 1) / g.tw;
+  g.nh = (g.OH + g.th - 1) / g.th;
+  g.tps = g.nw * g.nh * ((g.OD + g.td - 1) / g.td);
   return g;
 }
 
@@ -499,7 +774,7 @@ inline EncodeTiledFn encode_tiled() {
 }
 
 // 5-D map (halves x channels, W, H, D, batch) of one prepared operand; the box
-// is one tile's brick for one 32-channel chunk, sampled every stride voxels.
+// is 32 channels x the mode's box extent, sampled every stride voxels.
 inline int encode_operand(const nnb_segment& seg, int halves, int batch, const Geometry& g, CUtensorMap* map) {
   const EncodeTiledFn fn = encode_tiled();
   NNB_REQUIRE(fn != nullptr, "conv3d: cuTensorMapEncodeTiled is not available from the driver");
@@ -507,9 +782,9 @@ inline int encode_operand(const nnb_segment& seg, int halves, int batch, const G
   const cuuint64_t dims[5] = {inner, (cuuint64_t)g.IW, (cuuint64_t)g.IH, (cuuint64_t)g.ID, (cuuint64_t)batch};
   const cuuint64_t row = inner * sizeof(float);
   const cuuint64_t strides[4] = {row, row * g.IW, row * g.IW * g.IH, row * g.IW * g.IH * g.ID};
-  const cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)(g.tw * g.SW), (cuuint32_t)(g.th * g.SH),
-                             (cuuint32_t)(g.td * g.SD), 1u};
-  const cuuint32_t estr[5] = {1u, (cuuint32_t)g.SW, (cuuint32_t)g.SH, (cuuint32_t)g.SD, 1u};
+  const cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)g.box[0], (cuuint32_t)g.box[1], (cuuint32_t)g.box[2], 1u};
+  const cuuint32_t estr[5] = {1u, (cuuint32_t)(g.halo ? 1 : g.SW), (cuuint32_t)(g.halo ? 1 : g.SH),
+                              (cuuint32_t)(g.halo ? 1 : g.SD), 1u};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(seg.data), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -520,18 +795,30 @@ inline int encode_operand(const nnb_segment& seg, int halves, int batch, const G
 template <int BC, bool SPLIT>
 int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& maps, cudaStream_t stream) {
   using C = Cfg<BC, SPLIT>;
-  auto kern = conv3d_tc_kernel<BC, SPLIT>;
   int dev = 0;
   NNB_CUDA_CHECK(cudaGetDevice(&dev));
-  static int configured[64] = {0};  // dynamic shared memory opt-in done, per device
-  if (dev >= 64 || !configured[dev]) {
-    NNB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    if (dev < 64) configured[dev] = 1;
+  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, bit 1 halo), per device
+  const int bit = g.halo ? 2 : 1;
+  if (dev >= 64 || !(configured[dev] & bit)) {
+    if (g.halo)
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, SPLIT>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    else
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_tc_kernel<BC, SPLIT>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    if (dev < 64) configured[dev] |= bit;
   }
   int sms = 148;
   NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::min(g.total_tiles, sms);
-  kern<<<grid, kThreads, C::kSmem, stream>>>(a, g, maps);
+  if (g.halo) {
+    const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * C::kBBytes + kMiscBytes;
+    NNB_REQUIRE(smem <= kMaxSmem, "conv3d: halo plan exceeds shared memory (%d bytes)", smem);
+    conv3d_halo_kernel<BC, SPLIT><<<grid, kThreads, smem, stream>>>(a, g, maps);
+  } else {
+    const int smem = 1024 + C::S * C::kStageBytes + kMiscBytes + 4 * kMaxKsteps;
+    conv3d_tc_kernel<BC, SPLIT><<<grid, kThreads, smem, stream>>>(a, g, maps);
+  }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }
@@ -555,6 +842,7 @@ int dispatch(const nnb_conv3d_args& a, Geometry& g, cudaStream_t stream) {
     case 64:
       return split ? launch_bc<64, true>(a, g, maps, stream) : launch_bc<64, false>(a, g, maps, stream);
     default:
+      NNB_REQUIRE(!g.halo, "conv3d: internal: halo plan for a 128-column tile");
       return split ? launch_bc<128, true>(a, g, maps, stream) : launch_bc<128, false>(a, g, maps, stream);
   }
 }

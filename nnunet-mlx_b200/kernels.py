@@ -22,6 +22,7 @@ import torch
 from nnunet_mlx_b200 import _native
 from nnunet_mlx_b200.errors import ContractError
 
+
 class _Profile:
     """Optional CUDA-event timing of every device call (used by ``bench.py`` over its timed region).
 
@@ -41,12 +42,12 @@ class _Profile:
     def enable(self, on: bool) -> None:
         self.active = on
 
-    def start(self, name: str, flops: float = 0.0, nbytes: float = 0.0, launches: int = 1):
+    def start(self, name: str, flops: float = 0.0, nbytes: float = 0.0, launches: int = 1, detail=None):
         if not self.active:
             return None
         event = torch.cuda.Event(enable_timing=True)
         event.record()
-        return name, event, flops, nbytes, launches
+        return name, event, flops, nbytes, launches, detail() if callable(detail) else detail
 
     def stop(self, token) -> None:
         if token is None:
@@ -56,9 +57,14 @@ class _Profile:
         self.records.append((token, event))
         self.launches += token[4]
 
+    def trace(self) -> list[dict]:
+        """Every recorded call in order: name, detail, milliseconds, FLOPs, bytes."""
+        return [{"name": name, "detail": detail, "ms": e0.elapsed_time(e1), "flops": flops, "bytes": nbytes}
+                for (name, e0, flops, nbytes, _, detail), e1 in self.records]
+
     def summary(self) -> dict:
         out: dict[str, dict] = {}
-        for (name, e0, flops, nbytes, _), e1 in self.records:
+        for (name, e0, flops, nbytes, _, _), e1 in self.records:
             item = out.setdefault(name, {"calls": 0, "seconds": 0.0, "flops": 0.0, "bytes": 0.0})
             item["calls"] += 1
             item["seconds"] += e0.elapsed_time(e1) / 1e3
@@ -235,7 +241,10 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
         args.partials = partials.data_ptr()
     flops = 2.0 * batch * math.prod(out_dims) * cout * cin * math.prod(kernel)
     token = PROFILE.start("conv3d_tc" if tensor_cores else "conv3d_simt", flops,
-                          4.0 * (out.numel() + sum(item.raw.numel() for item in inputs)))
+                          4.0 * (out.numel() + sum(item.raw.numel() for item in inputs)),
+                          detail=lambda: (f"{batch}x{'x'.join(map(str, in_dims))} "
+                                          f"{'+'.join(str(i.channels) for i in inputs)}->{cout} "
+                                          f"k{'x'.join(map(str, kernel))} s{'x'.join(map(str, stride))}"))
     _native.check(_native.load().nnb_conv3d(ctypes.byref(args), _stream()), "conv3d")
     PROFILE.stop(token)
     return out, partials
@@ -340,7 +349,9 @@ def conv_transpose3d(x: Lazy, weight: torch.Tensor, bias: torch.Tensor | None, k
                     and precision in (_native.PREC_FP32, _native.PREC_TF32))
     seg = prepare_operand(x, precision, slope).segment() if tensor_cores else x.segment()
     token = PROFILE.start("conv_transpose3d_tc" if tensor_cores else "conv_transpose3d_simt",
-                          2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()))
+                          2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()),
+                          detail=lambda: (f"{batch}x{'x'.join(map(str, x.spatial))} {x.channels}->{cout} "
+                                          f"up{'x'.join(map(str, kernel))}"))
     _native.check(_native.load().nnb_conv_transpose3d(
         ctypes.byref(seg), batch, _native.dims3(x.spatial), _native.dims3(kernel), float(slope),
         weight.data_ptr(), _ptr(bias), cout, _ptr(packed) if tensor_cores else 0, int(precision), out.data_ptr(),

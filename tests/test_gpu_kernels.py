@@ -61,6 +61,12 @@ CONV_CASES = [
     (2, (16, 40, 40), [(32, True)], 64, (3, 3, 3), (1, 2, 2), (1, 1, 1), "tf32"),
     (1, (7, 9, 11), [(96, True)], 96, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
     (1, (9, 9, 9), [(32, True), (64, False)], 16, (3, 3, 3), (2, 1, 2), (1, 1, 1), "fp32"),
+    # halo mode (unit stride, 8x16 bricks, one plane box per kz feeds the kx/ky taps)
+    (2, (10, 12, 16), [(32, True), (32, False)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (1, (9, 20, 24), [(64, True)], 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (1, (5, 16, 16), [(32, True)], 32, (1, 3, 3), (1, 1, 1), (0, 1, 1), "fp32"),
+    (1, (6, 16, 8), [(32, True)], 32, (3, 1, 1), (1, 1, 1), (1, 0, 0), "tf32"),
+    (2, (7, 19, 13), [(64, True)], 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), "tf32"),
 ]
 
 
