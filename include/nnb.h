@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 4
+#define NNB_ABI_VERSION 5
 
 enum nnb_status {
   NNB_OK = 0,
@@ -231,6 +231,42 @@ int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const in
                             const float* seg_bias, int32_t classes, const float* gaussian,
                             float* acc, float* normalizer, const int32_t acc_dims[3],
                             const int32_t offset[3], int32_t add_normalizer, void* stream);
+
+/*
+ * nnunet-fp16 accumulation mode (reference sliding_window.py:96-113,415-433,
+ * 185-186, inference.py:75-90; the mode MedMLX runs and the predict CLI use,
+ * medmlx.py:41-42,121-134).  acc16 (AD, AH, AW, C) and normalizer16 (AD, AH, AW)
+ * are IEEE half; gaussian holds the float32 values of the half Gaussian
+ * (upstream's scaled impulse response).  Per tile voxel the window update is
+ * half(f32(acc) + pred * g) and the normaliser half(f32(n) + g), round to
+ * nearest even -- the float32 seg head / flip-back / view mean being
+ * nnb_accumulate_tile's.
+ */
+int32_t nnb_accumulate_tile_fp16(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                                 const int32_t patch[3], float slope, const float* seg_weight,
+                                 const float* seg_bias, int32_t classes, const float* gaussian, void* acc16,
+                                 void* normalizer16, const int32_t acc_dims[3], const int32_t offset[3],
+                                 int32_t add_normalizer, void* stream);
+
+/*
+ * One fold of the nnunet-fp16 mode: normalised half logits over the crop,
+ * n = half(f32(acc) / f32(norm)), into the channel-first half total
+ * (C, crop_dims): the first fold stores n, later folds half(f32(total) + n) in
+ * fold order.  invalid_count accumulates voxels with a non-finite n (the
+ * caller zeroes it once per fold ensemble).
+ */
+int32_t nnb_fold_add_fp16(const void* acc16, const void* normalizer16, int32_t classes,
+                          const int32_t acc_dims[3], const int32_t crop_lo[3], const int32_t crop_dims[3],
+                          void* total16, int32_t first_fold, int32_t* invalid_count, void* stream);
+
+/*
+ * Fold average of the half total in place, half(f32(total) / folds), then
+ * optional float32 channel-first logits of the half values and first-argmax
+ * labels (1 or 2 bytes; all-ones for a voxel with a non-finite value, counted
+ * in invalid_count, which this call zeroes first).
+ */
+int32_t nnb_fold_finalize_fp16(void* total16, int32_t classes, int64_t voxels, int32_t folds, float* logits,
+                               void* labels, int32_t label_bytes, int32_t* invalid_count, void* stream);
 
 /*
  * Normalise accumulated logits and reduce them to labels over the crop

@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 PREC_FP32 = 0   # split-TF32 hi/lo tensor cores, float32-level accuracy
 PREC_TF32 = 1   # single-pass TF32 tensor cores
@@ -74,6 +74,16 @@ SYMBOLS = {
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, I32x3, I32x3, ctypes.c_int32,
                                              ctypes.c_void_p]),
+    "nnb_accumulate_tile_fp16": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32,
+                                                  ctypes.POINTER(ctypes.c_int32), I32x3, ctypes.c_float,
+                                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                                  ctypes.c_void_p, ctypes.c_void_p, I32x3, I32x3, ctypes.c_int32,
+                                                  ctypes.c_void_p]),
+    "nnb_fold_add_fp16": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, I32x3,
+                                           ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_fold_finalize_fp16": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
+                                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                                ctypes.c_void_p]),
     "nnb_normalize_labels": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3,
                                               I32x3, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),

@@ -63,7 +63,10 @@ def main(argv=None) -> int:
                                    precision=args.precision)
         if args.disable_tta:
             bundle = replace(bundle, mirroring_axes=())
-        predictor = ModelFolderPredictor(bundle, step_fraction=args.step_size)
+        from nnunet_mlx_b200.medmlx import ACCUMULATION
+
+        # the predict command accumulates in float16 like upstream (reference commands/upstream.py:161-162)
+        predictor = ModelFolderPredictor(bundle, step_fraction=args.step_size, accumulation=ACCUMULATION)
         results = predictor.predict_folder(args.input_folder, args.output_folder,
                                            save_probabilities=args.save_probabilities,
                                            continue_prediction=args.continue_prediction,

@@ -44,8 +44,13 @@ int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const in
                         const int32_t patch[3], int views, const int32_t* masks, float* out, cudaStream_t stream);
 int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
                            float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
-                           float* acc, float* normalizer, const int32_t ad[3], const int32_t off[3],
+                           void* acc, void* normalizer, int fp16, const int32_t ad[3], const int32_t off[3],
                            int add_normalizer, cudaStream_t stream);
+int launch_fold_add_fp16(const void* acc, const void* normalizer, int classes, const int32_t ad[3],
+                         const int32_t lo[3], const int32_t cd[3], void* total, int first, int32_t* invalid_count,
+                         cudaStream_t stream);
+int launch_fold_finalize_fp16(void* total, int classes, int64_t vox, int folds, float* logits, void* labels,
+                              int label_bytes, int32_t* invalid_count, cudaStream_t stream);
 int launch_normalize_labels(const float* acc, const float* normalizer, int classes, const int32_t ad[3],
                             const int32_t lo[3], const int32_t cd[3], float fold_divisor, float* logits,
                             void* labels, int label_bytes, int32_t* invalid_count, cudaStream_t stream);
@@ -197,11 +202,10 @@ int32_t nnb_gather_views(const float* volume, int32_t cin, const int32_t vol_dim
   return launch_gather_views(volume, cin, vol_dims, offset, patch, views, flip_masks, out, (cudaStream_t)stream);
 }
 
-int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
-                            const int32_t patch[3], float slope, const float* seg_weight, const float* seg_bias,
-                            int32_t classes, const float* gaussian, float* acc, float* normalizer,
-                            const int32_t acc_dims[3], const int32_t offset[3], int32_t add_normalizer,
-                            void* stream) {
+static int check_accumulate(const nnb_segment* features, const int32_t* flip_masks, const int32_t patch[3],
+                            const float* seg_weight, const float* seg_bias, int32_t classes, const float* gaussian,
+                            const void* acc, const void* normalizer, const int32_t acc_dims[3],
+                            const int32_t offset[3], int32_t add_normalizer) {
   NNB_REQUIRE(features && flip_masks && seg_weight && seg_bias && gaussian && acc, "accumulate_tile: null pointer");
   int rc = check_segment(*features, "accumulate features");
   if (rc) return rc;
@@ -210,8 +214,53 @@ int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const in
   for (int i = 0; i < 3; ++i)
     NNB_REQUIRE(offset[i] >= 0 && patch[i] >= 1 && offset[i] + patch[i] <= acc_dims[i],
                 "accumulate_tile: tile outside accumulator on axis %d", i);
+  return NNB_OK;
+}
+
+int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                            const int32_t patch[3], float slope, const float* seg_weight, const float* seg_bias,
+                            int32_t classes, const float* gaussian, float* acc, float* normalizer,
+                            const int32_t acc_dims[3], const int32_t offset[3], int32_t add_normalizer,
+                            void* stream) {
+  int rc = check_accumulate(features, flip_masks, patch, seg_weight, seg_bias, classes, gaussian, acc, normalizer,
+                            acc_dims, offset, add_normalizer);
+  if (rc) return rc;
   return launch_accumulate_tile(*features, views, flip_masks, patch, slope, seg_weight, seg_bias, classes, gaussian,
-                                acc, normalizer, acc_dims, offset, add_normalizer, (cudaStream_t)stream);
+                                acc, normalizer, 0, acc_dims, offset, add_normalizer, (cudaStream_t)stream);
+}
+
+int32_t nnb_accumulate_tile_fp16(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                                 const int32_t patch[3], float slope, const float* seg_weight,
+                                 const float* seg_bias, int32_t classes, const float* gaussian, void* acc16,
+                                 void* normalizer16, const int32_t acc_dims[3], const int32_t offset[3],
+                                 int32_t add_normalizer, void* stream) {
+  int rc = check_accumulate(features, flip_masks, patch, seg_weight, seg_bias, classes, gaussian, acc16,
+                            normalizer16, acc_dims, offset, add_normalizer);
+  if (rc) return rc;
+  NNB_REQUIRE((reinterpret_cast<uintptr_t>(acc16) & 1) == 0 && (reinterpret_cast<uintptr_t>(normalizer16) & 1) == 0,
+              "accumulate_tile_fp16: half buffers must be 2-byte aligned");
+  return launch_accumulate_tile(*features, views, flip_masks, patch, slope, seg_weight, seg_bias, classes, gaussian,
+                                acc16, normalizer16, 1, acc_dims, offset, add_normalizer, (cudaStream_t)stream);
+}
+
+int32_t nnb_fold_add_fp16(const void* acc16, const void* normalizer16, int32_t classes, const int32_t acc_dims[3],
+                          const int32_t crop_lo[3], const int32_t crop_dims[3], void* total16, int32_t first_fold,
+                          int32_t* invalid_count, void* stream) {
+  NNB_REQUIRE(acc16 && normalizer16 && total16 && invalid_count && classes >= 1, "fold_add_fp16: bad arguments");
+  for (int i = 0; i < 3; ++i)
+    NNB_REQUIRE(crop_lo[i] >= 0 && crop_dims[i] >= 1 && crop_lo[i] + crop_dims[i] <= acc_dims[i],
+                "fold_add_fp16: crop outside accumulator on axis %d", i);
+  return launch_fold_add_fp16(acc16, normalizer16, classes, acc_dims, crop_lo, crop_dims, total16, first_fold,
+                              invalid_count, (cudaStream_t)stream);
+}
+
+int32_t nnb_fold_finalize_fp16(void* total16, int32_t classes, int64_t voxels, int32_t folds, float* logits,
+                               void* labels, int32_t label_bytes, int32_t* invalid_count, void* stream) {
+  NNB_REQUIRE(total16 && invalid_count && classes >= 1 && voxels >= 1 && folds >= 1,
+              "fold_finalize_fp16: bad arguments");
+  NNB_CUDA_CHECK(cudaMemsetAsync(invalid_count, 0, sizeof(int32_t), (cudaStream_t)stream));
+  return launch_fold_finalize_fp16(total16, classes, voxels, folds, logits, labels, label_bytes, invalid_count,
+                                   (cudaStream_t)stream);
 }
 
 int32_t nnb_normalize_labels(const float* acc, const float* normalizer, int32_t classes, const int32_t acc_dims[3],

@@ -1,6 +1,9 @@
 // Sliding-window kernels: mirrored tile gather, fused segmentation head +
-// flip-back + Gaussian accumulation, and normalise + label reduction.
-// All three are HBM-bound streaming kernels.
+// flip-back + Gaussian accumulation (float32 or float16 accumulator), and
+// normalise + label reduction (float32 accumulator, or the float16 per-fold
+// normalise / fold sum / fold average of the nnunet-fp16 mode).  All are
+// HBM-bound streaming kernels.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -73,11 +76,18 @@ int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const in
 // ---------------------------------------------------------------------------
 constexpr int kAccMaxC = 8;        // classes per pass
 
-template <int FV>  // FV = F / 4 (float4 chunks), compile-time for register arrays
+// Accumulator update: float32 add, or the float16 window update of the
+// nnunet-fp16 mode -- the float32 sum of the stored half value and the float32
+// weighted prediction, rounded to nearest-even half (reference
+// sliding_window.py:421-426: (logits.astype(f32) + weighted).astype(f16)).
+__device__ __forceinline__ void acc_add(float* p, float w) { *p += w; }
+__device__ __forceinline__ void acc_add(__half* p, float w) { *p = __float2half_rn(__half2float(*p) + w); }
+
+template <int FV, typename AccT>  // FV = F / 4 (float4 chunks), compile-time for register arrays
 __global__ void __launch_bounds__(256) accumulate_tile_vec_kernel(
     nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
-    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, float* __restrict__ acc,
-    float* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, AccT* __restrict__ acc,
+    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
   constexpr int F = FV * 4;
   __shared__ float s_sc[8][F];
   __shared__ float s_sh[8][F];
@@ -140,20 +150,20 @@ __global__ void __launch_bounds__(256) accumulate_tile_vec_kernel(
       }
       const float g = __ldg(gauss + p);
       const int64_t dst = ((int64_t)(off.d[0] + i) * ad.d[1] + (off.d[1] + j)) * ad.d[2] + (off.d[2] + k);
-      float* a = acc + dst * classes + c0;
+      AccT* a = acc + dst * classes + c0;
 #pragma unroll
       for (int c = 0; c < kAccMaxC; ++c)
-        if (c < nc) a[c] += (pred[c] * inv_views) * g;
-      if (add_normalizer && c0 == 0) normalizer[dst] += g;
+        if (c < nc) acc_add(a + c, (pred[c] * inv_views) * g);
+      if (add_normalizer && c0 == 0) acc_add(normalizer + dst, g);
     }
   }
 }
 
-template <int CC>
+template <int CC, typename AccT>
 __global__ void __launch_bounds__(256) accumulate_tile_kernel(
     nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
-    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, float* __restrict__ acc,
-    float* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, AccT* __restrict__ acc,
+    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
   const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
   const int F = feat.channels;
   const float inv_views = 1.0f / (float)views;
@@ -190,19 +200,17 @@ __global__ void __launch_bounds__(256) accumulate_tile_kernel(
       }
 #pragma unroll
       for (int c = 0; c < CC; ++c)
-        if (c0 + c < classes) {
-          float* a = acc + dst * classes + c0 + c;
-          *a += (pred[c] * inv_views) * g;
-        }
+        if (c0 + c < classes) acc_add(acc + dst * classes + c0 + c, (pred[c] * inv_views) * g);
     }
-    if (add_normalizer) normalizer[dst] += g;
+    if (add_normalizer) acc_add(normalizer + dst, g);
   }
 }
 
-int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
-                           float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
-                           float* acc, float* normalizer, const int32_t ad[3], const int32_t off[3],
-                           int add_normalizer, cudaStream_t stream) {
+template <typename AccT>
+int launch_accumulate_tile_t(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
+                             float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
+                             AccT* acc, AccT* normalizer, const int32_t ad[3], const int32_t off[3],
+                             int add_normalizer, cudaStream_t stream) {
   NNB_REQUIRE(views >= 1 && views <= 8, "accumulate_tile: 1..8 views supported");
   ViewMasks vm{};
   for (int v = 0; v < views; ++v) vm.m[v] = masks[v];
@@ -211,14 +219,28 @@ int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* ma
   const int blocks = (int)std::min<int64_t>((pvox + 255) / 256, 148 * 16);
   const bool aligned = (reinterpret_cast<uintptr_t>(feat.data) & 15) == 0;
   if (aligned && feat.channels == 32) {
-    accumulate_tile_vec_kernel<8><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes,
-                                                              gauss, acc, normalizer, dad, doff, add_normalizer);
+    accumulate_tile_vec_kernel<8, AccT><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b,
+                                                                    classes, gauss, acc, normalizer, dad, doff,
+                                                                    add_normalizer);
   } else {
-    accumulate_tile_kernel<4><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss,
-                                                          acc, normalizer, dad, doff, add_normalizer);
+    accumulate_tile_kernel<4, AccT><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes,
+                                                                gauss, acc, normalizer, dad, doff, add_normalizer);
   }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
+}
+
+int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
+                           float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
+                           void* acc, void* normalizer, int fp16, const int32_t ad[3], const int32_t off[3],
+                           int add_normalizer, cudaStream_t stream) {
+  if (fp16)
+    return launch_accumulate_tile_t<__half>(feat, views, masks, patch, slope, seg_w, seg_b, classes, gauss,
+                                            static_cast<__half*>(acc), static_cast<__half*>(normalizer), ad, off,
+                                            add_normalizer, stream);
+  return launch_accumulate_tile_t<float>(feat, views, masks, patch, slope, seg_w, seg_b, classes, gauss,
+                                         static_cast<float*>(acc), static_cast<float*>(normalizer), ad, off,
+                                         add_normalizer, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -278,6 +300,101 @@ int launch_normalize_labels(const float* acc, const float* normalizer, int class
     normalize_labels_kernel<uint16_t><<<blocks, 256, 0, stream>>>(acc, normalizer, classes, dad, dlo, dcd,
                                                                   fold_divisor, logits, (uint16_t*)labels,
                                                                   invalid_count, (uint16_t)0xFFFF);
+  }
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// nnunet-fp16 fold handling.  One fold's window -> normalised half logits over
+// the crop, n = half(f32(acc) / f32(norm)) (reference sliding_window.py:185,
+// 289: (logits.astype(f32) / normalizer.astype(f32)).astype(f16)), added into
+// the channel-first half total: the first fold stores n, later folds
+// half(f32(total) + f32(n)) in fold order (inference.py:75-85, IEEE half adds).
+// Non-finite fold logits are counted.
+// ---------------------------------------------------------------------------
+__global__ void fold_add_fp16_kernel(const __half* __restrict__ acc, const __half* __restrict__ normalizer,
+                                     int classes, Dims3 ad, Dims3 lo, Dims3 cd, __half* __restrict__ total,
+                                     int first, int* __restrict__ invalid_count) {
+  const int64_t vox = (int64_t)cd.d[0] * cd.d[1] * cd.d[2];
+  int local_invalid = 0;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < vox;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int x = (int)(o % cd.d[2]);
+    const int y = (int)((o / cd.d[2]) % cd.d[1]);
+    const int z = (int)(o / ((int64_t)cd.d[2] * cd.d[1]));
+    const int64_t src = ((int64_t)(lo.d[0] + z) * ad.d[1] + (lo.d[1] + y)) * ad.d[2] + (lo.d[2] + x);
+    const float den = __half2float(normalizer[src]);
+    bool invalid = false;
+    for (int c = 0; c < classes; ++c) {
+      const __half n = __float2half_rn(__half2float(acc[src * classes + c]) / den);
+      const float nf = __half2float(n);
+      invalid |= !isfinite(nf);
+      __half* t = total + (int64_t)c * vox + o;
+      *t = first ? n : __float2half_rn(__half2float(*t) + nf);
+    }
+    local_invalid += invalid ? 1 : 0;
+  }
+  if (local_invalid) atomicAdd(invalid_count, local_invalid);
+}
+
+// Fold average of the half total: half(f32(total) / folds) in place
+// (inference.py:86-90, total /= float32(n)), then float32 logits of the half
+// values and first-argmax labels (invalid label for non-finite values).
+template <typename LabelT>
+__global__ void fold_finalize_fp16_kernel(__half* __restrict__ total, int classes, int64_t vox, float folds,
+                                          float* __restrict__ logits, LabelT* __restrict__ labels,
+                                          int* __restrict__ invalid_count, LabelT invalid_label) {
+  int local_invalid = 0;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < vox;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    bool invalid = false;
+    float best = 0.f;
+    int winner = 0;
+    for (int c = 0; c < classes; ++c) {
+      __half* t = total + (int64_t)c * vox + o;
+      const __half q = __float2half_rn(__half2float(*t) / folds);
+      *t = q;
+      const float qf = __half2float(q);
+      invalid |= !isfinite(qf);
+      if (logits != nullptr) logits[(int64_t)c * vox + o] = qf;
+      if (c == 0 || qf > best) {
+        best = qf;
+        winner = c;
+      }
+    }
+    if (labels != nullptr) labels[o] = invalid ? invalid_label : (LabelT)winner;
+    local_invalid += invalid ? 1 : 0;
+  }
+  if (local_invalid) atomicAdd(invalid_count, local_invalid);
+}
+
+int launch_fold_add_fp16(const void* acc, const void* normalizer, int classes, const int32_t ad[3],
+                         const int32_t lo[3], const int32_t cd[3], void* total, int first, int32_t* invalid_count,
+                         cudaStream_t stream) {
+  Dims3 dad{{ad[0], ad[1], ad[2]}}, dlo{{lo[0], lo[1], lo[2]}}, dcd{{cd[0], cd[1], cd[2]}};
+  const int64_t vox = (int64_t)cd[0] * cd[1] * cd[2];
+  const int blocks = (int)std::min<int64_t>((vox + 255) / 256, 148 * 16);
+  fold_add_fp16_kernel<<<blocks, 256, 0, stream>>>(static_cast<const __half*>(acc),
+                                                   static_cast<const __half*>(normalizer), classes, dad, dlo, dcd,
+                                                   static_cast<__half*>(total), first, invalid_count);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int launch_fold_finalize_fp16(void* total, int classes, int64_t vox, int folds, float* logits, void* labels,
+                              int label_bytes, int32_t* invalid_count, cudaStream_t stream) {
+  const int blocks = (int)std::min<int64_t>((vox + 255) / 256, 148 * 16);
+  __half* t = static_cast<__half*>(total);
+  if (labels == nullptr || label_bytes == 1) {
+    NNB_REQUIRE(labels == nullptr || classes <= 255, "fold_finalize_fp16: uint8 labels need <= 255 classes");
+    fold_finalize_fp16_kernel<uint8_t><<<blocks, 256, 0, stream>>>(t, classes, vox, (float)folds, logits,
+                                                                   (uint8_t*)labels, invalid_count, (uint8_t)0xFF);
+  } else {
+    NNB_REQUIRE(label_bytes == 2, "fold_finalize_fp16: label_bytes must be 1 or 2");
+    fold_finalize_fp16_kernel<uint16_t><<<blocks, 256, 0, stream>>>(t, classes, vox, (float)folds, logits,
+                                                                    (uint16_t*)labels, invalid_count,
+                                                                    (uint16_t)0xFFFF);
   }
   NNB_LAUNCH_CHECK();
   return NNB_OK;

@@ -393,19 +393,69 @@ def gather_views(volume: torch.Tensor, offset, patch, masks: list[int], out: tor
 def accumulate_tile(features: Lazy, masks: list[int], seg_weight: torch.Tensor, seg_bias: torch.Tensor,
                     gaussian: torch.Tensor, acc: torch.Tensor, normalizer: torch.Tensor, offset,
                     add_normalizer: bool, slope: float) -> None:
+    """Fused seg head + flip-back + view mean + Gaussian-weighted add of one tile.
+
+    ``acc`` / ``normalizer`` are float32, or float16 for the nnunet-fp16 mode
+    (half window updates rounded to nearest even).
+    """
     seg = features.segment()
     mask_arr = (ctypes.c_int32 * len(masks))(*masks)
-    _check_tensor(acc, "accumulator")
+    half = acc.dtype == torch.float16
+    for t, name in ((acc, "accumulator"), (normalizer, "normalizer")):
+        if not t.is_cuda or not t.is_contiguous() or t.dtype != (torch.float16 if half else torch.float32):
+            raise ContractError(f"{name} must be a contiguous CUDA tensor of the accumulator dtype")
+    _check_tensor(gaussian, "gaussian")
     classes = int(seg_weight.shape[0])
     pvox = math.prod(features.spatial)
     token = PROFILE.start("accumulate_tile", 2.0 * features.raw.numel() * classes,
-                          4.0 * (features.raw.numel() + pvox * (2 * classes + 3)))
-    _native.check(_native.load().nnb_accumulate_tile(
+                          4.0 * features.raw.numel() + pvox * (2 * classes + 2) * acc.element_size() + 4.0 * pvox)
+    entry = _native.load().nnb_accumulate_tile_fp16 if half else _native.load().nnb_accumulate_tile
+    _native.check(entry(
         ctypes.byref(seg), len(masks), mask_arr, _native.dims3(features.spatial), float(slope),
-        seg_weight.data_ptr(), seg_bias.data_ptr(), int(seg_weight.shape[0]), gaussian.data_ptr(),
+        seg_weight.data_ptr(), seg_bias.data_ptr(), classes, gaussian.data_ptr(),
         acc.data_ptr(), normalizer.data_ptr(), _native.dims3(acc.shape[:3]), _native.dims3(offset),
         1 if add_normalizer else 0, _stream()), "accumulate_tile")
     PROFILE.stop(token)
+
+
+def fold_add_fp16(acc16: torch.Tensor, normalizer16: torch.Tensor, crop_lo, crop_dims, total16: torch.Tensor,
+                  first: bool, invalid: torch.Tensor) -> None:
+    """nnunet-fp16: this fold's normalised half logits over the crop into the channel-first half total."""
+    classes = int(acc16.shape[-1])
+    if total16.dtype != torch.float16 or tuple(total16.shape) != (classes, *crop_dims):
+        raise ContractError("fold total must be float16 (C, *crop)")
+    voxels = math.prod(crop_dims)
+    token = PROFILE.start("fold_add_fp16", 0.0, 2.0 * voxels * (2 * classes + 1))
+    _native.check(_native.load().nnb_fold_add_fp16(
+        acc16.data_ptr(), normalizer16.data_ptr(), classes, _native.dims3(acc16.shape[:3]), _native.dims3(crop_lo),
+        _native.dims3(crop_dims), total16.data_ptr(), 1 if first else 0, invalid.data_ptr(), _stream()),
+        "fold_add_fp16")
+    PROFILE.stop(token)
+
+
+def fold_finalize_fp16(total16: torch.Tensor, folds: int, *, want_logits: bool = True,
+                       label_dtype: torch.dtype | None = torch.uint8):
+    """Fold average of the half total (in place); float32 logits of the half values, labels, invalid count."""
+    classes = int(total16.shape[0])
+    crop = tuple(int(v) for v in total16.shape[1:])
+    voxels = math.prod(crop)
+    logits = torch.empty((classes, *crop), dtype=torch.float32, device=total16.device) if want_logits else None
+    labels, label_bytes = None, 1
+    if label_dtype is not None:
+        if label_dtype == torch.uint8:
+            label_bytes = 1
+        elif label_dtype in (torch.uint16, torch.int16):
+            label_bytes = 2
+        else:
+            raise ContractError("labels must be uint8 or uint16")
+        labels = torch.empty(crop, dtype=label_dtype, device=total16.device)
+    invalid = torch.zeros((1,), dtype=torch.int32, device=total16.device)
+    token = PROFILE.start("fold_finalize_fp16", 0.0, voxels * (4.0 * classes + label_bytes), launches=2)
+    _native.check(_native.load().nnb_fold_finalize_fp16(
+        total16.data_ptr(), classes, voxels, int(folds), _ptr(logits), _ptr(labels), label_bytes, invalid.data_ptr(),
+        _stream()), "fold_finalize_fp16")
+    PROFILE.stop(token)
+    return logits, labels, invalid
 
 
 def normalize_labels(acc: torch.Tensor, normalizer: torch.Tensor, crop_lo, crop_dims, *, fold_divisor: float = 1.0,

@@ -20,6 +20,10 @@ from nnunet_mlx_b200.errors import ContractError
 
 _PRECISIONS = {"native": "fp32", "fp32": "fp32", "tf32": "tf32"}
 
+# Runner windows and folds accumulate in float16 as upstream nnU-Net does (reference medmlx.py:41-42,
+# 121-134); ModelFolderPredictor's own float32 default is for direct Python use.
+ACCUMULATION = "nnunet-fp16"
+
 
 class NnUNetModel:
     """One loaded model folder reused for serial cases until closed."""
@@ -43,7 +47,8 @@ class NnUNetModel:
                                    device=device)
         if not use_mirroring:
             bundle = replace(bundle, mirroring_axes=())
-        self._predictor: ModelFolderPredictor | None = ModelFolderPredictor(bundle, step_fraction=step_fraction)
+        self._predictor: ModelFolderPredictor | None = ModelFolderPredictor(
+            bundle, step_fraction=step_fraction, accumulation=ACCUMULATION)
 
     def run(self, *, image_paths, output_dir, overwrite: bool = False, save_probabilities: bool = False) -> dict:
         if self._predictor is None:

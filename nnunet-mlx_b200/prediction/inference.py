@@ -22,23 +22,28 @@ from nnunet_mlx_b200.prediction.sliding_window import _check_accumulation, predi
 
 def average_fold_logits(models, data_channels_first, *, patch_size, num_outputs: int, mirroring_axes=(),
                         step_fraction: float = 0.5, accumulation: str = "float32") -> np.ndarray:
-    """Host float32 ``(num_outputs, *spatial)`` fold-averaged logits."""
+    """Host ``(num_outputs, *spatial)`` fold-averaged logits: float32, or float16 for ``nnunet-fp16``
+    (each fold rounded to float16, summed in order and divided, as upstream keeps half tensors)."""
     _check_accumulation(accumulation)
     if not models:
         raise ContractError("fold inference requires at least one model")
+    half = accumulation == "nnunet-fp16"
     logits, _ = predict_volume(list(models), data_channels_first, patch_size=patch_size, num_classes=num_outputs,
-                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None)
+                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None,
+                               accumulation=accumulation, half_logits=half)
     return logits.cpu().numpy()
 
 
 def average_fold_device_logits(models, data_channels_first, *, patch_size, num_outputs: int, mirroring_axes=(),
                                step_fraction: float = 0.5, accumulation: str = "float32") -> torch.Tensor:
-    """Device fold-averaged logits, channels-last ``(*spatial, C)`` (a view of the channel-first result)."""
+    """Device fold-averaged logits, channels-last ``(*spatial, C)`` (a view of the channel-first result);
+    float16 for ``nnunet-fp16``."""
     _check_accumulation(accumulation)
     if not models:
         raise ContractError("fold inference requires at least one model")
     logits, _ = predict_volume(list(models), data_channels_first, patch_size=patch_size, num_classes=num_outputs,
-                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None)
+                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None,
+                               accumulation=accumulation, half_logits=True)
     return logits.permute(1, 2, 3, 0)
 
 
@@ -117,5 +122,6 @@ class ArrayPredictor:
         _, labels = predict_volume(list(self.models), data_channels_first, patch_size=self.patch_size,
                                    num_classes=self.num_outputs, mirroring_axes=self.mirroring_axes,
                                    step_fraction=self.step_fraction, want_logits=False,
-                                   label_dtype=torch.uint8 if self.num_outputs <= 255 else torch.uint16)
+                                   label_dtype=torch.uint8 if self.num_outputs <= 255 else torch.uint16,
+                                   accumulation=self.accumulation)
         return labels.cpu().numpy().astype(np.uint16)

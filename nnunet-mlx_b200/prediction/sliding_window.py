@@ -15,6 +15,14 @@ API names follow reference ``src/nnunet_mlx/prediction/sliding_window.py``:
 * normalised logits ``acc / normalizer`` (then ``/ n_folds``), label = first
   argmax (reference ``kernels/metal_normalized_labels.py``).
 
+``accumulation="nnunet-fp16"`` is the reference's upstream-compatible mode
+(reference 96-113, 415-433; what its MedMLX runners and predict CLI use): the
+Gaussian is upstream's scaled impulse response rounded to float16, the window
+and normaliser are float16 with every update ``half(f32(acc) + pred * g)``,
+each fold is normalised to float16 on its own, and folds are summed in float16
+in order and divided in float32 (reference ``inference.py:65-90``).  That mode
+keeps one float16 window per fold instead of the shared float32 accumulator.
+
 Execution is B200-native: the input volume is uploaded once, every mirrored
 view of a tile runs as one batch through the network, the segmentation head
 + flip-back + view mean + Gaussian accumulation is one fused kernel per tile
@@ -73,6 +81,28 @@ def gaussian_importance(patch_size: tuple[int, ...]) -> np.ndarray:
     values[values == 0] = np.finfo(np.float32).tiny
     values.setflags(write=False)
     return values
+
+
+@lru_cache(maxsize=8)
+def nnunet_fp16_gaussian(patch_size: tuple[int, ...]) -> np.ndarray:
+    """Upstream nnU-Net's importance map: a unit impulse at ``size // 2`` filtered by a Gaussian of
+    sigma ``size / 8`` per axis (constant mode), scaled to maximum 10 and cast to float16; entries
+    that round to zero take the smallest nonzero value (reference sliding_window.py:96-113)."""
+    from scipy.ndimage import gaussian_filter
+
+    patch = tuple(int(v) for v in patch_size)
+    if any(size < 1 for size in patch):
+        raise ContractError(f"invalid patch size {patch}")
+    impulse = np.zeros(patch)
+    impulse[tuple(size // 2 for size in patch)] = 1
+    weights = gaussian_filter(impulse, [size / 8 for size in patch], mode="constant")
+    rounded = (weights / (weights.max() / 10)).astype(np.float16)
+    rounded[rounded == 0] = rounded[rounded != 0].min()
+    rounded.setflags(write=False)
+    return rounded
+
+
+ACCUMULATIONS = ("float32", "nnunet-fp16")
 
 
 def mirror_masks(axes: Sequence[int]) -> list[int]:
@@ -155,10 +185,16 @@ def run_tiles(models, volume: torch.Tensor, acc: VolumeAccumulator, offsets, pat
 
 
 def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes=(), step_fraction: float = 0.5,
-                   want_logits: bool = True, label_dtype=torch.uint8, device=None):
-    """Device logits ``(C, *spatial)`` (float32) and labels for a preprocessed ``(C, *spatial)`` volume."""
+                   want_logits: bool = True, label_dtype=torch.uint8, device=None, accumulation: str = "float32",
+                   half_logits: bool = False):
+    """Device logits ``(C, *spatial)`` (float32) and labels for a preprocessed ``(C, *spatial)`` volume.
+
+    With ``accumulation="nnunet-fp16"`` the logits are the float16 fold average
+    (as float32 values, or the float16 tensor itself when ``half_logits``).
+    """
     if not models:
         raise ContractError("fold inference requires at least one model")
+    _check_accumulation(accumulation)
     shape = tuple(data.shape)
     patch, axes = validate_request(shape, None, patch_size, num_classes, mirroring_axes)
     device = torch.device(device) if device is not None else models[0].device
@@ -171,10 +207,13 @@ def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes
         volume = padded
     spatial = tuple(volume.shape[1:])
     masks = mirror_masks(axes)
-    accumulator = VolumeAccumulator(spatial, num_classes, patch, device)
-    run_tiles(models, volume, accumulator, tile_offsets(spatial, patch, step_fraction), patch, masks)
     lo = [c.start for c in crop]
     dims = [c.stop - c.start for c in crop]
+    if accumulation == "nnunet-fp16":
+        return _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims,
+                                    want_logits, label_dtype, half_logits)
+    accumulator = VolumeAccumulator(spatial, num_classes, patch, device)
+    run_tiles(models, volume, accumulator, tile_offsets(spatial, patch, step_fraction), patch, masks)
     logits, labels, invalid = kernels.normalize_labels(accumulator.acc, accumulator.normalizer, lo, dims,
                                                        fold_divisor=float(len(models)), want_logits=want_logits,
                                                        label_dtype=label_dtype)
@@ -183,23 +222,61 @@ def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes
     return logits, labels
 
 
+def _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims, want_logits,
+                         label_dtype, half_logits):
+    """nnunet-fp16: per fold a float16 window + normaliser, normalised to float16 and summed in fold order."""
+    device = volume.device
+    gaussian = torch.from_numpy(nnunet_fp16_gaussian(tuple(patch)).astype(np.float32)).to(device)
+    offsets = tile_offsets(spatial, patch, step_fraction)
+    total = torch.empty((num_classes, *dims), dtype=torch.float16, device=device)
+    invalid = torch.zeros((1,), dtype=torch.int32, device=device)
+    acc = torch.empty((*spatial, num_classes), dtype=torch.float16, device=device)
+    normalizer = torch.empty(spatial, dtype=torch.float16, device=device)
+    batch = None
+    for index, model in enumerate(models):
+        acc.zero_()
+        normalizer.zero_()
+        for offset in offsets:
+            batch = kernels.gather_views(volume, offset, patch, masks, out=batch)
+            features = model.forward_features(batch)
+            kernels.accumulate_tile(features, masks, model.seg_weight, model.seg_bias, gaussian, acc, normalizer,
+                                    offset, add_normalizer=True, slope=model.spec.leaky_slope)
+            del features
+        kernels.fold_add_fp16(acc, normalizer, lo, dims, total, index == 0, invalid)
+    if int(invalid.item()) != 0:
+        raise ContractError("sliding-window inference produced non-finite logits")
+    logits, labels, invalid = kernels.fold_finalize_fp16(total, len(models), want_logits=want_logits and not half_logits,
+                                                         label_dtype=label_dtype)
+    if int(invalid.item()) != 0:
+        raise ContractError("fold averaging produced non-finite logits")
+    if half_logits and want_logits:
+        logits = total
+    return logits, labels
+
+
 def predict_logits(model, data_channels_first, *, patch_size, num_classes: int, mirroring_axes=(),
                    step_fraction: float = 0.5, accumulation: str = "float32") -> np.ndarray:
-    """Host float32 ``(num_classes, *spatial)`` logits (reference sliding_window.py:116-159)."""
+    """Host float32 ``(num_classes, *spatial)`` logits (reference sliding_window.py:116-159).
+
+    ``nnunet-fp16`` logits are the float16-rounded values, returned as float32.
+    """
     _check_accumulation(accumulation)
     models = model if isinstance(model, (list, tuple)) else [model]
     logits, _ = predict_volume(models, data_channels_first, patch_size=patch_size, num_classes=num_classes,
-                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None)
+                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None,
+                               accumulation=accumulation)
     return logits.cpu().numpy()
 
 
 def predict_device_logits(model, data_channels_first, *, patch_size, num_classes: int, mirroring_axes=(),
                           step_fraction: float = 0.5, accumulation: str = "float32") -> torch.Tensor:
-    """Device logits as channels-last ``(*spatial, C)`` (a view of the channel-first result)."""
+    """Device logits as channels-last ``(*spatial, C)`` (a view of the channel-first result);
+    float16 for ``nnunet-fp16`` (reference 219-254)."""
     _check_accumulation(accumulation)
     models = model if isinstance(model, (list, tuple)) else [model]
     logits, _ = predict_volume(models, data_channels_first, patch_size=patch_size, num_classes=num_classes,
-                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None)
+                               mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None,
+                               accumulation=accumulation, half_logits=True)
     return logits.permute(1, 2, 3, 0)
 
 
@@ -210,14 +287,14 @@ def predict_labels(model, data_channels_first, *, patch_size, num_classes: int, 
     models = model if isinstance(model, (list, tuple)) else [model]
     _, labels = predict_volume(models, data_channels_first, patch_size=patch_size, num_classes=num_classes,
                                mirroring_axes=mirroring_axes, step_fraction=step_fraction, want_logits=False,
-                               label_dtype=torch.uint16 if num_classes > 255 else torch.uint8)
+                               label_dtype=torch.uint16 if num_classes > 255 else torch.uint8,
+                               accumulation=accumulation)
     return labels.cpu().numpy().astype(np.uint16)
 
 
 def _check_accumulation(accumulation: str) -> None:
-    if accumulation != "float32":
-        raise ContractError(f"unsupported sliding-window accumulation {accumulation!r}: "
-                            "the B200 path implements the float32 accumulator")
+    if accumulation not in ACCUMULATIONS:
+        raise ContractError(f"unsupported sliding-window accumulation {accumulation!r}")
 
 
 def volume_work(shape, patch, step_fraction: float, views: int, folds: int) -> dict:

@@ -117,25 +117,81 @@ def accumulate(model, padded_cf: np.ndarray, patch, axes, num_classes: int, step
     return logits, normalizer
 
 
+def nnunet_fp16_gaussian(patch_size: Sequence[int]) -> np.ndarray:
+    """Upstream's importance map (reference sliding_window.py:96-113): impulse at ``size // 2``,
+    scipy ``gaussian_filter`` with sigma ``size / 8`` (constant mode), scaled to max 10, cast to
+    float16, zeros replaced by the smallest nonzero value."""
+    from scipy.ndimage import gaussian_filter
+
+    patch = tuple(int(p) for p in patch_size)
+    impulse = np.zeros(patch)
+    impulse[tuple(s // 2 for s in patch)] = 1
+    weights = gaussian_filter(impulse, [s / 8 for s in patch], mode="constant")
+    rounded = (weights / (weights.max() / 10)).astype(np.float16)
+    rounded[rounded == 0] = rounded[rounded != 0].min()
+    return rounded
+
+
+def accumulate_fp16(model, padded_cf: np.ndarray, patch, axes, num_classes: int, step_fraction: float):
+    """nnunet-fp16 window (reference sliding_window.py:415-433): float16 logits and normaliser, each
+    tile ``half(f32(logits) + pred * g32)`` and ``half(f32(norm) + g32)`` (IEEE half add)."""
+    spatial = padded_cf.shape[1:]
+    steps = compute_steps(spatial, patch, step_fraction)
+    g16 = nnunet_fp16_gaussian(patch)[..., None]
+    g32 = g16.astype(np.float32)
+    volume = np.ascontiguousarray(np.moveaxis(padded_cf, 0, -1))
+    logits = np.zeros((*spatial, num_classes), dtype=np.float16)
+    normalizer = np.zeros((*spatial, 1), dtype=np.float16)
+    for offsets in product(*steps):
+        sl = tuple(slice(o, o + p) for o, p in zip(offsets, patch))
+        pred = mirrored_prediction(model, volume[sl][None], axes)
+        weighted = (pred[0] * g32).astype(np.float32)
+        logits[sl] = (logits[sl].astype(np.float32) + weighted).astype(np.float16)
+        normalizer[sl] = (normalizer[sl].astype(np.float32) + g32).astype(np.float16)
+    return logits, normalizer
+
+
 def predict_logits(model, data_cf: np.ndarray, *, patch_size, num_classes: int,
-                   mirroring_axes=(), step_fraction: float = 0.5) -> np.ndarray:
-    """Channel-first ``(C, *spatial)`` normalized float32 logits (reference 116-216)."""
+                   mirroring_axes=(), step_fraction: float = 0.5, accumulation: str = "float32") -> np.ndarray:
+    """Channel-first ``(C, *spatial)`` normalized logits (reference 116-216): float32, or the
+    float16 values ``half(f32(logits) / f32(norm))`` for ``nnunet-fp16`` (as a float16 array)."""
     patch = tuple(int(p) for p in patch_size)
     padded, crop = pad_minimum(np.asarray(data_cf, dtype=np.float32), patch)
-    logits, normalizer = accumulate(model, padded, patch, tuple(mirroring_axes), num_classes, step_fraction)
-    normalized = (logits / normalizer).astype(np.float32)
+    if accumulation == "nnunet-fp16":
+        logits, normalizer = accumulate_fp16(model, padded, patch, tuple(mirroring_axes), num_classes,
+                                             step_fraction)
+        normalized = (logits.astype(np.float32) / normalizer.astype(np.float32)).astype(np.float16)
+    else:
+        logits, normalizer = accumulate(model, padded, patch, tuple(mirroring_axes), num_classes, step_fraction)
+        normalized = (logits / normalizer).astype(np.float32)
     return np.ascontiguousarray(np.moveaxis(normalized[crop], -1, 0))
 
 
 def average_fold_logits(models, data_cf, *, patch_size, num_outputs, mirroring_axes=(),
-                        step_fraction: float = 0.5) -> np.ndarray:
+                        step_fraction: float = 0.5, accumulation: str = "float32") -> np.ndarray:
+    """Fold ensemble (reference inference.py:65-90): float32 sum / n, or for ``nnunet-fp16`` each
+    fold rounded to float16, summed in fold order in float16 and divided by float32(n) (float16)."""
+    folds = [predict_logits(model, data_cf, patch_size=patch_size, num_classes=num_outputs,
+                            mirroring_axes=mirroring_axes, step_fraction=step_fraction,
+                            accumulation=accumulation) for model in models]
+    return average_folds(folds, accumulation)
+
+
+def average_folds(folds, accumulation: str = "float32") -> np.ndarray:
+    """The fold-sum-and-divide step alone, on given per-fold logits."""
+    half = accumulation == "nnunet-fp16"
     total = None
-    for model in models:
-        current = predict_logits(model, data_cf, patch_size=patch_size, num_classes=num_outputs,
-                                 mirroring_axes=mirroring_axes, step_fraction=step_fraction)
-        total = current if total is None else total + current
-    total = total / np.float32(len(models))
-    return total.astype(np.float32)
+    for current in folds:
+        values = np.asarray(current, dtype=np.float16 if half else np.float32)
+        if total is None:
+            total = values.copy()
+        elif half:
+            total = (total.astype(np.float32) + values.astype(np.float32)).astype(np.float16)
+        else:
+            total = total + values
+    if half:
+        return (total.astype(np.float32) / np.float32(len(folds))).astype(np.float16)
+    return (total / np.float32(len(folds))).astype(np.float32)
 
 
 def normalized_labels(logits_cl: np.ndarray, normalizer_cl: np.ndarray) -> np.ndarray:

@@ -154,3 +154,48 @@ def test_oracle_normalized_labels_invalid_and_ties():
     assert labels[0, 0, 0] == 0  # tie -> first
     assert labels[0, 0, 1] == osw.INVALID_LABEL  # NaN
     assert labels[0, 0, 2] == osw.INVALID_LABEL  # zero normaliser
+
+
+def test_nnunet_fp16_gaussian_matches_reference():
+    """Upstream's float16 importance map (reference sliding_window.py:96-113), oracle and product."""
+    from nnunet_mlx_b200.prediction.sliding_window import nnunet_fp16_gaussian
+
+    z = np.load(GOLDEN / "gaussian.npz")
+    keys = [k for k in z.files if k.startswith("fp16_")]
+    assert keys
+    for key in keys:
+        patch = tuple(int(v) for v in key[5:].split("x"))
+        assert z[key].dtype == np.float16
+        np.testing.assert_array_equal(osw.nnunet_fp16_gaussian(patch), z[key])
+        np.testing.assert_array_equal(nnunet_fp16_gaussian(patch), z[key])
+
+
+@pytest.mark.parametrize("count", [1, 2, 3, 7])
+def test_oracle_fp16_fold_rounding_matches_recorded_upstream(count):
+    """Fold rounding of nnunet-fp16 (reference tests/host/test_upstream_runner_recording.py:225-246):
+    each fold rounded to float16, summed in order, divided by float32(count), bitwise."""
+    z = np.load(GOLDEN / "upstream_runner_subset.npz")
+    folds = [z[f"rounding_input_{i}"] for i in range(count)]
+    got = osw.average_folds(folds, "nnunet-fp16")
+    assert got.dtype == np.float16
+    np.testing.assert_array_equal(got.astype(np.float32), z[f"rounding_output_{count}"])
+
+
+def test_oracle_fp16_window_is_rounded_float32_sum():
+    """The fp16 window equals the half-rounded float32 sum tile by tile (single tile: exact)."""
+    patch = (4, 4, 4)
+    rng = np.random.default_rng(9)
+    data = rng.standard_normal((1, 4, 4, 4)).astype(np.float32)
+
+    def model(tile):
+        return np.concatenate([tile, 2 * tile], axis=-1)
+
+    got = osw.predict_logits(model, data, patch_size=patch, num_classes=2, accumulation="nnunet-fp16")
+    g = osw.nnunet_fp16_gaussian(patch).astype(np.float32)
+    x = np.moveaxis(data, 0, -1)
+    expect_acc = np.concatenate([x, 2 * x], axis=-1) * g[..., None]
+    acc16 = expect_acc.astype(np.float16)
+    norm16 = g.astype(np.float16)[..., None]
+    expect = (acc16.astype(np.float32) / norm16.astype(np.float32)).astype(np.float16)
+    assert got.dtype == np.float16
+    np.testing.assert_array_equal(got, np.moveaxis(expect, -1, 0))
