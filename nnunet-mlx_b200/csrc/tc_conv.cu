@@ -86,7 +86,7 @@ struct Geometry {
   int halo;                    // 1: halo mode
   int box[3];                  // TMA box extent along w, h, d (elements, before element strides)
   int pw, plane_rows, plane_bytes;  // halo plane: row pitch, rows, bytes per half (1024-aligned)
-  int sa, sb;                  // halo-mode ring depths (A planes, B taps)
+  int sa, sb, tb;              // halo-mode ring depths (A planes, B stages) and taps per B stage
 };
 
 struct OperandMaps {
@@ -345,8 +345,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *sm.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  const int taps = g.KD * g.KH * g.KW;
   for (int ks = threadIdx.x; ks < g.ksteps; ks += blockDim.x) {
-    const int tap = ks / g.nchunk, chunk = ks - tap * g.nchunk;
+    // chunk-major K order, the order of the weight image
+    const int chunk = ks / taps, tap = ks - chunk * taps;
     const int kx = tap % g.KW, ky = (tap / g.KW) % g.KH, kz = tap / (g.KW * g.KH);
     kstab[ks] = kx | (ky << 4) | (kz << 8) | (chunk << 12);
   }
@@ -456,9 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int SA = g.sa, SB = g.sb;
   const int a_stage = C::kHalves * g.plane_bytes;
+  const uint32_t b_stage = (uint32_t)(g.tb * C::kBBytes);
+  const int taps = g.KD * g.KH * g.KW;
   uint8_t* a_ring = smem;                    // SA x [plane hi | plane lo], 1024-aligned
-  uint8_t* b_ring = smem + SA * a_stage;     // SB x B tile, 1024-aligned
-  const SharedMisc sm = shared_misc(b_ring + SB * C::kBBytes);
+  uint8_t* b_ring = smem + SA * a_stage;     // SB x tb B tiles, 1024-aligned
+  const SharedMisc sm = shared_misc(b_ring + SB * b_stage);
   uint64_t* a_full = sm.bars;
   uint64_t* a_empty = sm.bars + SA;
   uint64_t* b_full = sm.bars + 2 * SA;
@@ -519,17 +523,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_5d(dst, src.map, src.c_hi, wb, hb, db + kz, o.b, fa);
             if constexpr (SPLIT) tma_load_5d(dst + g.plane_bytes, src.map, src.c_lo, wb, hb, db + kz, o.b, fa);
             ++P;
-            for (int t2 = 0; t2 < taps2d; ++t2) {
+            for (int t2 = 0; t2 < taps2d; t2 += g.tb) {
               const int sb = T % SB;
               if (T >= SB && !mbar_wait(smem_u32(&b_empty[sb]), ((T / SB) - 1) & 1, sm.abort_flag, 23)) {
                 alive = false;
                 break;
               }
+              // tb consecutive taps of one (chunk, kz, ky) row: contiguous in the chunk-major image
               const int tap = kz * taps2d + t2;
               const uint32_t fb = smem_u32(&b_full[sb]);
-              mbar_arrive_expect_tx(fb, C::kBBytes);
-              bulk_g2s(smem_u32(b_ring + sb * C::kBBytes), bsrc + (int64_t)(tap * g.nchunk + c) * C::kBBytes,
-                       C::kBBytes, fb);
+              mbar_arrive_expect_tx(fb, b_stage);
+              bulk_g2s(smem_u32(b_ring + sb * b_stage), bsrc + (int64_t)(c * taps + tap) * C::kBBytes, b_stage, fb);
               ++T;
             }
           }
@@ -552,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t adesc0 = sw128_desc(smem_u32(a_ring), (uint32_t)g.pw * 128);
       const uint64_t bdesc0 = sw128_desc(smem_u32(b_ring));
       const uint32_t a_stage16 = (uint32_t)a_stage >> 4, lo16 = (uint32_t)g.plane_bytes >> 4;
+      const uint32_t b_stage16 = b_stage >> 4;
       constexpr uint32_t kB16 = C::kBBytes >> 4;
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
@@ -572,26 +577,39 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             fence_after();
-            for (int ky = 0; ky < g.KH && alive; ++ky) {
-              for (int kx = 0; kx < g.KW; ++kx) {
-                const uint64_t ad = ap + (uint64_t)((ky * g.pw + kx) * 8);
-                const uint64_t bd = bdesc0 + (uint64_t)(sb * kB16);
-                if (!mbar_wait(smem_u32(&b_full[sb]), pb, sm.abort_flag, 27)) {
-                  alive = false;
-                  break;
+            // A row offset of tap (kx, ky) in 16-byte units, advanced incrementally (no divisions
+            // between MMA groups): +8 per kx, +8 * (pw - KW + 1) at the end of a kx row.
+            uint32_t aoff = 0;
+            int kx = 0;
+            const uint32_t row_wrap = (uint32_t)(g.pw - g.KW + 1) * 8;
+            for (int t2 = 0; t2 < taps2d && alive; t2 += g.tb) {
+              const uint64_t bstage_desc = bdesc0 + (uint64_t)(sb * b_stage16);
+              if (!mbar_wait(smem_u32(&b_full[sb]), pb, sm.abort_flag, 27)) {
+                alive = false;
+                break;
+              }
+              fence_after();
+              uint64_t bd = bstage_desc;
+              for (int j = 0; j < g.tb; ++j) {
+                const uint64_t ad = ap + aoff;
+                if (++kx == g.KW) {
+                  kx = 0;
+                  aoff += row_wrap;
+                } else {
+                  aoff += 8;
                 }
-                fence_after();
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
                   mma_tf32_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (accumulate | kk) ? 1u : 0u);
                   if constexpr (SPLIT) mma_tf32_ss(d, ad + lo16 + 2 * kk, bd + 2 * kk, idesc, 1u);
                 }
                 accumulate = 1;
-                mma_commit(smem_u32(&b_empty[sb]));
-                if (++sb == SB) {
-                  sb = 0;
-                  pb ^= 1u;
-                }
+                bd += kB16;
+              }
+              mma_commit(smem_u32(&b_empty[sb]));
+              if (++sb == SB) {
+                sb = 0;
+                pb ^= 1u;
               }
             }
             mma_commit(smem_u32(&a_empty[sa]));
@@ -617,9 +635,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Weight image: [n_tile][kstep][N rows][128 B], natural K order within the
-// 32-channel step, 16-byte chunks XOR-swizzled by row % 8 (the SW128 K-major
-// layout).  Rows [0, BC) hold W_hi of the tile's BC GEMM columns and rows
+// Weight image: [n_tile][kstep = chunk * taps + tap][N rows][128 B] (so the taps
+// of one 32-channel chunk are contiguous), natural K order within the 32-channel
+// step, 16-byte chunks XOR-swizzled by row % 8 (the SW128 K-major layout).  Rows [0, BC) hold W_hi of the tile's BC GEMM columns and rows
 // [BC, 2 BC) W_lo (float32 mode), or BC rows of TF32.  GEMM column n is output
 // channel n, or for a transposed convolution (row_taps > 1) the pair
 // (tap = n / up_cout, channel = n % up_cout) reading weight (channel, tap, ci).
@@ -639,7 +657,7 @@ __global__ void pack_kernel(const float* __restrict__ w, int cols_total, int kvo
     const int k = ((word >> 2) ^ (n & 7)) * 4 + (word & 3);
     const int half = n / bc;
     const int col = nt * bc + (n - half * bc);
-    const int tap = ks / nchunk, chunk = ks - tap * nchunk;
+    const int chunk = ks / kvol, tap = ks - chunk * kvol;  // chunk-major K-step order
     const int ci = chunk * BK + k;
     float val = 0.f;
     if (col < cols_total && ci < cin_total) {
@@ -704,8 +722,10 @@ inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bby
   const int a_stage = halves * g.plane_bytes;
   const int budget = kMaxSmem - 1024 - kMiscBytes;
   g.sa = (3 * a_stage + 4 * bbytes <= budget) ? 3 : 2;
-  g.sb = std::min(16, (budget - g.sa * a_stage) / bbytes);
-  if (g.sb < 4 || 2 * g.sa + 2 * g.sb + 5 > kMaxBars) return false;
+  // B stages hold a whole kx row of taps when three such stages fit, else one tap
+  g.tb = (g.sa * a_stage + 3 * g.KW * bbytes <= budget) ? g.KW : 1;
+  g.sb = std::min(16, (budget - g.sa * a_stage) / (g.tb * bbytes));
+  if (g.sb < (g.tb > 1 ? 3 : 4) || 2 * g.sa + 2 * g.sb + 5 > kMaxBars) return false;
   g.box[0] = g.pw;
   g.box[1] = ph;
   g.box[2] = 1;
@@ -812,7 +832,7 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::min(g.total_tiles, sms);
   if (g.halo) {
-    const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * C::kBBytes + kMiscBytes;
+    const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * g.tb * C::kBBytes + kMiscBytes;
     NNB_REQUIRE(smem <= kMaxSmem, "conv3d: halo plan exceeds shared memory (%d bytes)", smem);
     conv3d_halo_kernel<BC, SPLIT><<<grid, kThreads, smem, stream>>>(a, g, maps);
   } else {
