@@ -36,9 +36,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "voxels/sec full-volume 3D U-Net inference (8x mirror TTA)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per launch of the dominant convolution launch, from the
-# ncu capture summarised in profiles/ (batch-1 capture scaled to the 8-view launch).
-DOMINANT_TRAFFIC = {}
+# DRAM bytes (read + write) per launch of the dominant convolution launch, from the ncu capture
+# summarised in profiles/conv3d_halo_kernel_32to32_128cube_fp32.md: the one-view launch read 537.2 MB
+# and wrote 252.1 MB; views are independent samples of the batch, so an 8-view launch moves 8x that.
+DOMINANT_TRAFFIC = {"8x128x128x128 32->32 k3x3x3 s1x1x1": 8 * (537.210624e6 + 252.089088e6)}
 
 
 def parse_args():
