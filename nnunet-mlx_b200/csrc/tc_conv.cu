@@ -449,7 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Halo mode: one TMA box per (chunk, kz plane, half) feeds every (kx, ky) tap.
 // ---------------------------------------------------------------------------
-template <int BC, bool SPLIT>
+// TB = taps per B stage: 3 (a whole kx row of a 3-wide kernel, fully unrolled) or 1 (any kernel).
+template <int BC, bool SPLIT, int TB>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_halo_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
   using C = Cfg<BC, SPLIT>;
@@ -577,6 +578,35 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             fence_after();
+            if constexpr (TB > 1) {
+              // one B stage per kx row (TB == KW): compile-time tap offsets, no control flow between
+              // the row's 8 x TB MMAs
+              for (int ky = 0; ky < g.KH && alive; ++ky) {
+                const uint64_t arow = ap + (uint64_t)(ky * g.pw * 8);
+                const uint64_t bstage_desc = bdesc0 + (uint64_t)(sb * b_stage16);
+                if (!mbar_wait(smem_u32(&b_full[sb]), pb, sm.abort_flag, 27)) {
+                  alive = false;
+                  break;
+                }
+                fence_after();
+#pragma unroll
+                for (int j = 0; j < TB; ++j) {
+#pragma unroll
+                  for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint64_t ad = arow + (uint64_t)(8 * j + 2 * kk);
+                    const uint64_t bd = bstage_desc + (uint64_t)(j * kB16 + 2 * kk);
+                    mma_tf32_ss(d, ad, bd, idesc, (accumulate | j | kk) ? 1u : 0u);
+                    if constexpr (SPLIT) mma_tf32_ss(d, ad + lo16, bd, idesc, 1u);
+                  }
+                }
+                accumulate = 1;
+                mma_commit(smem_u32(&b_empty[sb]));
+                if (++sb == SB) {
+                  sb = 0;
+                  pb ^= 1u;
+                }
+              }
+            } else {
             // A row offset of tap (kx, ky) in 16-byte units, advanced incrementally (no divisions
             // between MMA groups): +8 per kx, +8 * (pw - KW + 1) at the end of a kx row.
             uint32_t aoff = 0;
@@ -611,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sb = 0;
                 pb ^= 1u;
               }
+            }
             }
             mma_commit(smem_u32(&a_empty[sa]));
             if (++sa == SA) {
@@ -721,11 +752,20 @@ inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bby
   g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
   const int a_stage = halves * g.plane_bytes;
   const int budget = kMaxSmem - 1024 - kMiscBytes;
-  g.sa = (3 * a_stage + 4 * bbytes <= budget) ? 3 : 2;
-  // B stages hold a whole kx row of taps when three such stages fit, else one tap
-  g.tb = (g.sa * a_stage + 3 * g.KW * bbytes <= budget) ? g.KW : 1;
+  // Ring plan, first that fits: B stages of a whole kx row (3-wide kernels) with 3 A planes and
+  // >= 3 B stages, then with 2 A planes and >= 2 B stages, else one tap per B stage.
+  if (g.KW == 3 && 3 * a_stage + 3 * 3 * bbytes <= budget) {
+    g.sa = 3;
+    g.tb = 3;
+  } else if (g.KW == 3 && 2 * a_stage + 2 * 3 * bbytes <= budget) {
+    g.sa = 2;
+    g.tb = 3;
+  } else {
+    g.sa = (3 * a_stage + 4 * bbytes <= budget) ? 3 : 2;
+    g.tb = 1;
+  }
   g.sb = std::min(16, (budget - g.sa * a_stage) / (g.tb * bbytes));
-  if (g.sb < (g.tb > 1 ? 3 : 4) || 2 * g.sa + 2 * g.sb + 5 > kMaxBars) return false;
+  if (g.sb < (g.tb > 1 ? 2 : 4) || 2 * g.sa + 2 * g.sb + 5 > kMaxBars) return false;
   g.box[0] = g.pw;
   g.box[1] = ph;
   g.box[2] = 1;
@@ -817,11 +857,14 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   using C = Cfg<BC, SPLIT>;
   int dev = 0;
   NNB_CUDA_CHECK(cudaGetDevice(&dev));
-  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, bit 1 halo), per device
-  const int bit = g.halo ? 2 : 1;
+  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, 1/2 halo TB 1/3), per device
+  const int bit = g.halo ? (g.tb == 3 ? 4 : 2) : 1;
   if (dev >= 64 || !(configured[dev] & bit)) {
-    if (g.halo)
-      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, SPLIT>,
+    if (g.halo && g.tb == 3)
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, SPLIT, 3>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    else if (g.halo)
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, SPLIT, 1>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     else
       NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_tc_kernel<BC, SPLIT>,
@@ -834,7 +877,10 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   if (g.halo) {
     const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * g.tb * C::kBBytes + kMiscBytes;
     NNB_REQUIRE(smem <= kMaxSmem, "conv3d: halo plan exceeds shared memory (%d bytes)", smem);
-    conv3d_halo_kernel<BC, SPLIT><<<grid, kThreads, smem, stream>>>(a, g, maps);
+    if (g.tb == 3)
+      conv3d_halo_kernel<BC, SPLIT, 3><<<grid, kThreads, smem, stream>>>(a, g, maps);
+    else
+      conv3d_halo_kernel<BC, SPLIT, 1><<<grid, kThreads, smem, stream>>>(a, g, maps);
   } else {
     const int smem = 1024 + C::S * C::kStageBytes + kMiscBytes + 4 * kMaxKsteps;
     conv3d_tc_kernel<BC, SPLIT><<<grid, kThreads, smem, stream>>>(a, g, maps);
