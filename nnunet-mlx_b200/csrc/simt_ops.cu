@@ -194,9 +194,150 @@ __global__ void __launch_bounds__(kTileRows) conv3d_small_cin_kernel(nnb_conv3d_
   }
 }
 
+// ---------------------------------------------------------------------------
+// The first layer's shape (1, 2 or 4 raw input channels, 3x3x3, stride 1,
+// padding 1, 32-channel output groups): compile-time taps and channels, each
+// of 64 threads computes two voxels of the 128-voxel tile (rows r and r + 64)
+// so every float4 weight read from shared memory feeds 8 FMAs, and the padding
+// test is three per-axis 3-bit masks computed once.  Same output staging,
+// coalesced stores and (sum, M2, n) partials as conv3d_small_cin_kernel.
+// ---------------------------------------------------------------------------
+template <int CIN>
+__global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int tps) {
+  __shared__ float4 w_s[27 * CIN * 8];  // [tap][ci][co/4]
+  __shared__ float out_s[kTileRows][33];
+  const int t = blockIdx.x % tps;
+  const int b = blockIdx.x / tps;
+  const int co0 = blockIdx.y * 32;
+  for (int i = threadIdx.x; i < 27 * CIN * 32; i += blockDim.x) {
+    const int co = i % 32, ci = (i / 32) % CIN, tap = i / (32 * CIN);
+    reinterpret_cast<float*>(w_s)[i] = co0 + co < a.cout ? a.weight[((int64_t)(co0 + co) * 27 + tap) * CIN + ci] : 0.f;
+  }
+  __syncthreads();
+  const int D = a.out_dims[0], H = a.out_dims[1], W = a.out_dims[2];
+  const int64_t ovox = (int64_t)D * H * W;
+  const float* x = a.seg[0].data + (int64_t)b * ovox * CIN;
+  float acc[2][32];
+  int base[2];
+  uint32_t mask[2];  // bits 0-8: kx, ky, kz validity (3 bits each)
+#pragma unroll
+  for (int v = 0; v < 2; ++v) {
+    const int64_t m = (int64_t)t * kTileRows + threadIdx.x + 64 * v;
+    const bool valid = m < ovox;
+    const int ox = (int)(m % W), oy = (int)((m / W) % H), oz = (int)(m / ((int64_t)W * H));
+    uint32_t mk = 0;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      mk |= (uint32_t)(valid && ox + k - 1 >= 0 && ox + k - 1 < W) << k;
+      mk |= (uint32_t)(valid && oy + k - 1 >= 0 && oy + k - 1 < H) << (3 + k);
+      mk |= (uint32_t)(valid && oz + k - 1 >= 0 && oz + k - 1 < D) << (6 + k);
+    }
+    mask[v] = mk;
+    base[v] = valid ? (int)((((int64_t)(oz - 1) * H + (oy - 1)) * W + (ox - 1)) * CIN) : 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[v][j] = 0.f;
+  }
+#pragma unroll
+  for (int kz = 0; kz < 3; ++kz) {
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const int tap = (kz * 3 + ky) * 3 + kx;
+        const int off = ((kz * H + ky) * W + kx) * CIN;
+        float xv[2][CIN];
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+          const bool in = (mask[v] >> kx & 1) & (mask[v] >> (3 + ky) & 1) & (mask[v] >> (6 + kz) & 1);
+#pragma unroll
+          for (int ci = 0; ci < CIN; ++ci) xv[v][ci] = in ? __ldg(x + base[v] + off + ci) : 0.f;
+        }
+#pragma unroll
+        for (int ci = 0; ci < CIN; ++ci) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 w = w_s[(tap * CIN + ci) * 8 + q];
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+              acc[v][4 * q + 0] = fmaf(xv[v][ci], w.x, acc[v][4 * q + 0]);
+              acc[v][4 * q + 1] = fmaf(xv[v][ci], w.y, acc[v][4 * q + 1]);
+              acc[v][4 * q + 2] = fmaf(xv[v][ci], w.z, acc[v][4 * q + 2]);
+              acc[v][4 * q + 3] = fmaf(xv[v][ci], w.w, acc[v][4 * q + 3]);
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < 2; ++v) {
+    const int r = threadIdx.x + 64 * v;
+    const bool valid = (int64_t)t * kTileRows + r < ovox;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float y = acc[v][j];
+      if (a.bias != nullptr && co0 + j < a.cout) y += __ldg(a.bias + co0 + j);
+      out_s[r][j] = valid ? y : 0.f;
+    }
+  }
+  __syncthreads();
+  const int rows = (int)min((int64_t)kTileRows, ovox - (int64_t)t * kTileRows);
+  const int ncols = min(32, a.cout - co0);
+  float* dst = a.out + ((int64_t)b * ovox + (int64_t)t * kTileRows) * a.cout + co0;
+  if (ncols == 32 && (a.cout % 4) == 0) {
+    for (int i = threadIdx.x; i < rows * 8; i += blockDim.x) {
+      const int row = i >> 3, c4 = (i & 7) * 4;
+      *reinterpret_cast<float4*>(dst + (int64_t)row * a.cout + c4) =
+          make_float4(out_s[row][c4], out_s[row][c4 + 1], out_s[row][c4 + 2], out_s[row][c4 + 3]);
+    }
+  } else {
+    for (int i = threadIdx.x; i < rows * 32; i += blockDim.x) {
+      const int row = i >> 5, c = i & 31;
+      if (c < ncols) dst[(int64_t)row * a.cout + c] = out_s[row][c];
+    }
+  }
+  if (a.partials == nullptr) return;
+  if (threadIdx.x < ncols) {
+    const int c = threadIdx.x;
+    float sum = 0.f;
+    for (int i = 0; i < rows; ++i) sum += out_s[i][c];
+    const float mean = sum / rows;
+    float m2 = 0.f;
+    for (int i = 0; i < rows; ++i) {
+      const float d = out_s[i][c] - mean;
+      m2 = fmaf(d, d, m2);
+    }
+    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + c) * 3;
+    p[0] = sum;
+    p[1] = m2;
+    p[2] = (float)rows;
+  }
+}
+
+static bool first_layer_shape(const nnb_conv3d_args& a) {
+  if (a.num_segments != 1 || a.seg[0].scale != nullptr) return false;
+  const int c = a.seg[0].channels;
+  if (c != 1 && c != 2 && c != 4) return false;
+  for (int i = 0; i < 3; ++i)
+    if (a.kernel[i] != 3 || a.stride[i] != 1 || a.pad[i] != 1 || a.in_dims[i] != a.out_dims[i]) return false;
+  // per-sample element offsets fit in int (base[] arithmetic)
+  return (int64_t)a.out_dims[0] * a.out_dims[1] * a.out_dims[2] * c < (1LL << 31);
+}
+
 int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
   const int64_t ovox = (int64_t)a.out_dims[0] * a.out_dims[1] * a.out_dims[2];
   const int tps = tiles_per_sample(ovox);
+  if (first_layer_shape(a)) {
+    dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + 31) / 32));
+    NNB_REQUIRE((int64_t)tps * a.batch < (1LL << 31), "conv3d: too many tiles");
+    switch (a.seg[0].channels) {
+      case 1: conv3d_first_kernel<1><<<grid, 64, 0, stream>>>(a, tps); break;
+      case 2: conv3d_first_kernel<2><<<grid, 64, 0, stream>>>(a, tps); break;
+      default: conv3d_first_kernel<4><<<grid, 64, 0, stream>>>(a, tps); break;
+    }
+    NNB_LAUNCH_CHECK();
+    return NNB_OK;
+  }
   if (a.num_segments == 1 && a.seg[0].channels <= kSmallCin &&
       a.kernel[0] * a.kernel[1] * a.kernel[2] <= kSmallMaxTaps) {
     dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + 31) / 32));
