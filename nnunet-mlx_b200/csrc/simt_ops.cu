@@ -314,6 +314,66 @@ __global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pointwise head (1x1x1, one lazy segment of <= 64 channels, <= 8 outputs, no
+// statistics): the segmentation head of the network's tile-callable seam.  One
+// thread per voxel reads its features with 16-byte loads, applies the lazy
+// affine + LeakyReLU, and writes its logits; HBM-bound on the feature read.
+// ---------------------------------------------------------------------------
+constexpr int kPointMaxCin = 64;
+constexpr int kPointMaxCout = 8;
+
+__global__ void __launch_bounds__(256) conv3d_pointwise_kernel(nnb_conv3d_args a, int64_t ovox) {
+  __shared__ float w_s[kPointMaxCout][kPointMaxCin];
+  __shared__ float b_s[kPointMaxCout];
+  const nnb_segment seg = a.seg[0];
+  const int cin = seg.channels, cout = a.cout;
+  const int b = blockIdx.y;
+  for (int i = threadIdx.x; i < kPointMaxCout * kPointMaxCin; i += blockDim.x) {
+    const int co = i / kPointMaxCin, ci = i % kPointMaxCin;
+    w_s[co][ci] = (co < cout && ci < cin) ? a.weight[(int64_t)co * cin + ci] : 0.f;
+  }
+  if (threadIdx.x < kPointMaxCout)
+    b_s[threadIdx.x] = (a.bias != nullptr && (int)threadIdx.x < cout) ? a.bias[threadIdx.x] : 0.f;
+  __syncthreads();
+  const float* sc = seg.scale ? seg.scale + (int64_t)b * cin : nullptr;
+  const float* sh = seg.scale ? seg.shift + (int64_t)b * cin : nullptr;
+  for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < ovox; m += (int64_t)gridDim.x * blockDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(seg.data + ((int64_t)b * ovox + m) * cin);
+    float y[kPointMaxCout];
+#pragma unroll
+    for (int co = 0; co < kPointMaxCout; ++co) y[co] = b_s[co];
+    for (int c4 = 0; c4 < cin / 4; ++c4) {
+      const float4 x4 = __ldg(src + c4);
+      const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int ci = c4 * 4 + e;
+        float v = xs[e];
+        if (sc != nullptr) {
+          v = fmaf(v, __ldg(sc + ci), __ldg(sh + ci));
+          if (seg.leaky) v = leaky(v, a.slope);
+        }
+#pragma unroll
+        for (int co = 0; co < kPointMaxCout; ++co) y[co] = fmaf(v, w_s[co][ci], y[co]);
+      }
+    }
+    float* dst = a.out + ((int64_t)b * ovox + m) * cout;
+#pragma unroll
+    for (int co = 0; co < kPointMaxCout; ++co)
+      if (co < cout) dst[co] = y[co];
+  }
+}
+
+static bool pointwise_shape(const nnb_conv3d_args& a) {
+  if (a.num_segments != 1 || a.partials != nullptr) return false;
+  if (a.seg[0].channels % 4 != 0 || a.seg[0].channels > kPointMaxCin || a.cout > kPointMaxCout) return false;
+  if ((reinterpret_cast<uintptr_t>(a.seg[0].data) & 15) != 0) return false;
+  for (int i = 0; i < 3; ++i)
+    if (a.kernel[i] != 1 || a.stride[i] != 1 || a.pad[i] != 0) return false;
+  return true;
+}
+
 static bool first_layer_shape(const nnb_conv3d_args& a) {
   if (a.num_segments != 1 || a.seg[0].scale != nullptr) return false;
   const int c = a.seg[0].channels;
@@ -327,6 +387,13 @@ static bool first_layer_shape(const nnb_conv3d_args& a) {
 int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
   const int64_t ovox = (int64_t)a.out_dims[0] * a.out_dims[1] * a.out_dims[2];
   const int tps = tiles_per_sample(ovox);
+  if (pointwise_shape(a)) {
+    NNB_REQUIRE(a.batch < 65536, "conv3d: batch too large for the pointwise grid");
+    const int blocks = (int)std::min<int64_t>((ovox + 255) / 256, 148 * 8);
+    conv3d_pointwise_kernel<<<dim3((unsigned)blocks, (unsigned)a.batch), 256, 0, stream>>>(a, ovox);
+    NNB_LAUNCH_CHECK();
+    return NNB_OK;
+  }
   if (first_layer_shape(a)) {
     dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + 31) / 32));
     NNB_REQUIRE((int64_t)tps * a.batch < (1LL << 31), "conv3d: too many tiles");

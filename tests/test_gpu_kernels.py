@@ -262,3 +262,19 @@ def test_c_abi_rejects_bad_arguments(cuda_device):
     w = torch.zeros((8, 3, 3, 3, 8), device=cuda_device)
     with pytest.raises(ContractError):
         kernels.conv3d([x], w, kernel=(3, 3, 3), stride=(1, 1, 1), pad=(1, 1, 1), cout=8, precision=7)
+
+
+@pytest.mark.parametrize("cin,cout,lazy", [(32, 3, True), (4, 2, False), (64, 8, True)])
+def test_pointwise_head_matches_reference(cuda_device, cin, cout, lazy):
+    """1x1x1 head without statistics (the network's tile-callable seam) on the pointwise kernel."""
+    from nnunet_mlx_b200 import _native, kernels
+
+    rng = np.random.default_rng(cin + cout)
+    lz, raw, sc, sh = _make_segment(rng, 2, (5, 6, 7), cin, lazy, cuda_device)
+    w = torch.from_numpy(rng.standard_normal((cout, 1, 1, 1, cin)).astype(np.float32))
+    b = torch.from_numpy(rng.standard_normal(cout).astype(np.float32))
+    out, partials = kernels.conv3d([lz], w.to(cuda_device), kernel=(1, 1, 1), stride=(1, 1, 1), pad=(0, 0, 0),
+                                   cout=cout, bias=b.to(cuda_device), precision=_native.PREC_SIMT, stats=False)
+    assert partials is None
+    ref = _conv_ref([_lazy_ref(raw, sc, sh, lazy)], w, (1, 1, 1), (0, 0, 0), bias=b)
+    np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), rtol=1e-5, atol=1e-5)
