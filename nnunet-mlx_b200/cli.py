@@ -2,12 +2,15 @@
 
 Option names follow reference ``src/nnunet_mlx/commands/upstream.py:56-118``
 (nnUNetv2_predict's flags).  Inputs are preprocessed ``(C, *spatial)``
-``.npy`` / ``.npz`` cases in the ``-i`` folder; ``-m`` is a converted model
-folder.  Flags that only concern raw-image I/O or the reference's process
+``.npy`` / ``.npz`` cases in the ``-i`` folder.  The model is ``-m`` (a
+converted model folder, or a trained upstream folder with
+``fold_*/checkpoint_final.pth``) or ``-d DATASET [-tr TRAINER] [-p PLANS]``
+resolved under ``$nnUNet_results``; upstream folders are converted once into
+the conversion cache (``storage.upstream.cached_conversion``).  Flags that only concern raw-image I/O or the reference's process
 pools (``-npp``, ``-nps``, ``-prev_stage_predictions``, ``--max-inflight-bytes``)
 are accepted and ignored.
 
-    python -m nnunet_mlx_b200.cli predict -i IN -o OUT -m MODEL [-f 0 1 ...] [-step_size 0.5]
+    python -m nnunet_mlx_b200.cli predict -i IN -o OUT (-m MODEL | -d DATASET [-tr T] [-p P]) [-f 0 1 ...]
         [--disable_tta] [--save_probabilities] [--continue_prediction] [-num_parts N -part_id K]
         [-c 3d_fullres] [-chk checkpoint_final] [--precision fp32|tf32] [--json]
 """
@@ -18,6 +21,7 @@ import argparse
 import json
 import sys
 from dataclasses import replace
+from pathlib import Path
 
 from nnunet_mlx_b200.errors import ContractError
 
@@ -28,7 +32,10 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("predict", help="predict a folder of preprocessed cases")
     p.add_argument("-i", dest="input_folder", required=True)
     p.add_argument("-o", dest="output_folder", required=True)
-    p.add_argument("-m", dest="model_folder", required=True)
+    p.add_argument("-m", dest="model_folder", default=None)
+    p.add_argument("-d", dest="dataset", default=None)
+    p.add_argument("-tr", dest="trainer", default="nnUNetTrainer")
+    p.add_argument("-p", dest="plans", default="nnUNetPlans")
     p.add_argument("-c", dest="configuration", default="3d_fullres")
     p.add_argument("-f", dest="folds", nargs="+", default=None)
     p.add_argument("-chk", dest="checkpoint_name", default="checkpoint_final")
@@ -47,6 +54,21 @@ def build_parser() -> argparse.ArgumentParser:
     return parser
 
 
+def resolve_model(args, folds) -> tuple[Path, str]:
+    """(converted model folder, checkpoint directory name) for ``-m`` or ``-d``; trained upstream
+    folders (``fold_*/<checkpoint>.pth``) go through the conversion cache."""
+    from nnunet_mlx_b200.storage.upstream import CONVERTED_CHECKPOINT, cached_conversion, resolve_results_folder
+
+    if (args.model_folder is None) == (args.dataset is None):
+        raise ContractError("pass exactly one of -m MODEL_FOLDER and -d DATASET")
+    folder = Path(args.model_folder) if args.model_folder is not None else resolve_results_folder(
+        args.dataset, configuration=args.configuration, trainer=args.trainer, plans=args.plans)
+    name = args.checkpoint_name.removesuffix(".pth")
+    if any(folder.glob(f"fold_*/{name}.pth")):
+        return cached_conversion(folder, folds=folds, checkpoint_name=f"{name}.pth"), CONVERTED_CHECKPOINT
+    return folder, name
+
+
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
     try:
@@ -58,9 +80,9 @@ def main(argv=None) -> int:
         from nnunet_mlx_b200.prediction.pipeline import ModelFolderPredictor
 
         folds = None if args.folds is None else [f if f == "all" else int(f) for f in args.folds]
-        bundle = load_model_bundle(args.model_folder, configuration=args.configuration, folds=folds,
-                                   checkpoint_name=args.checkpoint_name.removesuffix(".pth"),
-                                   precision=args.precision)
+        model_folder, checkpoint_name = resolve_model(args, folds)
+        bundle = load_model_bundle(model_folder, configuration=args.configuration, folds=folds,
+                                   checkpoint_name=checkpoint_name, precision=args.precision)
         if args.disable_tta:
             bundle = replace(bundle, mirroring_axes=())
         from nnunet_mlx_b200.medmlx import ACCUMULATION
