@@ -36,10 +36,16 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "voxels/sec full-volume 3D U-Net inference (8x mirror TTA)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per launch of the dominant convolution launch, from the ncu capture
-# summarised in profiles/conv3d_halo_kernel_32to32_128cube_fp32.md: the one-view launch read 537.2 MB
-# and wrote 252.1 MB; views are independent samples of the batch, so an 8-view launch moves 8x that.
-DOMINANT_TRAFFIC = {"8x128x128x128 32->32 k3x3x3 s1x1x1": 8 * (537.210624e6 + 252.089088e6)}
+# DRAM bytes (read + write) per launch of the dominant convolution launch, by precision, from the ncu
+# captures summarised in profiles/ (one view per capture; views are independent samples of the batch,
+# so an 8-view launch moves 8x that): split TF32 read 537.2 MB (the hi/lo operand) and wrote 252.1 MB.
+DOMINANT_TRAFFIC = {("fp32-tf32x2", "8x128x128x128 32->32 k3x3x3 s1x1x1"): 8 * (537.210624e6 + 252.089088e6)}
+
+
+# tensor products per useful product of each precision, relative to the dense bf16 rate
+MODE_PRODUCTS = {"fp32": 3.0, "fp32-tf32x2": 8.0, "tf32": 2.0}
+DTYPES = {"fp32": "fp32 (fp16-pair tensor-core products, fp32 accumulation)",
+          "fp32-tf32x2": "fp32 (split-TF32 tensor cores)", "tf32": "tf32"}
 
 
 def parse_args():
@@ -49,7 +55,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--config", type=int, default=2, help="BASELINE config number (2, 3, 4 or 5)")
-    p.add_argument("--precision", choices=["fp32", "tf32"], default="fp32")
+    p.add_argument("--precision", choices=["fp32", "fp32-tf32x2", "tf32"], default="fp32")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -365,7 +371,7 @@ def main():
         conv = prof.get("conv3d_tc", {})
         conv_all = conv.get("flops", 0.0) / conv["seconds"] / 1e12 if conv.get("seconds") else 0.0
         peak = pk["bf16_tflops_sustained"]
-        ceiling = peak / (8.0 if args.precision == "fp32" else 2.0)
+        ceiling = peak / MODE_PRODUCTS[args.precision]
         roofline = {"bound": "tensor", "kernel": "conv3d_tc_kernel", "achieved": None, "peak": peak,
                     "unit": "TFLOP/s", "frac": None, "traffic": None}
         if dominant is not None:
@@ -373,21 +379,21 @@ def main():
             achieved = flops / (mean_ms / 1e3) / 1e12
             roofline.update({
                 "launch": detail, "launches": count, "mean_ms": mean_ms, "achieved": achieved,
-                "frac": achieved / peak, "traffic": DOMINANT_TRAFFIC.get(detail),
+                "frac": achieved / peak, "traffic": DOMINANT_TRAFFIC.get((args.precision, detail)),
                 "algorithmic_flops_per_launch": flops,
                 "mode_ceiling": ceiling, "frac_of_mode_ceiling": achieved / ceiling,
                 "all_conv_launches_tflops": conv_all})
         roofline.update({
             "peak_source": f"{pk['source']} dense bf16, sustained (kernel timed inside a long step)",
             "note": "achieved = algorithmic FLOPs (2 x MACs) of the dominant launch / its mean CUDA-event "
-                    "duration over the timed region; fp32 mode computes split TF32: two TF32 MMAs of doubled N per "
-                    "8-channel sub-step (4 tensor products per useful product) at half the bf16 tensor rate, so its "
-                    "arithmetic ceiling is peak/8 (tf32 mode: peak/2)"})
+                    "duration over the timed region; fp32 mode computes fp16 operand pairs: per 16-channel "
+                    "sub-step A_hi x [W0;W1'] and A_lo' x W0 (3 tensor products per useful product at the "
+                    "bf16/fp16 rate), so its arithmetic ceiling is peak/3 (fp32-tf32x2: 4 products at half "
+                    "rate, peak/8; tf32: peak/2)"})
         line = {
             "metric": METRIC, "value": value, "unit": "voxels/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (split-TF32 tensor cores)"
-            if args.precision == "fp32" else "tf32",
+            "scaling": "strong", "vs_baseline": None, "dtype": DTYPES[args.precision],
             "data": "synthetic",
             "config": {"workload": f"config{args.config}", "volume": list(shape), "patch": list(patch),
                        "step_fraction": 0.5, "mirror_views": views, "folds": len(models), "tiles": work["tiles"],

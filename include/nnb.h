@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 5
+#define NNB_ABI_VERSION 6
 
 enum nnb_status {
   NNB_OK = 0,
@@ -43,9 +43,13 @@ enum nnb_status {
 
 /* Arithmetic of the convolution contractions. */
 enum nnb_precision {
-  NNB_PREC_FP32 = 0,   /* split-TF32 (hi/lo products): float32-level accuracy   */
-  NNB_PREC_TF32 = 1,   /* single-pass TF32 tensor cores (fast, looser bound)     */
-  NNB_PREC_SIMT = 2    /* plain float32 FMA on CUDA cores (any shape)            */
+  NNB_PREC_FP32 = 0,      /* split fp16 pairs (hi + 2^-11 lo', 3 products): float32-level
+                             accuracy; activations must stay below 65504 in magnitude
+                             (out-of-range values are counted, see nnb_operand_range_events) */
+  NNB_PREC_TF32 = 1,      /* single-pass TF32 tensor cores (fast, looser bound)     */
+  NNB_PREC_SIMT = 2,      /* plain float32 FMA on CUDA cores (any shape)            */
+  NNB_PREC_FP32_TF32 = 3  /* split TF32 (hi/lo products): float32-level accuracy at any
+                             float32 magnitude; half the speed of NNB_PREC_FP32      */
 };
 
 /* One channel segment of a convolution input (two segments = decoder concat). */
@@ -107,15 +111,31 @@ int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
 
 /*
  * Tensor-core operand preparation: apply a lazy activation's affine +
- * LeakyReLU once per element and write the TF32 form the tensor-core
- * convolution gathers -- split (NNB_PREC_FP32): per voxel [hi(C) | lo(C)],
- * hi = x with the 13 low mantissa bits cleared, lo = x - hi; NNB_PREC_TF32:
- * x rounded to TF32.  out holds batch * voxels * C * (2 or 1) floats.  Replaces
- * the affine pass of src/nnunet_mlx/kernels/metal_native_norm.py:62-70,155-168
- * (there the normalised activation is materialised in float32).
+ * LeakyReLU once per element and write the form the tensor-core convolution
+ * gathers:
+ *   NNB_PREC_FP32       per voxel and 32-channel group, 64 halves
+ *                       [hi(32) | lo'(32)], hi = fp16(x), lo' = fp16(2^11 (x - hi));
+ *                       |x| >= 65504 increments the range-event counter
+ *                       (C % 32 == 0; out holds batch * voxels * C floats' bytes);
+ *   NNB_PREC_FP32_TF32  per voxel [hi(C) | lo(C)], hi = x with the 13 low
+ *                       mantissa bits cleared, lo = x - hi (2 C floats);
+ *   NNB_PREC_TF32       x rounded to TF32 (C floats).
+ * Replaces the affine pass of
+ * src/nnunet_mlx/kernels/metal_native_norm.py:62-70,155-168 (there the
+ * normalised activation is materialised in float32).
  */
 int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t voxels, float slope,
                             int32_t precision, float* out, void* stream);
+
+/*
+ * Number of activation elements nnb_prepare_operand(NNB_PREC_FP32) found at or
+ * above 65504 in magnitude (outside the fp16 range of the split operand) on
+ * the current device since the last reset; reset != 0 zeroes the counter.
+ * Synchronises with the device.  A non-zero count means results computed with
+ * NNB_PREC_FP32 since the reset must be recomputed with NNB_PREC_FP32_TF32.
+ * No reference counterpart (the reference computes in float32).
+ */
+int64_t nnb_operand_range_events(int32_t reset);
 
 /*
  * Tiles per sample of the partials nnb_conv3d writes for `args` (only the
@@ -130,9 +150,12 @@ int64_t nnb_conv3d_partial_tiles(const nnb_conv3d_args* args);
 int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision);
 
 /*
- * Build the tensor-core weight image (per N-tile, per K-step, [W_hi; W_lo]
- * stacked along N, 128-byte swizzled K-major rows) from converted-layout
- * weights.  The image must start on a 1024-byte boundary.  Replaces the
+ * Build the tensor-core weight image from converted-layout weights: per N-tile
+ * and K-step, [W_hi; W_lo] stacked along N -- NNB_PREC_FP32: fp16 rows
+ * W0 = fp16(s w), W1' = fp16(2^11 (s w - W0)) in 64-byte swizzled K-major
+ * rows, s a power of two per output column (max |s w| < 2^14), followed by
+ * the float 1/s of every column; NNB_PREC_FP32_TF32: TF32 hi/lo rows;
+ * NNB_PREC_TF32: TF32 rows (128-byte swizzled K-major rows).  The image must start on a 1024-byte boundary.  Replaces the
  * weight layout work MLX does inside `mx.conv3d` for
  * src/nnunet_mlx/model/network.py:261-269.
  */

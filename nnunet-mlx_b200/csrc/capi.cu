@@ -36,8 +36,9 @@ int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_
                              cudaStream_t stream);
 int launch_conv3d_pack_rows(const float* w, int rows, int kvol, int cin_total, int precision, int row_taps,
                             int up_cout, void* packed, cudaStream_t stream);
-int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int split, float* out,
+int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int op, float* out,
                            cudaStream_t stream);
+int64_t operand_range_events(int reset);
 int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch, int64_t voxels, float slope,
                          float* out, cudaStream_t stream);
 int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const int32_t off[3],
@@ -91,8 +92,8 @@ int32_t nnb_conv3d(const nnb_conv3d_args* a, void* stream) {
   }
   NNB_REQUIRE(a->cout >= 1 && a->weight != nullptr && a->out != nullptr, "conv3d: missing weight/output");
   const cudaStream_t st = (cudaStream_t)stream;
-  NNB_REQUIRE(a->precision == NNB_PREC_FP32 || a->precision == NNB_PREC_TF32 || a->precision == NNB_PREC_SIMT,
-              "conv3d: unknown precision %d", a->precision);
+  NNB_REQUIRE(tensor_precision(a->precision) || a->precision == NNB_PREC_SIMT, "conv3d: unknown precision %d",
+              a->precision);
   if (a->operand_format == 1) {
     NNB_REQUIRE(a->precision != NNB_PREC_SIMT && a->packed != nullptr, "conv3d: prepared operands need a packed "
                 "weight image and a tensor-core precision");
@@ -114,10 +115,11 @@ int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t vox
   int rc = check_segment(*input, "prepare_operand input");
   if (rc) return rc;
   NNB_REQUIRE(batch >= 1 && voxels >= 1, "prepare_operand: bad shape");
-  NNB_REQUIRE(precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32, "prepare_operand: precision");
-  return launch_prepare_operand(*input, batch, voxels, slope, precision == NNB_PREC_FP32 ? 1 : 0, out,
-                                (cudaStream_t)stream);
+  NNB_REQUIRE(tensor_precision(precision), "prepare_operand: precision %d has no prepared operand", precision);
+  return launch_prepare_operand(*input, batch, voxels, slope, operand_kind(precision), out, (cudaStream_t)stream);
 }
+
+int64_t nnb_operand_range_events(int32_t reset) { return operand_range_events(reset); }
 
 int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision) {
   return conv3d_tc_packed_bytes(cout, kvol, cin_total, precision);
@@ -159,8 +161,7 @@ int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int3
   if (rc) return rc;
   NNB_REQUIRE(batch >= 1 && positive3(in_dims) && positive3(kernel), "conv_transpose3d: bad shape");
   NNB_REQUIRE(weight && out && cout >= 1, "conv_transpose3d: missing weight/output");
-  if (packed != nullptr && (precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32) && input->channels % 32 == 0 &&
-      cout % 32 == 0)
+  if (packed != nullptr && tensor_precision(precision) && input->channels % 32 == 0 && cout % 32 == 0)
     return launch_conv_transpose_tc(*input, batch, in_dims, kernel, slope, bias, cout, packed, precision, out,
                                     (cudaStream_t)stream);
   return launch_conv_transpose_simt(*input, batch, in_dims, kernel, slope, weight, bias, cout, out,

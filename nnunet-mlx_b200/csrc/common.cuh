@@ -44,6 +44,19 @@ void set_error(const char* fmt, ...);
     }                                                                               \
   } while (0)
 
+// Tensor-core operand formats (see nnb_prepare_operand).
+constexpr int kOperandTf32 = 0;    // one TF32 value per element
+constexpr int kOperandTf32x2 = 1;  // TF32 hi/lo pair
+constexpr int kOperandF16x2 = 2;   // fp16 hi + 2^-11 lo' pair
+
+inline bool tensor_precision(int precision) {
+  return precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32 || precision == NNB_PREC_FP32_TF32;
+}
+
+inline int operand_kind(int precision) {
+  return precision == NNB_PREC_FP32 ? kOperandF16x2 : precision == NNB_PREC_FP32_TF32 ? kOperandTf32x2 : kOperandTf32;
+}
+
 inline int tiles_per_sample(int64_t voxels) { return (int)((voxels + kTileRows - 1) / kTileRows); }
 
 __device__ __forceinline__ float leaky(float v, float slope) { return v >= 0.f ? v : v * slope; }

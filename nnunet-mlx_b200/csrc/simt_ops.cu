@@ -2,6 +2,7 @@
 // the few-channel first layer and for shapes outside the tensor-core
 // envelope), the transposed convolution, instance-norm finalisation and the
 // residual join.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -565,57 +566,113 @@ namespace nnb {
 // Operand preparation for the tensor-core convolution: one pass over a lazy
 // activation that applies its instance-norm affine + LeakyReLU once per
 // element (instead of once per tap inside the convolution) and writes the
-// TF32 form the MMA consumes.  split != 0: per voxel [hi(C) | lo(C)] with
-// hi = x with the 13 low mantissa bits cleared and lo = x - hi (both exact);
-// split == 0: x rounded to TF32 (nearest).  HBM-bound: 4 bytes read and 8
-// (split) or 4 bytes written per element.
+// form the MMA consumes:
+//   kOperandF16x2   per voxel and 32-channel group [hi(32) | lo'(32)] as
+//                   halves, hi = fp16(x), lo' = fp16(2^11 (x - hi)); an element
+//                   with |x| >= 65504 (no finite fp16 hi) increments
+//                   g_operand_range_events.  4 bytes read, 4 written.
+//   kOperandTf32x2  per voxel [hi(C) | lo(C)], hi = x with the 13 low mantissa
+//                   bits cleared, lo = x - hi (both exact).  4 read, 8 written.
+//   kOperandTf32    x rounded to TF32 (nearest).  4 read, 4 written.
 // ---------------------------------------------------------------------------
+__device__ unsigned long long g_operand_range_events = 0;
+
 __global__ void prepare_operand_kernel(nnb_segment in, int64_t voxels_total, int64_t per_sample_vox, float slope,
-                                       int split, float* __restrict__ out) {
+                                       int op, float* __restrict__ out, unsigned long long* range_events) {
   const int C = in.channels;
-  const int c4n = C / 4;
-  const int64_t total = voxels_total * c4n;
+  const int c8n = C / 8;  // 8 channels per thread
+  const int64_t total = voxels_total * c8n;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t vox = i / c4n;
-    const int c4 = (int)(i - vox * c4n) * 4;
+    const int64_t vox = i / c8n;
+    const int c8 = (int)(i - vox * c8n) * 8;
     const int b = (int)(vox / per_sample_vox);
-    const float4 x = __ldg(reinterpret_cast<const float4*>(in.data) + i);
-    float v[4] = {x.x, x.y, x.z, x.w};
+    const float4 x0 = __ldg(reinterpret_cast<const float4*>(in.data) + 2 * i);
+    const float4 x1 = __ldg(reinterpret_cast<const float4*>(in.data) + 2 * i + 1);
+    float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = activate(v[e], in.scale, in.shift, in.leaky, slope, b * C + c4 + e);
-    if (split) {
-      float hi[4], lo[4];
+    for (int e = 0; e < 8; ++e) v[e] = activate(v[e], in.scale, in.shift, in.leaky, slope, b * C + c8 + e);
+    if (op == kOperandF16x2) {
+      uint32_t hi[4], lo[4];
+      int over = 0;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 8; e += 2) {
+        const __half h0 = __float2half_rn(v[e]), h1 = __float2half_rn(v[e + 1]);
+        const __half l0 = __float2half_rn((v[e] - __half2float(h0)) * 2048.f);
+        const __half l1 = __float2half_rn((v[e + 1] - __half2float(h1)) * 2048.f);
+        hi[e / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        lo[e / 2] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        over += (fabsf(v[e]) >= 65504.f) + (fabsf(v[e + 1]) >= 65504.f);
+      }
+      if (over) atomicAdd(range_events, (unsigned long long)over);
+      // group g = c8 / 32 occupies halves [64 g, 64 g + 64) of the voxel's 2 C
+      __half* base = reinterpret_cast<__half*>(out) + vox * 2 * C + (c8 / 32) * 64 + (c8 % 32);
+      *reinterpret_cast<uint4*>(base) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(base + 32) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    } else if (op == kOperandTf32x2) {
+      float hi[8], lo[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
         hi[e] = __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u);
         lo[e] = v[e] - hi[e];
       }
-      float* dst = out + vox * 2 * C + c4;
-      *reinterpret_cast<float4*>(dst) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<float4*>(dst + C) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+      float* dst = out + vox * 2 * C + c8;
+      reinterpret_cast<float4*>(dst)[0] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(hi[4], hi[5], hi[6], hi[7]);
+      reinterpret_cast<float4*>(dst + C)[0] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+      reinterpret_cast<float4*>(dst + C)[1] = make_float4(lo[4], lo[5], lo[6], lo[7]);
     } else {
-      float r[4];
+      float r[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 8; ++e) {
         uint32_t t;
         asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(t) : "f"(v[e]));
         r[e] = __uint_as_float(t);
       }
-      *reinterpret_cast<float4*>(out + vox * C + c4) = make_float4(r[0], r[1], r[2], r[3]);
+      float* dst = out + vox * C + c8;
+      reinterpret_cast<float4*>(dst)[0] = make_float4(r[0], r[1], r[2], r[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(r[4], r[5], r[6], r[7]);
     }
   }
 }
 
-int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int split, float* out,
+static unsigned long long* range_events_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_operand_range_events) != cudaSuccess) return nullptr;
+  return static_cast<unsigned long long*>(p);
+}
+
+int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int op, float* out,
                            cudaStream_t stream) {
-  NNB_REQUIRE(in.channels % 4 == 0, "prepare_operand: channels must be a multiple of 4");
+  NNB_REQUIRE(in.channels % (op == kOperandF16x2 ? 32 : 8) == 0,
+              "prepare_operand: channels must be a multiple of %d", op == kOperandF16x2 ? 32 : 8);
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(in.data) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
               "prepare_operand: 16-byte aligned tensors required");
-  const int64_t total = (int64_t)batch * voxels * (in.channels / 4);
+  unsigned long long* events = range_events_ptr();
+  NNB_REQUIRE(events != nullptr, "prepare_operand: range-event counter unavailable: %s",
+              cudaGetErrorString(cudaGetLastError()));
+  const int64_t total = (int64_t)batch * voxels * (in.channels / 8);
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
-  prepare_operand_kernel<<<blocks, 256, 0, stream>>>(in, (int64_t)batch * voxels, voxels, slope, split, out);
+  prepare_operand_kernel<<<blocks, 256, 0, stream>>>(in, (int64_t)batch * voxels, voxels, slope, op, out, events);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
+}
+
+int64_t operand_range_events(int reset) {
+  unsigned long long count = 0;
+  // every stream's preparation kernels, not only those ordered with the legacy default stream
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(&count, g_operand_range_events, sizeof(count)) != cudaSuccess) {
+    set_error("operand_range_events: %s", cudaGetErrorString(cudaGetLastError()));
+    return NNB_E_CUDA;
+  }
+  if (reset) {
+    const unsigned long long zero = 0;
+    if (cudaMemcpyToSymbol(g_operand_range_events, &zero, sizeof(zero)) != cudaSuccess) {
+      set_error("operand_range_events: %s", cudaGetErrorString(cudaGetLastError()));
+      return NNB_E_CUDA;
+    }
+  }
+  return count > (unsigned long long)INT64_MAX ? INT64_MAX : (int64_t)count;
 }
 
 }  // namespace nnb

@@ -147,9 +147,26 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t sbo = 10
   return d;
 }
 
+// K-major, 64-byte swizzle: 64-byte rows, 8-row groups of 512 bytes (16-byte
+// chunk c of row r stored at chunk c ^ ((r >> 1) & 3)), descriptor version 1.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;  // SWIZZLE_64B
+  return d;
+}
+
 // Instruction descriptor: D=f32, A=B=tf32, K-major both, N>>3, M>>4.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor: D=f32, A=B=f16, K-major both, N>>3, M>>4.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,

@@ -1,18 +1,27 @@
 // Tensor-core (tcgen05 / TMEM / TMA) implicit-GEMM 3-D convolution for sm_100a.
 //
 // GEMM view: M = output voxels of one sample, N = output channels, K = taps x
-// input channels, walked in steps of 32 channels (128 bytes of float32).
-// Operands are prepared once per activation by nnb_prepare_operand (the
-// producing layer's instance-norm affine + LeakyReLU applied, split into TF32
-// hi/lo halves), so no thread touches activations in the main loop.
+// input channels, walked in steps of 32 channels.  Operands are prepared once
+// per activation by nnb_prepare_operand (the producing layer's instance-norm
+// affine + LeakyReLU applied, converted to the MMA's operand format), so no
+// thread touches activations in the main loop.  Operand formats (template OP):
 //
-// Weights: B stacks [W_hi ; W_lo] along N (N = 2 x the tile's output
-// channels), so per 8-channel sub-step two MMAs, A_hi x [W_hi;W_lo] and
-// A_lo x [W_hi;W_lo], form every hi/lo product in the two halves of the
-// accumulator; the epilogue adds the halves (float32-level accuracy).  A
-// tcgen05.mma costs at least ~46 cycles at M = 128 whatever N is, so stacking
-// halves the instruction count of the 32- and 64-channel layers.  Single-pass
-// TF32 mode uses B = W_tf32 and one MMA per sub-step.
+//  * kOperandF16x2 (float32-level accuracy, the default): per 32 channels one
+//    128-byte row [hi(32) | lo'(32)] of halves, x ~ hi + 2^-11 lo'.  B stacks
+//    [W0 ; W1'] along N (W0 = fp16(s w), W1' = fp16(2^11 (s w - W0)), s a
+//    power of two per output column), so per 16-channel sub-step
+//    A_hi x [W0;W1'] (N = 2 BC) and A_lo' x W0 (N = BC, into the second half)
+//    form the three leading products in two MMAs of kind::f16; the epilogue
+//    returns (D0 + 2^-11 D1) / s.
+//  * kOperandTf32x2 (split TF32, any float32 magnitude): A hi and lo rows of 32
+//    TF32 values, B = [W_hi ; W_lo]; per 8-channel sub-step A_hi x [W_hi;W_lo]
+//    and A_lo x [W_hi;W_lo]; the epilogue adds the halves.
+//  * kOperandTf32 (fast): one TF32 row, B = W_tf32, one MMA per sub-step.
+//
+// A tcgen05.mma costs at least ~46 cycles at M = 128 whatever N is (up to 64),
+// so stacking the split weights along N halves the instruction count of the
+// 32- and 64-channel layers, and fp16's 16-channel K per instruction halves it
+// again relative to TF32.
 //
 // Two ways to feed A, both from tiled TMA box loads (5-D map (channels, W, H,
 // D, batch), 128-byte swizzle, zero fill outside the volume = the padding):
@@ -49,6 +58,7 @@
 // copies and MMAs in flight, frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -93,13 +103,15 @@ struct OperandMaps {
   CUtensorMap seg[2];
 };
 
-template <int BC, bool SPLIT>
+template <int BC, int OP>
 struct Cfg {
-  static constexpr int kHalves = SPLIT ? 2 : 1;
-  static constexpr int N = SPLIT ? 2 * BC : BC;  // MMA N: stacked [W_hi; W_lo] rows
+  static constexpr bool kSplit = OP != kOperandTf32;
+  static constexpr int kHalves = OP == kOperandTf32x2 ? 2 : 1;  // A boxes (128-byte rows) per K-step
+  static constexpr int N = kSplit ? 2 * BC : BC;                // accumulator columns: stacked [W_hi; W_lo] rows
+  static constexpr int kBRow = OP == kOperandF16x2 ? 64 : 128;  // bytes of one B row (32 channels)
   static constexpr int kAccBufs = (2 * N <= kTmemCols) ? 2 : 1;
   static constexpr int kABytes = kHalves * BM * 128;
-  static constexpr int kBBytes = N * 128;
+  static constexpr int kBBytes = N * kBRow;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kS0 = kStageBudget / kStageBytes;
   static constexpr int S = kS0 > 8 ? 8 : kS0;
@@ -125,6 +137,45 @@ __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// B-tile descriptor of the operand format (64-byte rows for the fp16 pair).
+template <int OP>
+__device__ __forceinline__ uint64_t b_desc_at(uint32_t saddr) {
+  if constexpr (OP == kOperandF16x2) return sw64_desc(saddr);
+  else return sw128_desc(saddr);
+}
+
+// The MMAs of one K-step (32 input channels) into accumulator d.  ad: A rows
+// (hi part), bd: B tile, lo16: offset of the TF32 lo rows (kOperandTf32x2),
+// acc: 0 for the first K-step of a tile.  Descriptor offsets are in 16-byte
+// units: the fp16 lo' half of an A row starts 64 bytes in.
+template <int BC, int OP>
+__device__ __forceinline__ void kstep_mmas(uint32_t d, uint64_t ad, uint64_t bd, uint32_t lo16, uint32_t acc) {
+  if constexpr (OP == kOperandF16x2) {
+    constexpr uint32_t id2 = idesc_f16(BM, 2 * BC), id1 = idesc_f16(BM, BC);
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      mma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, id2, (acc | kk) ? 1u : 0u);
+      mma_f16_ss(d + BC, ad + 4 + 2 * kk, bd + 2 * kk, id1, 1u);
+    }
+  } else {
+    constexpr uint32_t id = idesc_tf32(BM, Cfg<BC, OP>::N);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      mma_tf32_ss(d, ad + 2 * kk, bd + 2 * kk, id, (acc | kk) ? 1u : 0u);
+      if constexpr (OP == kOperandTf32x2) mma_tf32_ss(d, ad + lo16 + 2 * kk, bd + 2 * kk, id, 1u);
+    }
+  }
+}
+
 struct TileOrigin {
   int b, nt, t, d0, h0, w0;
 };
@@ -145,19 +196,21 @@ __device__ __forceinline__ TileOrigin tile_origin(const Geometry& g, int tile) {
   return o;
 }
 
-// Channel chunk -> (tensor map, channel coordinate of hi, of lo) for the two segments.
+// Channel chunk -> (tensor map, element coordinate of the hi box, of the lo box) for the two segments.
 struct ChunkSource {
   const CUtensorMap* map;
   int c_hi, c_lo;
 };
 
+template <int OP>
 __device__ __forceinline__ ChunkSource chunk_source(const nnb_conv3d_args& a, const Geometry& g,
                                                     const OperandMaps& maps, int chunk) {
   const int cg = chunk * BK;
   const bool second = cg >= g.c0len;
   const int cl = second ? cg - g.c0len : cg;
   const int cs = second ? a.seg[1].channels : g.c0len;
-  return ChunkSource{&maps.seg[second ? 1 : 0], cl, cs + cl};
+  if constexpr (OP == kOperandF16x2) return ChunkSource{&maps.seg[second ? 1 : 0], 2 * cl, 0};  // [hi | lo'] halves
+  else return ChunkSource{&maps.seg[second ? 1 : 0], cl, cs + cl};
 }
 
 struct SharedMisc {
@@ -181,9 +234,10 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
 }
 
 // One finished accumulator -> outputs + partials (or the transposed-conv scatter).
-template <int BC, bool SPLIT>
+template <int BC, int OP>
 __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Geometry& g, const TileOrigin& o,
-                                              uint32_t acc, int q, int lane, float* red, float* col_mean) {
+                                              uint32_t acc, int q, int lane, float* red, float* col_mean,
+                                              const float* __restrict__ col_inv) {
   const int row = q * 32 + lane;
   const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
   const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
@@ -197,7 +251,13 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
     if (nbase >= a.cout) break;  // uniform across the epilogue warps
     float v[32];
     tmem_ld32(acc + cc * 32, v);
-    if constexpr (SPLIT) {
+    if constexpr (OP == kOperandF16x2) {
+      // (sum a0 W0 + 2^-11 sum (a0 W1' + a1' W0)) / s of the column
+      float u[32];
+      tmem_ld32(acc + BC + cc * 32, u);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaf(u[i], 1.f / 2048.f, v[i]) * __ldg(col_inv + nbase + i);
+    } else if constexpr (OP == kOperandTf32x2) {
       float u[32];
       tmem_ld32(acc + BC + cc * 32, u);
 #pragma unroll
@@ -270,11 +330,14 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
 }
 
 // Epilogue warps' loop over this CTA's tiles (accumulator full/empty handshake).
-template <int BC, bool SPLIT>
+template <int BC, int OP>
 __device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Geometry& g, int my_tiles,
                                               uint32_t tmem, const SharedMisc& sm, uint64_t* accf, uint64_t* acce,
                                               int warp, int lane) {
-  using C = Cfg<BC, SPLIT>;
+  using C = Cfg<BC, OP>;
+  // fp16-pair images end with the per-column 1/s after the B tiles
+  const float* col_inv = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.packed) +
+                                                        (int64_t)g.n_tiles * g.ksteps * C::kBBytes);
   constexpr int NB = C::kAccBufs;
   const int q = warp & 3;  // warps 2..5 own TMEM lane quarters 2, 3, 0, 1
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
@@ -289,7 +352,7 @@ __device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Ge
     if (stop) break;
     fence_after();
     const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
-    epilogue_tile<BC, SPLIT>(a, g, o, tmem + ab * C::N + lane_base, q, lane, sm.red, sm.col_mean);
+    epilogue_tile<BC, OP>(a, g, o, tmem + ab * C::N + lane_base, q, lane, sm.red, sm.col_mean, col_inv);
     fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&acce[ab]));
@@ -311,10 +374,10 @@ __device__ __forceinline__ void tmem_free_all(uint32_t tmem) {
 // ---------------------------------------------------------------------------
 // Box mode: one TMA box per half and one B tile per K-step (tap x 32 channels).
 // ---------------------------------------------------------------------------
-template <int BC, bool SPLIT>
+template <int BC, int OP>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_tc_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
-  using C = Cfg<BC, SPLIT>;
+  using C = Cfg<BC, OP>;
   constexpr int S = C::S;
   constexpr int NB = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -376,13 +439,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const int e = kstab[ks];
-          const ChunkSource src = chunk_source(a, g, maps, e >> 12);
+          const ChunkSource src = chunk_source<OP>(a, g, maps, e >> 12);
           const int w = wb + (e & 15), h = hb + ((e >> 4) & 15), d = db + ((e >> 8) & 15);
           const uint32_t fb = smem_u32(&full[s]);
           const uint32_t st = smem_u32(stages + s * C::kStageBytes);
           mbar_arrive_expect_tx(fb, tx);
           tma_load_5d(st, src.map, src.c_hi, w, h, d, o.b, fb);
-          if constexpr (SPLIT) tma_load_5d(st + BM * 128, src.map, src.c_lo, w, h, d, o.b, fb);
+          if constexpr (C::kHalves == 2) tma_load_5d(st + BM * 128, src.map, src.c_lo, w, h, d, o.b, fb);
           bulk_g2s(st + C::kABytes, bsrc + (int64_t)ks * C::kBBytes, C::kBBytes, fb);
           issued = G + 1;
         }
@@ -397,11 +460,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer -------------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM, C::N);
       // Descriptors are stage-0 bases plus constant offsets (start address in 16-byte units), so the
       // 4-8 MMAs of a K-step issue back to back with only adds between them.
       const uint64_t desc0 = sw128_desc(smem_u32(stages));
-      constexpr uint32_t kLo = (BM * 128) >> 4, kB = C::kABytes >> 4, kStage = C::kStageBytes >> 4;
+      const uint64_t bdesc0 = b_desc_at<OP>(smem_u32(stages) + C::kABytes);
+      constexpr uint32_t kLo = (BM * 128) >> 4, kStage = C::kStageBytes >> 4;
       bool alive = true;
       int s = 0;
       uint32_t phase = 0;
@@ -414,16 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem + ab * C::N;
         for (int ks = 0; ks < g.ksteps; ++ks) {
           const uint64_t ad = desc0 + (uint64_t)(s * kStage);
+          const uint64_t bd = bdesc0 + (uint64_t)(s * kStage);
           if (!mbar_wait(smem_u32(&full[s]), phase, sm.abort_flag, 11)) {
             alive = false;
             break;
           }
           fence_after();
-#pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            mma_tf32_ss(d, ad + 2 * kk, ad + kB + 2 * kk, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-            if constexpr (SPLIT) mma_tf32_ss(d, ad + kLo + 2 * kk, ad + kB + 2 * kk, idesc, 1u);
-          }
+          kstep_mmas<BC, OP>(d, ad, bd, kLo, ks > 0 ? 1u : 0u);
           mma_commit(smem_u32(&empty[s]));
           if (++s == S) {
             s = 0;
@@ -440,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    epilogue_role<BC, SPLIT>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
+    epilogue_role<BC, OP>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
   }
   __syncthreads();
   if (warp == 1) tmem_free_all(tmem);
@@ -450,10 +510,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Halo mode: one TMA box per (chunk, kz plane, half) feeds every (kx, ky) tap.
 // ---------------------------------------------------------------------------
 // TB = taps per B stage: 3 (a whole kx row of a 3-wide kernel, fully unrolled) or 1 (any kernel).
-template <int BC, bool SPLIT, int TB>
+template <int BC, int OP, int TB>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3d_halo_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
-  using C = Cfg<BC, SPLIT>;
+  using C = Cfg<BC, OP>;
   constexpr int NB = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -511,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int wb = o.w0 - g.PW, hb = o.h0 - g.PH, db = o.d0 - g.PD;
         const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(a.packed) + (int64_t)o.nt * g.ksteps * C::kBBytes;
         for (int c = 0; c < g.nchunk && alive; ++c) {
-          const ChunkSource src = chunk_source(a, g, maps, c);
+          const ChunkSource src = chunk_source<OP>(a, g, maps, c);
           for (int kz = 0; kz < g.KD && alive; ++kz) {
             const int sa = P % SA;
             if (P >= SA && !mbar_wait(smem_u32(&a_empty[sa]), ((P / SA) - 1) & 1, sm.abort_flag, 22)) {
@@ -522,7 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t dst = smem_u32(a_ring + sa * a_stage);
             mbar_arrive_expect_tx(fa, tx_a);
             tma_load_5d(dst, src.map, src.c_hi, wb, hb, db + kz, o.b, fa);
-            if constexpr (SPLIT) tma_load_5d(dst + g.plane_bytes, src.map, src.c_lo, wb, hb, db + kz, o.b, fa);
+            if constexpr (C::kHalves == 2)
+              tma_load_5d(dst + g.plane_bytes, src.map, src.c_lo, wb, hb, db + kz, o.b, fa);
             ++P;
             for (int t2 = 0; t2 < taps2d; t2 += g.tb) {
               const int sb = T % SB;
@@ -551,11 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer -------------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM, C::N);
       // Stage-0 descriptor bases plus constant offsets (16-byte units): A planes with 8-row groups
-      // pw rows apart, B tiles with the usual 1024-byte groups.
+      // pw rows apart, B tiles with the format's usual groups.
       const uint64_t adesc0 = sw128_desc(smem_u32(a_ring), (uint32_t)g.pw * 128);
-      const uint64_t bdesc0 = sw128_desc(smem_u32(b_ring));
+      const uint64_t bdesc0 = b_desc_at<OP>(smem_u32(b_ring));
       const uint32_t a_stage16 = (uint32_t)a_stage >> 4, lo16 = (uint32_t)g.plane_bytes >> 4;
       const uint32_t b_stage16 = b_stage >> 4;
       constexpr uint32_t kB16 = C::kBBytes >> 4;
@@ -590,15 +650,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fence_after();
 #pragma unroll
-                for (int j = 0; j < TB; ++j) {
-#pragma unroll
-                  for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint64_t ad = arow + (uint64_t)(8 * j + 2 * kk);
-                    const uint64_t bd = bstage_desc + (uint64_t)(j * kB16 + 2 * kk);
-                    mma_tf32_ss(d, ad, bd, idesc, (accumulate | j | kk) ? 1u : 0u);
-                    if constexpr (SPLIT) mma_tf32_ss(d, ad + lo16, bd, idesc, 1u);
-                  }
-                }
+                for (int j = 0; j < TB; ++j)
+                  kstep_mmas<BC, OP>(d, arow + (uint64_t)(8 * j), bstage_desc + (uint64_t)(j * kB16), lo16,
+                                     accumulate | (uint32_t)j);
                 accumulate = 1;
                 mma_commit(smem_u32(&b_empty[sb]));
                 if (++sb == SB) {
@@ -628,11 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 } else {
                   aoff += 8;
                 }
-#pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                  mma_tf32_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (accumulate | kk) ? 1u : 0u);
-                  if constexpr (SPLIT) mma_tf32_ss(d, ad + lo16 + 2 * kk, bd + 2 * kk, idesc, 1u);
-                }
+                kstep_mmas<BC, OP>(d, ad, bd, lo16, accumulate);
                 accumulate = 1;
                 bd += kB16;
               }
@@ -659,20 +709,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    epilogue_role<BC, SPLIT>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
+    epilogue_role<BC, OP>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
   }
   __syncthreads();
   if (warp == 1) tmem_free_all(tmem);
 }
 
 // ---------------------------------------------------------------------------
-// Weight image: [n_tile][kstep = chunk * taps + tap][N rows][128 B] (so the taps
-// of one 32-channel chunk are contiguous), natural K order within the 32-channel
-// step, 16-byte chunks XOR-swizzled by row % 8 (the SW128 K-major layout).  Rows [0, BC) hold W_hi of the tile's BC GEMM columns and rows
-// [BC, 2 BC) W_lo (float32 mode), or BC rows of TF32.  GEMM column n is output
-// channel n, or for a transposed convolution (row_taps > 1) the pair
-// (tap = n / up_cout, channel = n % up_cout) reading weight (channel, tap, ci).
+// Weight image: [n_tile][kstep = chunk * taps + tap][N rows][row bytes] (so
+// the taps of one 32-channel chunk are contiguous), natural K order within the
+// 32-channel step.  GEMM column n is output channel n, or for a transposed
+// convolution (row_taps > 1) the pair (tap = n / up_cout, channel = n % up_cout)
+// reading weight (channel, tap, ci).
+//   TF32 formats: 128-byte rows, 16-byte chunks XOR-swizzled by row % 8 (the
+//   SW128 K-major layout); rows [0, BC) W_hi of the tile's BC columns and rows
+//   [BC, 2 BC) W_lo (kOperandTf32x2), or BC rows of TF32.
+//   kOperandF16x2: 64-byte rows of halves, 16-byte chunks XOR-swizzled by
+//   (row / 2) % 4 (the SW64 K-major layout); rows [0, BC) W0 = fp16(s w), rows
+//   [BC, 2 BC) W1' = fp16(2^11 (s w - W0)); after the tiles, 1/s of every
+//   column (n_tiles * BC floats).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float weight_at(const float* __restrict__ w, int col, int tap, int ci, int kvol,
+                                           int cin_total, int row_taps, int up_cout) {
+  if (row_taps > 1) {
+    const int co = col % up_cout, utap = col / up_cout;
+    return w[((int64_t)co * row_taps + utap) * cin_total + ci];
+  }
+  return w[((int64_t)col * kvol + tap) * cin_total + ci];
+}
+
 __global__ void pack_kernel(const float* __restrict__ w, int cols_total, int kvol, int cin_total, int bc,
                             int halves, int nchunk, int row_taps, int up_cout, int64_t total_words,
                             uint32_t* __restrict__ out) {
@@ -691,14 +756,7 @@ __global__ void pack_kernel(const float* __restrict__ w, int cols_total, int kvo
     const int chunk = ks / kvol, tap = ks - chunk * kvol;  // chunk-major K-step order
     const int ci = chunk * BK + k;
     float val = 0.f;
-    if (col < cols_total && ci < cin_total) {
-      if (row_taps > 1) {
-        const int co = col % up_cout, utap = col / up_cout;
-        val = w[((int64_t)co * row_taps + utap) * cin_total + ci];
-      } else {
-        val = w[((int64_t)col * kvol + tap) * cin_total + ci];
-      }
-    }
+    if (col < cols_total && ci < cin_total) val = weight_at(w, col, tap, ci, kvol, cin_total, row_taps, up_cout);
     uint32_t res;
     if (halves == 2) {
       const uint32_t hi = __float_as_uint(val) & 0xFFFFE000u;
@@ -708,6 +766,73 @@ __global__ void pack_kernel(const float* __restrict__ w, int cols_total, int kvo
     }
     out[o] = res;
   }
+}
+
+// 1/s per GEMM column for the fp16-pair image: s = 2^(14 - e) with max |w| =
+// f 2^e, f in [0.5, 1), so max |s w| < 2^14 (W0 stays far from fp16 overflow
+// and small weights stay normal); all-zero or padding columns get s = 1.
+__global__ void column_scale_kernel(const float* __restrict__ w, int cols_total, int kvol, int cin_total,
+                                    int row_taps, int up_cout, float* __restrict__ inv_scale) {
+  const int col = blockIdx.x;
+  float m = 0.f;
+  if (col < cols_total) {
+    const int64_t K = (int64_t)kvol * cin_total;
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+      const int tap = (int)(k / cin_total), ci = (int)(k - (int64_t)tap * cin_total);
+      m = fmaxf(m, fabsf(weight_at(w, col, tap, ci, kvol, cin_total, row_taps, up_cout)));
+    }
+  }
+  __shared__ float part[32];
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, part[i]);
+    float inv = 1.f;
+    if (m > 0.f && isfinite(m)) {
+      int e = 0;
+      frexpf(m, &e);
+      inv = ldexpf(1.f, max(-100, min(100, e - 14)));
+    }
+    inv_scale[col] = inv;
+  }
+}
+
+__global__ void pack_f16x2_kernel(const float* __restrict__ w, int cols_total, int kvol, int cin_total, int bc,
+                                  int nchunk, int row_taps, int up_cout, int64_t total_words,
+                                  const float* __restrict__ inv_scale, uint32_t* __restrict__ out) {
+  const int nrows = 2 * bc;
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total_words;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int word = (int)(o % 16);  // 4-byte word (two halves) within the 64-byte row (physical position)
+    int64_t r = o / 16;
+    const int n = (int)(r % nrows);
+    r /= nrows;
+    const int ks = (int)(r % ((int64_t)kvol * nchunk));
+    const int nt = (int)(r / ((int64_t)kvol * nchunk));
+    const int k = (((word >> 2) ^ ((n >> 1) & 3)) * 4 + (word & 3)) * 2;  // first of the word's two channels
+    const int half = n / bc;
+    const int col = nt * bc + (n - half * bc);
+    const int chunk = ks / kvol, tap = ks - chunk * kvol;
+    const float s = 1.f / __ldg(inv_scale + nt * bc + (n - half * bc));  // exact: a power of two
+    uint32_t res = 0;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int ci = chunk * BK + k + e;
+      float val = 0.f;
+      if (col < cols_total && ci < cin_total) val = weight_at(w, col, tap, ci, kvol, cin_total, row_taps, up_cout) * s;
+      const __half h0 = __float2half_rn(val);
+      const __half h = half == 0 ? h0 : __float2half_rn((val - __half2float(h0)) * 2048.f);
+      res |= (uint32_t)__half_as_ushort(h) << (16 * e);
+    }
+    out[o] = res;
+  }
+}
+
+// Bytes of one B tile (one K-step of BC columns) in the operand format.
+inline int b_tile_bytes(int op, int bc) {
+  return op == kOperandF16x2 ? 2 * bc * 64 : op == kOperandTf32x2 ? 2 * bc * 128 : bc * 128;
 }
 
 inline int pick_bc(int cols) {
@@ -740,7 +865,8 @@ inline void choose_brick(const int od, const int oh, const int ow, const int sd,
 
 // Halo mode when the layer is a unit-stride multi-tap conv over at least one
 // 8-wide brick row, <= 64 output channels per tile, and two A planes plus four
-// B tiles fit the shared-memory budget.
+// B tiles fit the shared-memory budget.  halves: A boxes per chunk; bbytes:
+// bytes of one B tile.
 inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bbytes) {
   if (g.SD != 1 || g.SH != 1 || g.SW != 1) return false;
   if (g.KD * g.KH * g.KW < 2 || g.OW < kHaloW || g.OH < kHaloH / 2) return false;
@@ -802,8 +928,8 @@ inline Geometry make_geometry(const nnb_conv3d_args& a) {
   const int bc = pick_bc(a.cout);
   g.n_tiles = (a.cout + bc - 1) / bc;
   g.up_cout = 0;
-  const int halves = a.precision == NNB_PREC_FP32 ? 2 : 1;
-  g.halo = plan_halo(a, g, halves, halves * bc * 128) ? 1 : 0;
+  const int op = operand_kind(a.precision);
+  g.halo = plan_halo(a, g, op == kOperandTf32x2 ? 2 : 1, b_tile_bytes(op, bc)) ? 1 : 0;
   if (!g.halo) {
     choose_brick(g.OD, g.OH, g.OW, g.SD, g.SH, g.SW, g.tw, g.th, g.td);
     g.box[0] = g.tw * g.SW;
@@ -833,41 +959,46 @@ inline EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// 5-D map (halves x channels, W, H, D, batch) of one prepared operand; the box
-// is 32 channels x the mode's box extent, sampled every stride voxels.
-inline int encode_operand(const nnb_segment& seg, int halves, int batch, const Geometry& g, CUtensorMap* map) {
+// 5-D map (elements per voxel, W, H, D, batch) of one prepared operand; the box
+// is one 128-byte row (32 floats, or 64 halves = [hi | lo'] of 32 channels) x
+// the mode's box extent, sampled every stride voxels.
+inline int encode_operand(const nnb_segment& seg, int op, int batch, const Geometry& g, CUtensorMap* map) {
   const EncodeTiledFn fn = encode_tiled();
   NNB_REQUIRE(fn != nullptr, "conv3d: cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t inner = (cuuint64_t)halves * seg.channels;
+  const bool f16 = op == kOperandF16x2;
+  const cuuint64_t inner = (cuuint64_t)(op == kOperandTf32 ? 1 : 2) * seg.channels;
+  const cuuint64_t esize = f16 ? 2 : 4;
   const cuuint64_t dims[5] = {inner, (cuuint64_t)g.IW, (cuuint64_t)g.IH, (cuuint64_t)g.ID, (cuuint64_t)batch};
-  const cuuint64_t row = inner * sizeof(float);
+  const cuuint64_t row = inner * esize;
   const cuuint64_t strides[4] = {row, row * g.IW, row * g.IW * g.IH, row * g.IW * g.IH * g.ID};
-  const cuuint32_t box[5] = {(cuuint32_t)BK, (cuuint32_t)g.box[0], (cuuint32_t)g.box[1], (cuuint32_t)g.box[2], 1u};
+  const cuuint32_t box[5] = {(cuuint32_t)(128 / esize), (cuuint32_t)g.box[0], (cuuint32_t)g.box[1],
+                             (cuuint32_t)g.box[2], 1u};
   const cuuint32_t estr[5] = {1u, (cuuint32_t)(g.halo ? 1 : g.SW), (cuuint32_t)(g.halo ? 1 : g.SH),
                               (cuuint32_t)(g.halo ? 1 : g.SD), 1u};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(seg.data), dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5,
+                        const_cast<float*>(seg.data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   NNB_REQUIRE(r == CUDA_SUCCESS, "conv3d: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return NNB_OK;
 }
 
-template <int BC, bool SPLIT>
+template <int BC, int OP>
 int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& maps, cudaStream_t stream) {
-  using C = Cfg<BC, SPLIT>;
+  using C = Cfg<BC, OP>;
   int dev = 0;
   NNB_CUDA_CHECK(cudaGetDevice(&dev));
   static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, 1/2 halo TB 1/3), per device
   const int bit = g.halo ? (g.tb == 3 ? 4 : 2) : 1;
   if (dev >= 64 || !(configured[dev] & bit)) {
     if (g.halo && g.tb == 3)
-      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, SPLIT, 3>,
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, OP, 3>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     else if (g.halo)
-      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, SPLIT, 1>,
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, OP, 1>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     else
-      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_tc_kernel<BC, SPLIT>,
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_tc_kernel<BC, OP>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     if (dev < 64) configured[dev] |= bit;
   }
@@ -878,12 +1009,12 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
     const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * g.tb * C::kBBytes + kMiscBytes;
     NNB_REQUIRE(smem <= kMaxSmem, "conv3d: halo plan exceeds shared memory (%d bytes)", smem);
     if (g.tb == 3)
-      conv3d_halo_kernel<BC, SPLIT, 3><<<grid, kThreads, smem, stream>>>(a, g, maps);
+      conv3d_halo_kernel<BC, OP, 3><<<grid, kThreads, smem, stream>>>(a, g, maps);
     else
-      conv3d_halo_kernel<BC, SPLIT, 1><<<grid, kThreads, smem, stream>>>(a, g, maps);
+      conv3d_halo_kernel<BC, OP, 1><<<grid, kThreads, smem, stream>>>(a, g, maps);
   } else {
     const int smem = 1024 + C::S * C::kStageBytes + kMiscBytes + 4 * kMaxKsteps;
-    conv3d_tc_kernel<BC, SPLIT><<<grid, kThreads, smem, stream>>>(a, g, maps);
+    conv3d_tc_kernel<BC, OP><<<grid, kThreads, smem, stream>>>(a, g, maps);
   }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
@@ -894,29 +1025,32 @@ int dispatch(const nnb_conv3d_args& a, Geometry& g, cudaStream_t stream) {
   NNB_REQUIRE(tiles < (1LL << 31), "conv3d: too many tiles");
   g.total_tiles = (int)tiles;
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(a.packed) & 1023) == 0, "conv3d: packed weights must be 1024-aligned");
-  const bool split = a.precision == NNB_PREC_FP32;
-  const int halves = split ? 2 : 1;
+  const int op = operand_kind(a.precision);
   OperandMaps maps;
   for (int s = 0; s < a.num_segments; ++s) {
-    const int rc = encode_operand(a.seg[s], halves, a.batch, g, &maps.seg[s]);
+    const int rc = encode_operand(a.seg[s], op, a.batch, g, &maps.seg[s]);
     if (rc) return rc;
   }
   if (a.num_segments == 1) maps.seg[1] = maps.seg[0];
-  switch (pick_bc(a.cout)) {
-    case 32:
-      return split ? launch_bc<32, true>(a, g, maps, stream) : launch_bc<32, false>(a, g, maps, stream);
-    case 64:
-      return split ? launch_bc<64, true>(a, g, maps, stream) : launch_bc<64, false>(a, g, maps, stream);
-    default:
-      NNB_REQUIRE(!g.halo, "conv3d: internal: halo plan for a 128-column tile");
-      return split ? launch_bc<128, true>(a, g, maps, stream) : launch_bc<128, false>(a, g, maps, stream);
+  const int bc = pick_bc(a.cout);
+  NNB_REQUIRE(bc <= 64 || !g.halo, "conv3d: internal: halo plan for a 128-column tile");
+  switch (op * 4 + (bc == 32 ? 0 : bc == 64 ? 1 : 2)) {
+    case kOperandF16x2 * 4 + 0: return launch_bc<32, kOperandF16x2>(a, g, maps, stream);
+    case kOperandF16x2 * 4 + 1: return launch_bc<64, kOperandF16x2>(a, g, maps, stream);
+    case kOperandF16x2 * 4 + 2: return launch_bc<128, kOperandF16x2>(a, g, maps, stream);
+    case kOperandTf32x2 * 4 + 0: return launch_bc<32, kOperandTf32x2>(a, g, maps, stream);
+    case kOperandTf32x2 * 4 + 1: return launch_bc<64, kOperandTf32x2>(a, g, maps, stream);
+    case kOperandTf32x2 * 4 + 2: return launch_bc<128, kOperandTf32x2>(a, g, maps, stream);
+    case kOperandTf32 * 4 + 0: return launch_bc<32, kOperandTf32>(a, g, maps, stream);
+    case kOperandTf32 * 4 + 1: return launch_bc<64, kOperandTf32>(a, g, maps, stream);
+    default: return launch_bc<128, kOperandTf32>(a, g, maps, stream);
   }
 }
 
 }  // namespace tc
 
 bool conv3d_tc_supported(const nnb_conv3d_args& a) {
-  if (a.precision != NNB_PREC_FP32 && a.precision != NNB_PREC_TF32) return false;
+  if (!tensor_precision(a.precision)) return false;
   int cin_total = 0;
   for (int s = 0; s < a.num_segments; ++s) {
     if (a.seg[s].channels % tc::BK != 0) return false;
@@ -933,26 +1067,38 @@ bool conv3d_tc_supported(const nnb_conv3d_args& a) {
 
 int64_t conv3d_tc_packed_bytes(int cols, int kvol, int cin_total, int precision) {
   if (cols < 1 || kvol < 1 || cin_total < 1 || cin_total % tc::BK != 0) return 0;
-  if (precision != NNB_PREC_FP32 && precision != NNB_PREC_TF32) return 0;
+  if (!tensor_precision(precision)) return 0;
+  const int op = operand_kind(precision);
   const int bc = tc::pick_bc(cols);
   const int n_tiles = (cols + bc - 1) / bc;
-  const int halves = precision == NNB_PREC_FP32 ? 2 : 1;
-  return (int64_t)n_tiles * kvol * (cin_total / tc::BK) * halves * bc * 128;
+  const int64_t tiles = (int64_t)n_tiles * kvol * (cin_total / tc::BK) * tc::b_tile_bytes(op, bc);
+  return tiles + (op == kOperandF16x2 ? (int64_t)n_tiles * bc * (int64_t)sizeof(float) : 0);
 }
 
 int launch_conv3d_pack_rows(const float* w, int cols, int kvol, int cin_total, int precision, int row_taps,
                             int up_cout, void* packed, cudaStream_t stream) {
   NNB_REQUIRE(cin_total % tc::BK == 0, "pack: input channels must be a multiple of %d", tc::BK);
-  NNB_REQUIRE(precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32, "pack: precision");
+  NNB_REQUIRE(tensor_precision(precision), "pack: precision %d has no weight image", precision);
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(packed) & 1023) == 0, "pack: image must be 1024-byte aligned");
+  const int op = operand_kind(precision);
   const int bc = tc::pick_bc(cols);
   const int n_tiles = (cols + bc - 1) / bc;
-  const int halves = precision == NNB_PREC_FP32 ? 2 : 1;
   const int nchunk = cin_total / tc::BK;
-  const int64_t words = (int64_t)n_tiles * kvol * nchunk * halves * bc * 32;
+  const int64_t tile_bytes = (int64_t)n_tiles * kvol * nchunk * tc::b_tile_bytes(op, bc);
+  const int64_t words = tile_bytes / 4;
   const int blocks = (int)std::min<int64_t>((words + 255) / 256, 148 * 32);
-  tc::pack_kernel<<<blocks, 256, 0, stream>>>(w, cols, kvol, cin_total, bc, halves, nchunk, row_taps, up_cout,
-                                              words, reinterpret_cast<uint32_t*>(packed));
+  if (op == kOperandF16x2) {
+    float* inv_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(packed) + tile_bytes);
+    tc::column_scale_kernel<<<n_tiles * bc, 256, 0, stream>>>(w, cols, kvol, cin_total, row_taps, up_cout,
+                                                               inv_scale);
+    NNB_LAUNCH_CHECK();
+    tc::pack_f16x2_kernel<<<blocks, 256, 0, stream>>>(w, cols, kvol, cin_total, bc, nchunk, row_taps, up_cout, words,
+                                                      inv_scale, reinterpret_cast<uint32_t*>(packed));
+  } else {
+    const int halves = op == kOperandTf32x2 ? 2 : 1;
+    tc::pack_kernel<<<blocks, 256, 0, stream>>>(w, cols, kvol, cin_total, bc, halves, nchunk, row_taps, up_cout,
+                                                words, reinterpret_cast<uint32_t*>(packed));
+  }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }
@@ -1009,6 +1155,7 @@ int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_
 
 extern "C" int32_t nnb_device_status(int32_t* where, int32_t reset) {
   int status = 0, loc = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return NNB_E_CUDA;
   if (cudaMemcpyFromSymbol(&status, nnb::g_device_status, sizeof(int)) != cudaSuccess) return NNB_E_CUDA;
   cudaMemcpyFromSymbol(&loc, nnb::g_device_status_where, sizeof(int));
   if (where) *where = loc;

@@ -92,6 +92,15 @@ def run_units(models, volume: torch.Tensor, accumulator: VolumeAccumulator, offs
         del features
 
 
+def _any_rank(flag: bool, device, world: int, group) -> bool:
+    """Logical OR of a per-rank flag (one small all-reduce; every rank calls it)."""
+    if world <= 1:
+        return flag
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return bool(t.item())
+
+
 def predict_volume_sharded(models, volume: torch.Tensor, *, patch_size, num_classes: int, mirroring_axes=(),
                            step_fraction: float = 0.5, group=None, want_logits: bool = True,
                            label_dtype=torch.uint8):
@@ -115,7 +124,14 @@ def predict_volume_sharded(models, volume: torch.Tensor, *, patch_size, num_clas
     masks = mirror_masks(axes)
     accumulator = VolumeAccumulator(spatial, num_classes, patch, volume.device)
     units = shard_units(len(offsets), len(models), rank, world)
+    guarded = any(getattr(m, "range_guarded", False) for m in models)
+    if guarded:
+        kernels.operand_range_events(reset=True)
     run_units(models, volume, accumulator, offsets, units, patch, masks)
+    if guarded and _any_rank(kernels.operand_range_events(reset=True) > 0, volume.device, world, group):
+        # an activation left the fp16-pair range on some rank: every rank recomputes in split TF32
+        accumulator = VolumeAccumulator(spatial, num_classes, patch, volume.device)
+        run_units([m.range_fallback() for m in models], volume, accumulator, offsets, units, patch, masks)
 
     if world > 1:
         z_lo, z_hi, acc, normalizer = exchange_slabs(accumulator.acc, accumulator.normalizer, group)

@@ -126,8 +126,13 @@ def _ptr(t: torch.Tensor | None) -> int:
     return 0 if t is None else t.data_ptr()
 
 
+def _operand_floats(precision: int) -> int:
+    """32-bit words per channel of a prepared operand (fp16 pair: 1, TF32 pair: 2, TF32: 1)."""
+    return 2 if precision == _native.PREC_FP32_TF32 else 1
+
+
 def prepare_operand(x: Lazy, precision: int, slope: float) -> Lazy:
-    """The tensor-core operand of ``x`` (affine + LeakyReLU applied once, TF32 hi/lo or TF32).
+    """The tensor-core operand of ``x`` (affine + LeakyReLU applied once, in the precision's format).
 
     Cached on ``x`` so an activation read by two convolutions (an encoder output
     and its skip connection) is prepared once.
@@ -135,7 +140,7 @@ def prepare_operand(x: Lazy, precision: int, slope: float) -> Lazy:
     cached = x.prepared.get(precision)
     if cached is not None:
         return cached
-    halves = 2 if precision == _native.PREC_FP32 else 1
+    halves = _operand_floats(precision)
     out = torch.empty((*x.raw.shape[:-1], halves * x.channels), dtype=torch.float32, device=x.raw.device)
     seg = x.segment()
     voxels = math.prod(x.spatial)
@@ -150,7 +155,7 @@ def prepare_operand(x: Lazy, precision: int, slope: float) -> Lazy:
 
 
 class _Prepared(Lazy):
-    """A prepared operand: ``raw`` holds ``halves * logical`` floats per voxel."""
+    """A prepared operand: ``raw`` holds the format's 32-bit words (1 or 2 per logical channel) per voxel."""
 
     def __init__(self, raw: torch.Tensor, logical_channels: int) -> None:
         super().__init__(raw)
@@ -159,6 +164,14 @@ class _Prepared(Lazy):
     @property
     def channels(self) -> int:
         return self.logical_channels
+
+
+def operand_range_events(reset: bool = False) -> int:
+    """Activations found outside the fp16-pair operand's range since the last reset (synchronises)."""
+    count = int(_native.load().nnb_operand_range_events(1 if reset else 0))
+    if count < 0:
+        _native.check(int(count), "operand_range_events")
+    return count
 
 
 def packed_bytes(cout: int, kvol: int, cin: int, precision: int) -> int:
@@ -171,7 +184,7 @@ def pack_weights(weight: torch.Tensor, precision: int) -> torch.Tensor | None:
     Returns ``None`` when the layer is outside the tensor-core envelope (it
     then runs on the CUDA-core kernel).
     """
-    if precision not in (_native.PREC_FP32, _native.PREC_TF32):
+    if precision not in _native.TENSOR_PRECISIONS:
         return None
     _check_tensor(weight, "weight")
     cout, cin = int(weight.shape[0]), int(weight.shape[-1])
@@ -224,7 +237,7 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
     args.out = out.data_ptr()
     args.precision = int(precision)
     cin = sum(item.channels for item in inputs)
-    tensor_cores = (packed is not None and precision in (_native.PREC_FP32, _native.PREC_TF32)
+    tensor_cores = (packed is not None and precision in _native.TENSOR_PRECISIONS
                     and all(item.channels % 32 == 0 for item in inputs) and cout % 16 == 0)
     if tensor_cores:
         for index, item in enumerate(inputs):
@@ -291,7 +304,7 @@ def conv3d_norm_static(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stri
     out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=device)
     scale = torch.empty((batch, cout), dtype=torch.float32, device=device)
     shift = torch.empty_like(scale)
-    tensor_cores = (packed is not None and precision in (_native.PREC_FP32, _native.PREC_TF32)
+    tensor_cores = (packed is not None and precision in _native.TENSOR_PRECISIONS
                     and all(item.channels % 32 == 0 for item in inputs) and cout % 16 == 0)
     args = _native.Conv3dArgs()
     args.batch = batch
@@ -321,7 +334,7 @@ def conv3d_norm_static(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stri
 
 def pack_transposed_weights(weight: torch.Tensor, precision: int) -> torch.Tensor | None:
     """Tensor-core image of a stride == kernel transposed-convolution weight ``(C_out, kD, kH, kW, C_in)``."""
-    if precision not in (_native.PREC_FP32, _native.PREC_TF32):
+    if precision not in _native.TENSOR_PRECISIONS:
         return None
     _check_tensor(weight, "weight")
     cout, cin = int(weight.shape[0]), int(weight.shape[-1])
@@ -346,7 +359,7 @@ def conv_transpose3d(x: Lazy, weight: torch.Tensor, bias: torch.Tensor | None, k
     out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=x.raw.device)
     _check_tensor(weight, "weight")
     tensor_cores = (packed is not None and x.channels % 32 == 0 and cout % 32 == 0
-                    and precision in (_native.PREC_FP32, _native.PREC_TF32))
+                    and precision in _native.TENSOR_PRECISIONS)
     seg = prepare_operand(x, precision, slope).segment() if tensor_cores else x.segment()
     token = PROFILE.start("conv_transpose3d_tc" if tensor_cores else "conv_transpose3d_simt",
                           2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()),

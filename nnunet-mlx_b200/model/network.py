@@ -32,7 +32,8 @@ sliding-window predictor passes the mirrored views of a tile as the batch.
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+import copy
+from dataclasses import dataclass, replace
 
 import numpy as np
 import torch
@@ -43,7 +44,11 @@ from nnunet_mlx_b200.kernels import Lazy
 from nnunet_mlx_b200.model.topology import NetworkSpec, PlainConvUNetSpec, ResidualEncoderUNetSpec
 from nnunet_mlx_b200.storage.weights import validate_weights
 
-PRECISIONS = {"fp32": _native.PREC_FP32, "tf32": _native.PREC_TF32, "simt": _native.PREC_SIMT}
+PRECISIONS = {"fp32": _native.PREC_FP32, "tf32": _native.PREC_TF32, "simt": _native.PREC_SIMT,
+              "fp32-tf32x2": _native.PREC_FP32_TF32}
+# "fp32" runs split fp16 pairs, exact to float32 level while every activation stays below 65504 in
+# magnitude; a forward that met a larger one is recomputed in split TF32 (see range_fallback).
+RANGE_FALLBACK = {"fp32": "fp32-tf32x2"}
 
 
 @dataclass
@@ -84,6 +89,7 @@ class _UNetBase:
         self.seg_weight: torch.Tensor | None = None
         self.seg_bias: torch.Tensor | None = None
         self._loaded = False
+        self._fallback: _UNetBase | None = None
 
     # ------------------------------------------------------------------ weights
     def _tensor(self, array: np.ndarray) -> torch.Tensor:
@@ -122,12 +128,40 @@ class _UNetBase:
     def load_weights(self, weights) -> "_UNetBase":
         """Strictly validate converted weights (reference ``load_converted_state``) and upload them."""
         checked = validate_weights(self.spec, weights)
-        self.layers.clear()
-        self.up.clear()
+        self.layers = {}
+        self.up = {}
+        self._fallback = None
         self._load(checked)
         self._load_decoder(checked)
         self._loaded = True
         return self
+
+    @property
+    def range_guarded(self) -> bool:
+        """True when this network's tensor-core operands have a bounded range (split fp16 pairs)."""
+        return self.precision in RANGE_FALLBACK
+
+    def range_fallback(self) -> "_UNetBase":
+        """This network computing in split TF32 (same device weights, own weight images, built once).
+
+        Used to recompute a volume in which an activation exceeded the fp16-pair
+        operand range (``kernels.operand_range_events``).
+        """
+        target = RANGE_FALLBACK.get(self.precision)
+        if target is None:
+            return self
+        if self._fallback is None:
+            if not self._loaded:
+                raise ContractError("network weights are not loaded")
+            prec = PRECISIONS[target]
+            twin = copy.copy(self)
+            twin.precision = target
+            twin._fallback = None
+            twin.layers = {name: replace(layer, packed=kernels.pack_weights(layer.weight, prec))
+                           for name, layer in self.layers.items()}
+            twin.up = {d: (w, b, k, kernels.pack_transposed_weights(w, prec)) for d, (w, b, k, _) in self.up.items()}
+            self._fallback = twin
+        return self._fallback
 
     def _load(self, weights) -> None:  # encoder, per subclass
         raise NotImplementedError

@@ -184,6 +184,23 @@ def run_tiles(models, volume: torch.Tensor, acc: VolumeAccumulator, offsets, pat
             del features
 
 
+def range_guarded(models, run):
+    """``run(models)``, recomputed with the split-TF32 twins when an fp16-pair operand was out of range.
+
+    Networks in the default ``fp32`` precision compute with fp16 hi/lo operand
+    pairs, exact to float32 level while every activation stays below 65504 in
+    magnitude; the operand preparation counts the elements that do not.  The
+    count is read once per volume (one device synchronisation).
+    """
+    guarded = any(getattr(m, "range_guarded", False) for m in models)
+    if guarded:
+        kernels.operand_range_events(reset=True)
+    result = run(models)
+    if guarded and kernels.operand_range_events(reset=True) > 0:
+        result = run([m.range_fallback() for m in models])
+    return result
+
+
 def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes=(), step_fraction: float = 0.5,
                    want_logits: bool = True, label_dtype=torch.uint8, device=None, accumulation: str = "float32",
                    half_logits: bool = False):
@@ -210,13 +227,17 @@ def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes
     lo = [c.start for c in crop]
     dims = [c.stop - c.start for c in crop]
     if accumulation == "nnunet-fp16":
-        return _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims,
-                                    want_logits, label_dtype, half_logits)
-    accumulator = VolumeAccumulator(spatial, num_classes, patch, device)
-    run_tiles(models, volume, accumulator, tile_offsets(spatial, patch, step_fraction), patch, masks)
-    logits, labels, invalid = kernels.normalize_labels(accumulator.acc, accumulator.normalizer, lo, dims,
-                                                       fold_divisor=float(len(models)), want_logits=want_logits,
-                                                       label_dtype=label_dtype)
+        return range_guarded(models, lambda ms: _predict_volume_fp16(
+            ms, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims, want_logits, label_dtype,
+            half_logits))
+
+    def run(ms):
+        accumulator = VolumeAccumulator(spatial, num_classes, patch, device)
+        run_tiles(ms, volume, accumulator, tile_offsets(spatial, patch, step_fraction), patch, masks)
+        return kernels.normalize_labels(accumulator.acc, accumulator.normalizer, lo, dims,
+                                        fold_divisor=float(len(ms)), want_logits=want_logits, label_dtype=label_dtype)
+
+    logits, labels, invalid = range_guarded(models, run)
     if int(invalid.item()) != 0:
         raise ContractError("sliding-window inference produced non-finite logits")
     return logits, labels

@@ -179,3 +179,45 @@ def tf32_round(t: torch.Tensor) -> torch.Tensor:
     lsb = (bits >> 13) & 1
     rounded = (bits + 0x0FFF + lsb) & ~0x1FFF
     return rounded.view(torch.float32)
+
+
+def fp16_pair(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split float32 values into the fp16-pair operand: ``hi = fp16(t)``, ``lo' = fp16(2^11 (t - hi))``.
+
+    ``hi + 2^-11 lo'`` reproduces ``t`` to ~2^-22 relative while ``|t| < 65504``.
+    Used only by tests that check the numerics of the default tensor-core mode.
+    """
+    hi = t.to(torch.float16).to(torch.float32)
+    lo = ((t - hi) * 2048.0).to(torch.float16).to(torch.float32)
+    return hi, lo
+
+
+def fp16_pair_products(op, transposed: bool = False):
+    """``op`` (a float32 convolution) recomputed with the default mode's three fp16-pair products.
+
+    Activations split with :func:`fp16_pair`; weights scaled by a power of two
+    per GEMM column (output channel, or (output channel, tap) for a stride ==
+    kernel transposed convolution) so that their maximum is below 2^14, then
+    split.  The result is ``conv(a_hi, w_hi) + 2^-11 (conv(a_hi, w_lo') +
+    conv(a_lo', w_hi))`` divided by the column scale, the sum the tensor-core
+    epilogue forms.  Test infrastructure only.
+    """
+    def conv(x, w, b=None, **kwargs):
+        # weight layout: conv (C_out, C_in, *k); transposed conv (C_in, C_out, *k)
+        reduce_dims = (0,) if transposed else tuple(range(1, w.ndim))
+        m = w.abs().amax(dim=reduce_dims, keepdim=True).double().numpy()
+        _, e = np.frexp(np.where(m > 0, m, 1.0))
+        scale = torch.from_numpy(np.where(m > 0, np.ldexp(1.0, 14 - e), 1.0).astype(np.float32))
+        a_hi, a_lo = fp16_pair(x)
+        w_hi, w_lo = fp16_pair(w * scale)
+        out = op(a_hi, w_hi, None, **kwargs) + (op(a_hi, w_lo, None, **kwargs) + op(a_lo, w_hi, None, **kwargs)) / 2048.0
+        channel = (1, -1) + (1,) * (x.ndim - 2)
+        if transposed:
+            # output position p along an axis was produced by tap p % k
+            k = tuple(int(v) for v in w.shape[2:])
+            inv = (1.0 / scale).reshape(w.shape[1], *k)
+            out = out * inv.repeat(1, *(o // kk for o, kk in zip(out.shape[2:], k))).unsqueeze(0)
+        else:
+            out = out / scale.reshape(channel)
+        return out if b is None else out + b.reshape(channel)
+    return conv

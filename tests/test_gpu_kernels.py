@@ -13,7 +13,7 @@ import torch.nn.functional as F
 
 pytestmark = pytest.mark.gpu
 
-FP32_TOL = dict(rtol=2e-4, atol=2e-4)     # split-TF32 / CUDA-core float32 vs float32 reference
+FP32_TOL = dict(rtol=2e-4, atol=2e-4)     # split fp16 pairs / split TF32 / CUDA-core float32 vs float32 reference
 TF32_TOL = dict(rtol=2e-2, atol=2e-2)     # single-pass TF32 (fast mode)
 
 
@@ -67,7 +67,14 @@ CONV_CASES = [
     (1, (5, 16, 16), [(32, True)], 32, (1, 3, 3), (1, 1, 1), (0, 1, 1), "fp32"),
     (1, (6, 16, 8), [(32, True)], 32, (3, 1, 1), (1, 1, 1), (1, 0, 0), "tf32"),
     (2, (7, 19, 13), [(64, True)], 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), "tf32"),
+    # split TF32 (the range fallback of the default fp16-pair mode): halo, box, 128-column and concat shapes
+    (2, (10, 12, 16), [(32, True), (32, False)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32-tf32x2"),
+    (2, (9, 10, 11), [(32, True)], 64, (3, 3, 3), (2, 2, 2), (1, 1, 1), "fp32-tf32x2"),
+    (1, (4, 5, 6), [(64, True)], 128, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32-tf32x2"),
+    (1, (9, 20, 24), [(64, True)], 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32-tf32x2"),
 ]
+
+PRECISION_CODES = {"fp32": 0, "tf32": 1, "simt": 2, "fp32-tf32x2": 3}
 
 
 @pytest.mark.parametrize("case", CONV_CASES, ids=lambda c: f"{c[7]}-cin{[s[0] for s in c[2]]}-co{c[3]}-s{c[5][0]}")
@@ -83,10 +90,10 @@ def test_conv3d_matches_float32_reference(cuda_device, case):
         refs.append(_lazy_ref(raw, sc, sh, lazy))
     cin = sum(c for c, _ in segs)
     w = torch.from_numpy((rng.standard_normal((cout, *kernel, cin)) / np.sqrt(cin * np.prod(kernel))).astype(np.float32))
-    prec = {"fp32": _native.PREC_FP32, "tf32": _native.PREC_TF32, "simt": _native.PREC_SIMT}[precision]
+    prec = PRECISION_CODES[precision]
     wd = w.to(cuda_device)
     packed = kernels.pack_weights(wd, prec)
-    if precision in ("fp32", "tf32") and cin % 32 == 0:
+    if precision != "simt" and cin % 32 == 0:
         assert packed is not None, "expected the tensor-core path for this shape"
     out, partials = kernels.conv3d(lazies, wd, kernel=kernel, stride=stride, pad=pad, cout=cout, packed=packed,
                                    precision=prec)
@@ -132,6 +139,7 @@ def test_instance_norm_finalize_with_affine_matches_torch(cuda_device):
     ((2, 2, 2), 320, 320, "fp32"),
     ((1, 2, 2), 32, 64, "fp32"),
     ((2, 2, 2), 128, 64, "tf32"),
+    ((2, 2, 2), 64, 32, "fp32-tf32x2"),
 ])
 def test_conv_transpose_matches_torch(cuda_device, kernel, cin, cout, precision):
     from nnunet_mlx_b200 import _native, kernels
@@ -140,7 +148,7 @@ def test_conv_transpose_matches_torch(cuda_device, kernel, cin, cout, precision)
     lz, raw, sc, sh = _make_segment(rng, 2, (3, 4, 5), cin, True, cuda_device)
     w = torch.from_numpy((rng.standard_normal((cout, *kernel, cin)) / np.sqrt(cin)).astype(np.float32))
     b = torch.from_numpy(rng.standard_normal(cout).astype(np.float32))
-    prec = {"fp32": _native.PREC_FP32, "tf32": _native.PREC_TF32, "simt": _native.PREC_SIMT}[precision]
+    prec = PRECISION_CODES[precision]
     wd = w.to(cuda_device)
     packed = kernels.pack_transposed_weights(wd, prec)
     if precision != "simt":
@@ -278,3 +286,45 @@ def test_pointwise_head_matches_reference(cuda_device, cin, cout, lazy):
     assert partials is None
     ref = _conv_ref([_lazy_ref(raw, sc, sh, lazy)], w, (1, 1, 1), (0, 0, 0), bias=b)
     np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("cin,cout,stride", [(32, 32, 1), (64, 128, 1), (32, 64, 2)])
+def test_fp16_pair_column_scales_cover_weight_magnitudes(cuda_device, cin, cout, stride):
+    """Per-column power-of-two weight scales: columns from 1e-9 to 1e4 keep float32-level accuracy."""
+    from nnunet_mlx_b200 import _native, kernels
+    from nnunet_mlx_b200.kernels import Lazy
+
+    rng = np.random.default_rng(cin + cout + stride)
+    x = torch.from_numpy(rng.standard_normal((1, 8, 16, 16, cin)).astype(np.float32))
+    w = rng.standard_normal((cout, 3, 3, 3, cin)) / np.sqrt(27 * cin)
+    w *= 10.0 ** rng.uniform(-9, 4, (cout, 1, 1, 1, 1))
+    w = torch.from_numpy(w.astype(np.float32))
+    packed = kernels.pack_weights(w.to(cuda_device), _native.PREC_FP32)
+    out, _ = kernels.conv3d([Lazy(x.to(cuda_device))], w.to(cuda_device), kernel=(3, 3, 3), stride=(stride,) * 3,
+                            pad=(1, 1, 1), cout=cout, packed=packed, precision=_native.PREC_FP32)
+    ref = _conv_ref([x], w, (stride,) * 3, (1, 1, 1)).numpy()
+    got = out.cpu().numpy()
+    col_scale = np.abs(ref).reshape(-1, cout).max(axis=0)
+    err = np.abs(got - ref).reshape(-1, cout).max(axis=0)
+    assert (err <= 2e-5 * col_scale).all(), (err / col_scale).max()
+
+
+def test_fp16_pair_operand_format_and_range_events(cuda_device):
+    """Prepared fp16-pair operand: hi + 2^-11 lo' reproduces the activation to ~2^-22; |x| >= 65504 is counted."""
+    from nnunet_mlx_b200 import _native, kernels
+    from nnunet_mlx_b200.kernels import Lazy
+
+    rng = np.random.default_rng(31)
+    raw = rng.standard_normal((2, 3, 4, 5, 64)).astype(np.float32) * 50
+    raw[0, 0, 0, 0, :5] = [65503.0, 65504.0, -70000.0, 1e9, -65504.0]  # four counted (|x| >= 65504)
+    raw[1, 2, 3, 4, 7] = 3e-7                                            # subnormal hi, still reproduced
+    lazy = Lazy(torch.from_numpy(raw).to(cuda_device))
+    kernels.operand_range_events(reset=True)
+    prepared = kernels.prepare_operand(lazy, _native.PREC_FP32, 0.01)
+    assert kernels.operand_range_events(reset=True) == 4
+    halves = prepared.raw.view(torch.float16).cpu().numpy().astype(np.float64)
+    pairs = halves.reshape(*raw.shape[:-1], raw.shape[-1] // 32, 2, 32)
+    recon = (pairs[..., 0, :] + pairs[..., 1, :] / 2048.0).reshape(raw.shape)
+    finite = np.abs(raw) < 65504
+    err = np.abs(recon - raw.astype(np.float64))[finite]
+    assert (err <= 2.0 ** -21 * np.abs(raw[finite]) + 2.0 ** -35).all(), err.max()

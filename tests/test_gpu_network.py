@@ -1,9 +1,10 @@
 """Network forward and sliding-window parity on B200 against the CPU oracle.
 
 Tolerance (BASELINE): logits within rel 1e-3 / abs 1e-3 of the float32
-oracle in the default ("fp32": split-TF32 tensor cores) mode and argmax
-agreement >= 99.95% with disagreements only at near-ties.  The single-pass
-TF32 fast mode is checked against its own stated, looser bound.
+oracle in the default ("fp32": split fp16-pair tensor cores) mode and in its
+split-TF32 range fallback ("fp32-tf32x2"), argmax agreement >= 99.95% with
+disagreements only at near-ties.  The single-pass TF32 fast mode is checked
+against its own stated, looser bound.
 """
 
 from __future__ import annotations
@@ -91,12 +92,13 @@ def test_forward_matches_oracle(cuda_device, kind, shape):
     _assert_logits(got, ref)
 
 
-def test_full_network_forward_64_matches_oracle(cuda_device):
+@pytest.mark.parametrize("precision", ["fp32", "fp32-tf32x2"])
+def test_full_network_forward_64_matches_oracle(cuda_device, precision):
     """The benchmark network (6 stages, 32..320) on a 64^3 synthetic CT tile."""
     from nnunet_mlx_b200.synthetic import config_spec, synthetic_ct
 
     spec = config_spec(1)
-    net, weights = _network(spec, 0, cuda_device)
+    net, weights = _network(spec, 0, cuda_device, precision=precision)
     x = np.moveaxis(synthetic_ct((64, 96, 96), seed=1)[:, :, :64, :64], 0, -1)[None].copy()
     got = net(torch.from_numpy(x).to(cuda_device)).cpu().numpy()
     ref = onet.forward(x, weights, spec)
@@ -164,3 +166,36 @@ def test_mid_network_sliding_window_tensor_cores(cuda_device):
                              mirroring_axes=(0, 1, 2))
     np.testing.assert_allclose(logits.cpu().numpy(), ref, **LOGIT_TOL)
     assert (labels.cpu().numpy() == ref.argmax(0)).mean() >= 0.9995
+
+
+def test_fp32_range_fallback_recomputes_in_split_tf32(cuda_device):
+    """An activation beyond the fp16-pair range (norm gain 2e5) sends the volume to the split-TF32 twin."""
+    from nnunet_mlx_b200.model.network import build_network
+    from nnunet_mlx_b200.prediction.sliding_window import predict_volume
+
+    spec = _spec("mid")
+    net, weights = _network(spec, 8, cuda_device)
+    weights["enc0.block0.norm.weight"] = np.full_like(weights["enc0.block0.norm.weight"], 2e5)
+    net = build_network(spec, precision="fp32", device=cuda_device).load_weights(weights)
+    twin = build_network(spec, precision="fp32-tf32x2", device=cuda_device).load_weights(weights)
+    data = np.random.default_rng(15).standard_normal((2, 16, 20, 16)).astype(np.float32)
+    args = dict(patch_size=(16, 16, 16), num_classes=4, mirroring_axes=(0, 2))
+    logits, labels = predict_volume([net], data, **args)
+    assert net._fallback is not None, "the range guard did not fire"
+    ref_logits, ref_labels = predict_volume([twin], data, **args)
+    assert twin._fallback is None
+    np.testing.assert_array_equal(logits.cpu().numpy(), ref_logits.cpu().numpy())
+    np.testing.assert_array_equal(labels.cpu().numpy(), ref_labels.cpu().numpy())
+    ref = osw.predict_logits(_oracle_model(weights, spec), data, num_classes=4, patch_size=(16, 16, 16),
+                             mirroring_axes=(0, 2))
+    np.testing.assert_allclose(logits.cpu().numpy(), ref, **LOGIT_TOL)
+
+
+def test_fp32_mode_stays_on_fp16_pairs_for_normalised_activations(cuda_device):
+    from nnunet_mlx_b200.prediction.sliding_window import predict_volume
+
+    spec = _spec("mid")
+    net, _ = _network(spec, 9, cuda_device)
+    data = np.random.default_rng(16).standard_normal((2, 16, 16, 16)).astype(np.float32)
+    predict_volume([net], data, patch_size=(16, 16, 16), num_classes=4, mirroring_axes=(0,))
+    assert net._fallback is None
