@@ -97,6 +97,7 @@ struct Geometry {
   int box[3];                  // TMA box extent along w, h, d (elements, before element strides)
   int pw, plane_rows, plane_bytes;  // halo plane: row pitch, rows, bytes per half (1024-aligned)
   int sa, sb, tb;              // halo-mode ring depths (A planes, B stages) and taps per B stage
+  int zs;                      // 1: z-streaming mode (sb = 0: weights resident in shared memory)
 };
 
 struct OperandMaps {
@@ -234,10 +235,12 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
 }
 
 // One finished accumulator -> outputs + partials (or the transposed-conv scatter).
+// acc: TMEM address of the tile's (hi) accumulator columns for this warp's lanes; acc_lo: of the lo / mix
+// columns (split formats).
 template <int BC, int OP>
 __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Geometry& g, const TileOrigin& o,
-                                              uint32_t acc, int q, int lane, float* red, float* col_mean,
-                                              const float* __restrict__ col_inv) {
+                                              uint32_t acc, uint32_t acc_lo, int q, int lane, float* red,
+                                              float* col_mean, const float* __restrict__ col_inv) {
   const int row = q * 32 + lane;
   const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
   const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
@@ -254,12 +257,12 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
     if constexpr (OP == kOperandF16x2) {
       // (sum a0 W0 + 2^-11 sum (a0 W1' + a1' W0)) / s of the column
       float u[32];
-      tmem_ld32(acc + BC + cc * 32, u);
+      tmem_ld32(acc_lo + cc * 32, u);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = fmaf(u[i], 1.f / 2048.f, v[i]) * __ldg(col_inv + nbase + i);
     } else if constexpr (OP == kOperandTf32x2) {
       float u[32];
-      tmem_ld32(acc + BC + cc * 32, u);
+      tmem_ld32(acc_lo + cc * 32, u);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] += u[i];
     }
@@ -352,7 +355,8 @@ __device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Ge
     if (stop) break;
     fence_after();
     const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
-    epilogue_tile<BC, OP>(a, g, o, tmem + ab * C::N + lane_base, q, lane, sm.red, sm.col_mean, col_inv);
+    const uint32_t acc = tmem + ab * C::N + lane_base;
+    epilogue_tile<BC, OP>(a, g, o, acc, acc + BC, q, lane, sm.red, sm.col_mean, col_inv);
     fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&acce[ab]));
@@ -716,6 +720,339 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Z-streaming mode (fp16 pairs; 3x3x3, stride 1, padding 1, <= 32 output
+// channels).  The 128^3 stages' layers: a CTA walks a contiguous run of the
+// output planes of 8 (w) x 16 (h) brick columns (column-major, z fastest; the
+// runs of all CTAs split the volume's planes evenly).  Each input plane u of a
+// column is loaded once (one halo plane box per 32-channel chunk) and, per
+// (ky, kx) tap and 16-channel sub-step, multiplied by the weights of all
+// three kz taps stacked along N:
+//   A_hi  x [W0(kz0); W0(kz1); W0(kz2)]   -> hi ring
+//   A_hi  x [W1'(kz0); W1'(kz1); W1'(kz2)] -> mix ring
+//   A_lo' x [W0(kz0); W0(kz1); W0(kz2)]   -> mix ring
+// (N = 96), where block kz feeds output plane u + 1 - kz.  The accumulators
+// of consecutive output planes sit in a TMEM ring of 8 slots of 32 columns
+// (hi: columns [0, 256), mix: [256, 512)), slot 7 - (P mod 8) for the P-th
+// plane of the CTA's sequence, so the three planes an input feeds occupy
+// adjacent ascending slots and one MMA covers them (two where the ring wraps).
+// Output plane u - 1 is complete after input u.  The epilogue reads a
+// complete plane, writes it (planes outside the run -- the halo planes of a
+// partial column -- are only discarded), zeroes its slots and releases them,
+// so every MMA accumulates.  A column costs 3 MMAs per (tap, sub-step, input
+// plane) instead of 6 per output plane, and each input plane is read once
+// instead of three times.  The 27 taps' weights of a single-chunk layer stay
+// resident in shared memory for the whole kernel (rearranged from the weight
+// image by bulk copies); wider inputs stream one (chunk, ky) row of stacked
+// weights per stage.
+// ---------------------------------------------------------------------------
+constexpr int kZsSlots = 8;
+constexpr int kZsRows = 6 * 32;  // stacked rows per (ky, kx) tap: [W0 x 3 kz ; W1' x 3 kz]
+
+struct ZsRun {
+  int64_t idx, end;  // [idx, end) of the column-major, z-fastest output-plane sequence
+};
+
+struct ZsSegment {
+  int col, z0, z1;  // output planes [z0, z1) of brick column col
+  int ua, ub;       // input planes loaded: [ua, ub]
+};
+
+__device__ __forceinline__ ZsRun zs_run(const Geometry& g) {
+  const int64_t total = (int64_t)g.total_tiles;  // columns x OD
+  return ZsRun{total * blockIdx.x / gridDim.x, total * (blockIdx.x + 1) / gridDim.x};
+}
+
+__device__ __forceinline__ bool zs_next(const Geometry& g, ZsRun& r, ZsSegment& s) {
+  if (r.idx >= r.end) return false;
+  s.col = (int)(r.idx / g.OD);
+  s.z0 = (int)(r.idx - (int64_t)s.col * g.OD);
+  const int64_t stop = min(r.end, (int64_t)(s.col + 1) * g.OD);
+  s.z1 = s.z0 + (int)(stop - r.idx);
+  r.idx = stop;
+  s.ua = max(s.z0 - 1, 0);
+  s.ub = min(s.z1, g.ID - 1);
+  return true;
+}
+
+__device__ __forceinline__ int zs_slot(int P) { return kZsSlots - 1 - (P & (kZsSlots - 1)); }
+
+// The three MMAs of one (tap, 16-channel sub-step) into the planes' slots: ad / bd the A (hi) and
+// stacked-B descriptors, s0 the slot of block kz = 0.  Blocks past slot 7 continue at slot 0.
+__device__ __forceinline__ void zs_mmas(uint32_t tmem, int s0, uint64_t ad, uint64_t bd) {
+  constexpr uint32_t id96 = idesc_f16(BM, 96), id64 = idesc_f16(BM, 64), id32 = idesc_f16(BM, 32);
+  constexpr uint32_t kMix16 = (3 * 32 * 64) >> 4;  // W1' blocks start 96 rows in
+  const uint32_t hi = tmem + 32u * (uint32_t)s0, mix = hi + 256u;
+  if (s0 <= kZsSlots - 3) {
+    mma_f16_ss(hi, ad, bd, id96, 1u);
+    mma_f16_ss(mix, ad, bd + kMix16, id96, 1u);
+    mma_f16_ss(mix, ad + 4, bd, id96, 1u);
+  } else {
+    const int n1 = kZsSlots - s0;  // blocks before the wrap (1 or 2)
+    const uint32_t idA = n1 == 2 ? id64 : id32, idB = n1 == 2 ? id32 : id64;
+    const uint64_t bB = bd + (uint64_t)(n1 * ((32 * 64) >> 4));
+    mma_f16_ss(hi, ad, bd, idA, 1u);
+    mma_f16_ss(tmem, ad, bB, idB, 1u);
+    mma_f16_ss(mix, ad, bd + kMix16, idA, 1u);
+    mma_f16_ss(tmem + 256u, ad, bB + kMix16, idB, 1u);
+    mma_f16_ss(mix, ad + 4, bd, idA, 1u);
+    mma_f16_ss(tmem + 256u, ad + 4, bB, idB, 1u);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3d_zstream_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
+  constexpr int BC = 32;
+  using C = Cfg<BC, kOperandF16x2>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int SA = g.sa, SB = g.sb;
+  const bool resident = SB == 0;
+  const int a_entry = g.nchunk * g.plane_bytes;              // one input plane, all chunks
+  constexpr uint32_t kTapBytes = kZsRows * 64;              // stacked weights of one (ky, kx) tap
+  const uint32_t b_stage = 3u * kTapBytes;                  // one (chunk, ky) row of taps
+  const uint32_t b_bytes = resident ? 9u * kTapBytes : (uint32_t)SB * b_stage;
+  uint8_t* a_ring = smem;
+  uint8_t* b_ring = smem + SA * a_entry;
+  const SharedMisc sm = shared_misc(b_ring + b_bytes);
+  uint64_t* a_full = sm.bars;
+  uint64_t* a_empty = a_full + SA;
+  uint64_t* b_full = a_empty + SA;    // SB stages, or [0] = resident weights
+  uint64_t* b_empty = b_full + max(SB, 1);
+  uint64_t* accf = b_empty + max(SB, 1);
+  uint64_t* acce = accf + kZsSlots;
+  const uint32_t drain_bar = smem_u32(acce + kZsSlots);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bricks = g.nh * g.nw;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(smem_u32(&a_full[s]), 1);
+      mbar_init(smem_u32(&a_empty[s]), 1);
+    }
+    for (int s = 0; s < max(SB, 1); ++s) {
+      mbar_init(smem_u32(&b_full[s]), 1);
+      mbar_init(smem_u32(&b_empty[s]), 1);
+    }
+    for (int i = 0; i < kZsSlots; ++i) {
+      mbar_init(smem_u32(&accf[i]), 1);
+      mbar_init(smem_u32(&acce[i]), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *sm.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc_all(sm.tmem_slot);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *sm.tmem_slot;
+  if (warp >= 2) {
+    // every slot starts at zero: the MMAs always accumulate
+    const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+#pragma unroll 1
+    for (int c = 0; c < kTmemCols; c += 32) tmem_zero32(tmem + lanes + (uint32_t)c);
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+
+  const uint8_t* wimg = static_cast<const uint8_t*>(a.packed);
+  const int taps = 27;
+  if (warp == 0) {
+    // ------------------------------ TMA producer -----------------------------
+    if (lane == 0) {
+      bool alive = true;
+      if (resident) {
+        // stacked rows of tap (ky, kx): [W0(kz0..2) ; W1'(kz0..2)], 32 rows each, from the image's
+        // [W0 ; W1'] tile of tap (kz, ky, kx)
+        const uint32_t fb = smem_u32(&b_full[0]);
+        mbar_arrive_expect_tx(fb, 9u * kTapBytes);
+        for (int t = 0; t < 9; ++t)
+          for (int part = 0; part < 2; ++part)
+            for (int kz = 0; kz < 3; ++kz)
+              bulk_g2s(smem_u32(b_ring + t * kTapBytes + (part * 3 + kz) * 32 * 64),
+                       wimg + (int64_t)(kz * 9 + t) * C::kBBytes + part * 32 * 64, 32 * 64, fb);
+      }
+      int P = 0, T = 0;
+      ZsRun run = zs_run(g);
+      ZsSegment sg;
+      while (alive && zs_next(g, run, sg)) {
+        const int b = sg.col / bricks, rem = sg.col - b * bricks;
+        const int hb = rem / g.nw, wb = rem - hb * g.nw;
+        const int w0 = wb * kHaloW - 1, h0 = hb * kHaloH - 1;
+        for (int u = sg.ua; u <= sg.ub && alive; ++u) {
+          const int sa = P % SA;
+          if (P >= SA && !mbar_wait(smem_u32(&a_empty[sa]), ((P / SA) - 1) & 1, sm.abort_flag, 32)) {
+            alive = false;
+            break;
+          }
+          const uint32_t fa = smem_u32(&a_full[sa]);
+          mbar_arrive_expect_tx(fa, (uint32_t)(g.nchunk * g.plane_rows * 128));
+          for (int c = 0; c < g.nchunk; ++c) {
+            const ChunkSource src = chunk_source<kOperandF16x2>(a, g, maps, c);
+            tma_load_5d(smem_u32(a_ring + sa * a_entry + c * g.plane_bytes), src.map, src.c_hi, w0, h0, u, b, fa);
+          }
+          ++P;
+          if (!resident) {
+            for (int c = 0; c < g.nchunk && alive; ++c)
+              for (int ky = 0; ky < 3; ++ky) {
+                const int sb = T % SB;
+                if (T >= SB && !mbar_wait(smem_u32(&b_empty[sb]), ((T / SB) - 1) & 1, sm.abort_flag, 33)) {
+                  alive = false;
+                  break;
+                }
+                const uint32_t fb = smem_u32(&b_full[sb]);
+                mbar_arrive_expect_tx(fb, b_stage);
+                uint8_t* dst = b_ring + sb * b_stage;
+                for (int kx = 0; kx < 3; ++kx)
+                  for (int part = 0; part < 2; ++part)
+                    for (int kz = 0; kz < 3; ++kz)
+                      bulk_g2s(smem_u32(dst + kx * kTapBytes + (part * 3 + kz) * 32 * 64),
+                               wimg + (int64_t)(c * taps + kz * 9 + ky * 3 + kx) * C::kBBytes + part * 32 * 64,
+                               32 * 64, fb);
+                ++T;
+              }
+          }
+        }
+      }
+      if (*sm.abort_flag) {
+        for (int i = max(0, P - SA); i < P; ++i)
+          mbar_wait(smem_u32(&a_full[i % SA]), (i / SA) & 1, sm.abort_flag, 34, false);
+        if (resident) mbar_wait(smem_u32(&b_full[0]), 0, sm.abort_flag, 35, false);
+        for (int i = max(0, T - SB); i < T; ++i)
+          mbar_wait(smem_u32(&b_full[i % SB]), (i / SB) & 1, sm.abort_flag, 35, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer -------------------------------
+    if (lane == 0) {
+      const uint64_t adesc0 = sw128_desc(smem_u32(a_ring), (uint32_t)g.pw * 128);
+      const uint64_t bdesc0 = sw64_desc(smem_u32(b_ring));
+      const uint32_t entry16 = (uint32_t)a_entry >> 4, plane16 = (uint32_t)g.plane_bytes >> 4;
+      const uint32_t row16 = (uint32_t)g.pw * 8;  // one ky step of the plane in 16-byte units
+      constexpr uint32_t kTap16 = kTapBytes >> 4;
+      const uint32_t stage16 = b_stage >> 4;
+      bool alive = true;
+      if (resident) alive = mbar_wait(smem_u32(&b_full[0]), 0, sm.abort_flag, 36);
+      if (alive) fence_after();
+      int P = 0, PA = 0, T = 0;
+      int acquired = -1;  // planes [0, acquired] have had their slot released by its previous plane
+      ZsRun run = zs_run(g);
+      ZsSegment sg;
+      while (alive && zs_next(g, run, sg)) {
+        // planes ua - 1 .. ub + 1 of this segment are P .. P + (ub - ua) + 2
+        for (int u = sg.ua; u <= sg.ub && alive; ++u) {
+          const int Pn = P + (u - sg.ua) + 2;  // plane u + 1: this input's first contribution
+          for (int p = acquired + 1; p <= Pn && alive; ++p)
+            if (p >= kZsSlots && !mbar_wait(smem_u32(&acce[zs_slot(p)]), ((p / kZsSlots) - 1) & 1, sm.abort_flag, 37))
+              alive = false;
+          if (!alive) break;
+          acquired = Pn;
+          const int sa = PA % SA;
+          if (!mbar_wait(smem_u32(&a_full[sa]), (PA / SA) & 1, sm.abort_flag, 38)) {
+            alive = false;
+            break;
+          }
+          fence_after();
+          const int s0 = zs_slot(Pn);
+          for (int c = 0; c < g.nchunk && alive; ++c) {
+            const uint64_t ap = adesc0 + (uint64_t)(sa * entry16 + c * plane16);
+            if (resident) {
+#pragma unroll 1
+              for (int ky = 0; ky < 3; ++ky) {
+                const uint64_t arow = ap + (uint64_t)(ky * row16);
+                const uint64_t brow = bdesc0 + (uint64_t)(ky * 3 * kTap16);
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                  for (int kk = 0; kk < 2; ++kk)
+                    zs_mmas(tmem, s0, arow + (uint64_t)(8 * kx + 2 * kk), brow + (uint64_t)(kx * kTap16 + 2 * kk));
+              }
+            } else {
+              for (int ky = 0; ky < 3; ++ky) {
+                const int sb = T % SB;
+                if (!mbar_wait(smem_u32(&b_full[sb]), (T / SB) & 1, sm.abort_flag, 39)) {
+                  alive = false;
+                  break;
+                }
+                fence_after();
+                const uint64_t arow = ap + (uint64_t)(ky * row16);
+                const uint64_t brow = bdesc0 + (uint64_t)(sb * stage16);
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+                  for (int kk = 0; kk < 2; ++kk)
+                    zs_mmas(tmem, s0, arow + (uint64_t)(8 * kx + 2 * kk), brow + (uint64_t)(kx * kTap16 + 2 * kk));
+                mma_commit(smem_u32(&b_empty[sb]));
+                ++T;
+              }
+            }
+          }
+          if (!alive) break;
+          mma_commit(smem_u32(&a_empty[sa]));
+          ++PA;
+          mma_commit(smem_u32(&accf[zs_slot(Pn - 2)]));  // plane u - 1 is complete
+        }
+        if (!alive) break;
+        const int Pl = P + (sg.ub - sg.ua) + 2;  // plane ub + 1
+        mma_commit(smem_u32(&accf[zs_slot(Pl - 1)]));
+        mma_commit(smem_u32(&accf[zs_slot(Pl)]));
+        P = Pl + 1;
+      }
+      if (*sm.abort_flag) {
+        mma_commit(drain_bar);
+        mbar_wait(drain_bar, 0, sm.abort_flag, 16, false);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ---------------------------------
+    const int q = warp & 3;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const float* col_inv = reinterpret_cast<const float*>(wimg + (int64_t)g.ksteps * C::kBBytes);
+    int P = 0;
+    ZsRun run = zs_run(g);
+    ZsSegment sg;
+    bool stop = false;
+    while (!stop && zs_next(g, run, sg)) {
+      const int b = sg.col / bricks, rem = sg.col - b * bricks;
+      const int hb = rem / g.nw, wb = rem - hb * g.nw;
+      for (int z = sg.ua - 1; z <= sg.ub + 1; ++z, ++P) {
+        const int slot = zs_slot(P);
+        const bool ok = mbar_wait(smem_u32(&accf[slot]), (P / kZsSlots) & 1, sm.abort_flag, 40);
+        if (lane == 0) sm.votes[q] = (!ok || *sm.abort_flag) ? 1 : 0;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        stop = sm.votes[0] | sm.votes[1] | sm.votes[2] | sm.votes[3];
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (stop) break;
+        fence_after();
+        const uint32_t hi = tmem + lane_base + 32u * (uint32_t)slot, mix = hi + 256u;
+        if (z >= sg.z0 && z < sg.z1) {
+          TileOrigin o;
+          o.b = b;
+          o.nt = 0;
+          o.t = (z * g.nh + hb) * g.nw + wb;
+          o.d0 = z;
+          o.h0 = hb * kHaloH;
+          o.w0 = wb * kHaloW;
+          epilogue_tile<BC, kOperandF16x2>(a, g, o, hi, mix, q, lane, sm.red, sm.col_mean, col_inv);
+        }
+        tmem_zero32(hi);
+        tmem_zero32(mix);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&acce[slot]));
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) tmem_free_all(tmem);
+}
+
+// ---------------------------------------------------------------------------
 // Weight image: [n_tile][kstep = chunk * taps + tap][N rows][row bytes] (so
 // the taps of one 32-channel chunk are contiguous), natural K order within the
 // 32-channel step.  GEMM column n is output channel n, or for a transposed
@@ -901,6 +1238,43 @@ inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bby
   return true;
 }
 
+// Z-streaming mode (fp16 pairs) when the layer is a 3x3x3, stride-1, padding-1
+// conv with <= 32 output channels over at least one 8-wide brick row, and the
+// A ring plus the weights (resident for one 32-channel chunk, else >= 2
+// streamed (chunk, ky) stages) fit the shared-memory budget.
+inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
+  if (op != kOperandF16x2 || pick_bc(a.cout) != 32) return false;
+  for (int i = 0; i < 3; ++i)
+    if (a.kernel[i] != 3 || a.stride[i] != 1 || a.pad[i] != 1) return false;
+  if (g.OW < kHaloW || g.OH < kHaloH / 2 || g.nchunk < 1) return false;
+  g.pw = kHaloW + 2;
+  const int ph = kHaloH + 2;
+  g.plane_rows = g.pw * ph;
+  g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
+  const int entry = g.nchunk * g.plane_bytes;
+  const int budget = kMaxSmem - 1024 - kMiscBytes;
+  const int tap_bytes = kZsRows * 64;
+  if (g.nchunk == 1 && 2 * entry + 9 * tap_bytes <= budget) {
+    g.sb = 0;
+    g.sa = std::min(4, (budget - 9 * tap_bytes) / entry);
+  } else {
+    g.sa = 2;
+    g.sb = std::min(4, (budget - 2 * entry) / (3 * tap_bytes));
+    if (g.sb < 2) return false;
+  }
+  if (2 * g.sa + 2 * std::max(g.sb, 1) + 2 * kZsSlots + 1 > kMaxBars) return false;
+  g.box[0] = g.pw;
+  g.box[1] = ph;
+  g.box[2] = 1;
+  g.tw = kHaloW;
+  g.th = kHaloH;
+  g.td = 1;
+  g.tb = 3;
+  g.halo = 1;  // plane boxes with unit element strides
+  g.zs = 1;
+  return true;
+}
+
 // Row-space geometry shared by the launch, the weight image size and the
 // partials query.
 inline Geometry make_geometry(const nnb_conv3d_args& a) {
@@ -929,7 +1303,8 @@ inline Geometry make_geometry(const nnb_conv3d_args& a) {
   g.n_tiles = (a.cout + bc - 1) / bc;
   g.up_cout = 0;
   const int op = operand_kind(a.precision);
-  g.halo = plan_halo(a, g, op == kOperandTf32x2 ? 2 : 1, b_tile_bytes(op, bc)) ? 1 : 0;
+  g.zs = 0;
+  if (!plan_zstream(a, g, op)) g.halo = plan_halo(a, g, op == kOperandTf32x2 ? 2 : 1, b_tile_bytes(op, bc)) ? 1 : 0;
   if (!g.halo) {
     choose_brick(g.OD, g.OH, g.OW, g.SD, g.SH, g.SW, g.tw, g.th, g.td);
     g.box[0] = g.tw * g.SW;
@@ -988,10 +1363,13 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   using C = Cfg<BC, OP>;
   int dev = 0;
   NNB_CUDA_CHECK(cudaGetDevice(&dev));
-  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, 1/2 halo TB 1/3), per device
-  const int bit = g.halo ? (g.tb == 3 ? 4 : 2) : 1;
+  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, 1/2 halo TB 1/3, 3 zs)
+  const int bit = g.zs ? 8 : g.halo ? (g.tb == 3 ? 4 : 2) : 1;
   if (dev >= 64 || !(configured[dev] & bit)) {
-    if (g.halo && g.tb == 3)
+    if (g.zs)
+      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_zstream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kMaxSmem));
+    else if (g.halo && g.tb == 3)
       NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, OP, 3>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     else if (g.halo)
@@ -1005,7 +1383,16 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   int sms = 148;
   NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::min(g.total_tiles, sms);
-  if (g.halo) {
+  if (g.zs) {
+    if constexpr (BC == 32 && OP == kOperandF16x2) {
+      const int b_bytes = g.sb == 0 ? 9 * kZsRows * 64 : g.sb * 3 * kZsRows * 64;
+      const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes;
+      NNB_REQUIRE(smem <= kMaxSmem, "conv3d: z-streaming plan exceeds shared memory (%d bytes)", smem);
+      conv3d_zstream_kernel<<<grid, kThreads, smem, stream>>>(a, g, maps);
+    } else {
+      NNB_REQUIRE(false, "conv3d: internal: z-streaming plan for an unsupported tile");
+    }
+  } else if (g.halo) {
     const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * g.tb * C::kBBytes + kMiscBytes;
     NNB_REQUIRE(smem <= kMaxSmem, "conv3d: halo plan exceeds shared memory (%d bytes)", smem);
     if (g.tb == 3)

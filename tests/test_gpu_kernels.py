@@ -67,6 +67,13 @@ CONV_CASES = [
     (1, (5, 16, 16), [(32, True)], 32, (1, 3, 3), (1, 1, 1), (0, 1, 1), "fp32"),
     (1, (6, 16, 8), [(32, True)], 32, (3, 1, 1), (1, 1, 1), (1, 0, 0), "tf32"),
     (2, (7, 19, 13), [(64, True)], 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), "tf32"),
+    # z-streaming (fp16 pairs, 3x3x3 s1 p1, <= 32 output channels): partial bricks, 1-plane and short
+    # columns, 16 output channels, 2 and 3 chunks of streamed weights, several samples
+    (2, (5, 9, 17), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (1, (1, 8, 8), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (1, (3, 8, 8), [(32, True), (32, False)], 16, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (3, (4, 16, 8), [(96, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (1, (40, 24, 24), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
     # split TF32 (the range fallback of the default fp16-pair mode): halo, box, 128-column and concat shapes
     (2, (10, 12, 16), [(32, True), (32, False)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32-tf32x2"),
     (2, (9, 10, 11), [(32, True)], 64, (3, 3, 3), (2, 2, 2), (1, 1, 1), "fp32-tf32x2"),
