@@ -387,7 +387,7 @@ def main():
             "peak_source": f"{pk['source']} dense bf16, sustained (kernel timed inside a long step)",
             "note": "achieved = algorithmic FLOPs (2 x MACs) of the dominant launch / its mean CUDA-event "
                     "duration over the timed region; fp32 mode computes fp16 operand pairs: per 16-channel "
-                    "sub-step A_hi x [W0;W1'] and A_lo' x W0 (3 tensor products per useful product at the "
+                    "sub-step A_hi x [W0;W1] and A_lo x W0 (3 tensor products per useful product at the "
                     "bf16/fp16 rate), so its arithmetic ceiling is peak/3 (fp32-tf32x2: 4 products at half "
                     "rate, peak/8; tf32: peak/2)"})
         line = {

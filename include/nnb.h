@@ -43,7 +43,7 @@ enum nnb_status {
 
 /* Arithmetic of the convolution contractions. */
 enum nnb_precision {
-  NNB_PREC_FP32 = 0,      /* split fp16 pairs (hi + 2^-11 lo', 3 products): float32-level
+  NNB_PREC_FP32 = 0,      /* split fp16 pairs (hi + lo, 3 products): float32-level
                              accuracy; activations must stay below 65504 in magnitude
                              (out-of-range values are counted, see nnb_operand_range_events) */
   NNB_PREC_TF32 = 1,      /* single-pass TF32 tensor cores (fast, looser bound)     */
@@ -114,7 +114,7 @@ int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
  * LeakyReLU once per element and write the form the tensor-core convolution
  * gathers:
  *   NNB_PREC_FP32       per voxel and 32-channel group, 64 halves
- *                       [hi(32) | lo'(32)], hi = fp16(x), lo' = fp16(2^11 (x - hi));
+ *                       [hi(32) | lo(32)], hi = fp16(x), lo = fp16(x - hi);
  *                       |x| >= 65504 increments the range-event counter
  *                       (C % 32 == 0; out holds batch * voxels * C floats' bytes);
  *   NNB_PREC_FP32_TF32  per voxel [hi(C) | lo(C)], hi = x with the 13 low
@@ -152,7 +152,7 @@ int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, i
 /*
  * Build the tensor-core weight image from converted-layout weights: per N-tile
  * and K-step, [W_hi; W_lo] stacked along N -- NNB_PREC_FP32: fp16 rows
- * W0 = fp16(s w), W1' = fp16(2^11 (s w - W0)) in 64-byte swizzled K-major
+ * W0 = fp16(s w), W1 = fp16(s w - W0) in 64-byte swizzled K-major
  * rows, s a power of two per output column (max |s w| < 2^14), followed by
  * the float 1/s of every column; NNB_PREC_FP32_TF32: TF32 hi/lo rows;
  * NNB_PREC_TF32: TF32 rows (128-byte swizzled K-major rows).  The image must start on a 1024-byte boundary.  Replaces the

@@ -47,7 +47,7 @@ void set_error(const char* fmt, ...);
 // Tensor-core operand formats (see nnb_prepare_operand).
 constexpr int kOperandTf32 = 0;    // one TF32 value per element
 constexpr int kOperandTf32x2 = 1;  // TF32 hi/lo pair
-constexpr int kOperandF16x2 = 2;   // fp16 hi + 2^-11 lo' pair
+constexpr int kOperandF16x2 = 2;   // fp16 hi + lo pair
 
 inline bool tensor_precision(int precision) {
   return precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32 || precision == NNB_PREC_FP32_TF32;

@@ -567,8 +567,8 @@ namespace nnb {
 // activation that applies its instance-norm affine + LeakyReLU once per
 // element (instead of once per tap inside the convolution) and writes the
 // form the MMA consumes:
-//   kOperandF16x2   per voxel and 32-channel group [hi(32) | lo'(32)] as
-//                   halves, hi = fp16(x), lo' = fp16(2^11 (x - hi)); an element
+//   kOperandF16x2   per voxel and 32-channel group [hi(32) | lo(32)] as
+//                   halves, hi = fp16(x), lo = fp16(x - hi); an element
 //                   with |x| >= 65504 (no finite fp16 hi) increments
 //                   g_operand_range_events.  4 bytes read, 4 written.
 //   kOperandTf32x2  per voxel [hi(C) | lo(C)], hi = x with the 13 low mantissa
@@ -597,8 +597,8 @@ __global__ void prepare_operand_kernel(nnb_segment in, int64_t voxels_total, int
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
         const __half h0 = __float2half_rn(v[e]), h1 = __float2half_rn(v[e + 1]);
-        const __half l0 = __float2half_rn((v[e] - __half2float(h0)) * 2048.f);
-        const __half l1 = __float2half_rn((v[e + 1] - __half2float(h1)) * 2048.f);
+        const __half l0 = __float2half_rn(v[e] - __half2float(h0));
+        const __half l1 = __float2half_rn(v[e + 1] - __half2float(h1));
         hi[e / 2] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
         lo[e / 2] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
         over += (fabsf(v[e]) >= 65504.f) + (fabsf(v[e + 1]) >= 65504.f);

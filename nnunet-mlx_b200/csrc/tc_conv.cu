@@ -7,12 +7,13 @@
 // thread touches activations in the main loop.  Operand formats (template OP):
 //
 //  * kOperandF16x2 (float32-level accuracy, the default): per 32 channels one
-//    128-byte row [hi(32) | lo'(32)] of halves, x ~ hi + 2^-11 lo'.  B stacks
-//    [W0 ; W1'] along N (W0 = fp16(s w), W1' = fp16(2^11 (s w - W0)), s a
-//    power of two per output column), so per 16-channel sub-step
-//    A_hi x [W0;W1'] (N = 2 BC) and A_lo' x W0 (N = BC, into the second half)
-//    form the three leading products in two MMAs of kind::f16; the epilogue
-//    returns (D0 + 2^-11 D1) / s.
+//    128-byte row [hi(32) | lo(32)] of halves, x ~ hi + lo (lo = fp16(x - hi),
+//    subnormal for small x, whose absolute error then stays below 2^-25).  B
+//    stacks [W0 ; W1] along N (W0 = fp16(s w), W1 = fp16(s w - W0), s a power
+//    of two per output column), so per 16-channel sub-step A_hi x [W0;W1]
+//    (N = 2 BC) and A_lo x W0 (N = BC, into the second half) form the three
+//    leading products in two MMAs of kind::f16; the epilogue returns
+//    (D0 + D1) / s.
 //  * kOperandTf32x2 (split TF32, any float32 magnitude): A hi and lo rows of 32
 //    TF32 values, B = [W_hi ; W_lo]; per 8-channel sub-step A_hi x [W_hi;W_lo]
 //    and A_lo x [W_hi;W_lo]; the epilogue adds the halves.
@@ -157,7 +158,7 @@ __device__ __forceinline__ uint64_t b_desc_at(uint32_t saddr) {
 // The MMAs of one K-step (32 input channels) into accumulator d.  ad: A rows
 // (hi part), bd: B tile, lo16: offset of the TF32 lo rows (kOperandTf32x2),
 // acc: 0 for the first K-step of a tile.  Descriptor offsets are in 16-byte
-// units: the fp16 lo' half of an A row starts 64 bytes in.
+// units: the fp16 lo half of an A row starts 64 bytes in.
 template <int BC, int OP>
 __device__ __forceinline__ void kstep_mmas(uint32_t d, uint64_t ad, uint64_t bd, uint32_t lo16, uint32_t acc) {
   if constexpr (OP == kOperandF16x2) {
@@ -210,7 +211,7 @@ __device__ __forceinline__ ChunkSource chunk_source(const nnb_conv3d_args& a, co
   const bool second = cg >= g.c0len;
   const int cl = second ? cg - g.c0len : cg;
   const int cs = second ? a.seg[1].channels : g.c0len;
-  if constexpr (OP == kOperandF16x2) return ChunkSource{&maps.seg[second ? 1 : 0], 2 * cl, 0};  // [hi | lo'] halves
+  if constexpr (OP == kOperandF16x2) return ChunkSource{&maps.seg[second ? 1 : 0], 2 * cl, 0};  // [hi | lo] halves
   else return ChunkSource{&maps.seg[second ? 1 : 0], cl, cs + cl};
 }
 
@@ -221,6 +222,9 @@ struct SharedMisc {
   volatile int* votes;  // [4]
   float* red;           // [4][32]
   float* col_mean;      // [32]
+  volatile int* votes2;  // second epilogue group (z-streaming mode): [4], [4][32], [32]
+  float* red2;
+  float* col_mean2;
 };
 
 __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
@@ -231,16 +235,20 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
   m.votes = reinterpret_cast<volatile int*>(m.tmem_slot + 2);
   m.red = reinterpret_cast<float*>(misc + 512);
   m.col_mean = reinterpret_cast<float*>(misc + 1024);
+  m.red2 = reinterpret_cast<float*>(misc + 1152);
+  m.col_mean2 = reinterpret_cast<float*>(misc + 1664);
+  m.votes2 = reinterpret_cast<volatile int*>(misc + 1792);
   return m;
 }
 
 // One finished accumulator -> outputs + partials (or the transposed-conv scatter).
-// acc: TMEM address of the tile's (hi) accumulator columns for this warp's lanes; acc_lo: of the lo / mix
-// columns (split formats).
+// acc: TMEM address of the tile's (hi) accumulator columns for this warp's lanes; acc_lo: of the second
+// accumulator of the split formats, or 0 when one accumulator holds every product (z-streaming mode).
+// bar: named barrier of the four epilogue warps working on this tile.
 template <int BC, int OP>
 __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Geometry& g, const TileOrigin& o,
                                               uint32_t acc, uint32_t acc_lo, int q, int lane, float* red,
-                                              float* col_mean, const float* __restrict__ col_inv) {
+                                              float* col_mean, const float* __restrict__ col_inv, int bar = 1) {
   const int row = q * 32 + lane;
   const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
   const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
@@ -255,11 +263,15 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
     float v[32];
     tmem_ld32(acc + cc * 32, v);
     if constexpr (OP == kOperandF16x2) {
-      // (sum a0 W0 + 2^-11 sum (a0 W1' + a1' W0)) / s of the column
-      float u[32];
-      tmem_ld32(acc_lo + cc * 32, u);
+      // (sum a_hi W0 + sum (a_hi W1 + a_lo W0)) / s of the column; acc_lo == 0: one accumulator holds all
+      if (acc_lo != 0u) {
+        float u[32];
+        tmem_ld32(acc_lo + cc * 32, u);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = fmaf(u[i], 1.f / 2048.f, v[i]) * __ldg(col_inv + nbase + i);
+        for (int i = 0; i < 32; ++i) v[i] += u[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= __ldg(col_inv + nbase + i);
     } else if constexpr (OP == kOperandTf32x2) {
       float u[32];
       tmem_ld32(acc_lo + cc * 32, u);
@@ -309,10 +321,10 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
 #pragma unroll
       for (int i = 0; i < 32; ++i) xs[i] = v[i];
       red[q * 32 + lane] = warp_column_sums(xs);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
       const float total = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
       if (q == 0) col_mean[lane] = total / (float)nvalid;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float dv = valid ? v[i] - col_mean[i] : 0.f;
@@ -320,14 +332,14 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
       }
       const float colm2 = warp_column_sums(xs);
       red[q * 32 + lane] = colm2;  // every warp read red before the barrier above
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
       if (q == 0 && nbase + lane < a.cout) {
         float* p = a.partials + (((int64_t)o.b * g.tps + o.t) * a.cout + nbase + lane) * 3;
         p[0] = total;
         p[1] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
         p[2] = (float)nvalid;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
     }
   }
 }
@@ -726,27 +738,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 // runs of all CTAs split the volume's planes evenly).  Each input plane u of a
 // column is loaded once (one halo plane box per 32-channel chunk) and, per
 // (ky, kx) tap and 16-channel sub-step, multiplied by the weights of all
-// three kz taps stacked along N:
-//   A_hi  x [W0(kz0); W0(kz1); W0(kz2)]   -> hi ring
-//   A_hi  x [W1'(kz0); W1'(kz1); W1'(kz2)] -> mix ring
-//   A_lo' x [W0(kz0); W0(kz1); W0(kz2)]   -> mix ring
-// (N = 96), where block kz feeds output plane u + 1 - kz.  The accumulators
-// of consecutive output planes sit in a TMEM ring of 8 slots of 32 columns
-// (hi: columns [0, 256), mix: [256, 512)), slot 7 - (P mod 8) for the P-th
-// plane of the CTA's sequence, so the three planes an input feeds occupy
-// adjacent ascending slots and one MMA covers them (two where the ring wraps).
+// three kz taps stacked along N (N = 96; block kz feeds output plane
+// u + 1 - kz), three products into the same accumulators:
+//   A_hi x [W0(kz0); W0(kz1); W0(kz2)],  A_hi x [W1(kz0..2)],  A_lo x [W0(kz0..2)].
+// The accumulators of consecutive output planes sit in a TMEM ring of 16
+// slots of 32 columns, slot 15 - (P mod 16) for the P-th plane of the CTA's
+// sequence, so the three planes an input feeds occupy adjacent ascending
+// slots and one MMA covers them (two where the ring wraps, 1 plane in 8).
 // Output plane u - 1 is complete after input u.  The epilogue reads a
 // complete plane, writes it (planes outside the run -- the halo planes of a
-// partial column -- are only discarded), zeroes its slots and releases them,
-// so every MMA accumulates.  A column costs 3 MMAs per (tap, sub-step, input
+// partial column -- are only discarded), zeroes its slot and releases it, so
+// every MMA accumulates.  A column costs 3 MMAs per (tap, sub-step, input
 // plane) instead of 6 per output plane, and each input plane is read once
 // instead of three times.  The 27 taps' weights of a single-chunk layer stay
 // resident in shared memory for the whole kernel (rearranged from the weight
 // image by bulk copies); wider inputs stream one (chunk, ky) row of stacked
 // weights per stage.
 // ---------------------------------------------------------------------------
-constexpr int kZsSlots = 8;
-constexpr int kZsRows = 6 * 32;  // stacked rows per (ky, kx) tap: [W0 x 3 kz ; W1' x 3 kz]
+constexpr int kZsSlots = 16;
+constexpr int kZsRows = 6 * 32;  // stacked rows per (ky, kx) tap: [W0 x 3 kz ; W1 x 3 kz]
 
 struct ZsRun {
   int64_t idx, end;  // [idx, end) of the column-major, z-fastest output-plane sequence
@@ -776,30 +786,38 @@ __device__ __forceinline__ bool zs_next(const Geometry& g, ZsRun& r, ZsSegment& 
 
 __device__ __forceinline__ int zs_slot(int P) { return kZsSlots - 1 - (P & (kZsSlots - 1)); }
 
-// The three MMAs of one (tap, 16-channel sub-step) into the planes' slots: ad / bd the A (hi) and
-// stacked-B descriptors, s0 the slot of block kz = 0.  Blocks past slot 7 continue at slot 0.
-__device__ __forceinline__ void zs_mmas(uint32_t tmem, int s0, uint64_t ad, uint64_t bd) {
-  constexpr uint32_t id96 = idesc_f16(BM, 96), id64 = idesc_f16(BM, 64), id32 = idesc_f16(BM, 32);
-  constexpr uint32_t kMix16 = (3 * 32 * 64) >> 4;  // W1' blocks start 96 rows in
-  const uint32_t hi = tmem + 32u * (uint32_t)s0, mix = hi + 256u;
-  if (s0 <= kZsSlots - 3) {
-    mma_f16_ss(hi, ad, bd, id96, 1u);
-    mma_f16_ss(mix, ad, bd + kMix16, id96, 1u);
-    mma_f16_ss(mix, ad + 4, bd, id96, 1u);
-  } else {
-    const int n1 = kZsSlots - s0;  // blocks before the wrap (1 or 2)
-    const uint32_t idA = n1 == 2 ? id64 : id32, idB = n1 == 2 ? id32 : id64;
-    const uint64_t bB = bd + (uint64_t)(n1 * ((32 * 64) >> 4));
-    mma_f16_ss(hi, ad, bd, idA, 1u);
-    mma_f16_ss(tmem, ad, bB, idB, 1u);
-    mma_f16_ss(mix, ad, bd + kMix16, idA, 1u);
-    mma_f16_ss(tmem + 256u, ad, bB + kMix16, idB, 1u);
-    mma_f16_ss(mix, ad + 4, bd, idA, 1u);
-    mma_f16_ss(tmem + 256u, ad + 4, bB, idB, 1u);
-  }
+// The MMAs of one row of taps (ky fixed; kx = 0..2; two 16-channel sub-steps each) into the slots of the
+// three planes an input feeds (d: TMEM address of slot s0).  N1 = 3: the slots s0..s0+2 are adjacent, three
+// MMAs of N = 96 per (tap, sub-step); N1 = 1 or 2: the ring wraps after N1 blocks, so each MMA splits into
+// N = 32 N1 at s0 and N = 32 (3 - N1) at slot 0.  arow / brow: A (hi) and stacked-B descriptors of the
+// row's kx = 0 tap; the lo half of an A row starts 64 bytes in, the W1 blocks 96 B rows in.
+template <int N1>
+__device__ __forceinline__ void zs_row(uint32_t tmem, uint32_t d, uint64_t arow, uint64_t brow) {
+  constexpr uint32_t kTap16 = (kZsRows * 64) >> 4;
+  constexpr uint32_t kW116 = (3 * 32 * 64) >> 4;
+  constexpr uint32_t idA = idesc_f16(BM, 32 * N1);
+#pragma unroll
+  for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const uint64_t ad = arow + (uint64_t)(8 * kx + 2 * kk);
+      const uint64_t bd = brow + (uint64_t)(kx * kTap16 + 2 * kk);
+      mma_f16_ss(d, ad, bd, idA, 1u);
+      mma_f16_ss(d, ad, bd + kW116, idA, 1u);
+      mma_f16_ss(d, ad + 4, bd, idA, 1u);
+      if constexpr (N1 < 3) {
+        constexpr uint32_t idB = idesc_f16(BM, 32 * (3 - N1));
+        constexpr uint32_t kSplit16 = (N1 * 32 * 64) >> 4;
+        mma_f16_ss(tmem, ad, bd + kSplit16, idB, 1u);
+        mma_f16_ss(tmem, ad, bd + kW116 + kSplit16, idB, 1u);
+        mma_f16_ss(tmem, ad + 4, bd + kSplit16, idB, 1u);
+      }
+    }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+constexpr int kZsThreads = 10 * 32;  // producer, MMA issuer, two epilogue warpgroups taking alternate planes
+
+__global__ void __launch_bounds__(kZsThreads, 1)
     conv3d_zstream_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
   constexpr int BC = 32;
   using C = Cfg<BC, kOperandF16x2>;
@@ -848,7 +866,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *sm.tmem_slot;
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     // every slot starts at zero: the MMAs always accumulate
     const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
 #pragma unroll 1
@@ -865,8 +883,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       bool alive = true;
       if (resident) {
-        // stacked rows of tap (ky, kx): [W0(kz0..2) ; W1'(kz0..2)], 32 rows each, from the image's
-        // [W0 ; W1'] tile of tap (kz, ky, kx)
+        // stacked rows of tap (ky, kx): [W0(kz0..2) ; W1(kz0..2)], 32 rows each, from the image's
+        // [W0 ; W1] tile of tap (kz, ky, kx)
         const uint32_t fb = smem_u32(&b_full[0]);
         mbar_arrive_expect_tx(fb, 9u * kTapBytes);
         for (int t = 0; t < 9; ++t)
@@ -958,18 +976,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_after();
           const int s0 = zs_slot(Pn);
+          const uint32_t dslot = tmem + 32u * (uint32_t)s0;
           for (int c = 0; c < g.nchunk && alive; ++c) {
             const uint64_t ap = adesc0 + (uint64_t)(sa * entry16 + c * plane16);
             if (resident) {
+              // the wrap case is uniform per input plane: one straight-line row variant per case
+              if (s0 <= kZsSlots - 3) {
 #pragma unroll 1
-              for (int ky = 0; ky < 3; ++ky) {
-                const uint64_t arow = ap + (uint64_t)(ky * row16);
-                const uint64_t brow = bdesc0 + (uint64_t)(ky * 3 * kTap16);
-#pragma unroll
-                for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                  for (int kk = 0; kk < 2; ++kk)
-                    zs_mmas(tmem, s0, arow + (uint64_t)(8 * kx + 2 * kk), brow + (uint64_t)(kx * kTap16 + 2 * kk));
+                for (int ky = 0; ky < 3; ++ky)
+                  zs_row<3>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+              } else if (s0 == kZsSlots - 2) {
+#pragma unroll 1
+                for (int ky = 0; ky < 3; ++ky)
+                  zs_row<2>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+              } else {
+#pragma unroll 1
+                for (int ky = 0; ky < 3; ++ky)
+                  zs_row<1>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
               }
             } else {
               for (int ky = 0; ky < 3; ++ky) {
@@ -981,11 +1004,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 fence_after();
                 const uint64_t arow = ap + (uint64_t)(ky * row16);
                 const uint64_t brow = bdesc0 + (uint64_t)(sb * stage16);
-#pragma unroll
-                for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-                  for (int kk = 0; kk < 2; ++kk)
-                    zs_mmas(tmem, s0, arow + (uint64_t)(8 * kx + 2 * kk), brow + (uint64_t)(kx * kTap16 + 2 * kk));
+                if (s0 <= kZsSlots - 3)
+                  zs_row<3>(tmem, dslot, arow, brow);
+                else if (s0 == kZsSlots - 2)
+                  zs_row<2>(tmem, dslot, arow, brow);
+                else
+                  zs_row<1>(tmem, dslot, arow, brow);
                 mma_commit(smem_u32(&b_empty[sb]));
                 ++T;
               }
@@ -1010,7 +1034,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------ epilogue ---------------------------------
+    // group 0 (warps 2-5) takes the even planes of the sequence, group 1 (warps 6-9) the odd ones
     const int q = warp & 3;
+    const int grp = warp >= 6 ? 1 : 0;
+    const int bar = 1 + grp;
+    volatile int* votes = grp ? sm.votes2 : sm.votes;
+    float* red = grp ? sm.red2 : sm.red;
+    float* col_mean = grp ? sm.col_mean2 : sm.col_mean;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const float* col_inv = reinterpret_cast<const float*>(wimg + (int64_t)g.ksteps * C::kBBytes);
     int P = 0;
@@ -1021,15 +1051,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = sg.col / bricks, rem = sg.col - b * bricks;
       const int hb = rem / g.nw, wb = rem - hb * g.nw;
       for (int z = sg.ua - 1; z <= sg.ub + 1; ++z, ++P) {
+        if ((P & 1) != grp) continue;
         const int slot = zs_slot(P);
         const bool ok = mbar_wait(smem_u32(&accf[slot]), (P / kZsSlots) & 1, sm.abort_flag, 40);
-        if (lane == 0) sm.votes[q] = (!ok || *sm.abort_flag) ? 1 : 0;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        stop = sm.votes[0] | sm.votes[1] | sm.votes[2] | sm.votes[3];
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (lane == 0) votes[q] = (!ok || *sm.abort_flag) ? 1 : 0;
+        asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+        stop = votes[0] | votes[1] | votes[2] | votes[3];
+        asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
         if (stop) break;
         fence_after();
-        const uint32_t hi = tmem + lane_base + 32u * (uint32_t)slot, mix = hi + 256u;
+        const uint32_t acc = tmem + lane_base + 32u * (uint32_t)slot;
         if (z >= sg.z0 && z < sg.z1) {
           TileOrigin o;
           o.b = b;
@@ -1038,10 +1069,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           o.d0 = z;
           o.h0 = hb * kHaloH;
           o.w0 = wb * kHaloW;
-          epilogue_tile<BC, kOperandF16x2>(a, g, o, hi, mix, q, lane, sm.red, sm.col_mean, col_inv);
+          epilogue_tile<BC, kOperandF16x2>(a, g, o, acc, 0u, q, lane, red, col_mean, col_inv, bar);
         }
-        tmem_zero32(hi);
-        tmem_zero32(mix);
+        tmem_zero32(acc);
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&acce[slot]));
@@ -1063,8 +1093,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   [BC, 2 BC) W_lo (kOperandTf32x2), or BC rows of TF32.
 //   kOperandF16x2: 64-byte rows of halves, 16-byte chunks XOR-swizzled by
 //   (row / 2) % 4 (the SW64 K-major layout); rows [0, BC) W0 = fp16(s w), rows
-//   [BC, 2 BC) W1' = fp16(2^11 (s w - W0)); after the tiles, 1/s of every
-//   column (n_tiles * BC floats).
+//   [BC, 2 BC) W1 = fp16(s w - W0); after the tiles, 1/s of every column
+//   (n_tiles * BC floats).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float weight_at(const float* __restrict__ w, int col, int tap, int ci, int kvol,
                                            int cin_total, int row_taps, int up_cout) {
@@ -1160,7 +1190,7 @@ __global__ void pack_f16x2_kernel(const float* __restrict__ w, int cols_total, i
       float val = 0.f;
       if (col < cols_total && ci < cin_total) val = weight_at(w, col, tap, ci, kvol, cin_total, row_taps, up_cout) * s;
       const __half h0 = __float2half_rn(val);
-      const __half h = half == 0 ? h0 : __float2half_rn((val - __half2float(h0)) * 2048.f);
+      const __half h = half == 0 ? h0 : __float2half_rn(val - __half2float(h0));
       res |= (uint32_t)__half_as_ushort(h) << (16 * e);
     }
     out[o] = res;
@@ -1335,7 +1365,7 @@ inline EncodeTiledFn encode_tiled() {
 }
 
 // 5-D map (elements per voxel, W, H, D, batch) of one prepared operand; the box
-// is one 128-byte row (32 floats, or 64 halves = [hi | lo'] of 32 channels) x
+// is one 128-byte row (32 floats, or 64 halves = [hi | lo] of 32 channels) x
 // the mode's box extent, sampled every stride voxels.
 inline int encode_operand(const nnb_segment& seg, int op, int batch, const Geometry& g, CUtensorMap* map) {
   const EncodeTiledFn fn = encode_tiled();
@@ -1388,7 +1418,7 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
       const int b_bytes = g.sb == 0 ? 9 * kZsRows * 64 : g.sb * 3 * kZsRows * 64;
       const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes;
       NNB_REQUIRE(smem <= kMaxSmem, "conv3d: z-streaming plan exceeds shared memory (%d bytes)", smem);
-      conv3d_zstream_kernel<<<grid, kThreads, smem, stream>>>(a, g, maps);
+      conv3d_zstream_kernel<<<grid, kZsThreads, smem, stream>>>(a, g, maps);
     } else {
       NNB_REQUIRE(false, "conv3d: internal: z-streaming plan for an unsupported tile");
     }

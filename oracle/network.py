@@ -182,13 +182,14 @@ def tf32_round(t: torch.Tensor) -> torch.Tensor:
 
 
 def fp16_pair(t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """Split float32 values into the fp16-pair operand: ``hi = fp16(t)``, ``lo' = fp16(2^11 (t - hi))``.
+    """Split float32 values into the fp16-pair operand: ``hi = fp16(t)``, ``lo = fp16(t - hi)``.
 
-    ``hi + 2^-11 lo'`` reproduces ``t`` to ~2^-22 relative while ``|t| < 65504``.
-    Used only by tests that check the numerics of the default tensor-core mode.
+    ``hi + lo`` reproduces ``t`` to ~2^-22 relative, or 2^-25 absolute where
+    ``lo`` is subnormal, while ``|t| < 65504``.  Used only by tests that check
+    the numerics of the default tensor-core mode.
     """
     hi = t.to(torch.float16).to(torch.float32)
-    lo = ((t - hi) * 2048.0).to(torch.float16).to(torch.float32)
+    lo = (t - hi).to(torch.float16).to(torch.float32)
     return hi, lo
 
 
@@ -198,9 +199,9 @@ def fp16_pair_products(op, transposed: bool = False):
     Activations split with :func:`fp16_pair`; weights scaled by a power of two
     per GEMM column (output channel, or (output channel, tap) for a stride ==
     kernel transposed convolution) so that their maximum is below 2^14, then
-    split.  The result is ``conv(a_hi, w_hi) + 2^-11 (conv(a_hi, w_lo') +
-    conv(a_lo', w_hi))`` divided by the column scale, the sum the tensor-core
-    epilogue forms.  Test infrastructure only.
+    split.  The result is ``conv(a_hi, w_hi) + conv(a_hi, w_lo) + conv(a_lo,
+    w_hi)`` divided by the column scale, the sum the tensor cores form.  Test
+    infrastructure only.
     """
     def conv(x, w, b=None, **kwargs):
         # weight layout: conv (C_out, C_in, *k); transposed conv (C_in, C_out, *k)
@@ -210,7 +211,7 @@ def fp16_pair_products(op, transposed: bool = False):
         scale = torch.from_numpy(np.where(m > 0, np.ldexp(1.0, 14 - e), 1.0).astype(np.float32))
         a_hi, a_lo = fp16_pair(x)
         w_hi, w_lo = fp16_pair(w * scale)
-        out = op(a_hi, w_hi, None, **kwargs) + (op(a_hi, w_lo, None, **kwargs) + op(a_lo, w_hi, None, **kwargs)) / 2048.0
+        out = op(a_hi, w_hi, None, **kwargs) + (op(a_hi, w_lo, None, **kwargs) + op(a_lo, w_hi, None, **kwargs))
         channel = (1, -1) + (1,) * (x.ndim - 2)
         if transposed:
             # output position p along an axis was produced by tap p % k
