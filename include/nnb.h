@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 6
+#define NNB_ABI_VERSION 8
 
 enum nnb_status {
   NNB_OK = 0,
@@ -59,6 +59,9 @@ typedef struct nnb_segment {
   const float* shift;  /* (B, channels), required when scale != NULL */
   int32_t channels;
   int32_t leaky;       /* 1: LeakyReLU(slope) after the affine */
+  int32_t prepared;    /* operand_format 2 only: 1 = `data` holds nnb_prepare_operand(NNB_PREC_FP32)
+                          output of the activation (scale must be NULL); 0 = raw */
+  int32_t reserved;    /* 0 */
 } nnb_segment;
 
 typedef struct nnb_conv3d_args {
@@ -81,7 +84,11 @@ typedef struct nnb_conv3d_args {
   int32_t precision;    /* enum nnb_precision */
   int32_t operand_format; /* 0: raw float32 segments (lazy affine allowed; CUDA-core kernel);
                              1: segments prepared by nnb_prepare_operand for `precision`
-                             (tensor-core kernel; scale/shift must be NULL) */
+                             (tensor-core kernel; scale/shift must be NULL);
+                             2: raw float32 segments (lazy affine allowed) read by the
+                             tensor-core kernel, which prepares them itself, or segments
+                             flagged `prepared` -- only where nnb_conv3d_raw_operands(args)
+                             returns 1 */
 } nnb_conv3d_args;
 
 /* Library identity. */
@@ -110,6 +117,18 @@ int32_t nnb_device_status(int32_t* where, int32_t reset);
 int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
 
 /*
+ * 1 when the tensor-core path for `args` (shape fields, precision,
+ * num_segments and segment channels read) takes raw lazy segments
+ * (operand_format 2): NNB_PREC_FP32 3x3x3 stride-1 padding-1 convolutions
+ * with <= 32 output channels and a LeakyReLU slope in [0, 1], whose kernel
+ * applies the affine + LeakyReLU and the fp16-pair split to each input plane
+ * in shared memory (replacing the nnb_prepare_operand pass); 0 otherwise.  Replaces nothing in the reference
+ * (MLX materialises the normalised activation,
+ * src/nnunet_mlx/kernels/metal_native_norm.py:62-70).
+ */
+int32_t nnb_conv3d_raw_operands(const nnb_conv3d_args* args);
+
+/*
  * Tensor-core operand preparation: apply a lazy activation's affine +
  * LeakyReLU once per element and write the form the tensor-core convolution
  * gathers:
@@ -128,9 +147,11 @@ int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t vox
                             int32_t precision, float* out, void* stream);
 
 /*
- * Number of activation elements nnb_prepare_operand(NNB_PREC_FP32) found at or
- * above 65504 in magnitude (outside the fp16 range of the split operand) on
- * the current device since the last reset; reset != 0 zeroes the counter.
+ * Count of out-of-range fp16-pair operands on the current device since the
+ * last reset: activation elements nnb_prepare_operand(NNB_PREC_FP32) found at
+ * or above 65504 in magnitude, plus at least one per affected thread where a
+ * tensor-core convolution prepared raw operands itself (operand_format 2);
+ * reset != 0 zeroes the counter.
  * Synchronises with the device.  A non-zero count means results computed with
  * NNB_PREC_FP32 since the reset must be recomputed with NNB_PREC_FP32_TF32.
  * No reference counterpart (the reference computes in float32).

@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 6
+ABI_VERSION = 8
 
 PREC_FP32 = 0        # split fp16 pairs on the tensor cores, float32-level accuracy (|activation| < 65504)
 PREC_TF32 = 1        # single-pass TF32 tensor cores
@@ -32,7 +32,8 @@ I32x3 = ctypes.c_int32 * 3
 
 class Segment(ctypes.Structure):
     _fields_ = [("data", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("shift", ctypes.c_void_p),
-                ("channels", ctypes.c_int32), ("leaky", ctypes.c_int32)]
+                ("channels", ctypes.c_int32), ("leaky", ctypes.c_int32), ("prepared", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 class Conv3dArgs(ctypes.Structure):
@@ -54,6 +55,7 @@ SYMBOLS = {
                                                 ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_conv3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
     "nnb_operand_range_events": (ctypes.c_int64, [ctypes.c_int32]),
+    "nnb_conv3d_raw_operands": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs)]),
     "nnb_prepare_operand": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_conv3d_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

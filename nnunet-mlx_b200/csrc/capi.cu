@@ -21,6 +21,7 @@ void set_error(const char* fmt, ...) {
 // kernels implemented in the other translation units
 int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream);
 bool conv3d_tc_supported(const nnb_conv3d_args& a);
+bool conv3d_tc_raw_operands(const nnb_conv3d_args& a);
 int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream);
 int64_t conv3d_tc_packed_bytes(int cout, int kvol, int cin_total, int precision);
 int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int precision, void* packed,
@@ -102,11 +103,27 @@ int32_t nnb_conv3d(const nnb_conv3d_args* a, void* stream) {
     NNB_REQUIRE(conv3d_tc_supported(*a), "conv3d: shape outside the tensor-core envelope");
     return launch_conv3d_tc(*a, st);
   }
+  if (a->operand_format == 2) {
+    NNB_REQUIRE(a->packed != nullptr && conv3d_tc_supported(*a) && conv3d_tc_raw_operands(*a),
+                "conv3d: raw tensor-core operands are outside the z-streaming envelope");
+    for (int s = 0; s < a->num_segments; ++s) {
+      NNB_REQUIRE(a->seg[s].scale == nullptr || a->seg[s].shift != nullptr, "conv3d: lazy segment without shift");
+      NNB_REQUIRE(!a->seg[s].prepared || a->seg[s].scale == nullptr, "conv3d: prepared segments carry no lazy affine");
+    }
+    return launch_conv3d_tc(*a, st);
+  }
   NNB_REQUIRE(a->operand_format == 0, "conv3d: unknown operand_format %d", a->operand_format);
   // Raw float32 operands run on the CUDA-core kernel in plain float32 (used for
   // the few-channel first layer and shapes outside the tensor-core envelope),
   // which also satisfies the requested accuracy.
   return launch_conv3d_simt(*a, st);
+}
+
+int32_t nnb_conv3d_raw_operands(const nnb_conv3d_args* a) {
+  if (a == nullptr || a->num_segments < 1 || a->num_segments > 2) return 0;
+  for (int i = 0; i < 3; ++i)
+    if (a->in_dims[i] < 1 || a->out_dims[i] < 1 || a->kernel[i] < 1 || a->stride[i] < 1) return 0;
+  return conv3d_tc_raw_operands(*a) ? 1 : 0;
 }
 
 int32_t nnb_prepare_operand(const nnb_segment* input, int32_t batch, int64_t voxels, float slope, int32_t precision,
@@ -136,7 +153,7 @@ int64_t nnb_conv3d_partial_tiles(const nnb_conv3d_args* a) {
   NNB_REQUIRE(a != nullptr, "conv3d_partial_tiles: null args");
   NNB_REQUIRE(positive3(a->out_dims) && positive3(a->kernel) && positive3(a->stride),
               "conv3d_partial_tiles: dims, kernel and stride must be positive");
-  if (a->operand_format == 1) {
+  if (a->operand_format == 1 || a->operand_format == 2) {
     NNB_REQUIRE(a->num_segments == 1 || a->num_segments == 2, "conv3d_partial_tiles: 1 or 2 input segments");
     return conv3d_tc_partial_tiles(*a);
   }

@@ -635,7 +635,7 @@ __global__ void prepare_operand_kernel(nnb_segment in, int64_t voxels_total, int
   }
 }
 
-static unsigned long long* range_events_ptr() {
+unsigned long long* operand_range_events_ptr() {
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_operand_range_events) != cudaSuccess) return nullptr;
   return static_cast<unsigned long long*>(p);
@@ -647,7 +647,7 @@ int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, flo
               "prepare_operand: channels must be a multiple of %d", op == kOperandF16x2 ? 32 : 8);
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(in.data) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
               "prepare_operand: 16-byte aligned tensors required");
-  unsigned long long* events = range_events_ptr();
+  unsigned long long* events = operand_range_events_ptr();
   NNB_REQUIRE(events != nullptr, "prepare_operand: range-event counter unavailable: %s",
               cudaGetErrorString(cudaGetLastError()));
   const int64_t total = (int64_t)batch * voxels * (in.channels / 8);

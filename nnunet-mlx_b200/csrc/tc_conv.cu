@@ -98,7 +98,8 @@ struct Geometry {
   int box[3];                  // TMA box extent along w, h, d (elements, before element strides)
   int pw, plane_rows, plane_bytes;  // halo plane: row pitch, rows, bytes per half (1024-aligned)
   int sa, sb, tb;              // halo-mode ring depths (A planes, B stages) and taps per B stage
-  int zs;                      // 1: z-streaming mode (sb = 0: weights resident in shared memory)
+  int zs;                      // 1: z-streaming mode on raw lazy segments (sb = 0: resident weights)
+  unsigned long long* range_events;  // fp16-pair range counter (z-streaming mode's in-kernel preparation)
 };
 
 struct OperandMaps {
@@ -750,7 +751,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // partial column -- are only discarded), zeroes its slot and releases it, so
 // every MMA accumulates.  A column costs 3 MMAs per (tap, sub-step, input
 // plane) instead of 6 per output plane, and each input plane is read once
-// instead of three times.  The 27 taps' weights of a single-chunk layer stay
+// instead of three times.  The input planes are the raw float32 activation
+// (a lazy segment of the previous layer): two transform warps convert each
+// landed plane in place -- instance-norm affine + LeakyReLU, zero for the
+// padding rows, fp16 hi / lo split into the MMA's [hi | lo] row layout, and
+// the fp16 range count -- so the activation makes no extra trip through HBM.  The 27 taps' weights of a single-chunk layer stay
 // resident in shared memory for the whole kernel (rearranged from the weight
 // image by bulk copies); wider inputs stream one (chunk, ky) row of stacked
 // weights per stage.
@@ -815,7 +820,82 @@ __device__ __forceinline__ void zs_row(uint32_t tmem, uint32_t d, uint64_t arow,
     }
 }
 
-constexpr int kZsThreads = 10 * 32;  // producer, MMA issuer, two epilogue warpgroups taking alternate planes
+// producer, MMA issuer, two epilogue warpgroups taking alternate planes, two operand-transform warps
+constexpr int kZsThreads = 12 * 32;
+
+// In-place conversion of one landed raw plane box (rows of 32 float32 channels, 128-byte swizzled) into
+// the [hi(32) | lo(32)] fp16 rows the MMA reads, by 64 threads, one whole row per thread at a time (the
+// row's eight 16-byte chunks are all read before any is written, so no other thread touches it).  aff:
+// the chunk's 32 scales then 32 shifts (identity for a raw segment).  Padding rows become zeros.
+// Returns whether any value reached the fp16 range limit.
+__device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometry& g, const float* aff,
+                                                   bool leaky_act, int w0, int h0, float slope, int t) {
+  float amax = 0.f;
+  for (int r = t; r < g.plane_rows; r += 64) {
+    uint8_t* row = plane + r * 128;
+    const int sw = r & 7;
+    const int hh = r / g.pw, ww = r - hh * g.pw;
+    if ((unsigned)(w0 + ww) >= (unsigned)g.IW || (unsigned)(h0 + hh) >= (unsigned)g.IH) {
+      // padding row: the normalised activation there is zero
+#pragma unroll
+      for (int k = 0; k < 8; ++k) *reinterpret_cast<uint4*>(row + (k << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      continue;
+    }
+    float4 x[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] = *reinterpret_cast<const float4*>(row + ((k ^ sw) << 4));
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 sc = *reinterpret_cast<const float4*>(aff + 4 * k);
+      const float4 sh = *reinterpret_cast<const float4*>(aff + 32 + 4 * k);
+      float v[4] = {fmaf(x[k].x, sc.x, sh.x), fmaf(x[k].y, sc.y, sh.y), fmaf(x[k].z, sc.z, sh.z),
+                    fmaf(x[k].w, sc.w, sh.w)};
+      float h[4], l[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (leaky_act) v[e] = fmaxf(v[e], v[e] * slope);  // LeakyReLU for 0 <= slope <= 1
+        amax = fmaxf(amax, fabsf(v[e]));
+        // hi: v with the 13 low mantissa bits cleared (exactly an fp16 value in fp16's normal range),
+        // lo = v - hi exactly; both are then rounded to fp16
+        h[e] = __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u);
+        l[e] = v[e] - h[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const __half2 hh2 = __floats2half2_rn(h[e], h[e + 1]);
+        const __half2 ll2 = __floats2half2_rn(l[e], l[e + 1]);
+        hi[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&hh2);
+        lo[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&ll2);
+      }
+    }
+    // hi halves of channels 8m..8m+7 form logical chunk m, the lo halves chunk 4 + m
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      *reinterpret_cast<uint4*>(row + ((m ^ sw) << 4)) = make_uint4(hi[4 * m], hi[4 * m + 1], hi[4 * m + 2], hi[4 * m + 3]);
+      *reinterpret_cast<uint4*>(row + (((4 + m) ^ sw) << 4)) =
+          make_uint4(lo[4 * m], lo[4 * m + 1], lo[4 * m + 2], lo[4 * m + 3]);
+    }
+  }
+  return amax >= 65504.f;
+}
+
+// This warp's copy of the chunks' affine table for sample b (warp-local: no barrier another warp could miss).
+__device__ __forceinline__ void zs_load_affine(const nnb_conv3d_args& a, const Geometry& g, int b, float* aff,
+                                               int lane) {
+  __syncwarp();  // the warp no longer reads the previous sample's table
+  for (int i = lane; i < g.nchunk * 64; i += 32) {
+    const int c = i >> 6, k = i & 63, ch = k & 31;
+    const int cg = c * BK;
+    const bool second = cg >= g.c0len;
+    const nnb_segment& seg = a.seg[second ? 1 : 0];
+    const int idx = b * seg.channels + (second ? cg - g.c0len : cg) + ch;
+    float v = k < 32 ? 1.f : 0.f;
+    if (seg.scale != nullptr) v = k < 32 ? __ldg(seg.scale + idx) : __ldg(seg.shift + idx);
+    aff[i] = v;
+  }
+  __syncwarp();
+}
 
 __global__ void __launch_bounds__(kZsThreads, 1)
     conv3d_zstream_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
@@ -832,9 +912,10 @@ __global__ void __launch_bounds__(kZsThreads, 1)
   uint8_t* a_ring = smem;
   uint8_t* b_ring = smem + SA * a_entry;
   const SharedMisc sm = shared_misc(b_ring + b_bytes);
-  uint64_t* a_full = sm.bars;
+  uint64_t* a_full = sm.bars;         // raw plane landed (TMA)
   uint64_t* a_empty = a_full + SA;
-  uint64_t* b_full = a_empty + SA;    // SB stages, or [0] = resident weights
+  uint64_t* a_ready = a_empty + SA;   // plane converted to MMA operand rows (transform warps)
+  uint64_t* b_full = a_ready + SA;    // SB stages, or [0] = resident weights
   uint64_t* b_empty = b_full + max(SB, 1);
   uint64_t* accf = b_empty + max(SB, 1);
   uint64_t* acce = accf + kZsSlots;
@@ -843,11 +924,14 @@ __global__ void __launch_bounds__(kZsThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int bricks = g.nh * g.nw;
+  // per transform warp: [nchunk][scale 32 | shift 32]
+  float* aff = reinterpret_cast<float*>(b_ring + b_bytes + kMiscBytes) + (warp >= 10 ? (warp - 10) * g.nchunk * 64 : 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
       mbar_init(smem_u32(&a_full[s]), 1);
       mbar_init(smem_u32(&a_empty[s]), 1);
+      mbar_init(smem_u32(&a_ready[s]), 2);
     }
     for (int s = 0; s < max(SB, 1); ++s) {
       mbar_init(smem_u32(&b_full[s]), 1);
@@ -909,7 +993,10 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           const uint32_t fa = smem_u32(&a_full[sa]);
           mbar_arrive_expect_tx(fa, (uint32_t)(g.nchunk * g.plane_rows * 128));
           for (int c = 0; c < g.nchunk; ++c) {
-            const ChunkSource src = chunk_source<kOperandF16x2>(a, g, maps, c);
+            // raw float32 plane of the chunk's 32 channels, or its [hi | lo] fp16 rows when prepared
+            const ChunkSource src = a.seg[c * BK >= g.c0len ? 1 : 0].prepared
+                                        ? chunk_source<kOperandF16x2>(a, g, maps, c)
+                                        : chunk_source<kOperandTf32>(a, g, maps, c);
             tma_load_5d(smem_u32(a_ring + sa * a_entry + c * g.plane_bytes), src.map, src.c_hi, w0, h0, u, b, fa);
           }
           ++P;
@@ -970,7 +1057,7 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           if (!alive) break;
           acquired = Pn;
           const int sa = PA % SA;
-          if (!mbar_wait(smem_u32(&a_full[sa]), (PA / SA) & 1, sm.abort_flag, 38)) {
+          if (!mbar_wait(smem_u32(&a_ready[sa]), (PA / SA) & 1, sm.abort_flag, 38)) {
             alive = false;
             break;
           }
@@ -1032,6 +1119,45 @@ __global__ void __launch_bounds__(kZsThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= 10) {
+    // ----------------------- operand transform (2 warps) ----------------------
+    const int t = threadIdx.x - 10 * 32;
+    int PA = 0, cur_b = -1;
+    bool alive = true, over = false;
+    ZsRun run = zs_run(g);
+    ZsSegment sg;
+    while (alive && zs_next(g, run, sg)) {
+      const int b = sg.col / bricks, rem = sg.col - b * bricks;
+      const int hb = rem / g.nw, wb = rem - hb * g.nw;
+      const int w0 = wb * kHaloW - 1, h0 = hb * kHaloH - 1;
+      if (b != cur_b) {
+        zs_load_affine(a, g, b, aff, lane);
+        cur_b = b;
+      }
+      for (int u = sg.ua; u <= sg.ub; ++u, ++PA) {
+        const int sa = PA % SA;
+        // lane 0 waits (bounded) and the warp follows its verdict, so the warp never splits
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(smem_u32(&a_full[sa]), (PA / SA) & 1, sm.abort_flag, 41) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          alive = false;
+          break;
+        }
+        mbar_try_wait(smem_u32(&a_full[sa]), (PA / SA) & 1);  // completed phase: acquire for every lane
+        for (int c = 0; c < g.nchunk; ++c) {
+          const nnb_segment& seg = a.seg[c * BK >= g.c0len ? 1 : 0];
+          if (seg.prepared) continue;  // already [hi | lo] rows
+          const bool lazy_leaky = seg.scale != nullptr && seg.leaky;
+          over |= zs_transform_plane(a_ring + sa * a_entry + c * g.plane_bytes, g, aff + 64 * c, lazy_leaky,
+                                     w0, h0, a.slope, t);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
+        __syncwarp();
+        if ((t & 31) == 0) mbar_arrive(smem_u32(&a_ready[sa]));
+      }
+    }
+    if (over) atomicAdd(g.range_events, 1ull);
   } else {
     // ------------------------------ epilogue ---------------------------------
     // group 0 (warps 2-5) takes the even planes of the sequence, group 1 (warps 6-9) the odd ones
@@ -1273,7 +1399,7 @@ inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bby
 // A ring plus the weights (resident for one 32-channel chunk, else >= 2
 // streamed (chunk, ky) stages) fit the shared-memory budget.
 inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
-  if (op != kOperandF16x2 || pick_bc(a.cout) != 32) return false;
+  if (a.operand_format != 2 || op != kOperandF16x2 || pick_bc(a.cout) != 32) return false;
   for (int i = 0; i < 3; ++i)
     if (a.kernel[i] != 3 || a.stride[i] != 1 || a.pad[i] != 1) return false;
   if (g.OW < kHaloW || g.OH < kHaloH / 2 || g.nchunk < 1) return false;
@@ -1282,7 +1408,7 @@ inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
   g.plane_rows = g.pw * ph;
   g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
   const int entry = g.nchunk * g.plane_bytes;
-  const int budget = kMaxSmem - 1024 - kMiscBytes;
+  const int budget = kMaxSmem - 1024 - kMiscBytes - 2 * g.nchunk * 64 * 4;  // affine tables
   const int tap_bytes = kZsRows * 64;
   if (g.nchunk == 1 && 2 * entry + 9 * tap_bytes <= budget) {
     g.sb = 0;
@@ -1292,7 +1418,7 @@ inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
     g.sb = std::min(4, (budget - 2 * entry) / (3 * tap_bytes));
     if (g.sb < 2) return false;
   }
-  if (2 * g.sa + 2 * std::max(g.sb, 1) + 2 * kZsSlots + 1 > kMaxBars) return false;
+  if (3 * g.sa + 2 * std::max(g.sb, 1) + 2 * kZsSlots + 1 > kMaxBars) return false;
   g.box[0] = g.pw;
   g.box[1] = ph;
   g.box[2] = 1;
@@ -1370,8 +1496,10 @@ inline EncodeTiledFn encode_tiled() {
 inline int encode_operand(const nnb_segment& seg, int op, int batch, const Geometry& g, CUtensorMap* map) {
   const EncodeTiledFn fn = encode_tiled();
   NNB_REQUIRE(fn != nullptr, "conv3d: cuTensorMapEncodeTiled is not available from the driver");
-  const bool f16 = op == kOperandF16x2;
-  const cuuint64_t inner = (cuuint64_t)(op == kOperandTf32 ? 1 : 2) * seg.channels;
+  // z-streaming mode loads the raw float32 activation, or a segment already prepared as fp16 pairs
+  const bool raw = g.zs && !seg.prepared;
+  const bool f16 = op == kOperandF16x2 && !raw;
+  const cuuint64_t inner = (cuuint64_t)(op == kOperandTf32 || raw ? 1 : 2) * seg.channels;
   const cuuint64_t esize = f16 ? 2 : 4;
   const cuuint64_t dims[5] = {inner, (cuuint64_t)g.IW, (cuuint64_t)g.IH, (cuuint64_t)g.ID, (cuuint64_t)batch};
   const cuuint64_t row = inner * esize;
@@ -1416,7 +1544,7 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   if (g.zs) {
     if constexpr (BC == 32 && OP == kOperandF16x2) {
       const int b_bytes = g.sb == 0 ? 9 * kZsRows * 64 : g.sb * 3 * kZsRows * 64;
-      const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes;
+      const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes + 2 * g.nchunk * 64 * 4;
       NNB_REQUIRE(smem <= kMaxSmem, "conv3d: z-streaming plan exceeds shared memory (%d bytes)", smem);
       conv3d_zstream_kernel<<<grid, kZsThreads, smem, stream>>>(a, g, maps);
     } else {
@@ -1465,6 +1593,8 @@ int dispatch(const nnb_conv3d_args& a, Geometry& g, cudaStream_t stream) {
 }
 
 }  // namespace tc
+
+unsigned long long* operand_range_events_ptr();
 
 bool conv3d_tc_supported(const nnb_conv3d_args& a) {
   if (!tensor_precision(a.precision)) return false;
@@ -1525,11 +1655,30 @@ int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int pr
   return launch_conv3d_pack_rows(w, cout, kvol, cin_total, precision, 1, cout, packed, stream);
 }
 
+// Whether the tensor-core path reads raw lazy segments for these shapes (z-streaming mode).
+bool conv3d_tc_raw_operands(const nnb_conv3d_args& a) {
+  if (a.precision != NNB_PREC_FP32 || !(a.slope >= 0.f && a.slope <= 1.f)) return false;
+  int cin_total = 0;
+  for (int s = 0; s < a.num_segments; ++s) {
+    if (a.seg[s].channels % tc::BK != 0) return false;
+    cin_total += a.seg[s].channels;
+  }
+  if (a.cout % 16 != 0 || 27 * (cin_total / tc::BK) > tc::kMaxKsteps) return false;
+  nnb_conv3d_args r = a;
+  r.operand_format = 2;
+  return tc::make_geometry(r).zs == 1;
+}
+
 // Tiles per sample of the partials a tensor-core convolution writes.
 int conv3d_tc_partial_tiles(const nnb_conv3d_args& a) { return tc::make_geometry(a).tps; }
 
 int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream) {
   tc::Geometry g = tc::make_geometry(a);
+  if (g.zs) {
+    g.range_events = operand_range_events_ptr();
+    NNB_REQUIRE(g.range_events != nullptr, "conv3d: range-event counter unavailable");
+  }
+  NNB_REQUIRE(a.operand_format != 2 || g.zs, "conv3d: raw tensor-core operands outside the z-streaming envelope");
   return tc::dispatch(a, g, stream);
 }
 

@@ -201,6 +201,25 @@ def pack_weights(weight: torch.Tensor, precision: int) -> torch.Tensor | None:
     return image
 
 
+def _zstream_segments(inputs: list[Lazy], precision: int, slope: float, args) -> None:
+    """Segments of a convolution whose tensor-core kernel also accepts raw activations.
+
+    The kernel's in-shared-memory preparation competes with its MMAs for
+    shared-memory bandwidth, which pays only for a single 32-channel input
+    that nothing else prepares: such an input is passed raw.  Every other
+    segment is passed prepared (reusing an operand already prepared for
+    another consumer).
+    """
+    raw_ok = len(inputs) == 1 and inputs[0].channels == 32
+    for index, item in enumerate(inputs):
+        cached = item.prepared.get(precision)
+        if cached is None and raw_ok:
+            continue  # keeps the raw lazy segment set by the caller
+        seg = (cached if cached is not None else prepare_operand(item, precision, slope)).segment()
+        seg.prepared = 1
+        args.seg[index] = seg
+
+
 def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cout: int,
            packed: torch.Tensor | None = None, bias: torch.Tensor | None = None,
            precision: int = _native.PREC_FP32, slope: float = 0.01, stats: bool = True):
@@ -239,7 +258,10 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
     cin = sum(item.channels for item in inputs)
     tensor_cores = (packed is not None and precision in _native.TENSOR_PRECISIONS
                     and all(item.channels % 32 == 0 for item in inputs) and cout % 16 == 0)
-    if tensor_cores:
+    if tensor_cores and _native.load().nnb_conv3d_raw_operands(ctypes.byref(args)) == 1:
+        args.operand_format = 2  # raw lazy or prepared segments (z-streaming kernel)
+        _zstream_segments(inputs, precision, slope, args)
+    elif tensor_cores:
         for index, item in enumerate(inputs):
             args.seg[index] = prepare_operand(item, precision, slope).segment()
         args.operand_format = 1
@@ -287,8 +309,9 @@ def conv3d_norm_static(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stri
     library's fixed device scratch (``NNB_STATIC_PARTIALS_FLOATS`` floats, one
     per device, so calls on one device must not overlap).  Returns
     ``(out, scale, shift)``; a layer whose partials exceed the scratch raises
-    ``ContractError``.  Outputs (and a prepared operand on the tensor-core
-    path) are allocated here by torch, outside the native call.
+    ``ContractError``.  Outputs (and a prepared operand where the tensor-core
+    path does not read the raw activation) are allocated here by torch,
+    outside the native call.
     """
     first = inputs[0]
     batch = int(first.raw.shape[0])
@@ -314,18 +337,24 @@ def conv3d_norm_static(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stri
     args.stride = _native.dims3(stride)
     args.pad = _native.dims3(pad)
     args.num_segments = len(inputs)
+    args.precision = int(precision)
+    args.cout = int(cout)
     for index, item in enumerate(inputs):
-        seg_src = prepare_operand(item, precision, slope) if tensor_cores else item
-        args.seg[index] = seg_src.segment()
+        args.seg[index] = item.segment()
     args.slope = float(slope)
+    raw = tensor_cores and _native.load().nnb_conv3d_raw_operands(ctypes.byref(args)) == 1
+    if raw:
+        _zstream_segments(inputs, precision, slope, args)
+    if tensor_cores and not raw:
+        for index, item in enumerate(inputs):
+            args.seg[index] = prepare_operand(item, precision, slope).segment()
     args.cout = int(cout)
     args.weight = weight.data_ptr()
     args.packed = _ptr(packed) if tensor_cores else 0
     args.bias = 0
     args.out = out.data_ptr()
     args.partials = 0
-    args.precision = int(precision)
-    args.operand_format = 1 if tensor_cores else 0
+    args.operand_format = (2 if raw else 1) if tensor_cores else 0
     _native.check(_native.load().nnb_conv3d_norm_static(
         ctypes.byref(args), _ptr(gamma), _ptr(beta), float(eps), scale.data_ptr(), shift.data_ptr(), _stream()),
         "conv3d_norm_static")

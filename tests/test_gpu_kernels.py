@@ -335,3 +335,22 @@ def test_fp16_pair_operand_format_and_range_events(cuda_device):
     recon = (pairs[..., 0, :] + pairs[..., 1, :]).reshape(raw.shape)
     err = np.abs(recon[finite] - raw.astype(np.float64)[finite])
     assert (err <= 2.0 ** -21 * np.abs(raw[finite]) + 2.0 ** -25).all(), err.max()
+
+
+@pytest.mark.parametrize("prepared_first", [False, True])
+def test_zstream_mixes_raw_and_prepared_segments(cuda_device, prepared_first):
+    """A concat whose one segment already has a prepared operand: that segment is read prepared, the other raw."""
+    from nnunet_mlx_b200 import _native, kernels
+
+    rng = np.random.default_rng(41 + prepared_first)
+    dims = (6, 12, 20)
+    a, ra, sa, ha = _make_segment(rng, 2, dims, 32, True, cuda_device)
+    b, rb, sb, hb = _make_segment(rng, 2, dims, 32, True, cuda_device)
+    kernels.prepare_operand(a if prepared_first else b, _native.PREC_FP32, 0.01)  # cached on the activation
+    w = torch.from_numpy((rng.standard_normal((32, 3, 3, 3, 64)) / np.sqrt(27 * 64)).astype(np.float32))
+    packed = kernels.pack_weights(w.to(cuda_device), _native.PREC_FP32)
+    out, _ = kernels.conv3d([a, b], w.to(cuda_device), kernel=(3, 3, 3), stride=(1, 1, 1), pad=(1, 1, 1), cout=32,
+                            packed=packed, precision=_native.PREC_FP32)
+    ref = _conv_ref([_lazy_ref(ra, sa, ha, True), _lazy_ref(rb, sb, hb, True)], w, (1, 1, 1), (1, 1, 1))
+    scale = ref.abs().max().item()
+    np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), rtol=FP32_TOL["rtol"], atol=FP32_TOL["atol"] * scale)

@@ -159,3 +159,41 @@ def test_synthetic_volumes_have_config_shapes_and_ranges():
     assert (hu < -900).mean() > 0.3  # mostly air
     x = ct_normalize(hu)
     assert x.min() >= (-1000 - 100) / 50 and x.max() <= (400 - 100) / 50
+
+
+def _conv_args(cins, cout, dims, kernel, stride, pad, precision):
+    from nnunet_mlx_b200 import _native
+
+    args = _native.Conv3dArgs()
+    args.batch = 2
+    args.in_dims = _native.dims3(dims)
+    args.out_dims = _native.dims3(tuple((d + 2 * p - k) // s + 1 for d, p, k, s in zip(dims, pad, kernel, stride)))
+    args.kernel = _native.dims3(kernel)
+    args.stride = _native.dims3(stride)
+    args.pad = _native.dims3(pad)
+    args.num_segments = len(cins)
+    for i, c in enumerate(cins):
+        args.seg[i] = _native.Segment(0, 0, 0, c, 1)
+    args.cout = cout
+    args.precision = precision
+    return args
+
+
+@pytest.mark.parametrize("cins,cout,dims,kernel,stride,pad,precision,expect", [
+    ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 1),     # z-streaming, resident weights
+    ((32, 32), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 1),  # concat, streamed weights
+    ((32,), 16, (4, 8, 8), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 1),
+    ((32,), 64, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 0),     # > 32 output channels
+    ((32,), 32, (16, 16, 16), (3, 3, 3), (2, 2, 2), (1, 1, 1), 0, 0),     # strided
+    ((32,), 32, (16, 16, 16), (1, 3, 3), (1, 1, 1), (0, 1, 1), 0, 0),     # anisotropic kernel
+    ((32,), 32, (16, 4, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 0),      # rows shorter than a brick
+    ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 3, 0),     # split-TF32 fallback precision
+    ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 1, 0),     # TF32
+    ((16,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 0),     # channels not a multiple of 32
+])
+def test_raw_operand_query(cins, cout, dims, kernel, stride, pad, precision, expect):
+    """Which layers the tensor-core path reads as raw lazy activations (no device work: shape logic only)."""
+    from nnunet_mlx_b200 import _native
+
+    args = _conv_args(cins, cout, dims, kernel, stride, pad, precision)
+    assert _native.load().nnb_conv3d_raw_operands(ctypes.byref(args)) == expect
