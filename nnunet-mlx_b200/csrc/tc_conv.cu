@@ -78,10 +78,10 @@ __device__ int g_device_status_where = 0;
 namespace nnb {
 namespace tc {
 
-constexpr int kThreads = 6 * 32;
 constexpr int kMiscBytes = 2048;  // mbarriers, TMEM slot, flags, epilogue reduction scratch
 constexpr int kMaxBars = 48;
-constexpr int kStageBudget = kMaxSmem - 1024 /*alignment slack*/ - kMiscBytes - 4 * kMaxKsteps;
+constexpr int kStagingBytes = 2048;  // per epilogue warp: 16 output rows of 32 floats (coalesced stores)
+constexpr int kStageBudget = kMaxSmem - 1024 /*alignment slack*/ - kMiscBytes - 4 * kMaxKsteps - 8 * kStagingBytes;
 constexpr int kHaloW = 8;   // halo-mode brick: 8 (w) x 16 (h) x 1 (d)
 constexpr int kHaloH = 16;
 
@@ -113,6 +113,10 @@ struct Cfg {
   static constexpr int N = kSplit ? 2 * BC : BC;                // accumulator columns: stacked [W_hi; W_lo] rows
   static constexpr int kBRow = OP == kOperandF16x2 ? 64 : 128;  // bytes of one B row (32 channels)
   static constexpr int kAccBufs = (2 * N <= kTmemCols) ? 2 : 1;
+  // epilogue warpgroups: with two accumulators each group drains every other tile (one warp per SM
+  // sub-partition alone is latency-bound on the epilogue's dependent chains)
+  static constexpr int kEpiGroups = kAccBufs;
+  static constexpr int kThreadsC = 64 + 128 * kEpiGroups;
   static constexpr int kABytes = kHalves * BM * 128;
   static constexpr int kBBytes = N * kBRow;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -242,18 +246,58 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
   return m;
 }
 
+// Coalesced store of this warp's 32 rows of 32 floats (lane = row): the rows pass through the warp's 2 KB
+// shared staging buffer 16 at a time (16-byte chunks XOR-swizzled by row % 8) and every store
+// instruction then writes four whole 128-byte rows, instead of one 16-byte piece of 32 rows.  dst: this
+// lane's row destination (16-byte aligned), or nullptr to skip the row.  All 32 lanes must call it.
+__device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const float (&v)[32], float* dst) {
+  const unsigned long long d = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    if ((lane >> 4) == half) {
+      const int r = lane & 15;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        stg[r * 8 + (j ^ (r & 7))] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 4 * i + (lane >> 3);  // staged row, 0..15
+      const int c = lane & 7;
+      const unsigned long long rd = __shfl_sync(0xffffffffu, d, half * 16 + r);
+      const float4 val = stg[r * 8 + (c ^ (r & 7))];
+      if (rd != 0ull) reinterpret_cast<float4*>(rd)[c] = val;
+    }
+    __syncwarp();
+  }
+}
+
+// Brick coordinates of an epilogue thread's row (fixed for the whole kernel: decompose it once).
+struct RowPos {
+  int row, dz, dy, dx;
+};
+
+__device__ __forceinline__ RowPos row_pos(const Geometry& g, int q, int lane) {
+  RowPos r;
+  r.row = q * 32 + lane;
+  r.dz = r.row / (g.tw * g.th);
+  r.dy = (r.row / g.tw) % g.th;
+  r.dx = r.row % g.tw;
+  return r;
+}
+
 // One finished accumulator -> outputs + partials (or the transposed-conv scatter).
 // acc: TMEM address of the tile's (hi) accumulator columns for this warp's lanes; acc_lo: of the second
 // accumulator of the split formats, or 0 when one accumulator holds every product (z-streaming mode).
-// bar: named barrier of the four epilogue warps working on this tile.
+// bar: named barrier of the four epilogue warps working on this tile; stg: this warp's staging buffer.
 template <int BC, int OP>
 __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Geometry& g, const TileOrigin& o,
-                                              uint32_t acc, uint32_t acc_lo, int q, int lane, float* red,
-                                              float* col_mean, const float* __restrict__ col_inv, int bar = 1) {
-  const int row = q * 32 + lane;
-  const int dz = row / (g.tw * g.th), dy = (row / g.tw) % g.th, dx = row % g.tw;
-  const int z = o.d0 + dz, y = o.h0 + dy, x = o.w0 + dx;
-  const bool valid = row < g.rows && z < g.OD && y < g.OH && x < g.OW;
+                                              const RowPos& rp, uint32_t acc, uint32_t acc_lo, int q, int lane,
+                                              float* red, float* col_mean, const float* __restrict__ col_inv,
+                                              float4* stg, int bar = 1) {
+  const int z = o.d0 + rp.dz, y = o.h0 + rp.dy, x = o.w0 + rp.dx;
+  const bool valid = rp.row < g.rows && z < g.OD && y < g.OH && x < g.OW;
   const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
   const int64_t m = ((int64_t)z * g.OH + y) * g.OW + x;
   const int nvalid = min(g.td, g.OD - o.d0) * min(g.th, g.OH - o.h0) * min(g.tw, g.OW - o.w0);
@@ -271,8 +315,15 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += u[i];
       }
+      const float4* ci = reinterpret_cast<const float4*>(col_inv + nbase);  // 16-byte aligned
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= __ldg(col_inv + nbase + i);
+      for (int i = 0; i < 8; ++i) {
+        const float4 c4 = __ldg(ci + i);
+        v[4 * i] *= c4.x;
+        v[4 * i + 1] *= c4.y;
+        v[4 * i + 2] *= c4.z;
+        v[4 * i + 3] *= c4.w;
+      }
     } else if constexpr (OP == kOperandTf32x2) {
       float u[32];
       tmem_ld32(acc_lo + cc * 32, u);
@@ -283,20 +334,26 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
       // scatter: GEMM column n = tap * up_cout + channel of input voxel (z, y, x)
       const int tap = nbase / g.up_cout;
       const int co0 = nbase - tap * g.up_cout;
+      float* dst = nullptr;
       if (valid) {
         const int ux = tap % g.UKW, uy = (tap / g.UKW) % g.UKH, uz = tap / (g.UKW * g.UKH);
         const int64_t OH2 = (int64_t)g.OH * g.UKH, OW2 = (int64_t)g.OW * g.UKW;
         const int64_t OD2 = (int64_t)g.OD * g.UKD;
-        float* dst = a.out + ((((int64_t)o.b * OD2 + z * g.UKD + uz) * OH2 + y * g.UKH + uy) * OW2 +
-                              x * g.UKW + ux) * g.up_cout + co0;
-        if (a.bias != nullptr) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] += __ldg(a.bias + co0 + i);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        dst = a.out + ((((int64_t)o.b * OD2 + z * g.UKD + uz) * OH2 + y * g.UKH + uy) * OW2 + x * g.UKW + ux) *
+                          g.up_cout + co0;
       }
+      if (a.bias != nullptr) {
+        const float4* b4 = reinterpret_cast<const float4*>(a.bias + co0);  // 16-byte aligned (checked on launch)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 c4 = __ldg(b4 + i);
+          v[4 * i] += c4.x;
+          v[4 * i + 1] += c4.y;
+          v[4 * i + 2] += c4.z;
+          v[4 * i + 3] += c4.w;
+        }
+      }
+      store_rows_staged(stg, lane, v, dst);
       continue;
     }
 #pragma unroll
@@ -304,17 +361,13 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
       if (a.bias != nullptr && nbase + i < a.cout) v[i] += __ldg(a.bias + nbase + i);
       if (!valid) v[i] = 0.f;
     }
-    if (valid) {
+    if (nbase + 32 <= a.cout && (a.cout & 3) == 0) {  // uniform across the warp
+      store_rows_staged(stg, lane, v, valid ? a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase : nullptr);
+    } else if (valid) {
       float* dst = a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase;
-      if (nbase + 32 <= a.cout && (a.cout & 3) == 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (nbase + i < a.cout) dst[i] = v[i];
-      }
+      for (int i = 0; i < 32; ++i)
+        if (nbase + i < a.cout) dst[i] = v[i];
     }
     if (a.partials != nullptr) {
       // per-tile (sum, M2, n) of each column over the brick's valid rows
@@ -349,27 +402,34 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
 template <int BC, int OP>
 __device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Geometry& g, int my_tiles,
                                               uint32_t tmem, const SharedMisc& sm, uint64_t* accf, uint64_t* acce,
-                                              int warp, int lane) {
+                                              int warp, int lane, float4* stg_base) {
   using C = Cfg<BC, OP>;
   // fp16-pair images end with the per-column 1/s after the B tiles
   const float* col_inv = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.packed) +
                                                         (int64_t)g.n_tiles * g.ksteps * C::kBBytes);
   constexpr int NB = C::kAccBufs;
-  const int q = warp & 3;  // warps 2..5 own TMEM lane quarters 2, 3, 0, 1
+  const int q = warp & 3;  // warps 2..5 (and 6..9) own TMEM lane quarters 2, 3, 0, 1
+  const int grp = C::kEpiGroups == 2 ? (warp - 2) >> 2 : 0;  // group grp drains accumulator grp
+  const int bar = 1 + grp;
+  volatile int* votes = grp ? sm.votes2 : sm.votes;
+  float* red = grp ? sm.red2 : sm.red;
+  float* col_mean = grp ? sm.col_mean2 : sm.col_mean;
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-  for (int it = 0; it < my_tiles; ++it) {
+  const RowPos rp = row_pos(g, q, lane);
+  for (int it = grp; it < my_tiles; it += C::kEpiGroups) {
     const int ab = NB == 2 ? (it & 1) : 0;
     const bool ok = mbar_wait(smem_u32(&accf[ab]), (it / NB) & 1, sm.abort_flag, 13);
-    // consistent stop decision across the four epilogue warps
-    if (lane == 0) sm.votes[q] = (!ok || *sm.abort_flag) ? 1 : 0;
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    const bool stop = sm.votes[0] | sm.votes[1] | sm.votes[2] | sm.votes[3];
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // consistent stop decision across the group's four warps
+    if (lane == 0) votes[q] = (!ok || *sm.abort_flag) ? 1 : 0;
+    asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+    const bool stop = votes[0] | votes[1] | votes[2] | votes[3];
+    asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
     if (stop) break;
     fence_after();
     const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
     const uint32_t acc = tmem + ab * C::N + lane_base;
-    epilogue_tile<BC, OP>(a, g, o, acc, acc + BC, q, lane, sm.red, sm.col_mean, col_inv);
+    epilogue_tile<BC, OP>(a, g, o, rp, acc, acc + BC, q, lane, red, col_mean, col_inv,
+                          stg_base + (warp - 2) * (kStagingBytes / 16), bar);
     fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&acce[ab]));
@@ -392,7 +452,7 @@ __device__ __forceinline__ void tmem_free_all(uint32_t tmem) {
 // Box mode: one TMA box per half and one B tile per K-step (tap x 32 channels).
 // ---------------------------------------------------------------------------
 template <int BC, int OP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BC, OP>::kThreadsC, 1)
     conv3d_tc_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
   using C = Cfg<BC, OP>;
   constexpr int S = C::S;
@@ -402,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stages = smem;  // S x [A hi | A lo | B], each 1024-aligned
   const SharedMisc sm = shared_misc(smem + S * C::kStageBytes);
   int* kstab = reinterpret_cast<int*>(smem + S * C::kStageBytes + kMiscBytes);  // kx | ky<<4 | kz<<8 | chunk<<12
+  float4* stg = reinterpret_cast<float4*>(smem + S * C::kStageBytes + kMiscBytes + 4 * kMaxKsteps);
   uint64_t* full = sm.bars;
   uint64_t* empty = sm.bars + S;
   uint64_t* accf = sm.bars + 2 * S;
@@ -517,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    epilogue_role<BC, OP>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
+    epilogue_role<BC, OP>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane, stg);
   }
   __syncthreads();
   if (warp == 1) tmem_free_all(tmem);
@@ -528,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // TB = taps per B stage: 3 (a whole kx row of a 3-wide kernel, fully unrolled) or 1 (any kernel).
 template <int BC, int OP, int TB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BC, OP>::kThreadsC, 1)
     conv3d_halo_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
   using C = Cfg<BC, OP>;
   constexpr int NB = C::kAccBufs;
@@ -726,7 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    epilogue_role<BC, OP>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane);
+    epilogue_role<BC, OP>(a, g, my_tiles, tmem, sm, accf, acce, warp, lane,
+                          reinterpret_cast<float4*>(b_ring + SB * b_stage + kMiscBytes));
   }
   __syncthreads();
   if (warp == 1) tmem_free_all(tmem);
@@ -926,6 +988,8 @@ __global__ void __launch_bounds__(kZsThreads, 1)
   const int bricks = g.nh * g.nw;
   // per transform warp: [nchunk][scale 32 | shift 32]
   float* aff = reinterpret_cast<float*>(b_ring + b_bytes + kMiscBytes) + (warp >= 10 ? (warp - 10) * g.nchunk * 64 : 0);
+  // eight epilogue warps' staging buffers after the two affine tables
+  float4* zs_stg = reinterpret_cast<float4*>(b_ring + b_bytes + kMiscBytes + 2 * g.nchunk * 64 * 4);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
@@ -1169,6 +1233,7 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     float* col_mean = grp ? sm.col_mean2 : sm.col_mean;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const float* col_inv = reinterpret_cast<const float*>(wimg + (int64_t)g.ksteps * C::kBBytes);
+    const RowPos rp = row_pos(g, q, lane);
     int P = 0;
     ZsRun run = zs_run(g);
     ZsSegment sg;
@@ -1195,7 +1260,8 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           o.d0 = z;
           o.h0 = hb * kHaloH;
           o.w0 = wb * kHaloW;
-          epilogue_tile<BC, kOperandF16x2>(a, g, o, acc, 0u, q, lane, red, col_mean, col_inv, bar);
+          epilogue_tile<BC, kOperandF16x2>(a, g, o, rp, acc, 0u, q, lane, red, col_mean, col_inv,
+                                           zs_stg + (warp - 2) * (kStagingBytes / 16), bar);
         }
         tmem_zero32(acc);
         fence_before();
@@ -1370,7 +1436,7 @@ inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bby
   g.plane_rows = g.pw * ph;
   g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
   const int a_stage = halves * g.plane_bytes;
-  const int budget = kMaxSmem - 1024 - kMiscBytes;
+  const int budget = kMaxSmem - 1024 - kMiscBytes - 8 * kStagingBytes;
   // Ring plan, first that fits: B stages of a whole kx row (3-wide kernels) with 3 A planes and
   // >= 3 B stages, then with 2 A planes and >= 2 B stages, else one tap per B stage.
   if (g.KW == 3 && 3 * a_stage + 3 * 3 * bbytes <= budget) {
@@ -1408,7 +1474,7 @@ inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
   g.plane_rows = g.pw * ph;
   g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
   const int entry = g.nchunk * g.plane_bytes;
-  const int budget = kMaxSmem - 1024 - kMiscBytes - 2 * g.nchunk * 64 * 4;  // affine tables
+  const int budget = kMaxSmem - 1024 - kMiscBytes - 2 * g.nchunk * 64 * 4 - 8 * kStagingBytes;  // tables, staging
   const int tap_bytes = kZsRows * 64;
   if (g.nchunk == 1 && 2 * entry + 9 * tap_bytes <= budget) {
     g.sb = 0;
@@ -1544,22 +1610,24 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   if (g.zs) {
     if constexpr (BC == 32 && OP == kOperandF16x2) {
       const int b_bytes = g.sb == 0 ? 9 * kZsRows * 64 : g.sb * 3 * kZsRows * 64;
-      const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes + 2 * g.nchunk * 64 * 4;
+      const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes + 2 * g.nchunk * 64 * 4 +
+                       8 * kStagingBytes;
       NNB_REQUIRE(smem <= kMaxSmem, "conv3d: z-streaming plan exceeds shared memory (%d bytes)", smem);
       conv3d_zstream_kernel<<<grid, kZsThreads, smem, stream>>>(a, g, maps);
     } else {
       NNB_REQUIRE(false, "conv3d: internal: z-streaming plan for an unsupported tile");
     }
   } else if (g.halo) {
-    const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * g.tb * C::kBBytes + kMiscBytes;
+    const int smem = 1024 + g.sa * C::kHalves * g.plane_bytes + g.sb * g.tb * C::kBBytes + kMiscBytes +
+                     8 * kStagingBytes;
     NNB_REQUIRE(smem <= kMaxSmem, "conv3d: halo plan exceeds shared memory (%d bytes)", smem);
     if (g.tb == 3)
-      conv3d_halo_kernel<BC, OP, 3><<<grid, kThreads, smem, stream>>>(a, g, maps);
+      conv3d_halo_kernel<BC, OP, 3><<<grid, C::kThreadsC, smem, stream>>>(a, g, maps);
     else
-      conv3d_halo_kernel<BC, OP, 1><<<grid, kThreads, smem, stream>>>(a, g, maps);
+      conv3d_halo_kernel<BC, OP, 1><<<grid, C::kThreadsC, smem, stream>>>(a, g, maps);
   } else {
-    const int smem = 1024 + C::S * C::kStageBytes + kMiscBytes + 4 * kMaxKsteps;
-    conv3d_tc_kernel<BC, OP><<<grid, kThreads, smem, stream>>>(a, g, maps);
+    const int smem = 1024 + C::S * C::kStageBytes + kMiscBytes + 4 * kMaxKsteps + 8 * kStagingBytes;
+    conv3d_tc_kernel<BC, OP><<<grid, C::kThreadsC, smem, stream>>>(a, g, maps);
   }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
@@ -1708,6 +1776,7 @@ int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_
   a.precision = precision;
   a.operand_format = 1;
   NNB_REQUIRE(in.scale == nullptr, "conv_transpose3d: prepared operands carry no lazy affine");
+  NNB_REQUIRE((reinterpret_cast<uintptr_t>(bias) & 15) == 0, "conv_transpose3d: bias must be 16-byte aligned");
   NNB_REQUIRE(conv3d_tc_supported(a) && cout % 32 == 0, "conv_transpose3d: outside the tensor-core envelope");
   tc::Geometry g = tc::make_geometry(a);
   g.up_cout = cout;
