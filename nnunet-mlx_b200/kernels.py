@@ -15,8 +15,10 @@ from __future__ import annotations
 
 import ctypes
 import math
+import threading
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from nnunet_mlx_b200 import _native
@@ -111,6 +113,36 @@ class Lazy:
                                0 if self.scale is None else self.scale.data_ptr(),
                                0 if self.shift is None else self.shift.data_ptr(),
                                self.channels, 1 if self.leaky else 0)
+
+
+_STAGING: dict = {}
+_STAGING_LOCK = threading.Lock()
+
+
+def to_host(t: torch.Tensor) -> np.ndarray:
+    """A device tensor as a fresh host numpy array, through a cached page-locked staging buffer.
+
+    A device-to-pageable copy runs at a few GB/s (the driver stages it through
+    small page-locked buffers of its own: ~0.33 s for the 715 MB logits of a
+    768^2 x 101 CT on B200); the copy into a page-locked buffer runs at the
+    link's rate (~13 ms) and the multithreaded host copy into the result adds
+    the rest.  The staging buffer (the largest size seen, per device) lives for
+    the process; pinning it is a one-time cost.
+    """
+    if not t.is_cuda:
+        return t.numpy()
+    t = t.contiguous()
+    nbytes = t.numel() * t.element_size()
+    with _STAGING_LOCK:
+        buf = _STAGING.get(t.device.index)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 16), dtype=torch.uint8, pin_memory=True)
+            _STAGING[t.device.index] = buf
+        staging = buf[:nbytes].view(t.dtype).view(t.shape)
+        staging.copy_(t)  # waits for the stream's pending work, then copies at the link's rate
+        out = torch.empty(t.shape, dtype=t.dtype)
+        out.copy_(staging)  # parallel host copy into fresh pageable memory
+    return out.numpy()
 
 
 def _check_tensor(t: torch.Tensor | None, name: str) -> None:

@@ -16,6 +16,7 @@ from collections.abc import Sequence
 import numpy as np
 import torch
 
+from nnunet_mlx_b200 import kernels
 from nnunet_mlx_b200.errors import ContractError
 from nnunet_mlx_b200.prediction.sliding_window import _check_accumulation, predict_volume
 
@@ -31,7 +32,7 @@ def average_fold_logits(models, data_channels_first, *, patch_size, num_outputs:
     logits, _ = predict_volume(list(models), data_channels_first, patch_size=patch_size, num_classes=num_outputs,
                                mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None,
                                accumulation=accumulation, half_logits=half)
-    return logits.cpu().numpy()
+    return kernels.to_host(logits)
 
 
 def average_fold_device_logits(models, data_channels_first, *, patch_size, num_outputs: int, mirroring_axes=(),
@@ -124,4 +125,4 @@ class ArrayPredictor:
                                    step_fraction=self.step_fraction, want_logits=False,
                                    label_dtype=torch.uint8 if self.num_outputs <= 255 else torch.uint16,
                                    accumulation=self.accumulation)
-        return labels.cpu().numpy().astype(np.uint16)
+        return kernels.to_host(labels).astype(np.uint16)

@@ -286,7 +286,7 @@ def predict_logits(model, data_channels_first, *, patch_size, num_classes: int, 
     logits, _ = predict_volume(models, data_channels_first, patch_size=patch_size, num_classes=num_classes,
                                mirroring_axes=mirroring_axes, step_fraction=step_fraction, label_dtype=None,
                                accumulation=accumulation)
-    return logits.cpu().numpy()
+    return kernels.to_host(logits)
 
 
 def predict_device_logits(model, data_channels_first, *, patch_size, num_classes: int, mirroring_axes=(),
@@ -310,7 +310,7 @@ def predict_labels(model, data_channels_first, *, patch_size, num_classes: int, 
                                mirroring_axes=mirroring_axes, step_fraction=step_fraction, want_logits=False,
                                label_dtype=torch.uint16 if num_classes > 255 else torch.uint8,
                                accumulation=accumulation)
-    return labels.cpu().numpy().astype(np.uint16)
+    return kernels.to_host(labels).astype(np.uint16)
 
 
 def _check_accumulation(accumulation: str) -> None:

@@ -354,3 +354,18 @@ def test_zstream_mixes_raw_and_prepared_segments(cuda_device, prepared_first):
     ref = _conv_ref([_lazy_ref(ra, sa, ha, True), _lazy_ref(rb, sb, hb, True)], w, (1, 1, 1), (1, 1, 1))
     scale = ref.abs().max().item()
     np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), rtol=FP32_TOL["rtol"], atol=FP32_TOL["atol"] * scale)
+
+
+def test_to_host_returns_fresh_arrays(cuda_device):
+    """Results cross to the host through one cached page-locked buffer; each call returns its own array."""
+    from nnunet_mlx_b200 import kernels
+
+    a = torch.randn((3, 17, 33, 21), device=cuda_device)
+    b = torch.randint(0, 5, (40, 50), dtype=torch.uint8, device=cuda_device)
+    ha = kernels.to_host(a)
+    hb = kernels.to_host(b)
+    a.mul_(2)
+    ha2 = kernels.to_host(a)
+    np.testing.assert_array_equal(ha * 2, ha2)  # the first result was not overwritten by the second copy
+    np.testing.assert_array_equal(hb, b.cpu().numpy())
+    assert ha.dtype == np.float32 and hb.dtype == np.uint8 and ha.shape == (3, 17, 33, 21)
