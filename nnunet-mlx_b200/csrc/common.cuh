@@ -61,6 +61,22 @@ inline int tiles_per_sample(int64_t voxels) { return (int)((voxels + kTileRows -
 
 __device__ __forceinline__ float leaky(float v, float slope) { return v >= 0.f ? v : v * slope; }
 
+// Transpose-reduce: lane j ends with the sum over the warp's lanes of x[j] (x is clobbered).
+__device__ __forceinline__ float warp_column_sums(float (&x)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 16; h >= 1; h >>= 1) {
+    const bool up = (lane & h) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = up ? x[i] : x[i + h];
+      const float keep = up ? x[i + h] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  return x[0];
+}
+
 // Apply a segment's lazy affine + activation to one raw value.
 __device__ __forceinline__ float activate(float raw, const float* scale, const float* shift,
                                           int leaky_flag, float slope, int idx) {

@@ -198,17 +198,19 @@ __global__ void __launch_bounds__(kTileRows) conv3d_small_cin_kernel(nnb_conv3d_
 // ---------------------------------------------------------------------------
 // The first layer's shape (1, 2 or 4 raw input channels, 3x3x3, stride 1,
 // padding 1, 32-channel output groups): compile-time taps and channels, each
-// of 64 threads computes two voxels of the 128-voxel tile (rows r and r + 64)
+// of 64 threads computes two voxels of a 128-voxel tile (rows r and r + 64)
 // so every float4 weight read from shared memory feeds 8 FMAs, and the padding
-// test is three per-axis 3-bit masks computed once.  Same output staging,
-// coalesced stores and (sum, M2, n) partials as conv3d_small_cin_kernel.
+// test is three per-axis 3-bit masks computed once.  Persistent blocks (the
+// weights are staged once per block, not per tile); the (sum, M2, n) partials
+// come from warp transpose-reductions; rows leave through a swizzled shared
+// buffer as whole 128-byte rows.
 // ---------------------------------------------------------------------------
 template <int CIN>
-__global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int tps) {
-  __shared__ float4 w_s[27 * CIN * 8];  // [tap][ci][co/4]
-  __shared__ float out_s[kTileRows][33];
-  const int t = blockIdx.x % tps;
-  const int b = blockIdx.x / tps;
+__global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int tps, int64_t total_tiles) {
+  __shared__ float4 w_s[27 * CIN * 8];       // [tap][ci][co/4]
+  __shared__ float4 out_s[kTileRows * 8];    // 128 rows x 32 floats, 16-byte chunks XOR-swizzled by row % 8
+  __shared__ float red_s[2][32];
+  __shared__ float mean_s[32], sum_s[32];
   const int co0 = blockIdx.y * 32;
   for (int i = threadIdx.x; i < 27 * CIN * 32; i += blockDim.x) {
     const int co = i % 32, ci = (i / 32) % CIN, tap = i / (32 * CIN);
@@ -217,101 +219,133 @@ __global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int
   __syncthreads();
   const int D = a.out_dims[0], H = a.out_dims[1], W = a.out_dims[2];
   const int64_t ovox = (int64_t)D * H * W;
-  const float* x = a.seg[0].data + (int64_t)b * ovox * CIN;
-  float acc[2][32];
-  int base[2];
-  uint32_t mask[2];  // bits 0-8: kx, ky, kz validity (3 bits each)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ncols = min(32, a.cout - co0);
+  for (int64_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+    const int t = (int)(tile % tps);
+    const int b = (int)(tile / tps);
+    const float* x = a.seg[0].data + (int64_t)b * ovox * CIN;
+    float acc[2][32];
+    int base[2];
+    uint32_t mask[2];  // bits 0-8: kx, ky, kz validity (3 bits each)
+    bool valid[2];
 #pragma unroll
-  for (int v = 0; v < 2; ++v) {
-    const int64_t m = (int64_t)t * kTileRows + threadIdx.x + 64 * v;
-    const bool valid = m < ovox;
-    const int ox = (int)(m % W), oy = (int)((m / W) % H), oz = (int)(m / ((int64_t)W * H));
-    uint32_t mk = 0;
+    for (int v = 0; v < 2; ++v) {
+      const int64_t m = (int64_t)t * kTileRows + threadIdx.x + 64 * v;
+      valid[v] = m < ovox;
+      const int ox = (int)(m % W), oy = (int)((m / W) % H), oz = (int)(m / ((int64_t)W * H));
+      uint32_t mk = 0;
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      mk |= (uint32_t)(valid && ox + k - 1 >= 0 && ox + k - 1 < W) << k;
-      mk |= (uint32_t)(valid && oy + k - 1 >= 0 && oy + k - 1 < H) << (3 + k);
-      mk |= (uint32_t)(valid && oz + k - 1 >= 0 && oz + k - 1 < D) << (6 + k);
+      for (int k = 0; k < 3; ++k) {
+        mk |= (uint32_t)(valid[v] && ox + k - 1 >= 0 && ox + k - 1 < W) << k;
+        mk |= (uint32_t)(valid[v] && oy + k - 1 >= 0 && oy + k - 1 < H) << (3 + k);
+        mk |= (uint32_t)(valid[v] && oz + k - 1 >= 0 && oz + k - 1 < D) << (6 + k);
+      }
+      mask[v] = mk;
+      base[v] = valid[v] ? (int)((((int64_t)(oz - 1) * H + (oy - 1)) * W + (ox - 1)) * CIN) : 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[v][j] = 0.f;
     }
-    mask[v] = mk;
-    base[v] = valid ? (int)((((int64_t)(oz - 1) * H + (oy - 1)) * W + (ox - 1)) * CIN) : 0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc[v][j] = 0.f;
-  }
+    for (int kz = 0; kz < 3; ++kz) {
 #pragma unroll
-  for (int kz = 0; kz < 3; ++kz) {
+      for (int ky = 0; ky < 3; ++ky) {
 #pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
+        for (int kx = 0; kx < 3; ++kx) {
+          const int tap = (kz * 3 + ky) * 3 + kx;
+          const int off = ((kz * H + ky) * W + kx) * CIN;
+          float xv[2][CIN];
 #pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        const int tap = (kz * 3 + ky) * 3 + kx;
-        const int off = ((kz * H + ky) * W + kx) * CIN;
-        float xv[2][CIN];
+          for (int v = 0; v < 2; ++v) {
+            const bool in = (mask[v] >> kx & 1) & (mask[v] >> (3 + ky) & 1) & (mask[v] >> (6 + kz) & 1);
 #pragma unroll
-        for (int v = 0; v < 2; ++v) {
-          const bool in = (mask[v] >> kx & 1) & (mask[v] >> (3 + ky) & 1) & (mask[v] >> (6 + kz) & 1);
+            for (int ci = 0; ci < CIN; ++ci) xv[v][ci] = in ? __ldg(x + base[v] + off + ci) : 0.f;
+          }
 #pragma unroll
-          for (int ci = 0; ci < CIN; ++ci) xv[v][ci] = in ? __ldg(x + base[v] + off + ci) : 0.f;
-        }
+          for (int ci = 0; ci < CIN; ++ci) {
 #pragma unroll
-        for (int ci = 0; ci < CIN; ++ci) {
+            for (int q = 0; q < 8; ++q) {
+              const float4 w = w_s[(tap * CIN + ci) * 8 + q];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 w = w_s[(tap * CIN + ci) * 8 + q];
-#pragma unroll
-            for (int v = 0; v < 2; ++v) {
-              acc[v][4 * q + 0] = fmaf(xv[v][ci], w.x, acc[v][4 * q + 0]);
-              acc[v][4 * q + 1] = fmaf(xv[v][ci], w.y, acc[v][4 * q + 1]);
-              acc[v][4 * q + 2] = fmaf(xv[v][ci], w.z, acc[v][4 * q + 2]);
-              acc[v][4 * q + 3] = fmaf(xv[v][ci], w.w, acc[v][4 * q + 3]);
+              for (int v = 0; v < 2; ++v) {
+                acc[v][4 * q + 0] = fmaf(xv[v][ci], w.x, acc[v][4 * q + 0]);
+                acc[v][4 * q + 1] = fmaf(xv[v][ci], w.y, acc[v][4 * q + 1]);
+                acc[v][4 * q + 2] = fmaf(xv[v][ci], w.z, acc[v][4 * q + 2]);
+                acc[v][4 * q + 3] = fmaf(xv[v][ci], w.w, acc[v][4 * q + 3]);
+              }
             }
           }
         }
       }
     }
-  }
+    if (a.bias != nullptr) {
 #pragma unroll
-  for (int v = 0; v < 2; ++v) {
-    const int r = threadIdx.x + 64 * v;
-    const bool valid = (int64_t)t * kTileRows + r < ovox;
+      for (int j = 0; j < 32; ++j) {
+        const float bj = co0 + j < a.cout ? __ldg(a.bias + co0 + j) : 0.f;
+        acc[0][j] += bj;
+        acc[1][j] += bj;
+      }
+    }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float y = acc[v][j];
-      if (a.bias != nullptr && co0 + j < a.cout) y += __ldg(a.bias + co0 + j);
-      out_s[r][j] = valid ? y : 0.f;
+    for (int v = 0; v < 2; ++v)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[v][j] = valid[v] ? acc[v][j] : 0.f;
+    const int rows = (int)min((int64_t)kTileRows, ovox - (int64_t)t * kTileRows);
+    // rows leave through the staging buffer (the previous tile's readers finished at its last barrier)
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const int r = threadIdx.x + 64 * v;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        out_s[r * 8 + (q ^ (r & 7))] = make_float4(acc[v][4 * q], acc[v][4 * q + 1], acc[v][4 * q + 2], acc[v][4 * q + 3]);
     }
-  }
-  __syncthreads();
-  const int rows = (int)min((int64_t)kTileRows, ovox - (int64_t)t * kTileRows);
-  const int ncols = min(32, a.cout - co0);
-  float* dst = a.out + ((int64_t)b * ovox + (int64_t)t * kTileRows) * a.cout + co0;
-  if (ncols == 32 && (a.cout % 4) == 0) {
-    for (int i = threadIdx.x; i < rows * 8; i += blockDim.x) {
-      const int row = i >> 3, c4 = (i & 7) * 4;
-      *reinterpret_cast<float4*>(dst + (int64_t)row * a.cout + c4) =
-          make_float4(out_s[row][c4], out_s[row][c4 + 1], out_s[row][c4 + 2], out_s[row][c4 + 3]);
+    if (a.partials != nullptr) {
+      float xs[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) xs[j] = acc[0][j] + acc[1][j];
+      const float s = warp_column_sums(xs);
+      red_s[warp][lane] = s;
     }
-  } else {
-    for (int i = threadIdx.x; i < rows * 32; i += blockDim.x) {
-      const int row = i >> 5, c = i & 31;
-      if (c < ncols) dst[(int64_t)row * a.cout + c] = out_s[row][c];
+    __syncthreads();
+    float* dst = a.out + ((int64_t)b * ovox + (int64_t)t * kTileRows) * a.cout + co0;
+    if (ncols == 32 && (a.cout % 4) == 0) {
+      for (int i = threadIdx.x; i < rows * 8; i += blockDim.x) {
+        const int row = i >> 3, c = i & 7;
+        *reinterpret_cast<float4*>(dst + (int64_t)row * a.cout + 4 * c) = out_s[row * 8 + (c ^ (row & 7))];
+      }
+    } else {
+      for (int i = threadIdx.x; i < rows * 32; i += blockDim.x) {
+        const int row = i >> 5, c = i & 31;
+        if (c < ncols) dst[(int64_t)row * a.cout + c] = reinterpret_cast<const float*>(out_s)[row * 32 + (((c >> 2) ^ (row & 7)) << 2) + (c & 3)];
+      }
     }
-  }
-  if (a.partials == nullptr) return;
-  if (threadIdx.x < ncols) {
-    const int c = threadIdx.x;
-    float sum = 0.f;
-    for (int i = 0; i < rows; ++i) sum += out_s[i][c];
-    const float mean = sum / rows;
-    float m2 = 0.f;
-    for (int i = 0; i < rows; ++i) {
-      const float d = out_s[i][c] - mean;
-      m2 = fmaf(d, d, m2);
+    if (a.partials != nullptr) {
+      if (threadIdx.x < 32) {
+        const float sum = red_s[0][threadIdx.x] + red_s[1][threadIdx.x];
+        sum_s[threadIdx.x] = sum;
+        mean_s[threadIdx.x] = sum / (float)rows;
+      }
+      __syncthreads();
+      float xs[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float m = mean_s[j];
+        const float d0 = valid[0] ? acc[0][j] - m : 0.f, d1 = valid[1] ? acc[1][j] - m : 0.f;
+        xs[j] = fmaf(d0, d0, d1 * d1);
+      }
+      const float m2w = warp_column_sums(xs);
+      __syncthreads();  // every thread has read mean_s / red_s of this tile
+      red_s[warp][lane] = m2w;
+      __syncthreads();
+      if (threadIdx.x < ncols) {
+        const int c = threadIdx.x;
+        float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + c) * 3;
+        p[0] = sum_s[c];
+        p[1] = red_s[0][c] + red_s[1][c];
+        p[2] = (float)rows;
+      }
     }
-    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + c) * 3;
-    p[0] = sum;
-    p[1] = m2;
-    p[2] = (float)rows;
+    __syncthreads();  // staging and reduction buffers are free for the next tile
   }
 }
 
@@ -396,12 +430,23 @@ int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
     return NNB_OK;
   }
   if (first_layer_shape(a)) {
-    dim3 grid((unsigned)((int64_t)tps * a.batch), (unsigned)((a.cout + 31) / 32));
-    NNB_REQUIRE((int64_t)tps * a.batch < (1LL << 31), "conv3d: too many tiles");
+    const int64_t total_tiles = (int64_t)tps * a.batch;
+    const int groups = (a.cout + 31) / 32;
+    // persistent blocks: as many as are resident at once over all SMs, split across the channel groups
+    int per_sm = 0, sms = 148, dev = 0;
+    NNB_CUDA_CHECK(cudaGetDevice(&dev));
+    NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     switch (a.seg[0].channels) {
-      case 1: conv3d_first_kernel<1><<<grid, 64, 0, stream>>>(a, tps); break;
-      case 2: conv3d_first_kernel<2><<<grid, 64, 0, stream>>>(a, tps); break;
-      default: conv3d_first_kernel<4><<<grid, 64, 0, stream>>>(a, tps); break;
+      case 1: NNB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv3d_first_kernel<1>, 64, 0)); break;
+      case 2: NNB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv3d_first_kernel<2>, 64, 0)); break;
+      default: NNB_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv3d_first_kernel<4>, 64, 0)); break;
+    }
+    const int64_t resident = std::max<int64_t>(1, (int64_t)std::max(per_sm, 1) * sms / groups);
+    dim3 grid((unsigned)std::min<int64_t>(total_tiles, resident), (unsigned)groups);
+    switch (a.seg[0].channels) {
+      case 1: conv3d_first_kernel<1><<<grid, 64, 0, stream>>>(a, tps, total_tiles); break;
+      case 2: conv3d_first_kernel<2><<<grid, 64, 0, stream>>>(a, tps, total_tiles); break;
+      default: conv3d_first_kernel<4><<<grid, 64, 0, stream>>>(a, tps, total_tiles); break;
     }
     NNB_LAUNCH_CHECK();
     return NNB_OK;

@@ -194,22 +194,6 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
-// Transpose-reduce: lane j ends with sum over the warp's lanes of x[j].
-__device__ __forceinline__ float warp_column_sums(float (&x)[32]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int h = 16; h >= 1; h >>= 1) {
-    const bool up = (lane & h) != 0;
-#pragma unroll
-    for (int i = 0; i < h; ++i) {
-      const float send = up ? x[i] : x[i + h];
-      const float keep = up ? x[i + h] : x[i];
-      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
-    }
-  }
-  return x[0];
-}
-
 
 }  // namespace tc
 }  // namespace nnb

@@ -46,6 +46,10 @@ def _make_segment(rng, batch, dims, channels, lazy, device):
 CONV_CASES = [
     # (batch, in_dims, segments [(channels, lazy)], cout, kernel, stride, pad, precision)
     (2, (6, 7, 9), [(1, False)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "simt"),
+    # first-layer kernel (persistent blocks looping over tiles, partial last tile, two channel groups)
+    (3, (33, 40, 47), [(1, False)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "simt"),
+    (2, (17, 20, 23), [(2, False)], 64, (3, 3, 3), (1, 1, 1), (1, 1, 1), "simt"),
+    (1, (9, 31, 30), [(4, False)], 48, (3, 3, 3), (1, 1, 1), (1, 1, 1), "simt"),
     (2, (5, 6, 7), [(4, True), (8, False)], 8, (3, 3, 3), (2, 2, 2), (1, 1, 1), "simt"),
     (1, (8, 8, 8), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
     (2, (9, 10, 11), [(32, True)], 64, (3, 3, 3), (2, 2, 2), (1, 1, 1), "fp32"),
