@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 8
+#define NNB_ABI_VERSION 9
 
 enum nnb_status {
   NNB_OK = 0,
@@ -233,6 +233,20 @@ int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int3
                              const int32_t kernel[3], float slope, const float* weight,
                              const float* bias, int32_t cout, const void* packed, int32_t precision,
                              float* out, void* stream);
+
+/*
+ * nnb_conv_transpose3d on the NNB_PREC_FP32 tensor-core path whose output is
+ * written directly as the tensor-core operand of the up-sampled activation
+ * (the nnb_prepare_operand(NNB_PREC_FP32) layout: per voxel and 32-channel
+ * group [hi(32) | lo(32)] halves, 4 bytes per channel) instead of float32,
+ * so the decoder's concat convolution reads it without a preparation pass;
+ * out-of-range values count in nnb_operand_range_events.  Requires `packed`,
+ * 32-multiple channel counts and precision NNB_PREC_FP32 (else
+ * NNB_E_UNSUPPORTED).  Same reference call site as nnb_conv_transpose3d.
+ */
+int32_t nnb_conv_transpose3d_operand(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
+                                     const int32_t kernel[3], float slope, const float* bias, int32_t cout,
+                                     const void* packed, int32_t precision, void* out, void* stream);
 
 /* Bytes of the tensor-core image of a transposed-convolution weight (0: not eligible). */
 int64_t nnb_conv_transpose3d_packed_bytes(int32_t cout, int32_t ktaps, int32_t cin, int32_t precision);

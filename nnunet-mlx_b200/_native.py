@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 PREC_FP32 = 0        # split fp16 pairs on the tensor cores, float32-level accuracy (|activation| < 65504)
 PREC_TF32 = 1        # single-pass TF32 tensor cores
@@ -67,6 +67,10 @@ SYMBOLS = {
     "nnb_conv_transpose3d": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, I32x3, I32x3,
                                               ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                               ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_conv_transpose3d_operand": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, I32x3, I32x3,
+                                                      ctypes.c_float, ctypes.c_void_p, ctypes.c_int32,
+                                                      ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                                      ctypes.c_void_p]),
     "nnb_conv_transpose3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
     "nnb_conv_transpose3d_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                                    ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),

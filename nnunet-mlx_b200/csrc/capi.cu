@@ -34,7 +34,7 @@ int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t i
                                cudaStream_t stream);
 int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
                              float slope, const float* bias, int cout, const void* packed, int precision, float* out,
-                             cudaStream_t stream);
+                             int out_operand, cudaStream_t stream);
 int launch_conv3d_pack_rows(const float* w, int rows, int kvol, int cin_total, int precision, int row_taps,
                             int up_cout, void* packed, cudaStream_t stream);
 int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int op, float* out,
@@ -179,10 +179,27 @@ int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int3
   NNB_REQUIRE(batch >= 1 && positive3(in_dims) && positive3(kernel), "conv_transpose3d: bad shape");
   NNB_REQUIRE(weight && out && cout >= 1, "conv_transpose3d: missing weight/output");
   if (packed != nullptr && tensor_precision(precision) && input->channels % 32 == 0 && cout % 32 == 0)
-    return launch_conv_transpose_tc(*input, batch, in_dims, kernel, slope, bias, cout, packed, precision, out,
+    return launch_conv_transpose_tc(*input, batch, in_dims, kernel, slope, bias, cout, packed, precision, out, 0,
                                     (cudaStream_t)stream);
   return launch_conv_transpose_simt(*input, batch, in_dims, kernel, slope, weight, bias, cout, out,
                                     (cudaStream_t)stream);
+}
+
+int32_t nnb_conv_transpose3d_operand(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
+                                     const int32_t kernel[3], float slope, const float* bias, int32_t cout,
+                                     const void* packed, int32_t precision, void* out, void* stream) {
+  NNB_REQUIRE(input != nullptr, "conv_transpose3d_operand: null input");
+  int rc = check_segment(*input, "conv_transpose3d_operand input");
+  if (rc) return rc;
+  NNB_REQUIRE(batch >= 1 && positive3(in_dims) && positive3(kernel), "conv_transpose3d_operand: bad shape");
+  NNB_REQUIRE(out != nullptr && cout >= 1, "conv_transpose3d_operand: missing output");
+  if (packed == nullptr || precision != NNB_PREC_FP32 || input->channels % 32 != 0 || cout % 32 != 0) {
+    set_error("conv_transpose3d_operand: needs the NNB_PREC_FP32 tensor-core path (packed weights, 32-multiple "
+              "channels)");
+    return NNB_E_UNSUPPORTED;
+  }
+  return launch_conv_transpose_tc(*input, batch, in_dims, kernel, slope, bias, cout, packed, precision,
+                                  static_cast<float*>(out), 1, (cudaStream_t)stream);
 }
 
 int64_t nnb_conv_transpose3d_packed_bytes(int32_t cout, int32_t ktaps, int32_t cin, int32_t precision) {

@@ -94,6 +94,7 @@ struct Geometry {
   int n_tiles, total_tiles;
   int nchunk, ksteps, c0len;
   int up_cout, UKD, UKH, UKW;  // transposed convolution scatter (up_cout = 0 otherwise)
+  int up_operand;              // 1: the scatter writes the fp16-pair operand rows instead of float32
   int halo;                    // 1: halo mode
   int box[3];                  // TMA box extent along w, h, d (elements, before element strides)
   int pw, plane_rows, plane_bytes;  // halo plane: row pitch, rows, bytes per half (1024-aligned)
@@ -353,7 +354,25 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
           v[4 * i + 3] += c4.w;
         }
       }
-      store_rows_staged(stg, lane, v, dst);
+      if (g.up_operand) {
+        // the row's [hi(32) | lo(32)] fp16 operand (hi: 13 low mantissa bits cleared, lo = v - hi), 128 bytes
+        // at the same address as its 32 float32 values
+        float pk[32];
+        bool over = false;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float h0 = __uint_as_float(__float_as_uint(v[i]) & 0xFFFFE000u);
+          const float h1 = __uint_as_float(__float_as_uint(v[i + 1]) & 0xFFFFE000u);
+          const __half2 hh = __floats2half2_rn(h0, h1), ll = __floats2half2_rn(v[i] - h0, v[i + 1] - h1);
+          pk[i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&hh));
+          pk[16 + i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&ll));
+          over |= fabsf(v[i]) >= 65504.f || fabsf(v[i + 1]) >= 65504.f;
+        }
+        if (over && valid) atomicAdd(g.range_events, 1ull);
+        store_rows_staged(stg, lane, pk, dst);
+      } else {
+        store_rows_staged(stg, lane, v, dst);
+      }
       continue;
     }
 #pragma unroll
@@ -1754,7 +1773,7 @@ int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream) {
 // voxels, N = taps x cout) with the scatter epilogue.
 int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
                              float slope, const float* bias, int cout, const void* packed, int precision, float* out,
-                             cudaStream_t stream) {
+                             int out_operand, cudaStream_t stream) {
   nnb_conv3d_args a{};
   a.batch = batch;
   for (int i = 0; i < 3; ++i) {
@@ -1783,6 +1802,12 @@ int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_
   g.UKD = k[0];
   g.UKH = k[1];
   g.UKW = k[2];
+  g.up_operand = out_operand;
+  if (out_operand) {
+    NNB_REQUIRE(precision == NNB_PREC_FP32, "conv_transpose3d: operand output needs NNB_PREC_FP32");
+    g.range_events = operand_range_events_ptr();
+    NNB_REQUIRE(g.range_events != nullptr, "conv_transpose3d: range-event counter unavailable");
+  }
   return tc::dispatch(a, g, stream);
 }
 

@@ -198,6 +198,32 @@ class _Prepared(Lazy):
         return self.logical_channels
 
 
+class OperandOnly(Lazy):
+    """An activation that exists only as its fp32-mode tensor-core operand.
+
+    ``raw`` is the fp16-pair operand buffer (4 bytes per channel, so it has the
+    activation's shape as float32 words) and is not a float32 activation:
+    ``segment()`` refuses, and only consumers that take the prepared operand
+    (tensor-core convolutions in ``PREC_FP32``) can read it.
+    """
+
+    def __init__(self, operand: torch.Tensor) -> None:
+        super().__init__(operand)
+        self.prepared[_native.PREC_FP32] = _Prepared(operand, int(operand.shape[-1]))
+
+    def segment(self) -> _native.Segment:
+        raise ContractError("this activation exists only as a PREC_FP32 tensor-core operand")
+
+
+def _query_segment(item: Lazy) -> _native.Segment:
+    """The segment a shape query sees: an operand-only activation shows its prepared operand."""
+    if isinstance(item, OperandOnly):
+        seg = item.prepared[_native.PREC_FP32].segment()
+        seg.prepared = 1
+        return seg
+    return item.segment()
+
+
 def operand_range_events(reset: bool = False) -> int:
     """Activations found outside the fp16-pair operand's range since the last reset (synchronises)."""
     count = int(_native.load().nnb_operand_range_events(1 if reset else 0))
@@ -278,7 +304,7 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
     args.pad = _native.dims3(pad)
     args.num_segments = len(inputs)
     for index, item in enumerate(inputs):
-        args.seg[index] = item.segment()
+        args.seg[index] = _query_segment(item)
     args.slope = float(slope)
     args.cout = int(cout)
     _check_tensor(weight, "weight")
@@ -372,7 +398,7 @@ def conv3d_norm_static(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stri
     args.precision = int(precision)
     args.cout = int(cout)
     for index, item in enumerate(inputs):
-        args.seg[index] = item.segment()
+        args.seg[index] = _query_segment(item)
     args.slope = float(slope)
     raw = tensor_cores and _native.load().nnb_conv3d_raw_operands(ctypes.byref(args)) == 1
     if raw:
@@ -433,6 +459,30 @@ def conv_transpose3d(x: Lazy, weight: torch.Tensor, bias: torch.Tensor | None, k
         "conv_transpose3d")
     PROFILE.stop(token)
     return out
+
+
+def conv_transpose3d_operand(x: Lazy, weight: torch.Tensor, bias: torch.Tensor | None, kernel,
+                             slope: float = 0.01, packed: torch.Tensor | None = None,
+                             precision: int = _native.PREC_SIMT) -> Lazy:
+    """The up-sampled activation for the next convolution: an ``OperandOnly`` activation on the
+    fp32-mode tensor-core path (the transposed conv writes the fp16-pair operand itself, no
+    preparation pass), otherwise a plain ``Lazy`` of the float32 output."""
+    cout = int(weight.shape[0])
+    if not (packed is not None and precision == _native.PREC_FP32 and x.channels % 32 == 0 and cout % 32 == 0):
+        return Lazy(conv_transpose3d(x, weight, bias, kernel, slope, packed=packed, precision=precision))
+    batch = int(x.raw.shape[0])
+    out_dims = tuple(s * k for s, k in zip(x.spatial, kernel))
+    out = torch.empty((batch, *out_dims, cout), dtype=torch.float32, device=x.raw.device)
+    _check_tensor(weight, "weight")
+    seg = prepare_operand(x, precision, slope).segment()
+    token = PROFILE.start("conv_transpose3d_tc", 2.0 * out.numel() * x.channels, 4.0 * (out.numel() + x.raw.numel()),
+                          detail=lambda: (f"{batch}x{'x'.join(map(str, x.spatial))} {x.channels}->{cout} "
+                                          f"up{'x'.join(map(str, kernel))}"))
+    _native.check(_native.load().nnb_conv_transpose3d_operand(
+        ctypes.byref(seg), batch, _native.dims3(x.spatial), _native.dims3(kernel), float(slope), _ptr(bias), cout,
+        packed.data_ptr(), int(precision), out.data_ptr(), _stream()), "conv_transpose3d_operand")
+    PROFILE.stop(token)
+    return OperandOnly(out)
 
 
 def residual_join(branch: Lazy, skip: Lazy, slope: float) -> torch.Tensor:

@@ -181,8 +181,8 @@ class _UNetBase:
         for d in range(len(spec.features) - 1):
             weight, bias, kernel, packed = self.up[d]
             skip = skips.pop()
-            up = Lazy(kernels.conv_transpose3d(hidden, weight, bias, kernel, spec.leaky_slope, packed=packed,
-                                               precision=PRECISIONS[self.precision]))
+            up = kernels.conv_transpose3d_operand(hidden, weight, bias, kernel, spec.leaky_slope, packed=packed,
+                                                  precision=PRECISIONS[self.precision])
             up = _match_spatial(up, skip)
             hidden = self._conv_norm(f"dec{d}.block0", [up, skip], act=True)
             for blk in range(1, spec.decoder_convs[d]):
@@ -217,7 +217,11 @@ class _UNetBase:
 
 
 def _match_spatial(up: Lazy, skip: Lazy) -> Lazy:
-    """Centre crop / zero pad of the up-sampled tensor (reference network.py:898-916)."""
+    """Centre crop / zero pad of the up-sampled tensor (reference network.py:898-916).
+
+    An operand-only activation is cropped / padded in its operand form (zero is
+    the all-zero fp16 pair), so it stays operand-only.
+    """
     if up.spatial == skip.spatial:
         return up
     raw = up.raw
@@ -232,6 +236,8 @@ def _match_spatial(up: Lazy, skip: Lazy) -> Lazy:
             padded = torch.zeros(shape, dtype=raw.dtype, device=raw.device)
             padded.narrow(axis + 1, before, raw.shape[axis + 1]).copy_(raw)
             raw = padded
+    if isinstance(up, kernels.OperandOnly):
+        return kernels.OperandOnly(raw.contiguous())
     return Lazy(raw.contiguous())
 
 

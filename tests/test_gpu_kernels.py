@@ -373,3 +373,30 @@ def test_to_host_returns_fresh_arrays(cuda_device):
     np.testing.assert_array_equal(ha * 2, ha2)  # the first result was not overwritten by the second copy
     np.testing.assert_array_equal(hb, b.cpu().numpy())
     assert ha.dtype == np.float32 and hb.dtype == np.uint8 and ha.shape == (3, 17, 33, 21)
+
+
+def test_conv_transpose_operand_output_decodes_to_the_float32_output(cuda_device):
+    """The operand the fp32-mode transposed conv writes equals (hi + lo) its float32 result; overflow counts."""
+    from nnunet_mlx_b200 import _native, kernels
+
+    rng = np.random.default_rng(51)
+    lz, raw, sc, sh = _make_segment(rng, 2, (5, 6, 7), 64, True, cuda_device)
+    w = torch.from_numpy((rng.standard_normal((64, 2, 2, 2, 64)) / 8).astype(np.float32)).to(cuda_device)
+    b = torch.from_numpy(rng.standard_normal(64).astype(np.float32)).to(cuda_device)
+    packed = kernels.pack_transposed_weights(w, _native.PREC_FP32)
+    ref = kernels.conv_transpose3d(lz, w, b, (2, 2, 2), packed=packed, precision=_native.PREC_FP32)
+    kernels.operand_range_events(reset=True)
+    up = kernels.conv_transpose3d_operand(lz, w, b, (2, 2, 2), packed=packed, precision=_native.PREC_FP32)
+    assert isinstance(up, kernels.OperandOnly)
+    assert kernels.operand_range_events(reset=True) == 0
+    halves = up.raw.view(torch.float16).cpu().numpy().astype(np.float64)
+    pairs = halves.reshape(*ref.shape[:-1], 2, 2, 32)  # (..., group, hi/lo, 32)
+    decoded = (pairs[..., 0, :] + pairs[..., 1, :]).reshape(ref.shape)
+    r = ref.cpu().numpy().astype(np.float64)
+    assert (np.abs(decoded - r) <= 2.0 ** -21 * np.abs(r) + 2.0 ** -24).all()
+    with pytest.raises(Exception):
+        up.segment()  # not a float32 activation
+    big = kernels.conv_transpose3d_operand(lz, w * 1e6, b, (2, 2, 2),
+                                           packed=kernels.pack_transposed_weights(w * 1e6, _native.PREC_FP32),
+                                           precision=_native.PREC_FP32)
+    assert big is not None and kernels.operand_range_events(reset=True) > 0
