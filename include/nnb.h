@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 9
+#define NNB_ABI_VERSION 10
 
 enum nnb_status {
   NNB_OK = 0,
@@ -79,7 +79,7 @@ typedef struct nnb_conv3d_args {
   const void* packed;   /* tensor-core weight image from nnb_conv3d_pack, or NULL */
   const float* bias;    /* (cout) added to the output, or NULL */
   float* out;           /* (B, oD, oH, oW, cout) */
-  float* partials;      /* (B, nnb_conv3d_partial_tiles(args), cout, 3) per-tile
+  float* partials;      /* (B, cout, nnb_conv3d_partial_tiles(args), 3) per-tile
                            (sum, M2, n) of the output, or NULL */
   int32_t precision;    /* enum nnb_precision */
   int32_t operand_format; /* 0: raw float32 segments (lazy affine allowed; CUDA-core kernel);
@@ -185,7 +185,8 @@ int32_t nnb_conv3d_pack(const float* weight, int32_t cout, int32_t kvol, int32_t
 
 /*
  * Instance-norm statistics from `tiles` per-tile (sum, M2, n) partials per
- * (sample, channel) (Chan's parallel combination in float64) -> per-(sample, channel) scale = gamma*rsqrt(var+eps)
+ * (sample, channel), laid out (batch, channels, tiles, 3) (Chan's parallel
+ * combination in float64) -> per-(sample, channel) scale = gamma*rsqrt(var+eps)
  * and shift = beta - mean*scale.  Replaces the reduction passes of
  * src/nnunet_mlx/kernels/metal_native_norm.py:32-60,92-153 (the affine pass
  * 62-70,155-168 is applied lazily by consumers).

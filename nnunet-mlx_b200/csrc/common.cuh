@@ -85,21 +85,4 @@ __device__ __forceinline__ float activate(float raw, const float* scale, const f
   return leaky_flag ? leaky(v, slope) : v;
 }
 
-// Combine (count, mean, M2) triples (Chan et al. parallel variance).
-struct Moments {
-  double n, mean, m2;
-};
-
-__device__ __forceinline__ Moments merge(Moments a, Moments b) {
-  if (b.n == 0) return a;
-  if (a.n == 0) return b;
-  double n = a.n + b.n;
-  double delta = b.mean - a.mean;
-  Moments r;
-  r.n = n;
-  r.mean = a.mean + delta * (b.n / n);
-  r.m2 = a.m2 + b.m2 + delta * delta * (a.n * b.n / n);
-  return r;
-}
-
 }  // namespace nnb

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kTileRows) conv3d_simt_kernel(nnb_conv3d_args 
       const float d = red[i][r] - mean;
       m2 = fmaf(d, d, m2);
     }
-    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 3;
+    float* p = a.partials + (((int64_t)b * a.cout + co0 + r) * tps + t) * 3;
     p[0] = sum;
     p[1] = m2;
     p[2] = (float)rows;
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kTileRows) conv3d_small_cin_kernel(nnb_conv3d_
       const float d = out_s[i][r] - mean;
       m2 = fmaf(d, d, m2);
     }
-    float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + r) * 3;
+    float* p = a.partials + (((int64_t)b * a.cout + co0 + r) * tps + t) * 3;
     p[0] = sum;
     p[1] = m2;
     p[2] = (float)rows;
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int
       __syncthreads();
       if (threadIdx.x < ncols) {
         const int c = threadIdx.x;
-        float* p = a.partials + (((int64_t)b * tps + t) * a.cout + co0 + c) * 3;
+        float* p = a.partials + (((int64_t)b * a.cout + co0 + c) * tps + t) * 3;
         p[0] = sum_s[c];
         p[1] = red_s[0][c] + red_s[1][c];
         p[2] = (float)rows;
@@ -468,39 +468,58 @@ int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------------------
-// Instance-norm finalisation: one block per (channel, sample); each thread
-// merges its tiles' (sum, M2, n) partials in float64, then a tree merge.
+// Instance-norm finalisation: one block per (channel, sample) over its
+// contiguous run of per-tile (sum, M2, n) records, in float64 and two passes:
+// the mean from the summed sums and counts, then
+//   M2 = sum_t [ M2_t + (sum_t - n_t * mean)^2 / n_t ]
+// (the parallel-variance identity; every term is independent, so no chain of
+// merges and divisions serialises a thread).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restrict__ partials,
+__device__ __forceinline__ double block_sum(double v, double* red) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red is free (a previous call's readers are done)
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  return t;
+}
+
+__global__ void __launch_bounds__(1024) norm_finalize_kernel(const float* __restrict__ partials,
                                                             int channels, int tps,
                                                             const float* __restrict__ gamma,
                                                             const float* __restrict__ beta, float eps,
                                                             float* __restrict__ scale,
                                                             float* __restrict__ shift) {
-  __shared__ Moments sm[256];
+  __shared__ double red[32];
   const int c = blockIdx.x;
   const int b = blockIdx.y;
-  Moments acc{0.0, 0.0, 0.0};
+  const float* run = partials + ((int64_t)b * channels + c) * tps * 3;
+  double s = 0.0, n = 0.0;
+#pragma unroll 4
   for (int t = threadIdx.x; t < tps; t += blockDim.x) {
-    const float* p = partials + (((int64_t)b * tps + t) * channels + c) * 3;
-    const double n = (double)p[2];
-    if (n <= 0.0) continue;
-    Moments tile{n, (double)p[0] / n, (double)p[1]};
-    acc = merge(acc, tile);
+    s += (double)run[3 * t];
+    n += (double)run[3 * t + 2];
   }
-  sm[threadIdx.x] = acc;
-  __syncthreads();
-  for (int stride = blockDim.x / 2; stride > 0; stride >>= 1) {
-    if ((int)threadIdx.x < stride) sm[threadIdx.x] = merge(sm[threadIdx.x], sm[threadIdx.x + stride]);
-    __syncthreads();
+  const double total = block_sum(s, red), count = block_sum(n, red);
+  const double mean = count > 0.0 ? total / count : 0.0;
+  double m2 = 0.0;
+#pragma unroll 4
+  for (int t = threadIdx.x; t < tps; t += blockDim.x) {
+    const double nt = (double)run[3 * t + 2];
+    if (nt <= 0.0) continue;
+    const double d = (double)run[3 * t] - nt * mean;
+    m2 += (double)run[3 * t + 1] + d * d / nt;
   }
+  const double m2_total = block_sum(m2, red);
   if (threadIdx.x == 0) {
-    const Moments tot = sm[0];
-    double var = tot.n > 0.0 ? tot.m2 / tot.n : 0.0;
+    double var = count > 0.0 ? m2_total / count : 0.0;
     if (var < 0) var = 0;
     const double inv = 1.0 / sqrt(var + (double)eps);
     const double sc = gamma != nullptr ? (double)gamma[c] * inv : inv;
-    const double sh = (beta != nullptr ? (double)beta[c] : 0.0) - tot.mean * sc;
+    const double sh = (beta != nullptr ? (double)beta[c] : 0.0) - mean * sc;
     scale[(int64_t)b * channels + c] = (float)sc;
     shift[(int64_t)b * channels + c] = (float)sh;
   }
@@ -509,7 +528,9 @@ __global__ void __launch_bounds__(256) norm_finalize_kernel(const float* __restr
 int launch_norm_finalize(const float* partials, int batch, int tiles, int channels, const float* gamma,
                          const float* beta, float eps, float* scale, float* shift, cudaStream_t stream) {
   dim3 grid((unsigned)channels, (unsigned)batch);
-  norm_finalize_kernel<<<grid, 256, 0, stream>>>(partials, channels, tiles, gamma, beta, eps, scale, shift);
+  // 1024 threads: a 128^3 layer's 16384 records per (sample, channel) are 16 loads per thread, in flight together
+  norm_finalize_kernel<<<grid, tiles >= 4096 ? 1024 : 256, 0, stream>>>(partials, channels, tiles, gamma, beta, eps,
+                                                                          scale, shift);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }

@@ -407,7 +407,7 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
       red[q * 32 + lane] = colm2;  // every warp read red before the barrier above
       asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
       if (q == 0 && nbase + lane < a.cout) {
-        float* p = a.partials + (((int64_t)o.b * g.tps + o.t) * a.cout + nbase + lane) * 3;
+        float* p = a.partials + (((int64_t)o.b * a.cout + nbase + lane) * g.tps + o.t) * 3;
         p[0] = total;
         p[1] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
         p[2] = (float)nvalid;

@@ -206,6 +206,110 @@ __global__ void __launch_bounds__(256) accumulate_tile_kernel(
   }
 }
 
+// Row-staged variant (32 features, x extent <= 128, <= 8 classes): one block per
+// output x-row (i, j) of the patch.  For each view the source row -- the same
+// voxels, flipped -- is 128 contiguous bytes per voxel in HBM: cp.async copies it
+// whole-line into a shared buffer (16-byte chunks XOR-swizzled by voxel % 8;
+// two buffers, so the next view's copy overlaps this view's arithmetic), and
+// thread k reads its (x-flipped) voxel from shared memory.  Replaces per-thread
+// 128-byte reads whose every warp instruction touched 32 separate lines.
+constexpr int kRowMax = 128;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+
+template <typename AccT>
+__global__ void __launch_bounds__(kRowMax) accumulate_tile_rows_kernel(
+    nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
+    const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, AccT* __restrict__ acc,
+    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+  constexpr int F = 32;
+  __shared__ float4 rows[2][kRowMax * 8];
+  __shared__ float s_sc[8][F], s_sh[8][F];
+  __shared__ float s_w[kAccMaxC][F];
+  __shared__ float s_b[kAccMaxC];
+  const int PX = patch.d[2];
+  const int i = blockIdx.x / patch.d[1], j = blockIdx.x - i * patch.d[1];
+  for (int t = threadIdx.x; t < views * F; t += blockDim.x) {
+    const int v = t / F, f = t % F;
+    s_sc[v][f] = feat.scale ? feat.scale[v * F + f] : 1.f;
+    s_sh[v][f] = feat.scale ? feat.shift[v * F + f] : 0.f;
+  }
+  for (int t = threadIdx.x; t < kAccMaxC * F; t += blockDim.x) {
+    const int c = t / F, f = t % F;
+    s_w[c][f] = c < classes ? seg_w[c * F + f] : 0.f;
+  }
+  if (threadIdx.x < kAccMaxC) s_b[threadIdx.x] = threadIdx.x < classes ? seg_b[threadIdx.x] : 0.f;
+  // source row of view v: voxels (v, si, sj, 0 .. PX-1), x flipped on read
+  auto issue = [&](int v) {
+    const int m = masks.m[v];
+    const int si = (m & 1) ? patch.d[0] - 1 - i : i;
+    const int sj = (m & 2) ? patch.d[1] - 1 - j : j;
+    const float4* src = reinterpret_cast<const float4*>(
+        feat.data + ((((int64_t)v * patch.d[0] + si) * patch.d[1] + sj) * PX) * F);
+    float4* dst = rows[v & 1];
+    for (int c = threadIdx.x; c < PX * 8; c += blockDim.x) {
+      const int vox = c >> 3, part = c & 7;
+      cp_async16(dst + vox * 8 + (part ^ (vox & 7)), src + c);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue(0);
+  __syncthreads();  // tables ready
+  const bool lazy = feat.scale != nullptr;
+  const int k = threadIdx.x;
+  float pred[kAccMaxC];
+#pragma unroll
+  for (int c = 0; c < kAccMaxC; ++c) pred[c] = 0.f;
+  for (int v = 0; v < views; ++v) {
+    if (v + 1 < views) {
+      issue(v + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // view v's row has landed for every thread
+    if (k < PX) {
+      const int sk = (masks.m[v] & 4) ? PX - 1 - k : k;
+      const float4* r = rows[v & 1] + sk * 8;
+      float logit[kAccMaxC];
+#pragma unroll
+      for (int c = 0; c < kAccMaxC; ++c) logit[c] = s_b[c];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 x4 = r[q ^ (sk & 7)];
+        const float z4[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int f = 4 * q + e;
+          float z = z4[e];
+          if (lazy) {
+            z = fmaf(z, s_sc[v][f], s_sh[v][f]);
+            if (feat.leaky) z = leaky(z, slope);
+          }
+#pragma unroll
+          for (int c = 0; c < kAccMaxC; ++c) logit[c] = fmaf(z, s_w[c][f], logit[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kAccMaxC; ++c) pred[c] += logit[c];
+    }
+    __syncthreads();  // buffer v & 1 is free for view v + 2
+  }
+  if (k >= PX) return;
+  const int64_t p = ((int64_t)i * patch.d[1] + j) * PX + k;
+  const float g = __ldg(gauss + p);
+  const float inv_views = 1.0f / (float)views;
+  const int64_t dst = ((int64_t)(off.d[0] + i) * ad.d[1] + (off.d[1] + j)) * ad.d[2] + (off.d[2] + k);
+  AccT* a = acc + dst * classes;
+#pragma unroll
+  for (int c = 0; c < kAccMaxC; ++c)
+    if (c < classes) acc_add(a + c, (pred[c] * inv_views) * g);
+  if (add_normalizer) acc_add(normalizer + dst, g);
+}
+
 template <typename AccT>
 int launch_accumulate_tile_t(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
                              float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
@@ -218,7 +322,11 @@ int launch_accumulate_tile_t(const nnb_segment& feat, int views, const int32_t* 
   const int64_t pvox = (int64_t)patch[0] * patch[1] * patch[2];
   const int blocks = (int)std::min<int64_t>((pvox + 255) / 256, 148 * 16);
   const bool aligned = (reinterpret_cast<uintptr_t>(feat.data) & 15) == 0;
-  if (aligned && feat.channels == 32) {
+  if (aligned && feat.channels == 32 && patch[2] <= kRowMax && classes <= kAccMaxC &&
+      (int64_t)patch[0] * patch[1] < (1LL << 31)) {
+    accumulate_tile_rows_kernel<AccT><<<(unsigned)((int64_t)patch[0] * patch[1]), kRowMax, 0, stream>>>(
+        feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss, acc, normalizer, dad, doff, add_normalizer);
+  } else if (aligned && feat.channels == 32) {
     accumulate_tile_vec_kernel<8, AccT><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b,
                                                                     classes, gauss, acc, normalizer, dad, doff,
                                                                     add_normalizer);

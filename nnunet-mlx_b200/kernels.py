@@ -330,7 +330,7 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
         tiles = int(_native.load().nnb_conv3d_partial_tiles(ctypes.byref(args)))
         if tiles < 1:
             _native.check(tiles or -1, "conv3d_partial_tiles")
-        partials = torch.empty((batch, tiles, cout, 3), dtype=torch.float32, device=device)
+        partials = torch.empty((batch, cout, tiles, 3), dtype=torch.float32, device=device)
         args.partials = partials.data_ptr()
     flops = 2.0 * batch * math.prod(out_dims) * cout * cin * math.prod(kernel)
     token = PROFILE.start("conv3d_tc" if tensor_cores else "conv3d_simt", flops,
@@ -345,8 +345,8 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
 
 def instance_norm_finalize(partials: torch.Tensor, gamma: torch.Tensor | None, beta: torch.Tensor | None,
                            eps: float):
-    """Per-(sample, channel) ``(scale, shift)`` from ``(B, tiles, C, 3)`` (sum, M2, n) partials."""
-    batch, tiles, channels, _ = partials.shape
+    """Per-(sample, channel) ``(scale, shift)`` from ``(B, C, tiles, 3)`` (sum, M2, n) partials."""
+    batch, channels, tiles, _ = partials.shape
     scale = torch.empty((batch, channels), dtype=torch.float32, device=partials.device)
     shift = torch.empty_like(scale)
     token = PROFILE.start("instance_norm_finalize", 0.0, partials.numel() * 4.0)
