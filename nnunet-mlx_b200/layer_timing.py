@@ -2,7 +2,7 @@
 
     python -m nnunet_mlx_b200.layer_timing --config 2 --precision fp32 --batch 8 --patch 128
 
-Builds the BASELINE configuration's network with seeded synthetic weights, runs
+Builds a benchmark configuration's network with seeded synthetic weights, runs
 ``--warmup`` untimed forwards on a random ``(batch, patch^3, channels)`` input,
 then one forward with the library profiler on, and prints one line per device
 call (operation, shape, milliseconds, useful TFLOP/s or GB/s).  The batch of 8

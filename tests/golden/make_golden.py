@@ -30,7 +30,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 
-# Geometry cases: the BASELINE volumes (z padded to the patch where smaller),
+# Geometry cases: the benchmark volumes (z padded to the patch where smaller),
 # the reference tests' small shapes and odd edge cases.
 STEP_CASES = [
     ((128, 128, 128), (128, 128, 128), 0.5),

@@ -1,6 +1,6 @@
 """Network forward and sliding-window parity on B200 against the CPU oracle.
 
-Tolerance (BASELINE): logits within rel 1e-3 / abs 1e-3 of the float32
+Tolerance (the path's parity bar): logits within rel 1e-3 / abs 1e-3 of the float32
 oracle in the default ("fp32": split fp16-pair tensor cores) mode and in its
 split-TF32 range fallback ("fp32-tf32x2"), argmax agreement >= 99.95% with
 disagreements only at near-ties.  The single-pass TF32 fast mode is checked

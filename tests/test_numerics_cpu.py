@@ -3,7 +3,7 @@
 The default ``fp32`` precision computes every tensor-core convolution from
 fp16 operand pairs (``hi + lo``, three products, per-column power-of-two
 weight scales).  Emulating exactly those products with float32 convolutions on
-the benchmark network must stay inside the BASELINE tolerance (logits within
+the benchmark network must stay inside the parity tolerance (logits within
 rel/abs 1e-3 of float32, argmax >= 99.95%) with a wide margin, while a single
 fp16 product per element must not -- the reason the pair exists.
 """
