@@ -1,7 +1,7 @@
 """Benchmark: voxels/s of full-volume 8x-mirrored 3-D U-Net sliding-window inference on B200.
 
 One step = one full pass of the inference hot path over the benchmark volume
-(1 x 101 x 768 x 768 synthetic CT, PlainConvUNet 32..320,
+(benchmark config 2: 1 x 101 x 768 x 768 synthetic CT, PlainConvUNet 32..320,
 patch 128^3, step 0.5, 8 mirrored views, 1 fold; 121 tiles, 968 forwards):
 mirrored tile gather -> U-Net forward of the 8 views as one batch -> fused seg
 head + flip-back + Gaussian accumulation, for every tile; then normalise +
@@ -57,7 +57,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=3)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--config", type=int, default=2, help="BASELINE config number (2, 3, 4 or 5)")
+    p.add_argument("--config", type=int, default=2, help="benchmark config number (2, 3, 4 or 5)")
     p.add_argument("--precision", choices=["fp32", "fp32-tf32x2", "tf32"], default="fp32")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
