@@ -63,3 +63,19 @@ def _free_port() -> int:
 @pytest.mark.parametrize("world,shape,classes", [(2, (5, 6, 7), 3), (2, (1, 4, 4), 2), (3, (8, 3, 5), 5)])
 def test_exchange_slabs_sums_ranks_and_keeps_the_own_slab(world, shape, classes):
     mp.spawn(_exchange_worker, args=(world, _free_port(), shape, classes), nprocs=world, join=True)
+
+
+def _any_rank_worker(rank: int, world: int, port: int, flagged: tuple) -> None:
+    from nnunet_mlx_b200.distributed import _any_rank
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        assert _any_rank(rank in flagged, torch.device("cpu"), world, None) == bool(flagged)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,flagged", [(2, ()), (2, (1,)), (3, (0, 2))])
+def test_range_flag_is_or_reduced_over_ranks(world, flagged):
+    """Every rank recomputes in split TF32 when any rank met an out-of-range operand."""
+    mp.spawn(_any_rank_worker, args=(world, _free_port(), flagged), nprocs=world, join=True)
