@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 10
+#define NNB_ABI_VERSION 11
 
 enum nnb_status {
   NNB_OK = 0,
@@ -342,6 +342,50 @@ int32_t nnb_normalize_labels(const float* acc, const float* normalizer, int32_t 
                              const int32_t crop_dims[3], float fold_divisor, float* logits,
                              void* labels, int32_t label_bytes, int32_t* invalid_count,
                              void* stream);
+
+/*
+ * Device restoration of class labels: class logits on the network's grid ->
+ * resampled to the cropped original grid -> first-argmax labels -> written
+ * into the uncropped volume in the output axis order, in one pass.
+ *
+ * Interpolation is order-1 (trilinear) on a half-pixel grid with edge-clamped
+ * indices: per target index t of an axis with source size S and target size T,
+ * c = (t + 0.5) * (S / T) - 0.5, i0 = clamp(floor(c)), i1 = clamp(floor(c) + 1),
+ * w1 = c - floor(c), w0 = 1 - w1; the value is the float64 sum over the eight
+ * corners, axis-0 corner outermost, of ((v * w_0) * w_1) * w_2, rounded once to
+ * the logits' precision (float32, or IEEE half for half logits); the label is
+ * the first class with the largest rounded value.  This is the arithmetic of
+ * the host spline path at order 1 (scipy.ndimage.zoom, grid_mode, mode
+ * "nearest", as called through skimage resize), reproduced operation for
+ * operation, so values and labels equal that path's bit for bit.  Voxels of
+ * the volume outside the crop box get label 0.  Equal source and target grids
+ * reduce to the argmax of the logits.
+ *
+ * Replaces the fused Metal restoration
+ * src/nnunet_mlx/kernels/metal_restore.py:71-139 (kernel), :404-427 (launch),
+ * :462-495 (per-axis metadata), its callers :292-334 and :363-401, and the host
+ * uncrop + inverse transpose of src/nnunet_mlx/prediction/export.py:363-373.
+ * Unlike the Metal kernel (double-single arithmetic, logits limited to
+ * FLT_MAX / 16) any finite float32 or half logits are accepted.
+ */
+typedef struct nnb_restore_args {
+  const void* logits;           /* class logits on the source grid (device)                  */
+  int32_t half;                 /* 0: float32 logits, 1: IEEE half logits                    */
+  int32_t classes;              /* 1 .. 65536 (1 .. 255 for 1-byte labels)                  */
+  int32_t source_dims[3];       /* source grid (S0, S1, S2)                                  */
+  int32_t target_dims[3];       /* resampled grid = crop box extent (T0, T1, T2)             */
+  int64_t class_stride;         /* element strides of the logits: class, then axes 0..2      */
+  int64_t source_strides[3];    /*   (any layout: (C, S0, S1, S2), (S0, S1, S2, C), views)   */
+  int32_t volume_dims[3];       /* uncropped volume in the source axis order                 */
+  int32_t crop_lo[3];           /* start of the crop box in the volume                       */
+  int32_t axes[3];              /* output axis i is volume axis axes[i] (a permutation)      */
+  int32_t label_bytes;          /* 2: uint16 labels, 1: uint8                                */
+  void* labels;                 /* output, contiguous, shape volume_dims[axes[i]] (device)    */
+  int32_t* invalid_count;       /* device counter: += voxels whose interpolated value is not
+                                   finite (their label is all ones); zeroed by the call      */
+} nnb_restore_args;
+
+int32_t nnb_restore_class_labels(const nnb_restore_args* args, void* stream);
 
 #ifdef __cplusplus
 }

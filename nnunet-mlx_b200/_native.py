@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 10
+ABI_VERSION = 11
 
 PREC_FP32 = 0        # split fp16 pairs on the tensor cores, float32-level accuracy (|activation| < 65504)
 PREC_TF32 = 1        # single-pass TF32 tensor cores
@@ -43,6 +43,16 @@ class Conv3dArgs(ctypes.Structure):
                 ("packed", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p),
                 ("partials", ctypes.c_void_p), ("precision", ctypes.c_int32),
                 ("operand_format", ctypes.c_int32)]
+
+
+I64x3 = ctypes.c_int64 * 3
+
+
+class RestoreArgs(ctypes.Structure):
+    _fields_ = [("logits", ctypes.c_void_p), ("half", ctypes.c_int32), ("classes", ctypes.c_int32),
+                ("source_dims", I32x3), ("target_dims", I32x3), ("class_stride", ctypes.c_int64),
+                ("source_strides", I64x3), ("volume_dims", I32x3), ("crop_lo", I32x3), ("axes", I32x3),
+                ("label_bytes", ctypes.c_int32), ("labels", ctypes.c_void_p), ("invalid_count", ctypes.c_void_p)]
 
 
 SYMBOLS = {
@@ -96,6 +106,7 @@ SYMBOLS = {
     "nnb_normalize_labels": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3,
                                               I32x3, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_restore_class_labels": (ctypes.c_int32, [ctypes.POINTER(RestoreArgs), ctypes.c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

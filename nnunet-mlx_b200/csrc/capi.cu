@@ -56,6 +56,7 @@ int launch_fold_finalize_fp16(void* total, int classes, int64_t vox, int folds, 
 int launch_normalize_labels(const float* acc, const float* normalizer, int classes, const int32_t ad[3],
                             const int32_t lo[3], const int32_t cd[3], float fold_divisor, float* logits,
                             void* labels, int label_bytes, int32_t* invalid_count, cudaStream_t stream);
+int launch_restore_labels(const nnb_restore_args& a, cudaStream_t stream);
 
 static int check_segment(const nnb_segment& s, const char* what) {
   NNB_REQUIRE(s.data != nullptr, "%s: null data", what);
@@ -309,6 +310,29 @@ int32_t nnb_normalize_labels(const float* acc, const float* normalizer, int32_t 
                 "normalize_labels: crop outside accumulator on axis %d", i);
   return launch_normalize_labels(acc, normalizer, classes, acc_dims, crop_lo, crop_dims, fold_divisor, logits,
                                  labels, label_bytes, invalid_count, (cudaStream_t)stream);
+}
+
+int32_t nnb_restore_class_labels(const nnb_restore_args* a, void* stream) {
+  NNB_REQUIRE(a != nullptr, "restore_class_labels: null arguments");
+  NNB_REQUIRE(a->logits && a->labels && a->invalid_count, "restore_class_labels: null pointer");
+  NNB_REQUIRE(a->half == 0 || a->half == 1, "restore_class_labels: half must be 0 or 1");
+  NNB_REQUIRE(a->label_bytes == 1 || a->label_bytes == 2, "restore_class_labels: label_bytes must be 1 or 2");
+  NNB_REQUIRE(a->classes >= 1 && a->classes <= (a->label_bytes == 1 ? 256 : 65536),
+              "restore_class_labels: %d classes do not fit %d-byte labels", a->classes, a->label_bytes);
+  NNB_REQUIRE(positive3(a->source_dims) && positive3(a->target_dims) && positive3(a->volume_dims),
+              "restore_class_labels: dimensions must be positive");
+  NNB_REQUIRE(a->class_stride >= 0 && a->source_strides[0] >= 0 && a->source_strides[1] >= 0 &&
+                  a->source_strides[2] >= 0,
+              "restore_class_labels: strides must be non-negative");
+  int seen = 0;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(a->axes[i] >= 0 && a->axes[i] < 3 && !(seen & (1 << a->axes[i])),
+                "restore_class_labels: axes must be a permutation of (0, 1, 2)");
+    seen |= 1 << a->axes[i];
+    NNB_REQUIRE(a->crop_lo[i] >= 0 && (int64_t)a->crop_lo[i] + a->target_dims[i] <= a->volume_dims[i],
+                "restore_class_labels: crop box outside the volume on axis %d", i);
+  }
+  return launch_restore_labels(*a, (cudaStream_t)stream);
 }
 
 }  // extern "C"

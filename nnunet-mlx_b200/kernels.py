@@ -608,3 +608,58 @@ def normalize_labels(acc: torch.Tensor, normalizer: torch.Tensor, crop_lo, crop_
         invalid.data_ptr(), _stream()), "normalize_labels")
     PROFILE.stop(token)
     return logits, labels, invalid
+
+
+def restore_class_labels(logits: torch.Tensor, target, *, class_axis: int = 0, volume=None, crop_lo=(0, 0, 0),
+                         axes=(0, 1, 2), label_dtype: torch.dtype = torch.uint16):
+    """Labels of class logits resampled to ``target``, uncropped and axis-permuted, in one device pass.
+
+    ``logits``: 4-D float32 or float16 CUDA tensor, classes on ``class_axis`` (0: ``(C, S0, S1, S2)``,
+    3: ``(S0, S1, S2, C)``), any strides.  Each class is resampled to the ``target`` grid by order-1
+    interpolation on the half-pixel grid with edge-clamped indices (float64, one rounding to the logits'
+    dtype); the label is the first class with the largest value.  The ``target``-sized crop is placed at
+    ``crop_lo`` in a zero ``volume`` (default: ``target``) and the result is permuted so that output axis
+    ``i`` is volume axis ``axes[i]``.  Returns ``(labels, invalid)``: contiguous ``label_dtype`` labels and a
+    one-element int32 device count of voxels whose value was not finite (labelled all ones).
+    """
+    if not isinstance(logits, torch.Tensor) or not logits.is_cuda or logits.dim() != 4:
+        raise ContractError("restoration requires 4-D CUDA class logits")
+    if logits.dtype not in (torch.float32, torch.float16):
+        raise ContractError("restoration requires float32 or float16 logits")
+    if class_axis not in (0, 3, -1):
+        raise ContractError("class_axis must be 0 (classes first) or 3 (classes last)")
+    class_axis %= 4
+    spatial_axes = [a for a in range(4) if a != class_axis]
+    classes = int(logits.shape[class_axis])
+    source = tuple(int(logits.shape[a]) for a in spatial_axes)
+    target = tuple(int(v) for v in target)
+    volume = target if volume is None else tuple(int(v) for v in volume)
+    if label_dtype == torch.uint8:
+        label_bytes = 1
+    elif label_dtype in (torch.uint16, torch.int16):
+        label_bytes = 2
+    else:
+        raise ContractError("labels must be uint8 or uint16")
+    if len(target) != 3 or len(volume) != 3 or sorted(int(a) for a in axes) != [0, 1, 2]:
+        raise ContractError("restoration needs three target and volume sizes and an axis permutation")
+    labels = torch.empty(tuple(volume[int(a)] for a in axes), dtype=label_dtype, device=logits.device)
+    invalid = torch.zeros((1,), dtype=torch.int32, device=logits.device)
+    args = _native.RestoreArgs()
+    args.logits = logits.data_ptr()
+    args.half = 1 if logits.dtype == torch.float16 else 0
+    args.classes = classes
+    args.source_dims = _native.dims3(source)
+    args.target_dims = _native.dims3(target)
+    args.class_stride = int(logits.stride(class_axis))
+    args.source_strides = _native.I64x3(*(int(logits.stride(a)) for a in spatial_axes))
+    args.volume_dims = _native.dims3(volume)
+    args.crop_lo = _native.dims3(crop_lo)
+    args.axes = _native.dims3(axes)
+    args.label_bytes = label_bytes
+    args.labels = labels.data_ptr()
+    args.invalid_count = invalid.data_ptr()
+    token = PROFILE.start("restore_class_labels", 0.0,
+                          float(logits.element_size() * classes * math.prod(source) + label_bytes * labels.numel()))
+    _native.check(_native.load().nnb_restore_class_labels(ctypes.byref(args), _stream()), "restore_class_labels")
+    PROFILE.stop(token)
+    return labels, invalid

@@ -11,12 +11,17 @@ It imports only the reference's pure-host helpers, which run without MLX:
 * ``nnunet_mlx.storage.weights.map_key_and_layout`` / ``convert_state_dict``
   (reference 48-182) applied to upstream-style state-dict keys;
 * ``nnunet_mlx.prediction.inference.logits_to_probabilities`` /
-  ``probabilities_to_segmentation`` (reference 210-269).
+  ``probabilities_to_segmentation`` (reference 210-269);
+* ``nnunet_mlx.kernels.metal_restore._axis_metadata`` (reference 476-495, the
+  fused restoration's per-axis indices and double-single weights) and
+  ``device_class_restore_supported`` (336-360), and
+  ``nnunet_mlx.data.resampling.separate_z_axis`` (587-616).
 
 It also copies the reference's recorded upstream vectors from
 ``tests/fixtures/darwin-arm64/upstream_runner.npz`` (head conversion arrays and
 float16 fold-rounding probes).  Outputs: ``geometry.json``, ``gaussian.npz``,
-``weights_map.json``, ``upstream_runner_subset.npz``.  Nothing at test time
+``weights_map.json``, ``upstream_runner_subset.npz``, ``restore_axes.npz``,
+``restore_policy.json``.  Nothing at test time
 reads the reference checkout.
 """
 
@@ -50,6 +55,43 @@ STEP_CASES = [
 GAUSSIAN_FULL = [(4, 4, 4), (5, 6, 7), (16, 32, 32), (4, 5), (7, 9)]
 GAUSSIAN_SUMMARY = [(128, 128, 128), (96, 160, 160), (80, 192, 160)]
 FP16_GAUSSIAN = [(4, 4, 4), (16, 32, 32), (8, 8, 8)]
+
+# Restoration: (source, target) axis sizes (the reference tests' shapes, the
+# benchmark grids, up/down by odd ratios, size-1 axes) ...
+RESTORE_AXES = [(2, 3), (3, 5), (4, 7), (5, 3), (7, 4), (11, 6), (1, 3), (5, 7), (7, 1), (4, 7), (5, 8),
+                (6, 9), (3, 3), (128, 128), (101, 128), (614, 768), (768, 614), (240, 155), (400, 401),
+                (1, 1), (2, 1), (9, 2)]
+# ... support decisions: (source, target, current spacing, new spacing,
+# (function, order, order_z, force_separate_z, threshold), classes).
+_ORDER1 = ("resample_data_or_seg_to_shape", 1, 0, False, 3.0)
+_AUTO1 = ("resample_data_or_seg_to_shape", 1, 0, None, 3.0)
+_ORDER3 = ("resample_data_or_seg_to_shape", 3, 0, None, 3.0)
+_TORCH = ("resample_torch_fornnunet", 1, 0, None, 3.0)
+RESTORE_SUPPORT = [
+    ((4, 5, 6), (7, 8, 9), (1.0, 1.0, 1.0), (1.0, 1.0, 1.0), _ORDER1, 3),
+    ((4, 5, 6), (4, 5, 6), (1.0, 1.0, 1.0), (1.0, 1.0, 1.0), _ORDER3, 3),
+    ((4, 5, 6), (4, 5, 6), (5.0, 1.0, 1.0), (1.0, 1.0, 1.0), _TORCH, 3),
+    ((4, 5, 6), (7, 8, 9), (1.0, 1.0, 1.0), (1.0, 1.0, 1.0), _ORDER3, 3),
+    ((4, 5, 6), (7, 8, 9), (1.0, 1.0, 1.0), (1.0, 1.0, 1.0), _TORCH, 3),
+    ((40, 50, 50), (120, 60, 60), (3.0, 0.8, 0.8), (1.0, 0.7, 0.7), _AUTO1, 3),
+    ((40, 50, 50), (120, 60, 60), (2.5, 0.8, 0.8), (1.0, 0.7, 0.7), _AUTO1, 3),
+    ((40, 50, 50), (120, 60, 60), (1.0, 1.0, 1.0), (4.0, 1.0, 1.0), _AUTO1, 3),
+    ((40, 50, 50), (120, 60, 60), (1.0, 4.0, 4.0), (1.0, 1.0, 1.0), _AUTO1, 3),
+    ((40, 50, 50), (120, 60, 60), (1.0, 1.0, 1.0), (1.0, 1.0, 1.0),
+     ("resample_data_or_seg_to_shape", 1, 0, True, 3.0), 3),
+    ((40, 50, 50), (120, 60, 60), (2.0, 1.0, 1.0), (1.0, 1.0, 1.0),
+     ("resample_data_or_seg_to_shape", 1, 0, True, 3.0), 3),
+    ((40, 50, 50), (120, 60, 60), (2.0, 1.0, 1.0), (1.0, 1.0, 1.0), _ORDER1, 0),
+    ((40, 50, 50), (120, 60, 60), (2.0, 1.0, 1.0), (1.0, 1.0, 1.0), _ORDER1, 65536),
+    ((40, 50, 50), (120, 60, 60), (2.0, 1.0, 1.0), (1.0, 1.0, 1.0), _ORDER1, 65537),
+    ((101, 768, 768), (101, 768, 768), (2.5, 0.8, 0.8), (2.5, 0.8, 0.8), _AUTO1, 3),
+    ((101, 614, 614), (101, 768, 768), (2.5, 1.0, 1.0), (2.5, 0.8, 0.8), _AUTO1, 3),
+    ((101, 614, 614), (101, 768, 768), (5.0, 1.0, 1.0), (5.0, 0.8, 0.8), _AUTO1, 3),
+]
+SEPARATE_Z = [((3.0, 0.8, 0.8), (1.0, 1.0, 1.0), None, 3.0), ((1.0, 1.0, 1.0), (1.0, 1.0, 3.5), None, 3.0),
+              ((1.0, 1.0, 1.0), (3.5, 3.5, 1.0), None, 3.0), ((2.0, 1.0, 1.0), (1.0, 1.0, 1.0), True, 3.0),
+              ((1.0, 1.0, 1.0), (1.0, 1.0, 1.0), True, 3.0), ((5.0, 1.0, 1.0), (1.0, 1.0, 1.0), False, 3.0),
+              ((2.5, 0.8, 0.8), (2.5, 0.8, 0.8), None, 3.0), ((2.5, 0.8, 0.8), (2.5, 0.8, 0.8), None, 2.0)]
 
 
 def _upstream_plain_keys(stages: int, enc_convs, dec_convs, cin, feats, classes, k=3):
@@ -201,6 +243,31 @@ def main(reference: Path) -> None:
     subset["reference_probabilities_class"] = inference.logits_to_probabilities(
         recorded["head_logits_class"], has_regions=False)
     np.savez_compressed(HERE / "upstream_runner_subset.npz", **subset)
+
+    from nnunet_mlx.data.resampling import separate_z_axis
+    from nnunet_mlx.kernels.metal_restore import _axis_metadata, device_class_restore_supported
+    from nnunet_mlx.plans import ResamplingContract
+
+    axes: dict[str, np.ndarray] = {}
+    for source, target in RESTORE_AXES:
+        names = ("lower", "upper", "lower_high", "lower_low", "upper_high", "upper_low")
+        for name, array in zip(names, _axis_metadata(source, target), strict=True):
+            axes[f"{source}_{target}_{name}"] = array
+    np.savez_compressed(HERE / "restore_axes.npz", **axes)
+    support = []
+    for source, target, current, new, (fn, order, order_z, force, threshold), classes in RESTORE_SUPPORT:
+        contract = ResamplingContract(fn, order, order_z, force, separate_z_anisotropy_threshold=threshold)
+        decision = device_class_restore_supported(source, target, current, new, contract, classes=classes)
+        support.append({"source": list(source), "target": list(target), "current": list(current),
+                        "new": list(new), "contract": [fn, order, order_z, force, threshold],
+                        "classes": classes, "supported": bool(decision)})
+    separate = []
+    for current, new, force, threshold in SEPARATE_Z:
+        flag, axis = separate_z_axis(current, new, force=force, threshold=threshold)
+        separate.append({"current": list(current), "new": list(new), "force": force, "threshold": threshold,
+                         "separate": bool(flag), "axis": axis})
+    (HERE / "restore_policy.json").write_text(
+        json.dumps({"support": support, "separate_z": separate}, indent=1) + "\n")
 
 
 if __name__ == "__main__":
