@@ -290,52 +290,53 @@ __global__ void __launch_bounds__(256) restore_identity_kernel(const In* __restr
 }
 
 // ---------------------------------------------------------------------------
-// Resampling grid.  Per voxel: eight corner offsets and three weight pairs; an
-// axis whose upper weight is exactly 0 (every index of an axis that is not
-// resampled) drops out -- its lower weight is exactly 1 and the dropped
-// corners contribute +-0 -- so the sum equals the host path's eight-corner sum.
+// Resampling grid.  An axis whose upper weight is exactly 0 (every index of an
+// axis that is not resampled) drops out of a voxel's sum: its lower weight is
+// exactly 1 and the dropped corners contribute +-0, so the sum equals the host
+// path's eight-corner sum.  Each of the 8 patterns of active axes has its own
+// unrolled code (Z1, Y1, X1), so only the needed corners are loaded and
+// multiplied; within a warp the pattern is nearly always uniform.
 // ---------------------------------------------------------------------------
-struct VoxelTaps {
-  int64_t off[8];
-  double wz[2], wy[2], wx[2];
-  bool z1, y1, x1;
-};
 
-__device__ __forceinline__ VoxelTaps voxel_taps(const AxisTap& tz, const AxisTap& ty, const AxisTap& tx,
-                                                const int64_t (&st)[3]) {
-  VoxelTaps t;
-  t.z1 = tz.w1 != 0.0;
-  t.y1 = ty.w1 != 0.0;
-  t.x1 = tx.w1 != 0.0;
-  t.wz[0] = tz.w0, t.wz[1] = tz.w1, t.wy[0] = ty.w0, t.wy[1] = ty.w1, t.wx[0] = tx.w0, t.wx[1] = tx.w1;
+// The interpolant of one class: the corners' float64 terms ((v * w_0) * w_1) *
+// w_2 (active axes only, one rounding per operation) summed in (axis 0, axis 1,
+// axis 2) binary corner order, axis 2 fastest, rounded to the logits' dtype.
+template <bool Z1, bool Y1, bool X1, typename In>
+__device__ __forceinline__ float interpolant(const In* __restrict__ p, const int64_t (&zo)[2], const int64_t (&yo)[2],
+                                             const int64_t (&xo)[2], const double (&wz)[2], const double (&wy)[2],
+                                             const double (&wx)[2]) {
+  constexpr int NZ = Z1 ? 2 : 1, NY = Y1 ? 2 : 1, NX = X1 ? 2 : 1;
+  float raw[NZ][NY][NX];
 #pragma unroll
-  for (int corner = 0; corner < 8; ++corner) {
-    const int bz = corner >> 2, by = (corner >> 1) & 1, bx = corner & 1;
-    t.off[corner] = (bz ? tz.i1 : tz.i0) * st[0] + (by ? ty.i1 : ty.i0) * st[1] + (bx ? tx.i1 : tx.i0) * st[2];
-  }
-  return t;
-}
-
-__device__ __forceinline__ bool corner_used(const VoxelTaps& t, int corner) {
-  return !(((corner >> 2) && !t.z1) || (((corner >> 1) & 1) && !t.y1) || ((corner & 1) && !t.x1));
-}
-
-// The interpolant of one class from its loaded corner values, summed in float64
-// in (axis 0, axis 1, axis 2) binary corner order, axis 2 fastest, each term
-// ((v * w_0) * w_1) * w_2 with one rounding per operation.
-__device__ __forceinline__ double corner_sum(const VoxelTaps& t, const float (&raw)[8]) {
+  for (int bz = 0; bz < NZ; ++bz)
+#pragma unroll
+    for (int by = 0; by < NY; ++by)
+#pragma unroll
+      for (int bx = 0; bx < NX; ++bx) raw[bz][by][bx] = load_raw<In>(p, zo[bz] + yo[by] + xo[bx]);
   double s = 0.0;
 #pragma unroll
-  for (int corner = 0; corner < 8; ++corner) {
-    if (!corner_used(t, corner)) continue;
-    const int bz = corner >> 2, by = (corner >> 1) & 1, bx = corner & 1;
-    double term = (double)raw[corner];
-    if (t.z1) term = __dmul_rn(term, t.wz[bz]);
-    if (t.y1) term = __dmul_rn(term, t.wy[by]);
-    if (t.x1) term = __dmul_rn(term, t.wx[bx]);
-    s = __dadd_rn(s, term);
-  }
-  return s;
+  for (int bz = 0; bz < NZ; ++bz)
+#pragma unroll
+    for (int by = 0; by < NY; ++by)
+#pragma unroll
+      for (int bx = 0; bx < NX; ++bx) {
+        double term = (double)raw[bz][by][bx];
+        if (Z1) term = __dmul_rn(term, wz[bz]);
+        if (Y1) term = __dmul_rn(term, wy[by]);
+        if (X1) term = __dmul_rn(term, wx[bx]);
+        s = __dadd_rn(s, term);
+      }
+  return round_to_input<In>(s);
+}
+
+template <bool Z1, bool Y1, bool X1, typename In>
+__device__ __forceinline__ void classify(const In* __restrict__ logits, int classes, int64_t cstride,
+                                         const int64_t (&zo)[2], const int64_t (&yo)[2], const int64_t (&xo)[2],
+                                         const double (&wz)[2], const double (&wy)[2], const double (&wx)[2],
+                                         float& best, int& winner, bool& invalid) {
+  for (int c = 0; c < classes; ++c)
+    argmax_step(interpolant<Z1, Y1, X1, In>(logits + c * cstride, zo, yo, xo, wz, wy, wx), c, best, winner,
+                invalid);
 }
 
 // One output row whose voxels step along volume axis RA; the taps of the two
@@ -349,7 +350,9 @@ __device__ __forceinline__ int restore_row(const In* __restrict__ logits, const 
   constexpr int B = RA == 2 ? 1 : 2;
   const AxisTap ta = axis_tap(c_a, g.src[A], g.ratio[A]);
   const AxisTap tb = axis_tap(c_b, g.src[B], g.ratio[B]);
-  const int64_t st[3] = {g.sstride[0], g.sstride[1], g.sstride[2]};
+  const int64_t ao[2] = {ta.i0 * g.sstride[A], ta.i1 * g.sstride[A]};
+  const int64_t bo[2] = {tb.i0 * g.sstride[B], tb.i1 * g.sstride[B]};
+  const double aw[2] = {ta.w0, ta.w1}, bw[2] = {tb.w0, tb.w1};
   const int x_lo = g.lo[RA], x_hi = g.lo[RA] + g.tgt[RA];  // crop extent along the row
   int invalid_voxels = 0;
   for (int o2 = lane; o2 < g.out[2]; o2 += 32) {
@@ -358,29 +361,30 @@ __device__ __forceinline__ int restore_row(const In* __restrict__ logits, const 
       continue;
     }
     const AxisTap tv = axis_tap(o2 - x_lo, g.src[RA], g.ratio[RA]);
-    AxisTap tz, ty, tx;
-    if (RA == 0) {
-      tz = tv, ty = ta, tx = tb;
-    } else if (RA == 1) {
-      tz = ta, ty = tv, tx = tb;
-    } else {
-      tz = ta, ty = tb, tx = tv;
-    }
-    const VoxelTaps t = voxel_taps(tz, ty, tx, st);
+    const int64_t vo[2] = {tv.i0 * g.sstride[RA], tv.i1 * g.sstride[RA]};
+    const double vw[2] = {tv.w0, tv.w1};
+    // offsets and weights by volume axis 0, 1, 2
+    const int64_t(&zo)[2] = RA == 0 ? vo : ao;
+    const int64_t(&yo)[2] = RA == 1 ? vo : (RA == 0 ? ao : bo);
+    const int64_t(&xo)[2] = RA == 2 ? vo : bo;
+    const double(&wz)[2] = RA == 0 ? vw : aw;
+    const double(&wy)[2] = RA == 1 ? vw : (RA == 0 ? aw : bw);
+    const double(&wx)[2] = RA == 2 ? vw : bw;
+    const int pattern = (wz[1] != 0.0 ? 4 : 0) | (wy[1] != 0.0 ? 2 : 0) | (wx[1] != 0.0 ? 1 : 0);
     float best = 0.f;
     int winner = 0;
     bool invalid = false;
-    for (int c = 0; c < g.classes; ++c) {
-      // the class's corner loads issue together, ahead of its float64 sum
-      float raw[8];
-#pragma unroll
-      for (int corner = 0; corner < 8; ++corner) {
-        // a dropped corner re-reads corner 0 (always used, same cache line): no extra traffic
-        const bool used = corner_used(t, corner);
-        const float x = load_raw<In>(logits, c * g.cstride + (used ? t.off[corner] : t.off[0]));
-        raw[corner] = used ? x : 0.f;
-      }
-      argmax_step(round_to_input<In>(corner_sum(t, raw)), c, best, winner, invalid);
+    const int C = g.classes;
+    const int64_t cs = g.cstride;
+    switch (pattern) {
+      case 0: classify<false, false, false, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      case 1: classify<false, false, true, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      case 2: classify<false, true, false, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      case 3: classify<false, true, true, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      case 4: classify<true, false, false, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      case 5: classify<true, false, true, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      case 6: classify<true, true, false, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
+      default: classify<true, true, true, In>(logits, C, cs, zo, yo, xo, wz, wy, wx, best, winner, invalid); break;
     }
     row[o2] = invalid ? invalid_label : (LabelT)winner;
     invalid_voxels += invalid ? 1 : 0;
