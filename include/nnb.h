@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 11
+#define NNB_ABI_VERSION 12
 
 enum nnb_status {
   NNB_OK = 0,
@@ -386,6 +386,128 @@ typedef struct nnb_restore_args {
 } nnb_restore_args;
 
 int32_t nnb_restore_class_labels(const nnb_restore_args* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Raw-case preprocessing on the device: the step before the sliding window
+ * (reference src/nnunet_mlx/data/preprocessing.py:60-163, upstream
+ * DefaultPreprocessor.run_case_npy order): transpose to the plans' axis order,
+ * crop to the nonzero bounding box, normalise each channel, resample to the
+ * target spacing on the torch sampling grid.  All entry points are
+ * stream-ordered and allocate nothing; the transpose is folded into the reads
+ * of the raw volume (no transposed copy is made).
+ * ------------------------------------------------------------------------ */
+
+enum {
+  NNB_DTYPE_F32 = 0, NNB_DTYPE_F64 = 1, NNB_DTYPE_I16 = 2,
+  NNB_DTYPE_U8 = 3, NNB_DTYPE_U16 = 4, NNB_DTYPE_I32 = 5
+};
+
+/* A raw case as read from the image file: contiguous (C, R0, R1, R2) values of
+ * `dtype`; plans axis i is raw axis transpose[i] (the plans' transpose_forward). */
+typedef struct nnb_raw_case {
+  const void* data;        /* device */
+  int32_t dtype;           /* NNB_DTYPE_*                                      */
+  int32_t channels;
+  int32_t raw_dims[3];
+  int32_t transpose[3];    /* a permutation of (0, 1, 2)                        */
+} nnb_raw_case;
+
+/* Nonzero bounding box of the transposed case.  `bounds` (device int32[8]) gets
+ * lo[3], hi[3] (inclusive, plans axis order; lo > hi when no voxel is nonzero),
+ * [6] = values that are not finite after conversion to float32, [7] = 0.
+ * Replaces the bound projections of crop_to_nonzero,
+ * src/nnunet_mlx/data/preprocessing.py:166-217 (and the float32 finiteness
+ * check of :104-118). */
+int32_t nnb_nonzero_bounds(const nnb_raw_case* raw, int32_t* bounds, void* stream);
+
+/* Hole filling of the nonzero mask inside a crop box (scipy binary_fill_holes,
+ * 6-connected background, as resolved at preprocessing.py:340-343).  The box
+ * holds every nonzero voxel, so the background outside it is one component
+ * that touches every face of the box.  `state` (device int8, contiguous crop
+ * box in plans order): 1 = nonzero voxel, 2 = background connected to the
+ * outside, 0 = background not (yet) reached.
+ *   nnb_fill_holes_init: state of every voxel, background on the box faces = 2.
+ *   nnb_fill_holes_sweep: one forward + backward line sweep along each axis,
+ *   marking background next to marked background; adds the number of voxels it
+ *   marked to *changed (device int32).  Repeat until a sweep marks nothing; the
+ *   filled mask is then state != 2. */
+int32_t nnb_fill_holes_init(const nnb_raw_case* raw, const int32_t crop_lo[3], const int32_t crop_dims[3],
+                            int8_t* state, void* stream);
+int32_t nnb_fill_holes_sweep(int8_t* state, const int32_t crop_dims[3], int32_t* changed, void* stream);
+
+/* Cropped, transposed previous-stage labels (cascade input, contiguous int32
+ * (1, R0, R1, R2) on the device) with background (0) outside the filled mask set
+ * to -1 (preprocessing.py:209-215). */
+int32_t nnb_crop_labels(const int32_t* labels, const nnb_raw_case* raw, const int32_t crop_lo[3],
+                        const int32_t crop_dims[3], const int8_t* state, int32_t* out, void* stream);
+
+enum {
+  NNB_NORM_NONE = 0, NNB_NORM_CT = 1, NNB_NORM_ZSCORE = 2,
+  NNB_NORM_RESCALE01 = 3, NNB_NORM_RGB01 = 4
+};
+
+/* One channel's plans normalisation (preprocessing.py:272-319).  CT: clip to
+ * [lower, upper], subtract mean, divide by divisor = max(std, 1e-8), each
+ * already rounded to float32.  Z-score: mean and standard deviation of the
+ * selected voxels (all, or the crop mask when use_mask), applied to those
+ * voxels only.  Rescale: subtract the minimum, divide by max(max - min, 1e-8).
+ * RGB: divide by 255 (values must lie in [0, 255]).  All float32 arithmetic. */
+typedef struct nnb_norm_channel {
+  int32_t scheme;          /* NNB_NORM_*                                         */
+  int32_t use_mask;        /* z-score over the crop mask                         */
+  float lower, upper, mean, divisor;   /* CT parameters                          */
+} nnb_norm_channel;
+
+/* Bytes of the caller's device workspace for nnb_crop_normalize. */
+int64_t nnb_crop_normalize_workspace_bytes(int32_t channels);
+
+/* Crop the transposed raw case to the box and normalise it: `out` is the
+ * contiguous float32 (C, crop_dims) result.  `norm` is a HOST array of
+ * `channels` entries.  `state` (from nnb_fill_holes_*) is required when a
+ * z-score channel uses the mask; with `labels` (the cropped previous stage from
+ * nnb_crop_labels) the mask is labels >= 0 instead, as in the reference
+ * (preprocessing.py:137, previous-stage foreground stays eligible).  Statistics
+ * are float64 sums (mean and standard deviation rounded to float32, as NumPy
+ * returns them for float32 data).  `errors` (device int32[4], zeroed by the
+ * call): [0] non-finite outputs, [1] RGB values outside [0, 255], [2] z-score
+ * channels with an empty selection, [3] = 0.  Channels that need no statistics
+ * (none, CT) are normalised while they are cropped, in one pass.  Replaces
+ * preprocessing.py:206-207 (crop) and :222-319 (normalisation). */
+int32_t nnb_crop_normalize(const nnb_raw_case* raw, const int32_t crop_lo[3], const int32_t crop_dims[3],
+                           const nnb_norm_channel* norm, const int8_t* state, const int32_t* labels,
+                           void* workspace, float* out, int32_t* errors, void* stream);
+
+enum { NNB_RESIZE_LINEAR = 0, NNB_RESIZE_NEAREST = 1, NNB_RESIZE_NEAREST_EXACT = 2 };
+enum { NNB_TIE_LOWEST = 0, NNB_TIE_HIGHEST = 1, NNB_TIE_NEAREST = 2 };
+
+/* One pass of upstream's torch-grid resampler (resample_torch_fornnunet).
+ * Per axis scale = float32(S / T).  Nearest modes copy the sample at
+ * min(int(scale * (t + s)), S - 1), s = 0 (nearest) or 0.5 (nearest-exact).
+ * Linear: coordinate max(scale * (t + 0.5) - 0.5, 0) in float32, indices
+ * floor and floor + 1 clamped to S - 1, weights (1 - f, f); image values are
+ * the float64 sum over the eight corners (axis 0 outermost) of
+ * ((v * w0) * w1) * w2, rounded once to float32; labels score each distinct
+ * corner label by the summed 1000 * w0 * w1 * w2 of its corners, rounded
+ * float64 -> float32 -> float16, and keep the best score, ties by `tiebreak`
+ * (lowest label, highest label, or the nearest sample's label then the lowest).
+ * The source is read through element strides, so the separate-axis passes need
+ * no moved copy: resample in-plane with the separate axis kept, then that axis.
+ * Replaces src/nnunet_mlx/kernels/metal_torch_resample.py:51-131 (kernel),
+ * :154-194 (launch) and :196-216 (separate-axis composition). */
+typedef struct nnb_torch_resize_args {
+  const void* source;           /* float32 image values or int32 labels (device)     */
+  int32_t labels;               /* 0: image values, 1: int32 labels in [-1, 32767]  */
+  int32_t channels;
+  int32_t source_dims[3];
+  int64_t channel_stride;       /* element strides of the source                     */
+  int64_t source_strides[3];
+  int32_t target_dims[3];
+  int32_t mode;                 /* NNB_RESIZE_*                                      */
+  int32_t tiebreak;             /* NNB_TIE_* (labels with the linear mode)           */
+  void* target;                 /* contiguous (C, T0, T1, T2), the source's type     */
+} nnb_torch_resize_args;
+
+int32_t nnb_torch_resize(const nnb_torch_resize_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 11
+ABI_VERSION = 12
 
 PREC_FP32 = 0        # split fp16 pairs on the tensor cores, float32-level accuracy (|activation| < 65504)
 PREC_TF32 = 1        # single-pass TF32 tensor cores
@@ -53,6 +53,31 @@ class RestoreArgs(ctypes.Structure):
                 ("source_dims", I32x3), ("target_dims", I32x3), ("class_stride", ctypes.c_int64),
                 ("source_strides", I64x3), ("volume_dims", I32x3), ("crop_lo", I32x3), ("axes", I32x3),
                 ("label_bytes", ctypes.c_int32), ("labels", ctypes.c_void_p), ("invalid_count", ctypes.c_void_p)]
+
+
+# raw-case dtypes, normalisation schemes, torch-grid modes and label tie rules (include/nnb.h)
+RAW_DTYPES = {"float32": 0, "float64": 1, "int16": 2, "uint8": 3, "uint16": 4, "int32": 5}
+NORM_SCHEMES = {"NoNormalization": 0, "CTNormalization": 1, "ZScoreNormalization": 2,
+                "RescaleTo01Normalization": 3, "RGBTo01Normalization": 4}
+RESIZE_MODES = {"linear": 0, "nearest": 1, "nearest-exact": 2}
+TIEBREAKS = {"lowest": 0, "highest": 1, "nearest": 2}
+
+
+class RawCase(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("channels", ctypes.c_int32),
+                ("raw_dims", I32x3), ("transpose", I32x3)]
+
+
+class NormChannel(ctypes.Structure):
+    _fields_ = [("scheme", ctypes.c_int32), ("use_mask", ctypes.c_int32), ("lower", ctypes.c_float),
+                ("upper", ctypes.c_float), ("mean", ctypes.c_float), ("divisor", ctypes.c_float)]
+
+
+class TorchResizeArgs(ctypes.Structure):
+    _fields_ = [("source", ctypes.c_void_p), ("labels", ctypes.c_int32), ("channels", ctypes.c_int32),
+                ("source_dims", I32x3), ("channel_stride", ctypes.c_int64), ("source_strides", I64x3),
+                ("target_dims", I32x3), ("mode", ctypes.c_int32), ("tiebreak", ctypes.c_int32),
+                ("target", ctypes.c_void_p)]
 
 
 SYMBOLS = {
@@ -107,6 +132,17 @@ SYMBOLS = {
                                               I32x3, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_restore_class_labels": (ctypes.c_int32, [ctypes.POINTER(RestoreArgs), ctypes.c_void_p]),
+    "nnb_nonzero_bounds": (ctypes.c_int32, [ctypes.POINTER(RawCase), ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_fill_holes_init": (ctypes.c_int32, [ctypes.POINTER(RawCase), I32x3, I32x3, ctypes.c_void_p,
+                                             ctypes.c_void_p]),
+    "nnb_fill_holes_sweep": (ctypes.c_int32, [ctypes.c_void_p, I32x3, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_crop_labels": (ctypes.c_int32, [ctypes.c_void_p, ctypes.POINTER(RawCase), I32x3, I32x3, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_crop_normalize_workspace_bytes": (ctypes.c_int64, [ctypes.c_int32]),
+    "nnb_crop_normalize": (ctypes.c_int32, [ctypes.POINTER(RawCase), I32x3, I32x3, ctypes.POINTER(NormChannel),
+                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_torch_resize": (ctypes.c_int32, [ctypes.POINTER(TorchResizeArgs), ctypes.c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -11,7 +11,7 @@ import subprocess
 from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
-SOURCES = ("capi.cu", "simt_ops.cu", "window.cu", "tc_conv.cu", "noalloc.cu", "restore.cu")
+SOURCES = ("capi.cu", "simt_ops.cu", "window.cu", "tc_conv.cu", "noalloc.cu", "restore.cu", "preprocess.cu")
 OUTPUT = PACKAGE / "_nnb.so"
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr"]

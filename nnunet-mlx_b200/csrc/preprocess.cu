@@ -1,0 +1,693 @@
+// Raw-case preprocessing on the device: nonzero bounding box, hole filling of
+// the nonzero mask, fused transpose + crop + per-channel normalisation, and
+// upstream's torch-grid resampler (image values and labels).  Every kernel is a
+// streaming pass over HBM: grid-stride loops over output elements in output
+// order (coalesced stores), the plans' transpose folded into the source
+// strides, per-thread partial reductions combined by warp shuffles and one
+// atomic per warp.  The C entry points (declared in include/nnb.h) validate
+// their arguments here and allocate nothing.
+//
+// Reference: src/nnunet_mlx/data/preprocessing.py:60-163 (step order),
+// :166-217 (crop_to_nonzero), :222-319 (normalisation), :340-343 (hole filling
+// via scipy); src/nnunet_mlx/kernels/metal_torch_resample.py:51-131 (torch-grid
+// kernel), :154-216 (launch and separate-axis composition);
+// src/nnunet_mlx/data/resampling.py:87-172, 175-244 (policy).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace nnb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxChannels = 32;
+
+int grid_for(int64_t n, int per_sm = 16) {
+  int64_t blocks = (n + kThreads - 1) / kThreads;
+  const int64_t cap = 148LL * per_sm;
+  if (blocks > cap) blocks = cap;
+  return (int)(blocks < 1 ? 1 : blocks);
+}
+
+template <typename T>
+__device__ __forceinline__ float as_f32(T v) { return (float)v; }
+
+// Where the raw case is and how the plans' axes map onto it.
+struct RawView {
+  const void* data;
+  int64_t cstride;        // elements per channel (R0 R1 R2)
+  int64_t pstride[3];     // raw element stride of plans axis i
+  int32_t pdims[3];       // plans-order dims
+  int32_t rdims[3];
+  int32_t tr[3];          // plans axis i = raw axis tr[i]
+  int32_t channels;
+};
+
+RawView make_view(const nnb_raw_case& r) {
+  RawView v;
+  v.data = r.data;
+  v.channels = r.channels;
+  const int64_t rs[3] = {(int64_t)r.raw_dims[1] * r.raw_dims[2], (int64_t)r.raw_dims[2], 1};
+  v.cstride = (int64_t)r.raw_dims[0] * r.raw_dims[1] * r.raw_dims[2];
+  for (int i = 0; i < 3; ++i) {
+    v.rdims[i] = r.raw_dims[i];
+    v.tr[i] = r.transpose[i];
+    v.pstride[i] = rs[r.transpose[i]];
+    v.pdims[i] = r.raw_dims[r.transpose[i]];
+  }
+  return v;
+}
+
+// Order-preserving int key of a float (signed comparison), and its inverse.
+__device__ __forceinline__ int float_key(float f) {
+  const int k = __float_as_int(f);
+  return k >= 0 ? k : k ^ 0x7fffffff;
+}
+__device__ __forceinline__ float key_float(int k) { return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff); }
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ double warp_sum_double(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---- nonzero bounding box -------------------------------------------------
+
+__global__ void bounds_init_kernel(int32_t* bounds) {
+  if (threadIdx.x < 8) bounds[threadIdx.x] = threadIdx.x < 3 ? INT_MAX : (threadIdx.x < 6 ? -1 : 0);
+}
+
+// One pass over the raw volume in memory order; per voxel the channels are
+// tested after conversion to float32 (the reference's mask is taken on the
+// float32 transposed array).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) nonzero_bounds_kernel(RawView v, int32_t* bounds) {
+  const T* data = static_cast<const T*>(v.data);
+  int lo[3] = {INT_MAX, INT_MAX, INT_MAX}, hi[3] = {-1, -1, -1};
+  int bad = 0;
+  const int64_t n = v.cstride;
+  const int64_t plane = (int64_t)v.rdims[1] * v.rdims[2];
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    bool nonzero = false;
+    for (int c = 0; c < v.channels; ++c) {
+      const float f = as_f32(data[c * n + i]);
+      bad += isfinite(f) ? 0 : 1;
+      nonzero |= f != 0.f;
+    }
+    if (nonzero) {
+      const int r[3] = {(int)(i / plane), (int)((i / v.rdims[2]) % v.rdims[1]), (int)(i % v.rdims[2])};
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const int p = r[v.tr[a]];
+        lo[a] = min(lo[a], p);
+        hi[a] = max(hi[a], p);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    lo[a] = __reduce_min_sync(0xffffffffu, lo[a]);
+    hi[a] = __reduce_max_sync(0xffffffffu, hi[a]);
+  }
+  bad = warp_sum_int(bad);
+  if ((threadIdx.x & 31) == 0) {
+    for (int a = 0; a < 3; ++a) {
+      if (hi[a] >= 0) {
+        atomicMin(&bounds[a], lo[a]);
+        atomicMax(&bounds[3 + a], hi[a]);
+      }
+    }
+    if (bad) atomicAdd(&bounds[6], bad);
+  }
+}
+
+// ---- crop-box geometry ----------------------------------------------------
+
+struct Box {
+  int32_t lo[3];
+  int32_t dims[3];
+  int64_t voxels;
+};
+
+// Raw element offset (channel 0) of crop voxel o (contiguous in plans order).
+__device__ __forceinline__ int64_t raw_offset(const RawView& v, const Box& b, int64_t o, int c[3]) {
+  const int64_t d12 = (int64_t)b.dims[1] * b.dims[2];
+  c[0] = (int)(o / d12);
+  c[1] = (int)((o / b.dims[2]) % b.dims[1]);
+  c[2] = (int)(o % b.dims[2]);
+  return (b.lo[0] + c[0]) * v.pstride[0] + (b.lo[1] + c[1]) * v.pstride[1] + (b.lo[2] + c[2]) * v.pstride[2];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) fill_init_kernel(RawView v, Box b, int8_t* state) {
+  const T* data = static_cast<const T*>(v.data);
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    int c[3];
+    const int64_t off = raw_offset(v, b, o, c);
+    bool nonzero = false;
+    for (int ch = 0; ch < v.channels; ++ch) nonzero |= as_f32(data[ch * v.cstride + off]) != 0.f;
+    const bool face = c[0] == 0 || c[1] == 0 || c[2] == 0 || c[0] == b.dims[0] - 1 || c[1] == b.dims[1] - 1 ||
+                      c[2] == b.dims[2] - 1;
+    state[o] = nonzero ? 1 : (face ? 2 : 0);
+  }
+}
+
+// One thread per line along `axis`: forward then backward, background voxels
+// after reached background become reached.  Lines of one launch are disjoint.
+__global__ void __launch_bounds__(kThreads) fill_sweep_kernel(int8_t* state, Box b, int axis, int32_t* changed) {
+  const int64_t d0 = b.dims[0], d1 = b.dims[1], d2 = b.dims[2];
+  const int64_t len = axis == 0 ? d0 : axis == 1 ? d1 : d2;
+  const int64_t step = axis == 0 ? d1 * d2 : axis == 1 ? d2 : 1;
+  const int64_t lines = b.voxels / len;
+  int marked = 0;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < lines; t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t base;
+    if (axis == 0) base = t;                                   // t over (i1, i2)
+    else if (axis == 1) base = (t / d2) * d1 * d2 + t % d2;    // t over (i0, i2)
+    else base = t * d2;                                        // t over (i0, i1)
+    bool carry = false;
+    for (int64_t k = 0; k < len; ++k) {
+      int8_t* s = state + base + k * step;
+      const int8_t val = *s;
+      if (val == 1) carry = false;
+      else if (val == 2) carry = true;
+      else if (carry) { *s = 2; ++marked; }
+    }
+    carry = false;
+    for (int64_t k = len - 1; k >= 0; --k) {
+      int8_t* s = state + base + k * step;
+      const int8_t val = *s;
+      if (val == 1) carry = false;
+      else if (val == 2) carry = true;
+      else if (carry) { *s = 2; ++marked; }
+    }
+  }
+  marked = warp_sum_int(marked);
+  if ((threadIdx.x & 31) == 0 && marked) atomicAdd(changed, marked);
+}
+
+__global__ void __launch_bounds__(kThreads) crop_labels_kernel(const int32_t* labels, RawView v, Box b,
+                                                              const int8_t* state, int32_t* out) {
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    int c[3];
+    const int32_t l = labels[raw_offset(v, b, o, c)];
+    out[o] = (l == 0 && state[o] == 2) ? -1 : l;
+  }
+}
+
+// ---- crop + normalisation --------------------------------------------------
+
+// Per-channel statistics and the resolved affine, in the caller's workspace.
+struct ChannelStats {
+  double sum;
+  double m2;
+  unsigned long long count;
+  int min_key;
+  int max_key;
+  float lower, upper, shift, divisor;
+  int32_t pad[4];
+};
+static_assert(sizeof(ChannelStats) == 64, "workspace record is 64 bytes");
+
+struct NormTable {
+  nnb_norm_channel ch[kMaxChannels];
+};
+
+__global__ void stats_init_kernel(ChannelStats* st, int channels) {
+  const int c = threadIdx.x;
+  if (c < channels) {
+    st[c].sum = 0.0;
+    st[c].m2 = 0.0;
+    st[c].count = 0ull;
+    st[c].min_key = INT_MAX;
+    st[c].max_key = INT_MIN;
+  }
+}
+
+__device__ __forceinline__ bool zscore_selected(const nnb_norm_channel& n, const int8_t* state,
+                                                const int32_t* labels, int64_t o) {
+  if (!n.use_mask) return true;
+  return labels ? labels[o] >= 0 : state[o] != 2;
+}
+
+// The CT affine, float32 operations in NumPy's order (clip, subtract, divide).
+__device__ __forceinline__ float ct_apply(float x, const nnb_norm_channel& n) {
+  x = fminf(fmaxf(x, n.lower), n.upper);
+  return __fdiv_rn(__fsub_rn(x, n.mean), n.divisor);
+}
+
+// Fused path (no statistics needed): crop and normalise in one pass.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) crop_apply_kernel(RawView v, Box b, NormTable t, float* out,
+                                                             int32_t* errors) {
+  const T* data = static_cast<const T*>(v.data);
+  int bad = 0;
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    int c[3];
+    const int64_t off = raw_offset(v, b, o, c);
+    for (int ch = 0; ch < v.channels; ++ch) {
+      float x = as_f32(data[ch * v.cstride + off]);
+      if (t.ch[ch].scheme == NNB_NORM_CT) x = ct_apply(x, t.ch[ch]);
+      bad += isfinite(x) ? 0 : 1;
+      out[ch * b.voxels + o] = x;
+    }
+  }
+  bad = warp_sum_int(bad);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(&errors[0], bad);
+}
+
+// Statistics path, pass 1 (blockIdx.y = channel): write the cropped float32
+// values and accumulate the sums, counts and extrema the channel's scheme needs.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) crop_stats_kernel(RawView v, Box b, NormTable t, const int8_t* state,
+                                                             const int32_t* labels, float* out, ChannelStats* st) {
+  const T* data = static_cast<const T*>(v.data);
+  const int ch = blockIdx.y;
+  const nnb_norm_channel n = t.ch[ch];
+  double sum = 0.0;
+  unsigned long long count = 0;
+  float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    int c[3];
+    const float x = as_f32(data[ch * v.cstride + raw_offset(v, b, o, c)]);
+    out[ch * b.voxels + o] = x;
+    if (n.scheme == NNB_NORM_ZSCORE) {
+      if (zscore_selected(n, state, labels, o)) {
+        sum += (double)x;
+        ++count;
+      }
+    } else if (n.scheme == NNB_NORM_RESCALE01 || n.scheme == NNB_NORM_RGB01) {
+      mn = fminf(mn, x);
+      mx = fmaxf(mx, x);
+    }
+  }
+  if (n.scheme == NNB_NORM_ZSCORE) {
+    sum = warp_sum_double(sum);
+    count = warp_sum_u64(count);
+    if ((threadIdx.x & 31) == 0 && count) {
+      atomicAdd(&st[ch].sum, sum);
+      atomicAdd(&st[ch].count, count);
+    }
+  } else if (n.scheme == NNB_NORM_RESCALE01 || n.scheme == NNB_NORM_RGB01) {
+    const int kmn = __reduce_min_sync(0xffffffffu, float_key(mn));
+    const int kmx = __reduce_max_sync(0xffffffffu, float_key(mx));
+    if ((threadIdx.x & 31) == 0) {
+      atomicMin(&st[ch].min_key, kmn);
+      atomicMax(&st[ch].max_key, kmx);
+    }
+  }
+}
+
+// The float32 mean NumPy returns for the selection (rounded once here).
+__device__ __forceinline__ float zscore_mean(const ChannelStats& s) {
+  return s.count ? __double2float_rn(s.sum / (double)s.count) : 0.f;
+}
+
+// Statistics path, pass 2: squared deviations from the float32 mean (the
+// difference taken in float32, as NumPy's var does for float32 data).
+__global__ void __launch_bounds__(kThreads) zscore_m2_kernel(Box b, NormTable t, const int8_t* state,
+                                                            const int32_t* labels, const float* out,
+                                                            ChannelStats* st) {
+  const int ch = blockIdx.y;
+  const nnb_norm_channel n = t.ch[ch];
+  if (n.scheme != NNB_NORM_ZSCORE) return;
+  const float mean = zscore_mean(st[ch]);
+  double m2 = 0.0;
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    if (zscore_selected(n, state, labels, o)) {
+      const double d = (double)__fsub_rn(out[ch * b.voxels + o], mean);
+      m2 += d * d;
+    }
+  }
+  m2 = warp_sum_double(m2);
+  if ((threadIdx.x & 31) == 0 && m2 != 0.0) atomicAdd(&st[ch].m2, m2);
+}
+
+// Resolve each channel's affine from its statistics; flag empty selections and
+// RGB values outside [0, 255].
+__global__ void stats_finalize_kernel(NormTable t, int channels, ChannelStats* st, int32_t* errors) {
+  const int ch = threadIdx.x;
+  if (ch >= channels) return;
+  const nnb_norm_channel n = t.ch[ch];
+  ChannelStats& s = st[ch];
+  s.lower = n.lower;
+  s.upper = n.upper;
+  s.shift = n.mean;
+  s.divisor = n.divisor;
+  if (n.scheme == NNB_NORM_ZSCORE) {
+    if (s.count == 0) {
+      atomicAdd(&errors[2], 1);
+      s.shift = 0.f;
+      s.divisor = 1.f;
+      return;
+    }
+    const float mean = zscore_mean(s);
+    const float stdev = __double2float_rn(sqrt(s.m2 / (double)s.count));
+    s.shift = mean;
+    s.divisor = __double2float_rn(fmax((double)stdev, 1e-8));
+  } else if (n.scheme == NNB_NORM_RESCALE01) {
+    const float mn = key_float(s.min_key), mx = key_float(s.max_key);
+    s.shift = mn;
+    s.divisor = __double2float_rn(fmax((double)__fsub_rn(mx, mn), 1e-8));
+  } else if (n.scheme == NNB_NORM_RGB01) {
+    const float mn = key_float(s.min_key), mx = key_float(s.max_key);
+    if (mn < 0.f || mx > 255.f) atomicAdd(&errors[1], 1);
+    s.shift = 0.f;
+    s.divisor = 255.f;
+  }
+}
+
+// Statistics path, pass 3 (in place): apply every channel's affine.
+__global__ void __launch_bounds__(kThreads) norm_apply_kernel(Box b, NormTable t, const int8_t* state,
+                                                             const int32_t* labels, const ChannelStats* st,
+                                                             float* out, int32_t* errors) {
+  const int ch = blockIdx.y;
+  const nnb_norm_channel n = t.ch[ch];
+  const float shift = st[ch].shift, divisor = st[ch].divisor;
+  int bad = 0;
+  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    float x = out[ch * b.voxels + o];
+    switch (n.scheme) {
+      case NNB_NORM_CT: x = ct_apply(x, n); break;
+      case NNB_NORM_ZSCORE:
+        if (zscore_selected(n, state, labels, o)) x = __fdiv_rn(__fsub_rn(x, shift), divisor);
+        break;
+      case NNB_NORM_RESCALE01: x = __fdiv_rn(__fsub_rn(x, shift), divisor); break;
+      case NNB_NORM_RGB01: x = __fdiv_rn(x, 255.f); break;
+      default: break;
+    }
+    bad += isfinite(x) ? 0 : 1;
+    out[ch * b.voxels + o] = x;
+  }
+  bad = warp_sum_int(bad);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(&errors[0], bad);
+}
+
+// ---- torch-grid resampling -------------------------------------------------
+
+struct ResizeGeom {
+  int32_t src[3];
+  int32_t tgt[3];
+  float scale[3];        // float32(S / T)
+  int64_t cstride;
+  int64_t sstride[3];
+  int32_t channels;
+  int32_t mode;
+  int32_t tiebreak;
+};
+
+struct Tap {
+  int nearest, lo, hi;
+  double w0, w1;
+};
+
+// One axis of the torch grid in float32 with one rounding per operation.
+__device__ __forceinline__ Tap resize_tap(int t, int size, float scale, int mode) {
+  Tap a;
+  const float tf = (float)t;
+  const float scaled_n = __fmul_rn(scale, mode == NNB_RESIZE_NEAREST ? tf : __fadd_rn(tf, 0.5f));
+  a.nearest = min((int)scaled_n, size - 1);
+  const float scaled = __fmul_rn(scale, __fadd_rn(tf, 0.5f));
+  const float coord = fmaxf(__fsub_rn(scaled, 0.5f), 0.f);
+  a.lo = min((int)coord, size - 1);
+  a.hi = min(a.lo + 1, size - 1);
+  a.w1 = (double)__fsub_rn(coord, floorf(coord));
+  a.w0 = __dsub_rn(1.0, a.w1);
+  return a;
+}
+
+template <bool kLabels>
+__global__ void __launch_bounds__(kThreads) torch_resize_kernel(ResizeGeom g, const void* source, void* target) {
+  const int64_t t12 = (int64_t)g.tgt[1] * g.tgt[2];
+  const int64_t per_channel = (int64_t)g.tgt[0] * t12;
+  const int64_t total = per_channel * g.channels;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = e / per_channel;
+    const int64_t r = e - c * per_channel;
+    const int t[3] = {(int)(r / t12), (int)((r / g.tgt[2]) % g.tgt[1]), (int)(r % g.tgt[2])};
+    Tap a[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) a[i] = resize_tap(t[i], g.src[i], g.scale[i], g.mode);
+    const int64_t base = c * g.cstride;
+    const int64_t nearest = base + a[0].nearest * g.sstride[0] + a[1].nearest * g.sstride[1] +
+                            a[2].nearest * g.sstride[2];
+    if (!kLabels) {
+      const float* src = static_cast<const float*>(source);
+      float* dst = static_cast<float*>(target);
+      if (g.mode != NNB_RESIZE_LINEAR) {
+        dst[e] = src[nearest];
+        continue;
+      }
+      double sum = 0.0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int b0 = (k >> 2) & 1, b1 = (k >> 1) & 1, b2 = k & 1;
+        const int64_t idx = base + (b0 ? a[0].hi : a[0].lo) * g.sstride[0] +
+                            (b1 ? a[1].hi : a[1].lo) * g.sstride[1] + (b2 ? a[2].hi : a[2].lo) * g.sstride[2];
+        double term = __dmul_rn((double)src[idx], b0 ? a[0].w1 : a[0].w0);
+        term = __dmul_rn(term, b1 ? a[1].w1 : a[1].w0);
+        term = __dmul_rn(term, b2 ? a[2].w1 : a[2].w0);
+        sum = __dadd_rn(sum, term);
+      }
+      dst[e] = __double2float_rn(sum);
+    } else {
+      const int32_t* src = static_cast<const int32_t*>(source);
+      int32_t* dst = static_cast<int32_t*>(target);
+      if (g.mode != NNB_RESIZE_LINEAR) {
+        dst[e] = src[nearest];
+        continue;
+      }
+      int label[8];
+      double weight[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int b0 = (k >> 2) & 1, b1 = (k >> 1) & 1, b2 = k & 1;
+        const int64_t idx = base + (b0 ? a[0].hi : a[0].lo) * g.sstride[0] +
+                            (b1 ? a[1].hi : a[1].lo) * g.sstride[1] + (b2 ? a[2].hi : a[2].lo) * g.sstride[2];
+        label[k] = src[idx];
+        double w = __dmul_rn(1000.0, b0 ? a[0].w1 : a[0].w0);
+        w = __dmul_rn(w, b1 ? a[1].w1 : a[1].w0);
+        weight[k] = __dmul_rn(w, b2 ? a[2].w1 : a[2].w0);
+      }
+      const int near_label = src[nearest];
+      float best = -1.f;
+      int winner = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        bool seen = false;
+#pragma unroll
+        for (int p = 0; p < k; ++p) seen |= label[p] == label[k];
+        if (seen) continue;
+        double score = 0.0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (label[q] == label[k]) score = __dadd_rn(score, weight[q]);
+        const float rounded = __half2float(__float2half_rn(__double2float_rn(score)));
+        bool preferred;
+        if (g.tiebreak == NNB_TIE_LOWEST) preferred = label[k] < winner;
+        else if (g.tiebreak == NNB_TIE_HIGHEST) preferred = label[k] > winner;
+        else preferred = label[k] == near_label || (winner != near_label && label[k] < winner);
+        if (rounded > best || (rounded == best && preferred)) {
+          best = rounded;
+          winner = label[k];
+        }
+      }
+      dst[e] = winner;
+    }
+  }
+}
+
+int check_raw(const nnb_raw_case* r, const char* what) {
+  NNB_REQUIRE(r != nullptr && r->data != nullptr, "%s: null raw case", what);
+  NNB_REQUIRE(r->dtype >= NNB_DTYPE_F32 && r->dtype <= NNB_DTYPE_I32, "%s: unsupported dtype %d", what, r->dtype);
+  NNB_REQUIRE(r->channels >= 1, "%s: channels must be positive", what);
+  int seen = 0;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(r->raw_dims[i] >= 1, "%s: raw dims must be positive", what);
+    NNB_REQUIRE(r->transpose[i] >= 0 && r->transpose[i] < 3 && !(seen & (1 << r->transpose[i])),
+                "%s: transpose must be a permutation of (0, 1, 2)", what);
+    seen |= 1 << r->transpose[i];
+  }
+  return NNB_OK;
+}
+
+int check_box(const RawView& v, const int32_t lo[3], const int32_t dims[3], Box* b, const char* what) {
+  NNB_REQUIRE(lo != nullptr && dims != nullptr, "%s: null crop box", what);
+  b->voxels = 1;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(lo[i] >= 0 && dims[i] >= 1 && (int64_t)lo[i] + dims[i] <= v.pdims[i],
+                "%s: crop box outside the transposed case on axis %d", what, i);
+    b->lo[i] = lo[i];
+    b->dims[i] = dims[i];
+    b->voxels *= dims[i];
+  }
+  return NNB_OK;
+}
+
+#define NNB_DISPATCH_RAW(dtype, KERNEL, grid, block, stream, ...)                                   \
+  switch (dtype) {                                                                                \
+    case NNB_DTYPE_F32: KERNEL<float><<<grid, block, 0, stream>>>(__VA_ARGS__); break;           \
+    case NNB_DTYPE_F64: KERNEL<double><<<grid, block, 0, stream>>>(__VA_ARGS__); break;          \
+    case NNB_DTYPE_I16: KERNEL<int16_t><<<grid, block, 0, stream>>>(__VA_ARGS__); break;         \
+    case NNB_DTYPE_U8: KERNEL<uint8_t><<<grid, block, 0, stream>>>(__VA_ARGS__); break;          \
+    case NNB_DTYPE_U16: KERNEL<uint16_t><<<grid, block, 0, stream>>>(__VA_ARGS__); break;        \
+    default: KERNEL<int32_t><<<grid, block, 0, stream>>>(__VA_ARGS__); break;                    \
+  }
+
+}  // namespace
+}  // namespace nnb
+
+using namespace nnb;
+
+extern "C" {
+
+int32_t nnb_nonzero_bounds(const nnb_raw_case* raw, int32_t* bounds, void* stream) {
+  if (int rc = check_raw(raw, "nonzero_bounds")) return rc;
+  NNB_REQUIRE(bounds != nullptr, "nonzero_bounds: null bounds");
+  const RawView v = make_view(*raw);
+  cudaStream_t s = (cudaStream_t)stream;
+  bounds_init_kernel<<<1, 32, 0, s>>>(bounds);
+  NNB_DISPATCH_RAW(raw->dtype, nonzero_bounds_kernel, grid_for(v.cstride), kThreads, s, v, bounds);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int32_t nnb_fill_holes_init(const nnb_raw_case* raw, const int32_t crop_lo[3], const int32_t crop_dims[3],
+                            int8_t* state, void* stream) {
+  if (int rc = check_raw(raw, "fill_holes_init")) return rc;
+  NNB_REQUIRE(state != nullptr, "fill_holes_init: null state");
+  const RawView v = make_view(*raw);
+  Box b;
+  if (int rc = check_box(v, crop_lo, crop_dims, &b, "fill_holes_init")) return rc;
+  NNB_DISPATCH_RAW(raw->dtype, fill_init_kernel, grid_for(b.voxels), kThreads, (cudaStream_t)stream, v, b, state);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int32_t nnb_fill_holes_sweep(int8_t* state, const int32_t crop_dims[3], int32_t* changed, void* stream) {
+  NNB_REQUIRE(state != nullptr && changed != nullptr && crop_dims != nullptr, "fill_holes_sweep: null pointer");
+  Box b;
+  b.voxels = 1;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(crop_dims[i] >= 1, "fill_holes_sweep: dims must be positive");
+    b.lo[i] = 0;
+    b.dims[i] = crop_dims[i];
+    b.voxels *= crop_dims[i];
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int axis = 0; axis < 3; ++axis) {
+    const int64_t lines = b.voxels / b.dims[axis];
+    fill_sweep_kernel<<<grid_for(lines), kThreads, 0, s>>>(state, b, axis, changed);
+  }
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int32_t nnb_crop_labels(const int32_t* labels, const nnb_raw_case* raw, const int32_t crop_lo[3],
+                        const int32_t crop_dims[3], const int8_t* state, int32_t* out, void* stream) {
+  if (int rc = check_raw(raw, "crop_labels")) return rc;
+  NNB_REQUIRE(labels != nullptr && state != nullptr && out != nullptr, "crop_labels: null pointer");
+  const RawView v = make_view(*raw);
+  Box b;
+  if (int rc = check_box(v, crop_lo, crop_dims, &b, "crop_labels")) return rc;
+  crop_labels_kernel<<<grid_for(b.voxels), kThreads, 0, (cudaStream_t)stream>>>(labels, v, b, state, out);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int64_t nnb_crop_normalize_workspace_bytes(int32_t channels) {
+  return channels < 1 ? 0 : (int64_t)channels * (int64_t)sizeof(ChannelStats);
+}
+
+int32_t nnb_crop_normalize(const nnb_raw_case* raw, const int32_t crop_lo[3], const int32_t crop_dims[3],
+                           const nnb_norm_channel* norm, const int8_t* state, const int32_t* labels,
+                           void* workspace, float* out, int32_t* errors, void* stream) {
+  if (int rc = check_raw(raw, "crop_normalize")) return rc;
+  NNB_REQUIRE(norm != nullptr && out != nullptr && errors != nullptr, "crop_normalize: null pointer");
+  if (raw->channels > kMaxChannels) {
+    set_error("crop_normalize: %d channels exceed the supported %d", raw->channels, kMaxChannels);
+    return NNB_E_UNSUPPORTED;
+  }
+  const RawView v = make_view(*raw);
+  Box b;
+  if (int rc = check_box(v, crop_lo, crop_dims, &b, "crop_normalize")) return rc;
+  NormTable t;
+  bool stats = false;
+  for (int c = 0; c < raw->channels; ++c) {
+    const nnb_norm_channel& n = norm[c];
+    NNB_REQUIRE(n.scheme >= NNB_NORM_NONE && n.scheme <= NNB_NORM_RGB01, "crop_normalize: bad scheme %d", n.scheme);
+    if (n.scheme == NNB_NORM_CT)
+      NNB_REQUIRE(n.lower <= n.upper && n.divisor > 0.f, "crop_normalize: bad CT parameters on channel %d", c);
+    if (n.scheme == NNB_NORM_ZSCORE && n.use_mask)
+      NNB_REQUIRE(state != nullptr || labels != nullptr, "crop_normalize: masked z-score needs the crop mask");
+    stats |= n.scheme == NNB_NORM_ZSCORE || n.scheme == NNB_NORM_RESCALE01 || n.scheme == NNB_NORM_RGB01;
+    t.ch[c] = n;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  NNB_CUDA_CHECK(cudaMemsetAsync(errors, 0, 4 * sizeof(int32_t), s));
+  if (!stats) {
+    NNB_DISPATCH_RAW(raw->dtype, crop_apply_kernel, grid_for(b.voxels), kThreads, s, v, b, t, out, errors);
+    NNB_LAUNCH_CHECK();
+    return NNB_OK;
+  }
+  NNB_REQUIRE(workspace != nullptr, "crop_normalize: statistics need the workspace");
+  ChannelStats* st = static_cast<ChannelStats*>(workspace);
+  stats_init_kernel<<<1, kMaxChannels, 0, s>>>(st, raw->channels);
+  const dim3 grid(grid_for(b.voxels, 8), raw->channels);
+  NNB_DISPATCH_RAW(raw->dtype, crop_stats_kernel, grid, kThreads, s, v, b, t, state, labels, out, st);
+  zscore_m2_kernel<<<grid, kThreads, 0, s>>>(b, t, state, labels, out, st);
+  stats_finalize_kernel<<<1, kMaxChannels, 0, s>>>(t, raw->channels, st, errors);
+  norm_apply_kernel<<<grid, kThreads, 0, s>>>(b, t, state, labels, st, out, errors);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int32_t nnb_torch_resize(const nnb_torch_resize_args* a, void* stream) {
+  NNB_REQUIRE(a != nullptr && a->source != nullptr && a->target != nullptr, "torch_resize: null pointer");
+  NNB_REQUIRE(a->labels == 0 || a->labels == 1, "torch_resize: labels must be 0 or 1");
+  NNB_REQUIRE(a->channels >= 1, "torch_resize: channels must be positive");
+  NNB_REQUIRE(a->mode >= NNB_RESIZE_LINEAR && a->mode <= NNB_RESIZE_NEAREST_EXACT, "torch_resize: bad mode");
+  NNB_REQUIRE(a->tiebreak >= NNB_TIE_LOWEST && a->tiebreak <= NNB_TIE_NEAREST, "torch_resize: bad tiebreak");
+  NNB_REQUIRE(a->channel_stride >= 0, "torch_resize: strides must be non-negative");
+  ResizeGeom g;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(a->source_dims[i] >= 1 && a->target_dims[i] >= 1, "torch_resize: dims must be positive");
+    NNB_REQUIRE(a->source_strides[i] >= 0, "torch_resize: strides must be non-negative");
+    g.src[i] = a->source_dims[i];
+    g.tgt[i] = a->target_dims[i];
+    g.scale[i] = (float)((double)a->source_dims[i] / (double)a->target_dims[i]);
+    g.sstride[i] = a->source_strides[i];
+  }
+  g.cstride = a->channel_stride;
+  g.channels = a->channels;
+  g.mode = a->mode;
+  g.tiebreak = a->tiebreak;
+  const int64_t total = (int64_t)a->channels * a->target_dims[0] * a->target_dims[1] * a->target_dims[2];
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a->labels) torch_resize_kernel<true><<<grid_for(total), kThreads, 0, s>>>(g, a->source, a->target);
+  else torch_resize_kernel<false><<<grid_for(total), kThreads, 0, s>>>(g, a->source, a->target);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+}  // extern "C"

@@ -663,3 +663,155 @@ def restore_class_labels(logits: torch.Tensor, target, *, class_axis: int = 0, v
     _native.check(_native.load().nnb_restore_class_labels(ctypes.byref(args), _stream()), "restore_class_labels")
     PROFILE.stop(token)
     return labels, invalid
+
+
+# ---- raw-case preprocessing (reference data/preprocessing.py, kernels/metal_torch_resample.py) ----
+
+_FILL_SWEEPS_PER_CHECK = 4
+_FILL_MAX_ROUNDS = 100_000
+
+
+def _require_device(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ContractError(f"{name} must be a CUDA tensor")
+
+
+def _raw_case(raw: torch.Tensor, transpose) -> _native.RawCase:
+    """The C descriptor of a contiguous ``(C, R0, R1, R2)`` raw case; plans axis i = raw axis ``transpose[i]``."""
+    _require_device(raw, "raw case")
+    dtype = str(raw.dtype).removeprefix("torch.")
+    if raw.dim() != 4 or not raw.is_contiguous() or dtype not in _native.RAW_DTYPES:
+        raise ContractError("raw cases must be contiguous (C, X, Y, Z) float32/float64/int16/uint8/uint16/int32")
+    if sorted(int(a) for a in transpose) != [0, 1, 2]:
+        raise ContractError("transpose_forward must be a permutation of (0, 1, 2)")
+    case = _native.RawCase()
+    case.data = raw.data_ptr()
+    case.dtype = _native.RAW_DTYPES[dtype]
+    case.channels = int(raw.shape[0])
+    case.raw_dims = _native.dims3(raw.shape[1:])
+    case.transpose = _native.dims3(transpose)
+    return case
+
+
+def nonzero_bounds(raw: torch.Tensor, transpose=(0, 1, 2)) -> torch.Tensor:
+    """Device int32[8]: inclusive lo[3], hi[3] of the nonzero voxels in plans order, then the non-finite count."""
+    case = _raw_case(raw, transpose)
+    bounds = torch.empty((8,), dtype=torch.int32, device=raw.device)
+    token = PROFILE.start("nonzero_bounds", 0.0, float(raw.numel() * raw.element_size()))
+    _native.check(_native.load().nnb_nonzero_bounds(ctypes.byref(case), bounds.data_ptr(), _stream()),
+                  "nonzero_bounds")
+    PROFILE.stop(token)
+    return bounds
+
+
+def fill_holes(raw: torch.Tensor, transpose, crop_lo, crop_dims) -> torch.Tensor:
+    """int8 crop-box state of the hole-filled nonzero mask (2 = background reached from outside the box).
+
+    Line sweeps along the three axes repeat until a round of sweeps marks no
+    voxel; each round costs one synchronisation.
+    """
+    case = _raw_case(raw, transpose)
+    dims = tuple(int(v) for v in crop_dims)
+    state = torch.empty(dims, dtype=torch.int8, device=raw.device)
+    changed = torch.zeros((1,), dtype=torch.int32, device=raw.device)
+    lib = _native.load()
+    _native.check(lib.nnb_fill_holes_init(ctypes.byref(case), _native.dims3(crop_lo), _native.dims3(dims),
+                                          state.data_ptr(), _stream()), "fill_holes_init")
+    for _ in range(_FILL_MAX_ROUNDS):
+        changed.zero_()
+        for _ in range(_FILL_SWEEPS_PER_CHECK):
+            _native.check(lib.nnb_fill_holes_sweep(state.data_ptr(), _native.dims3(dims), changed.data_ptr(),
+                                                   _stream()), "fill_holes_sweep")
+        if int(changed.item()) == 0:
+            return state
+    raise ContractError("hole filling did not converge")
+
+
+def crop_labels(labels: torch.Tensor, raw: torch.Tensor, transpose, crop_lo, crop_dims,
+                state: torch.Tensor) -> torch.Tensor:
+    """Cropped, transposed int32 previous-stage labels; background outside the filled mask becomes -1."""
+    case = _raw_case(raw, transpose)
+    _require_device(labels, "previous-stage labels")
+    _require_device(state, "crop mask state")
+    if labels.dtype != torch.int32 or not labels.is_contiguous() or tuple(labels.shape) != (1, *raw.shape[1:]):
+        raise ContractError("previous-stage labels must be contiguous int32 (1, X, Y, Z) matching the image")
+    dims = tuple(int(v) for v in crop_dims)
+    out = torch.empty((1, *dims), dtype=torch.int32, device=raw.device)
+    _native.check(_native.load().nnb_crop_labels(labels.data_ptr(), ctypes.byref(case), _native.dims3(crop_lo),
+                                                 _native.dims3(dims), state.data_ptr(), out.data_ptr(), _stream()),
+                  "crop_labels")
+    return out
+
+
+@dataclass(frozen=True)
+class ChannelNormalization:
+    """One channel's plans normalisation: scheme name, mask use and CT parameters (float32-rounded)."""
+
+    scheme: str
+    use_mask: bool = False
+    lower: float = 0.0
+    upper: float = 0.0
+    mean: float = 0.0
+    divisor: float = 1.0
+
+
+def crop_normalize(raw: torch.Tensor, transpose, crop_lo, crop_dims, channels: list[ChannelNormalization], *,
+                   state: torch.Tensor | None = None, labels: torch.Tensor | None = None):
+    """``(out, errors)``: float32 ``(C, *crop_dims)`` normalised crop and device int32[4] error counts
+
+    (non-finite outputs, RGB range violations, empty z-score selections).
+    """
+    case = _raw_case(raw, transpose)
+    if len(channels) != int(raw.shape[0]):
+        raise ContractError("normalization schemes do not match the input channels")
+    table = (_native.NormChannel * len(channels))()
+    for entry, spec in zip(table, channels, strict=True):
+        if spec.scheme not in _native.NORM_SCHEMES:
+            raise ContractError(f"unsupported nnU-Net normalization scheme {spec.scheme!r}")
+        entry.scheme = _native.NORM_SCHEMES[spec.scheme]
+        entry.use_mask = 1 if spec.use_mask else 0
+        entry.lower, entry.upper, entry.mean, entry.divisor = spec.lower, spec.upper, spec.mean, spec.divisor
+    dims = tuple(int(v) for v in crop_dims)
+    out = torch.empty((len(channels), *dims), dtype=torch.float32, device=raw.device)
+    errors = torch.empty((4,), dtype=torch.int32, device=raw.device)
+    lib = _native.load()
+    workspace = torch.empty((int(lib.nnb_crop_normalize_workspace_bytes(len(channels))),), dtype=torch.uint8,
+                            device=raw.device)
+    token = PROFILE.start("crop_normalize", 0.0, float(out.numel() * (raw.element_size() + 4)))
+    _native.check(lib.nnb_crop_normalize(ctypes.byref(case), _native.dims3(crop_lo), _native.dims3(dims), table,
+                                         _ptr(state), _ptr(labels), workspace.data_ptr(), out.data_ptr(),
+                                         errors.data_ptr(), _stream()), "crop_normalize")
+    PROFILE.stop(token)
+    return out, errors
+
+
+def torch_resize(source: torch.Tensor, target, mode: str, *, labels: bool = False,
+                 tiebreak: str = "nearest") -> torch.Tensor:
+    """One pass of upstream's torch-grid resampler over a 4-D ``(C, S0, S1, S2)`` CUDA tensor (any strides).
+
+    float32 image values or int32 labels; the result is contiguous ``(C, *target)`` of the source's dtype.
+    """
+    _require_device(source, "resampling source")
+    if source.dim() != 4 or source.dtype != (torch.int32 if labels else torch.float32):
+        raise ContractError("torch-grid resampling needs (C, X, Y, Z) float32 values or int32 labels")
+    if mode not in _native.RESIZE_MODES or tiebreak not in _native.TIEBREAKS:
+        raise ContractError("unsupported torch-grid interpolation mode or label tie rule")
+    target = tuple(int(v) for v in target)
+    if len(target) != 3 or min(target) < 1 or max(*source.shape[1:], *target) >= 2**31:
+        raise ContractError("torch-grid resampling needs three positive sizes within the int32 range")
+    out = torch.empty((int(source.shape[0]), *target), dtype=source.dtype, device=source.device)
+    args = _native.TorchResizeArgs()
+    args.source = source.data_ptr()
+    args.labels = 1 if labels else 0
+    args.channels = int(source.shape[0])
+    args.source_dims = _native.dims3(source.shape[1:])
+    args.channel_stride = int(source.stride(0))
+    args.source_strides = _native.I64x3(*(int(s) for s in source.stride()[1:]))
+    args.target_dims = _native.dims3(target)
+    args.mode = _native.RESIZE_MODES[mode]
+    args.tiebreak = _native.TIEBREAKS[tiebreak]
+    args.target = out.data_ptr()
+    token = PROFILE.start("torch_resize", 0.0, float(out.numel() * 4 * 2))
+    _native.check(_native.load().nnb_torch_resize(ctypes.byref(args), _stream()), "torch_resize")
+    PROFILE.stop(token)
+    return out

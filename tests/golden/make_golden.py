@@ -19,10 +19,13 @@ It imports only the reference's pure-host helpers, which run without MLX:
 
 It also copies the reference's recorded upstream vectors from
 ``tests/fixtures/darwin-arm64/upstream_runner.npz`` (head conversion arrays and
-float16 fold-rounding probes).  Outputs: ``geometry.json``, ``gaussian.npz``,
-``weights_map.json``, ``upstream_runner_subset.npz``, ``restore_axes.npz``,
-``restore_policy.json``.  Nothing at test time
-reads the reference checkout.
+float16 fold-rounding probes) and from ``tests/fixtures/darwin-arm64/torch_resampling.npz``
+(upstream ``resample_torch_fornnunet`` label resampling for every tie rule, mode and
+separate-axis policy, and the cascade labels of twelve recorded ``preprocess_raw_case``
+runs with their nonzero mask, previous-stage input, plans and geometry).  Outputs:
+``geometry.json``, ``gaussian.npz``, ``weights_map.json``, ``upstream_runner_subset.npz``,
+``restore_axes.npz``, ``restore_policy.json``, ``torch_resampling_labels.npz``.  Nothing at
+test time reads the reference checkout.
 """
 
 from __future__ import annotations
@@ -268,6 +271,21 @@ def main(reference: Path) -> None:
                          "separate": bool(flag), "axis": axis})
     (HERE / "restore_policy.json").write_text(
         json.dumps({"support": support, "separate_z": separate}, indent=1) + "\n")
+
+    # upstream torch-grid label resampling and recorded preprocessing runs (labels only: the
+    # image inputs of those recordings are not tracked by the reference)
+    recorded = np.load(reference / "tests" / "fixtures" / "darwin-arm64" / "torch_resampling.npz")
+    metadata = json.loads(str(recorded["metadata"].item()))
+    cases = [c for c in metadata["cases"] if f"{c['name']}-input" in recorded.files]
+    labels = {k: recorded[k] for c in cases for k in (f"{c['name']}-input", f"{c['name']}-expected")}
+    for run in metadata["pipeline"]:
+        labels[f"{run['name']}-labels"] = recorded[f"{run['name']}-labels"]
+    labels["raw_nonzero"] = recorded["raw_nonzero"]
+    labels["previous"] = recorded["previous"]
+    pipeline = [{k: run[k] for k in ("name", "plans", "properties", "geometry")} for run in metadata["pipeline"]]
+    labels["metadata"] = np.array(json.dumps({"cases": cases, "pipeline": pipeline,
+                                              "torch": metadata["torch"], "numpy": metadata["numpy"]}))
+    np.savez_compressed(HERE / "torch_resampling_labels.npz", **labels)
 
 
 if __name__ == "__main__":
