@@ -490,6 +490,8 @@ enum { NNB_TIE_LOWEST = 0, NNB_TIE_HIGHEST = 1, NNB_TIE_NEAREST = 2 };
  * corner label by the summed 1000 * w0 * w1 * w2 of its corners, rounded
  * float64 -> float32 -> float16, and keep the best score, ties by `tiebreak`
  * (lowest label, highest label, or the nearest sample's label then the lowest).
+ * Image values must be finite: corners whose weight product is exactly 0 are
+ * not read (their term is +-0 and cannot change the float64 sum).
  * The source is read through element strides, so the separate-axis passes need
  * no moved copy: resample in-plane with the separate axis kept, then that axis.
  * Replaces src/nnunet_mlx/kernels/metal_torch_resample.py:51-131 (kernel),

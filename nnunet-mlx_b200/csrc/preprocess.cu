@@ -1,10 +1,11 @@
 // Raw-case preprocessing on the device: nonzero bounding box, hole filling of
 // the nonzero mask, fused transpose + crop + per-channel normalisation, and
 // upstream's torch-grid resampler (image values and labels).  Every kernel is a
-// streaming pass over HBM: grid-stride loops over output elements in output
-// order (coalesced stores), the plans' transpose folded into the source
-// strides, per-thread partial reductions combined by warp shuffles and one
-// atomic per warp.  The C entry points (declared in include/nnb.h) validate
+// streaming pass over HBM: the volume kernels give one warp to each row of
+// their output (row coordinates and the outer axes' interpolation taps from
+// one division per row, coalesced loads and stores along the row), the plans'
+// transpose is folded into the source strides, and per-thread partial
+// reductions are combined by warp shuffles with one atomic per warp.  The C entry points (declared in include/nnb.h) validate
 // their arguments here and allocate nothing.
 //
 // Reference: src/nnunet_mlx/data/preprocessing.py:60-163 (step order),
@@ -16,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <climits>
+#include <type_traits>
 #include <stdint.h>
 
 #include "common.cuh"
@@ -35,6 +37,20 @@ int grid_for(int64_t n, int per_sm = 16) {
 
 template <typename T>
 __device__ __forceinline__ float as_f32(T v) { return (float)v; }
+
+// Whether a raw value is nonzero after conversion to float32, counting values
+// that are not finite after it.  Integers convert exactly and are finite, so
+// they are tested directly.
+template <typename T>
+__device__ __forceinline__ bool nonzero_f32(T v, int& bad) {
+  if constexpr (std::is_integral<T>::value) {
+    return v != 0;
+  } else {
+    const float f = (float)v;
+    bad += isfinite(f) ? 0 : 1;
+    return f != 0.f;
+  }
+}
 
 // Where the raw case is and how the plans' axes map onto it.
 struct RawView {
@@ -91,47 +107,108 @@ __global__ void bounds_init_kernel(int32_t* bounds) {
   if (threadIdx.x < 8) bounds[threadIdx.x] = threadIdx.x < 3 ? INT_MAX : (threadIdx.x < 6 ? -1 : 0);
 }
 
-// One pass over the raw volume in memory order; per voxel the channels are
-// tested after conversion to float32 (the reference's mask is taken on the
-// float32 transposed array).
+// One warp per raw row (R0, R1 fixed, R2 along the lanes): the row's two
+// outer coordinates come from one division per row, the lanes read the row
+// with 16-byte vectors when it is 16-byte aligned (else coalesced scalars),
+// and each channel is tested after conversion to float32 (the reference's
+// mask is taken on the float32 transposed array).  Bounds are kept per raw
+// axis and stored per plans axis.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) nonzero_bounds_kernel(RawView v, int32_t* bounds) {
+__global__ void __launch_bounds__(kThreads, 5) nonzero_bounds_kernel(RawView v, int vec, int32_t* bounds) {
   const T* data = static_cast<const T*>(v.data);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t rows = (int64_t)v.rdims[0] * v.rdims[1];
+  const int len = v.rdims[2];
   int lo[3] = {INT_MAX, INT_MAX, INT_MAX}, hi[3] = {-1, -1, -1};
   int bad = 0;
-  const int64_t n = v.cstride;
-  const int64_t plane = (int64_t)v.rdims[1] * v.rdims[2];
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    bool nonzero = false;
-    for (int c = 0; c < v.channels; ++c) {
-      const float f = as_f32(data[c * n + i]);
-      bad += isfinite(f) ? 0 : 1;
-      nonzero |= f != 0.f;
-    }
-    if (nonzero) {
-      const int r[3] = {(int)(i / plane), (int)((i / v.rdims[2]) % v.rdims[1]), (int)(i % v.rdims[2])};
+  for (int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
+    const int64_t base = row * len;
+    int rlo = INT_MAX, rhi = -1;
+    if (vec) {
+      constexpr int N = 16 / sizeof(T);
+      constexpr int kBatch = 4;
+      const int chunks = len / N;
+      for (int j0 = 0; j0 < chunks; j0 += 32 * kBatch) {
+        unsigned mask[kBatch] = {};  // bit k: element k of the chunk is nonzero in some channel
+        for (int c = 0; c < v.channels; ++c) {
+          uint4 q[kBatch];
 #pragma unroll
-      for (int a = 0; a < 3; ++a) {
-        const int p = r[v.tr[a]];
-        lo[a] = min(lo[a], p);
-        hi[a] = max(hi[a], p);
+          for (int u = 0; u < kBatch; ++u) {
+            const int j = j0 + u * 32 + lane;
+            q[u] = j < chunks ? *reinterpret_cast<const uint4*>(data + c * v.cstride + base + (int64_t)j * N)
+                              : make_uint4(0u, 0u, 0u, 0u);
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            T e[N];
+            memcpy(e, &q[u], 16);
+#pragma unroll
+            for (int k = 0; k < N; ++k) mask[u] |= (unsigned)nonzero_f32(e[k], bad) << k;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (mask[u]) {
+            const int j = j0 + u * 32 + lane;
+            rlo = min(rlo, j * N + __ffs(mask[u]) - 1);
+            rhi = max(rhi, j * N + 31 - __clz(mask[u]));
+          }
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (int i = lane; i < len; i += 32) {
+        bool nz = false;
+        for (int c = 0; c < v.channels; ++c) nz |= nonzero_f32(data[c * v.cstride + base + i], bad);
+        if (nz) {
+          rlo = min(rlo, i);
+          rhi = max(rhi, i);
+        }
       }
     }
+    rlo = __reduce_min_sync(0xffffffffu, rlo);
+    rhi = __reduce_max_sync(0xffffffffu, rhi);
+    if (rhi >= 0) {
+      const int r0 = (int)(row / v.rdims[1]);
+      const int r1 = (int)(row - (int64_t)r0 * v.rdims[1]);
+      lo[0] = min(lo[0], r0);
+      hi[0] = max(hi[0], r0);
+      lo[1] = min(lo[1], r1);
+      hi[1] = max(hi[1], r1);
+      lo[2] = min(lo[2], rlo);
+      hi[2] = max(hi[2], rhi);
+    }
   }
-#pragma unroll
-  for (int a = 0; a < 3; ++a) {
-    lo[a] = __reduce_min_sync(0xffffffffu, lo[a]);
-    hi[a] = __reduce_max_sync(0xffffffffu, hi[a]);
-  }
+  // combine the block's warps in shared memory, then one set of atomics per block
+  __shared__ int part[kThreads / 32][7];
   bad = warp_sum_int(bad);
-  if ((threadIdx.x & 31) == 0) {
+  const int warp_in_block = threadIdx.x >> 5;
+  if (lane == 0) {
+    for (int r = 0; r < 3; ++r) {
+      part[warp_in_block][r] = lo[r];
+      part[warp_in_block][3 + r] = hi[r];
+    }
+    part[warp_in_block][6] = bad;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int blo[3] = {INT_MAX, INT_MAX, INT_MAX}, bhi[3] = {-1, -1, -1}, bbad = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      for (int r = 0; r < 3; ++r) {
+        blo[r] = min(blo[r], part[w][r]);
+        bhi[r] = max(bhi[r], part[w][3 + r]);
+      }
+      bbad += part[w][6];
+    }
     for (int a = 0; a < 3; ++a) {
-      if (hi[a] >= 0) {
-        atomicMin(&bounds[a], lo[a]);
-        atomicMax(&bounds[3 + a], hi[a]);
+      const int r = v.tr[a];
+      if (bhi[r] >= 0) {
+        atomicMin(&bounds[a], blo[r]);
+        atomicMax(&bounds[3 + a], bhi[r]);
       }
     }
-    if (bad) atomicAdd(&bounds[6], bad);
+    if (bbad) atomicAdd(&bounds[6], bbad);
   }
 }
 
@@ -151,6 +228,19 @@ __device__ __forceinline__ int64_t raw_offset(const RawView& v, const Box& b, in
   c[2] = (int)(o % b.dims[2]);
   return (b.lo[0] + c[0]) * v.pstride[0] + (b.lo[1] + c[1]) * v.pstride[1] + (b.lo[2] + c[2]) * v.pstride[2];
 }
+
+// Row form of the crop box: output row `row` = (c0, c1) of the box, its raw
+// element offset (channel 0) at c2 = 0, computed with one division per row.
+__device__ __forceinline__ int64_t raw_row_base(const RawView& v, const Box& b, int64_t row) {
+  const int c0 = (int)(row / b.dims[1]);
+  const int c1 = (int)(row - (int64_t)c0 * b.dims[1]);
+  return (b.lo[0] + c0) * v.pstride[0] + (b.lo[1] + c1) * v.pstride[1] + b.lo[2] * v.pstride[2];
+}
+
+#define NNB_WARP_ROWS(rows)                                                                       \
+  for (int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5,                        \
+               row_step_ = ((int64_t)gridDim.x * blockDim.x) >> 5;                                  \
+       row < (rows); row += row_step_)
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads) fill_init_kernel(RawView v, Box b, int8_t* state) {
@@ -252,25 +342,61 @@ __device__ __forceinline__ float ct_apply(float x, const nnb_norm_channel& n) {
   return __fdiv_rn(__fsub_rn(x, n.mean), n.divisor);
 }
 
-// Fused path (no statistics needed): crop and normalise in one pass.
+// Fused path (no statistics needed): crop and normalise in one pass, one
+// warp per output row (coalesced reads when the plans' last axis is the raw
+// contiguous axis, coalesced row stores).
 template <typename T>
-__global__ void __launch_bounds__(kThreads) crop_apply_kernel(RawView v, Box b, NormTable t, float* out,
+__device__ __forceinline__ void crop_apply_row(const T* src, int64_t step, int len, int lane,
+                                               const nnb_norm_channel& n, float* dst, int& bad) {
+  const bool ct = n.scheme == NNB_NORM_CT;
+  if (step == 1) {
+    // 8 independent loads per lane in flight before any is used
+    constexpr int kBatch = 8;
+    for (int i0 = 0; i0 < len; i0 += 32 * kBatch) {
+      float x[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int i = i0 + k * 32 + lane;
+        x[k] = i < len ? as_f32(src[i]) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int i = i0 + k * 32 + lane;
+        if (i < len) {
+          float y = ct ? ct_apply(x[k], n) : x[k];
+          bad += isfinite(y) ? 0 : 1;
+          dst[i] = y;
+        }
+      }
+    }
+  } else {
+#pragma unroll 4
+    for (int i = lane; i < len; i += 32) {
+      float x = as_f32(src[i * step]);
+      if (ct) x = ct_apply(x, n);
+      bad += isfinite(x) ? 0 : 1;
+      dst[i] = x;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 5) crop_apply_kernel(RawView v, Box b, NormTable t, float* out,
                                                              int32_t* errors) {
   const T* data = static_cast<const T*>(v.data);
+  const int lane = threadIdx.x & 31;
+  const int len = b.dims[2];
   int bad = 0;
-  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    int c[3];
-    const int64_t off = raw_offset(v, b, o, c);
+  NNB_WARP_ROWS((int64_t)b.dims[0] * b.dims[1]) {
+    const int64_t base = raw_row_base(v, b, row);
     for (int ch = 0; ch < v.channels; ++ch) {
-      float x = as_f32(data[ch * v.cstride + off]);
-      if (t.ch[ch].scheme == NNB_NORM_CT) x = ct_apply(x, t.ch[ch]);
-      bad += isfinite(x) ? 0 : 1;
-      out[ch * b.voxels + o] = x;
+      const nnb_norm_channel n = t.ch[ch];
+      crop_apply_row(data + ch * v.cstride + base, v.pstride[2], len, lane, n,
+                     out + ch * b.voxels + row * len, bad);
     }
   }
   bad = warp_sum_int(bad);
-  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(&errors[0], bad);
+  if (lane == 0 && bad) atomicAdd(&errors[0], bad);
 }
 
 // Statistics path, pass 1 (blockIdx.y = channel): write the cropped float32
@@ -284,19 +410,24 @@ __global__ void __launch_bounds__(kThreads) crop_stats_kernel(RawView v, Box b, 
   double sum = 0.0;
   unsigned long long count = 0;
   float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
-  for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < b.voxels;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    int c[3];
-    const float x = as_f32(data[ch * v.cstride + raw_offset(v, b, o, c)]);
-    out[ch * b.voxels + o] = x;
-    if (n.scheme == NNB_NORM_ZSCORE) {
-      if (zscore_selected(n, state, labels, o)) {
-        sum += (double)x;
-        ++count;
+  const int lane = threadIdx.x & 31;
+  const int len = b.dims[2];
+  NNB_WARP_ROWS((int64_t)b.dims[0] * b.dims[1]) {
+    const T* src = data + ch * v.cstride + raw_row_base(v, b, row);
+#pragma unroll 4
+    for (int i = lane; i < len; i += 32) {
+      const int64_t o = row * len + i;
+      const float x = as_f32(src[i * v.pstride[2]]);
+      out[ch * b.voxels + o] = x;
+      if (n.scheme == NNB_NORM_ZSCORE) {
+        if (zscore_selected(n, state, labels, o)) {
+          sum += (double)x;
+          ++count;
+        }
+      } else if (n.scheme == NNB_NORM_RESCALE01 || n.scheme == NNB_NORM_RGB01) {
+        mn = fminf(mn, x);
+        mx = fmaxf(mx, x);
       }
-    } else if (n.scheme == NNB_NORM_RESCALE01 || n.scheme == NNB_NORM_RGB01) {
-      mn = fminf(mn, x);
-      mx = fmaxf(mx, x);
     }
   }
   if (n.scheme == NNB_NORM_ZSCORE) {
@@ -437,18 +568,28 @@ __device__ __forceinline__ Tap resize_tap(int t, int size, float scale, int mode
 }
 
 template <bool kLabels>
-__global__ void __launch_bounds__(kThreads) torch_resize_kernel(ResizeGeom g, const void* source, void* target) {
-  const int64_t t12 = (int64_t)g.tgt[1] * g.tgt[2];
-  const int64_t per_channel = (int64_t)g.tgt[0] * t12;
-  const int64_t total = per_channel * g.channels;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t c = e / per_channel;
-    const int64_t r = e - c * per_channel;
-    const int t[3] = {(int)(r / t12), (int)((r / g.tgt[2]) % g.tgt[1]), (int)(r % g.tgt[2])};
+__global__ void __launch_bounds__(kThreads, 4) torch_resize_kernel(ResizeGeom g, const void* source, void* target) {
+  // one warp per output row (c, t0, t1): the outer two axes' taps once per row
+  const int lane = threadIdx.x & 31;
+  NNB_WARP_ROWS((int64_t)g.channels * g.tgt[0] * g.tgt[1]) {
+    const int64_t ct0 = row / g.tgt[1];
+    const int t1 = (int)(row - ct0 * g.tgt[1]);
+    const int64_t c = ct0 / g.tgt[0];
+    const int t0 = (int)(ct0 - c * g.tgt[0]);
     Tap a[3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i) a[i] = resize_tap(t[i], g.src[i], g.scale[i], g.mode);
+    a[0] = resize_tap(t0, g.src[0], g.scale[0], g.mode);
+    a[1] = resize_tap(t1, g.src[1], g.scale[1], g.mode);
     const int64_t base = c * g.cstride;
+    const int64_t corner_row[4] = {base + a[0].lo * g.sstride[0] + a[1].lo * g.sstride[1],
+                                   base + a[0].lo * g.sstride[0] + a[1].hi * g.sstride[1],
+                                   base + a[0].hi * g.sstride[0] + a[1].lo * g.sstride[1],
+                                   base + a[0].hi * g.sstride[0] + a[1].hi * g.sstride[1]};
+    // whether the (axis 0, axis 1) corner pair has a nonzero weight product (row-uniform)
+    const bool row_active[4] = {true, a[1].w1 != 0.0, a[0].w1 != 0.0, a[0].w1 != 0.0 && a[1].w1 != 0.0};
+#pragma unroll 2
+    for (int t2 = lane; t2 < g.tgt[2]; t2 += 32) {
+    const int64_t e = row * g.tgt[2] + t2;
+    a[2] = resize_tap(t2, g.src[2], g.scale[2], g.mode);
     const int64_t nearest = base + a[0].nearest * g.sstride[0] + a[1].nearest * g.sstride[1] +
                             a[2].nearest * g.sstride[2];
     if (!kLabels) {
@@ -458,16 +599,31 @@ __global__ void __launch_bounds__(kThreads) torch_resize_kernel(ResizeGeom g, co
         dst[e] = src[nearest];
         continue;
       }
+      // Corners whose weight product is exactly 0 are not read: their term
+      // is +-0, and the running sum starts at +0 and is never -0 (x + y is -0
+      // only for two -0 operands), so adding +-0 leaves it unchanged.  The
+      // lower weight 1 - f of an axis is never 0; the upper weight f is 0 on
+      // axes that keep their size (row-uniform for axes 0 and 1).
+      const bool h2 = a[2].w1 != 0.0;
+      const int64_t o_lo = a[2].lo * g.sstride[2], o_hi = a[2].hi * g.sstride[2];
+      float v[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const bool on = row_active[q];
+        v[2 * q] = on ? src[corner_row[q] + o_lo] : 0.f;
+        v[2 * q + 1] = on && h2 ? src[corner_row[q] + o_hi] : 0.f;
+      }
       double sum = 0.0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int b0 = (k >> 2) & 1, b1 = (k >> 1) & 1, b2 = k & 1;
-        const int64_t idx = base + (b0 ? a[0].hi : a[0].lo) * g.sstride[0] +
-                            (b1 ? a[1].hi : a[1].lo) * g.sstride[1] + (b2 ? a[2].hi : a[2].lo) * g.sstride[2];
-        double term = __dmul_rn((double)src[idx], b0 ? a[0].w1 : a[0].w0);
-        term = __dmul_rn(term, b1 ? a[1].w1 : a[1].w0);
-        term = __dmul_rn(term, b2 ? a[2].w1 : a[2].w0);
-        sum = __dadd_rn(sum, term);
+      for (int q = 0; q < 4; ++q) {
+        if (!row_active[q]) continue;
+        const double wa = (q >> 1) ? a[0].w1 : a[0].w0, wb = (q & 1) ? a[1].w1 : a[1].w0;
+        double t = __dmul_rn(__dmul_rn(__dmul_rn((double)v[2 * q], wa), wb), a[2].w0);
+        sum = __dadd_rn(sum, t);
+        if (h2) {
+          t = __dmul_rn(__dmul_rn(__dmul_rn((double)v[2 * q + 1], wa), wb), a[2].w1);
+          sum = __dadd_rn(sum, t);
+        }
       }
       dst[e] = __double2float_rn(sum);
     } else {
@@ -482,9 +638,7 @@ __global__ void __launch_bounds__(kThreads) torch_resize_kernel(ResizeGeom g, co
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int b0 = (k >> 2) & 1, b1 = (k >> 1) & 1, b2 = k & 1;
-        const int64_t idx = base + (b0 ? a[0].hi : a[0].lo) * g.sstride[0] +
-                            (b1 ? a[1].hi : a[1].lo) * g.sstride[1] + (b2 ? a[2].hi : a[2].lo) * g.sstride[2];
-        label[k] = src[idx];
+        label[k] = src[corner_row[(b0 << 1) | b1] + (b2 ? a[2].hi : a[2].lo) * g.sstride[2]];
         double w = __dmul_rn(1000.0, b0 ? a[0].w1 : a[0].w0);
         w = __dmul_rn(w, b1 ? a[1].w1 : a[1].w0);
         weight[k] = __dmul_rn(w, b2 ? a[2].w1 : a[2].w0);
@@ -513,6 +667,7 @@ __global__ void __launch_bounds__(kThreads) torch_resize_kernel(ResizeGeom g, co
         }
       }
       dst[e] = winner;
+    }
     }
   }
 }
@@ -567,7 +722,12 @@ int32_t nnb_nonzero_bounds(const nnb_raw_case* raw, int32_t* bounds, void* strea
   const RawView v = make_view(*raw);
   cudaStream_t s = (cudaStream_t)stream;
   bounds_init_kernel<<<1, 32, 0, s>>>(bounds);
-  NNB_DISPATCH_RAW(raw->dtype, nonzero_bounds_kernel, grid_for(v.cstride), kThreads, s, v, bounds);
+  static const int kElementBytes[] = {4, 8, 2, 1, 2, 4};
+  const int vec = ((int64_t)raw->raw_dims[2] * kElementBytes[raw->dtype]) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(raw->data) % 16 == 0;
+  const int64_t rows = (int64_t)raw->raw_dims[0] * raw->raw_dims[1];
+  // resident blocks only (5 per SM at this kernel's register use): every block stays to the end
+  NNB_DISPATCH_RAW(raw->dtype, nonzero_bounds_kernel, grid_for(rows * 32, 5), kThreads, s, v, vec, bounds);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }
@@ -646,7 +806,8 @@ int32_t nnb_crop_normalize(const nnb_raw_case* raw, const int32_t crop_lo[3], co
   cudaStream_t s = (cudaStream_t)stream;
   NNB_CUDA_CHECK(cudaMemsetAsync(errors, 0, 4 * sizeof(int32_t), s));
   if (!stats) {
-    NNB_DISPATCH_RAW(raw->dtype, crop_apply_kernel, grid_for(b.voxels), kThreads, s, v, b, t, out, errors);
+    const int64_t rows = (int64_t)b.dims[0] * b.dims[1];
+    NNB_DISPATCH_RAW(raw->dtype, crop_apply_kernel, grid_for(rows * 32), kThreads, s, v, b, t, out, errors);
     NNB_LAUNCH_CHECK();
     return NNB_OK;
   }
@@ -654,7 +815,8 @@ int32_t nnb_crop_normalize(const nnb_raw_case* raw, const int32_t crop_lo[3], co
   ChannelStats* st = static_cast<ChannelStats*>(workspace);
   stats_init_kernel<<<1, kMaxChannels, 0, s>>>(st, raw->channels);
   const dim3 grid(grid_for(b.voxels, 8), raw->channels);
-  NNB_DISPATCH_RAW(raw->dtype, crop_stats_kernel, grid, kThreads, s, v, b, t, state, labels, out, st);
+  const dim3 row_grid(grid_for((int64_t)b.dims[0] * b.dims[1] * 32, 8), raw->channels);
+  NNB_DISPATCH_RAW(raw->dtype, crop_stats_kernel, row_grid, kThreads, s, v, b, t, state, labels, out, st);
   zscore_m2_kernel<<<grid, kThreads, 0, s>>>(b, t, state, labels, out, st);
   stats_finalize_kernel<<<1, kMaxChannels, 0, s>>>(t, raw->channels, st, errors);
   norm_apply_kernel<<<grid, kThreads, 0, s>>>(b, t, state, labels, st, out, errors);
@@ -682,10 +844,10 @@ int32_t nnb_torch_resize(const nnb_torch_resize_args* a, void* stream) {
   g.channels = a->channels;
   g.mode = a->mode;
   g.tiebreak = a->tiebreak;
-  const int64_t total = (int64_t)a->channels * a->target_dims[0] * a->target_dims[1] * a->target_dims[2];
+  const int64_t rows = (int64_t)a->channels * a->target_dims[0] * a->target_dims[1];
   cudaStream_t s = (cudaStream_t)stream;
-  if (a->labels) torch_resize_kernel<true><<<grid_for(total), kThreads, 0, s>>>(g, a->source, a->target);
-  else torch_resize_kernel<false><<<grid_for(total), kThreads, 0, s>>>(g, a->source, a->target);
+  if (a->labels) torch_resize_kernel<true><<<grid_for(rows * 32), kThreads, 0, s>>>(g, a->source, a->target);
+  else torch_resize_kernel<false><<<grid_for(rows * 32), kThreads, 0, s>>>(g, a->source, a->target);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }
