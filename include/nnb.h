@@ -511,6 +511,46 @@ typedef struct nnb_torch_resize_args {
 
 int32_t nnb_torch_resize(const nnb_torch_resize_args* args, void* stream);
 
+/* Spline resampling of image values (resample_data_or_seg_to_shape; the
+ * reference's host path: skimage resize -> scipy.ndimage.zoom(order, mode
+ * "nearest", grid_mode=True), src/nnunet_mlx/data/resampling.py:476-502).
+ * Every axis in `axes` is resampled as scipy does: order 3 pads it with 12
+ * edge samples and prefilters it in float64 (cubic B-spline, pole sqrt(3) - 2,
+ * gain 6, causal and anticausal passes with half-sample-symmetric initial
+ * values), then samples the coefficients on the half-pixel grid
+ * c = (t + 0.5) * (S / T) - 0.5 with the four cubic B-spline weights; order 1
+ * interpolates the values with index clamping.  Per output the taps' products
+ * ((v * w0) * w1) * w2 (axis 0 outermost) are summed in float64 and rounded
+ * once to the target type.  Axes not in `axes` must keep their size and are
+ * read plane by plane (the in-plane pass of separate-axis resampling,
+ * src/nnunet_mlx/data/resampling.py:268-306).  `coefficients` is a caller
+ * workspace of nnb_spline_workspace_bytes(...) bytes. */
+typedef struct nnb_spline_resize_args {
+  const void* source;           /* float32 or float64 values (device)                  */
+  int32_t source_f64;
+  int32_t channels;
+  int32_t source_dims[3];
+  int64_t channel_stride;       /* element strides of the source                       */
+  int64_t source_strides[3];
+  int32_t target_dims[3];
+  int32_t axes;                 /* bit a set: axis a is resampled                       */
+  int32_t order;                /* 1 or 3                                              */
+  double* coefficients;         /* workspace (device)                                  */
+  void* target;                 /* contiguous (C, T0, T1, T2)                          */
+  int32_t target_f64;           /* 0: float32 target, 1: float64                       */
+} nnb_spline_resize_args;
+
+int64_t nnb_spline_workspace_bytes(int32_t channels, const int32_t source_dims[3], int32_t axes, int32_t order);
+int32_t nnb_spline_resize(const nnb_spline_resize_args* args, void* stream);
+
+/* Out-of-plane pass of separate-axis resampling at order 0 (reference
+ * resize_out_of_plane / nearest_axis_indices, src/nnunet_mlx/data/resampling.py:379-427):
+ * float64 (C, S0, S1, S2) -> float32 (C, T0, T1, T2) where at most one axis
+ * changes size; that axis takes index clamp(floor(S / T * (t + 0.5) - 0.5 + 0.5),
+ * 0, S - 1) (float64, one rounding per operation); the value is rounded once. */
+int32_t nnb_nearest_axis_resize(const double* source, int32_t channels, const int32_t source_dims[3],
+                                const int32_t target_dims[3], float* target, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,13 @@ class NormChannel(ctypes.Structure):
                 ("upper", ctypes.c_float), ("mean", ctypes.c_float), ("divisor", ctypes.c_float)]
 
 
+class SplineResizeArgs(ctypes.Structure):
+    _fields_ = [("source", ctypes.c_void_p), ("source_f64", ctypes.c_int32), ("channels", ctypes.c_int32),
+                ("source_dims", I32x3), ("channel_stride", ctypes.c_int64), ("source_strides", I64x3),
+                ("target_dims", I32x3), ("axes", ctypes.c_int32), ("order", ctypes.c_int32),
+                ("coefficients", ctypes.c_void_p), ("target", ctypes.c_void_p), ("target_f64", ctypes.c_int32)]
+
+
 class TorchResizeArgs(ctypes.Structure):
     _fields_ = [("source", ctypes.c_void_p), ("labels", ctypes.c_int32), ("channels", ctypes.c_int32),
                 ("source_dims", I32x3), ("channel_stride", ctypes.c_int64), ("source_strides", I64x3),
@@ -143,6 +150,10 @@ SYMBOLS = {
                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_torch_resize": (ctypes.c_int32, [ctypes.POINTER(TorchResizeArgs), ctypes.c_void_p]),
+    "nnb_spline_workspace_bytes": (ctypes.c_int64, [ctypes.c_int32, I32x3, ctypes.c_int32, ctypes.c_int32]),
+    "nnb_spline_resize": (ctypes.c_int32, [ctypes.POINTER(SplineResizeArgs), ctypes.c_void_p]),
+    "nnb_nearest_axis_resize": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, ctypes.c_void_p,
+                                                 ctypes.c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -672,6 +672,193 @@ __global__ void __launch_bounds__(kThreads, 4) torch_resize_kernel(ResizeGeom g,
   }
 }
 
+// ---- spline resampling (resample_data_or_seg_to_shape) --------------------
+
+constexpr int kSplinePad = 12;   // edge samples scipy adds before prefiltering (mode "nearest")
+
+struct SplineGeom {
+  int32_t src[3];       // source dims
+  int32_t pdim[3];      // coefficient dims: src + 2 * pad
+  int32_t pad[3];       // kSplinePad on prefiltered axes, else 0
+  int32_t tgt[3];
+  int32_t axes;         // bit a: axis a is resampled
+  int64_t cstride;      // source element strides
+  int64_t sstride[3];
+  int32_t channels;
+};
+
+// coef[c][p] = source[c][clamp(p - pad)] as float64 (edge padding).
+template <typename S>
+__global__ void __launch_bounds__(kThreads) spline_pad_kernel(const S* src, SplineGeom g, double* coef) {
+  const int lane = threadIdx.x & 31;
+  NNB_WARP_ROWS((int64_t)g.channels * g.pdim[0] * g.pdim[1]) {
+    const int64_t c0 = row / g.pdim[1];
+    const int p1 = (int)(row - c0 * g.pdim[1]);
+    const int64_t c = c0 / g.pdim[0];
+    const int p0 = (int)(c0 - c * g.pdim[0]);
+    const int s0 = min(max(p0 - g.pad[0], 0), g.src[0] - 1);
+    const int s1 = min(max(p1 - g.pad[1], 0), g.src[1] - 1);
+    const S* line = src + c * g.cstride + s0 * g.sstride[0] + s1 * g.sstride[1];
+    double* out = coef + row * g.pdim[2];
+    for (int p2 = lane; p2 < g.pdim[2]; p2 += 32) {
+      const int s2 = min(max(p2 - g.pad[2], 0), g.src[2] - 1);
+      out[p2] = (double)line[s2 * g.sstride[2]];
+    }
+  }
+}
+
+// Mirror index of j on the half-sample-symmetric extension of n samples.
+__device__ __forceinline__ int mirror_index(int j, int n) {
+  const int period = 2 * n;
+  j %= period;
+  if (j < 0) j += period;
+  return j < n ? j : period - 1 - j;
+}
+
+// Cubic B-spline prefilter of every line along `axis` (one thread per line):
+// gain, causal pass with the half-sample-symmetric initial value
+// c+(0) = sum_k z^k x(-k), anticausal pass with c-(n-1) = z / (z - 1) c+(n-1).
+__global__ void __launch_bounds__(kThreads) spline_filter_kernel(double* coef, SplineGeom g, int axis) {
+  const double z = sqrt(3.0) - 2.0;
+  const double gain = __dmul_rn(1.0 - z, 1.0 - 1.0 / z);
+  const int64_t d0 = g.pdim[0], d1 = g.pdim[1], d2 = g.pdim[2];
+  const int n = g.pdim[axis];
+  const int64_t step = axis == 0 ? d1 * d2 : axis == 1 ? d2 : 1;
+  const int64_t per_channel = d0 * d1 * d2;
+  const int64_t lines = g.channels * (per_channel / n);
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < lines; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t per = per_channel / n;
+    const int64_t ch = t / per, r = t - ch * per;
+    int64_t base;
+    if (axis == 0) base = r;
+    else if (axis == 1) base = (r / d2) * d1 * d2 + r % d2;
+    else base = r * d2;
+    double* c = coef + ch * per_channel + base;
+    // separate roundings (no fused multiply-add), as the host implementation computes them
+    for (int i = 0; i < n; ++i) c[i * step] = __dmul_rn(c[i * step], gain);
+    double acc = c[0], zk = z;
+    for (int k = 1; k < 64 && fabs(zk) > 1e-30; ++k) {
+      acc = __dadd_rn(acc, __dmul_rn(zk, c[mirror_index(-k, n) * step]));
+      zk = __dmul_rn(zk, z);
+    }
+    c[0] = acc;
+    for (int j = 1; j < n; ++j) c[j * step] = __dadd_rn(c[j * step], __dmul_rn(z, c[(j - 1) * step]));
+    c[(n - 1) * step] = __dmul_rn(c[(n - 1) * step], z / (z - 1.0));
+    for (int j = n - 2; j >= 0; --j) c[j * step] = __dmul_rn(z, __dsub_rn(c[(j + 1) * step], c[j * step]));
+  }
+}
+
+struct SplineTaps {
+  int idx[4];
+  double w[4];
+};
+
+// Taps of output index t on one axis: a resampled axis samples the half-pixel
+// grid (order 3: four cubic B-spline weights from floor(c) - 1; order 1: two
+// linear weights), clamped into the coefficient array; a kept axis reads t.
+template <int kOrder>
+__device__ __forceinline__ SplineTaps spline_taps(const SplineGeom& g, int axis, int t) {
+  SplineTaps a;
+  if (!((g.axes >> axis) & 1)) {
+    a.idx[0] = t + g.pad[axis];
+    a.w[0] = 1.0;
+#pragma unroll
+    for (int k = 1; k < 4; ++k) { a.idx[k] = a.idx[0]; a.w[k] = 0.0; }
+    return a;
+  }
+  const double ratio = (double)g.src[axis] / (double)g.tgt[axis];
+  const double c = __dadd_rn(__dsub_rn(__dmul_rn((double)t + 0.5, ratio), 0.5), (double)g.pad[axis]);
+  const double fl = floor(c);
+  const double f = __dsub_rn(c, fl);
+  const int i = (int)fl;
+  const int hi = g.pdim[axis] - 1;
+  if (kOrder == 3) {
+    // cubic B-spline weights of taps floor(c) - 1 .. floor(c) + 2, one rounding per operation
+    const double s = __dsub_rn(1.0, f);
+    const double f2 = __dmul_rn(f, f), s2 = __dmul_rn(s, s);
+    const double f3 = __dmul_rn(f2, f), s3 = __dmul_rn(s2, s);
+    a.w[0] = s3 / 6.0;
+    a.w[1] = __dadd_rn(__dsub_rn(2.0 / 3.0, f2), f3 / 2.0);
+    a.w[2] = __dadd_rn(__dsub_rn(2.0 / 3.0, s2), s3 / 2.0);
+    a.w[3] = f3 / 6.0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) a.idx[k] = min(max(i - 1 + k, 0), hi);
+  } else {
+    a.w[0] = __dsub_rn(1.0, f);
+    a.w[1] = f;
+    a.w[2] = a.w[3] = 0.0;
+    a.idx[0] = min(max(i, 0), hi);
+    a.idx[1] = min(max(i + 1, 0), hi);
+    a.idx[2] = a.idx[3] = a.idx[1];
+  }
+  return a;
+}
+
+// One warp per output row (c, t0, t1); per output the sum over the taps
+// (axis 0 outermost) of ((v * w0) * w1) * w2 in float64, rounded once.
+template <int kOrder, typename O>
+__global__ void __launch_bounds__(kThreads) spline_interp_kernel(const double* coef, SplineGeom g, O* out) {
+  const int lane = threadIdx.x & 31;
+  constexpr int K = kOrder == 3 ? 4 : 2;
+  const int k0 = ((g.axes >> 0) & 1) ? K : 1, k1 = ((g.axes >> 1) & 1) ? K : 1, k2 = ((g.axes >> 2) & 1) ? K : 1;
+  const int64_t per_channel = (int64_t)g.pdim[0] * g.pdim[1] * g.pdim[2];
+  NNB_WARP_ROWS((int64_t)g.channels * g.tgt[0] * g.tgt[1]) {
+    const int64_t ct0 = row / g.tgt[1];
+    const int t1 = (int)(row - ct0 * g.tgt[1]);
+    const int64_t c = ct0 / g.tgt[0];
+    const int t0 = (int)(ct0 - c * g.tgt[0]);
+    const SplineTaps a0 = spline_taps<kOrder>(g, 0, t0), a1 = spline_taps<kOrder>(g, 1, t1);
+    const double* base = coef + c * per_channel;
+    for (int t2 = lane; t2 < g.tgt[2]; t2 += 32) {
+      const SplineTaps a2 = spline_taps<kOrder>(g, 2, t2);
+      double sum = 0.0;
+      for (int i = 0; i < k0; ++i) {
+        for (int j = 0; j < k1; ++j) {
+          const double* r = base + ((int64_t)a0.idx[i] * g.pdim[1] + a1.idx[j]) * g.pdim[2];
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            if (k < k2) {
+              const double v = __dmul_rn(__dmul_rn(__dmul_rn(r[a2.idx[k]], a0.w[i]), a1.w[j]), a2.w[k]);
+              sum = __dadd_rn(sum, v);
+            }
+          }
+        }
+      }
+      out[row * g.tgt[2] + t2] = (O)sum;
+    }
+  }
+}
+
+// Out-of-plane order-0 pass: gather along the one changed axis, round once.
+__global__ void __launch_bounds__(kThreads) nearest_axis_kernel(const double* src, int channels, Box in,
+                                                               Box outb, int axis, float* out) {
+  const double ratio = (double)in.dims[axis] / (double)outb.dims[axis];
+  const int lane = threadIdx.x & 31;
+  NNB_WARP_ROWS((int64_t)channels * outb.dims[0] * outb.dims[1]) {
+    const int64_t ct0 = row / outb.dims[1];
+    const int t1 = (int)(row - ct0 * outb.dims[1]);
+    const int64_t c = ct0 / outb.dims[0];
+    const int t0 = (int)(ct0 - c * outb.dims[0]);
+    int s[2] = {t0, t1};
+    for (int a = 0; a < 2; ++a) {
+      if (a == axis) {
+        const double x = __dadd_rn(__dsub_rn(__dmul_rn(ratio, (double)s[a] + 0.5), 0.5), 0.5);
+        s[a] = min(max((int)floor(x), 0), in.dims[a] - 1);
+      }
+    }
+    const double* line = src + c * in.voxels + ((int64_t)s[0] * in.dims[1] + s[1]) * in.dims[2];
+    float* dst = out + row * outb.dims[2];
+    for (int t2 = lane; t2 < outb.dims[2]; t2 += 32) {
+      int s2 = t2;
+      if (axis == 2) {
+        const double x = __dadd_rn(__dsub_rn(__dmul_rn(ratio, (double)t2 + 0.5), 0.5), 0.5);
+        s2 = min(max((int)floor(x), 0), in.dims[2] - 1);
+      }
+      dst[t2] = __double2float_rn(line[s2]);
+    }
+  }
+}
+
 int check_raw(const nnb_raw_case* r, const char* what) {
   NNB_REQUIRE(r != nullptr && r->data != nullptr, "%s: null raw case", what);
   NNB_REQUIRE(r->dtype >= NNB_DTYPE_F32 && r->dtype <= NNB_DTYPE_I32, "%s: unsupported dtype %d", what, r->dtype);
@@ -848,6 +1035,89 @@ int32_t nnb_torch_resize(const nnb_torch_resize_args* a, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   if (a->labels) torch_resize_kernel<true><<<grid_for(rows * 32), kThreads, 0, s>>>(g, a->source, a->target);
   else torch_resize_kernel<false><<<grid_for(rows * 32), kThreads, 0, s>>>(g, a->source, a->target);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int64_t nnb_spline_workspace_bytes(int32_t channels, const int32_t source_dims[3], int32_t axes, int32_t order) {
+  if (channels < 1 || source_dims == nullptr) return 0;
+  int64_t n = channels;
+  for (int a = 0; a < 3; ++a) n *= source_dims[a] + ((order == 3 && ((axes >> a) & 1)) ? 2 * kSplinePad : 0);
+  return n * (int64_t)sizeof(double);
+}
+
+int32_t nnb_spline_resize(const nnb_spline_resize_args* a, void* stream) {
+  NNB_REQUIRE(a != nullptr && a->source && a->target && a->coefficients, "spline_resize: null pointer");
+  NNB_REQUIRE(a->order == 1 || a->order == 3, "spline_resize: order must be 1 or 3");
+  NNB_REQUIRE(a->channels >= 1 && a->channel_stride >= 0, "spline_resize: bad channels");
+  NNB_REQUIRE(a->axes >= 0 && a->axes <= 7, "spline_resize: axes must be a 3-bit mask");
+  SplineGeom g;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(a->source_dims[i] >= 1 && a->target_dims[i] >= 1 && a->source_strides[i] >= 0,
+                "spline_resize: dims must be positive and strides non-negative");
+    const bool on = (a->axes >> i) & 1;
+    NNB_REQUIRE(on || a->source_dims[i] == a->target_dims[i], "spline_resize: axis %d is kept but changes size", i);
+    g.src[i] = a->source_dims[i];
+    g.tgt[i] = a->target_dims[i];
+    g.pad[i] = (a->order == 3 && on) ? kSplinePad : 0;
+    g.pdim[i] = g.src[i] + 2 * g.pad[i];
+    g.sstride[i] = a->source_strides[i];
+  }
+  g.axes = a->axes;
+  g.cstride = a->channel_stride;
+  g.channels = a->channels;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t pad_rows = (int64_t)g.channels * g.pdim[0] * g.pdim[1];
+  if (a->source_f64)
+    spline_pad_kernel<double><<<grid_for(pad_rows * 32), kThreads, 0, s>>>(static_cast<const double*>(a->source), g,
+                                                                            a->coefficients);
+  else
+    spline_pad_kernel<float><<<grid_for(pad_rows * 32), kThreads, 0, s>>>(static_cast<const float*>(a->source), g,
+                                                                           a->coefficients);
+  if (a->order == 3) {
+    for (int axis = 0; axis < 3; ++axis) {
+      if (!((a->axes >> axis) & 1)) continue;
+      const int64_t lines = (int64_t)g.channels * g.pdim[0] * g.pdim[1] * g.pdim[2] / g.pdim[axis];
+      spline_filter_kernel<<<grid_for(lines), kThreads, 0, s>>>(a->coefficients, g, axis);
+    }
+  }
+  const int64_t rows = (int64_t)g.channels * g.tgt[0] * g.tgt[1];
+  if (a->order == 3) {
+    if (a->target_f64) spline_interp_kernel<3, double><<<grid_for(rows * 32), kThreads, 0, s>>>(
+        a->coefficients, g, static_cast<double*>(a->target));
+    else spline_interp_kernel<3, float><<<grid_for(rows * 32), kThreads, 0, s>>>(
+        a->coefficients, g, static_cast<float*>(a->target));
+  } else {
+    if (a->target_f64) spline_interp_kernel<1, double><<<grid_for(rows * 32), kThreads, 0, s>>>(
+        a->coefficients, g, static_cast<double*>(a->target));
+    else spline_interp_kernel<1, float><<<grid_for(rows * 32), kThreads, 0, s>>>(
+        a->coefficients, g, static_cast<float*>(a->target));
+  }
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
+}
+
+int32_t nnb_nearest_axis_resize(const double* source, int32_t channels, const int32_t source_dims[3],
+                                const int32_t target_dims[3], float* target, void* stream) {
+  NNB_REQUIRE(source && target && source_dims && target_dims && channels >= 1, "nearest_axis_resize: bad arguments");
+  Box in, outb;
+  in.voxels = outb.voxels = 1;
+  int axis = -1;
+  for (int i = 0; i < 3; ++i) {
+    NNB_REQUIRE(source_dims[i] >= 1 && target_dims[i] >= 1, "nearest_axis_resize: dims must be positive");
+    in.lo[i] = outb.lo[i] = 0;
+    in.dims[i] = source_dims[i];
+    outb.dims[i] = target_dims[i];
+    in.voxels *= source_dims[i];
+    outb.voxels *= target_dims[i];
+    if (source_dims[i] != target_dims[i]) {
+      NNB_REQUIRE(axis < 0, "nearest_axis_resize: more than one axis changes size");
+      axis = i;
+    }
+  }
+  const int64_t rows = (int64_t)channels * outb.dims[0] * outb.dims[1];
+  nearest_axis_kernel<<<grid_for(rows * 32), kThreads, 0, (cudaStream_t)stream>>>(source, channels, in, outb, axis,
+                                                                                  target);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }

@@ -14,17 +14,18 @@ every pass runs there:
    outside it (``nnb_crop_labels``);
 3. crop + per-channel normalisation (``nnb_crop_normalize``; CT and no-op channels in the same
    pass as the crop, z-score / rescale / RGB after float64 statistics);
-4. resampling to the target spacing with upstream's torch sampling grid
-   (``resample_torch_fornnunet``: ``nnb_torch_resize``, in-plane then along the separate axis
-   when the anisotropy policy asks for it), for the image and the cascade labels.
+4. resampling to the target spacing: upstream's torch sampling grid (``resample_torch_fornnunet``:
+   ``nnb_torch_resize``, in-plane then along the separate axis when the anisotropy policy asks for
+   it) for the image and the cascade labels, or the spline path for the image (below).
 
 The result stays on the device: ``PreprocessedRawCase.data`` is a contiguous float32
 ``(C, *spatial)`` CUDA tensor that the predictors accept as is.
 
-Plans that resample the image with the spline path (``resample_data_or_seg_to_shape``: order-3
-skimage/scipy spline with prefiltering) are accepted only when the grid does not change; with a
-changed grid they raise ``ContractError``, as the reference's device path also covers the torch
-grid only (``src/nnunet_mlx/data/resampling.py:134-148``).
+Plans that resample the image with the spline path (``resample_data_or_seg_to_shape``, nnU-Net's
+default: order 3 with a separate order-0 axis for anisotropic spacing) run on the device too
+(``nnb_spline_resize`` + ``nnb_nearest_axis_resize``), reproducing the reference's host path
+(skimage ``resize`` = scipy ``zoom``, float64) to one float32 rounding.  Cascade labels with a
+spline plan and a changed grid raise ``ContractError``.
 """
 
 from __future__ import annotations
@@ -240,6 +241,38 @@ def resample_torch_device(values: torch.Tensor, new_shape: Sequence[int], curren
                                 tiebreak=contract.seg_tiebreak)
 
 
+def resample_spline_device(values: torch.Tensor, new_shape: Sequence[int], current_spacing: Sequence[float],
+                           new_spacing: Sequence[float], contract: ResamplingContract) -> torch.Tensor:
+    """Spline resampling of device ``(C, X, Y, Z)`` float32 image values (``resample_data_or_seg_to_shape``).
+
+    Reference ``data/resampling.py:87-172`` (host path: skimage ``resize`` = scipy ``zoom(order,
+    mode="nearest", grid_mode=True)`` per channel, float64 arithmetic, one rounding to float32): without a
+    separate axis every axis is resampled at ``order``; with one (``separate_z_axis``) the other two are
+    resampled plane by plane into a float64 intermediate (``:268-306``), then that axis at ``order_z``
+    (0: half-pixel nearest indices, ``:379-427``) and the result rounded once.  Orders 1 and 3 and
+    ``order_z`` 0 (nnU-Net's defaults are 3 and 0) run on the device; others raise ``ContractError``.
+    """
+    target = tuple(int(v) for v in new_shape)
+    if len(target) != 3 or min(target) < 1:
+        raise ContractError("resampling target shape must be positive")
+    current = validate_spacing(current_spacing, name="current spacing")
+    new = validate_spacing(new_spacing, name="new spacing")
+    if tuple(values.shape[1:]) == target:
+        return values.contiguous()
+    if contract.order not in (1, 3):
+        raise ContractError(f"device preprocessing supports spline orders 1 and 3, not {contract.order}")
+    separate, axis = separate_z_axis(current, new, force=contract.force_separate_z,
+                                     threshold=contract.separate_z_anisotropy_threshold)
+    if not separate or axis is None:
+        return kernels.spline_resize(values, target, axes=7, order=contract.order)
+    intermediate_shape = tuple(target[i] if i != axis else int(values.shape[1 + i]) for i in range(3))
+    intermediate = kernels.spline_resize(values, intermediate_shape, axes=7 & ~(1 << axis), order=contract.order,
+                                         float64_out=True)
+    if intermediate_shape != target and contract.order_z != 0:
+        raise ContractError(f"device preprocessing supports out-of-plane order 0, not {contract.order_z}")
+    return kernels.nearest_axis_resize(intermediate, target)
+
+
 def crop_to_nonzero_device(raw: torch.Tensor, transpose: Sequence[int], previous: torch.Tensor | None, *,
                            mask_required: bool):
     """Device ``crop_to_nonzero`` of the transposed raw case (reference ``preprocessing.py:166-217``).
@@ -329,13 +362,15 @@ def preprocess_raw_case(data: np.ndarray | torch.Tensor, properties: Mapping[str
     if min(new_shape) < 1:
         raise ContractError("resampling target shape must be positive")
     changed = tuple(new_shape) != tuple(dims)
-    for contract, what in ((plans.data_resampling, "image"), (plans.seg_resampling, "segmentation")):
-        if changed and contract.function_name != "resample_torch_fornnunet" and (what == "image" or
-                                                                                   cropped_previous is not None):
-            raise ContractError(f"device preprocessing resamples the {what} on the torch grid only "
-                                f"({contract.function_name} with a changed grid is not supported)")
-    resampled = resample_torch_device(normalized, new_shape, original_spacing, target_spacing,
-                                      plans.data_resampling, is_seg=False)
+    if changed and cropped_previous is not None and plans.seg_resampling.function_name != "resample_torch_fornnunet":
+        raise ContractError("device preprocessing resamples cascade labels on the torch grid only "
+                            f"({plans.seg_resampling.function_name} with a changed grid is not supported)")
+    if plans.data_resampling.function_name == "resample_torch_fornnunet":
+        resampled = resample_torch_device(normalized, new_shape, original_spacing, target_spacing,
+                                          plans.data_resampling, is_seg=False)
+    else:
+        resampled = resample_spline_device(normalized, new_shape, original_spacing, target_spacing,
+                                           plans.data_resampling)
     resampled_previous = None
     if cropped_previous is not None:
         if plans.seg_resampling.function_name == "resample_torch_fornnunet" and (

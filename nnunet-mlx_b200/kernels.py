@@ -815,3 +815,57 @@ def torch_resize(source: torch.Tensor, target, mode: str, *, labels: bool = Fals
     _native.check(_native.load().nnb_torch_resize(ctypes.byref(args), _stream()), "torch_resize")
     PROFILE.stop(token)
     return out
+
+
+def spline_resize(source: torch.Tensor, target, *, axes: int = 7, order: int = 3,
+                  float64_out: bool = False) -> torch.Tensor:
+    """scipy-``zoom``-equivalent spline resampling of a 4-D ``(C, S0, S1, S2)`` float32/float64 CUDA tensor.
+
+    Axes in the bit mask ``axes`` are resampled (order 3: edge padding, cubic B-spline prefilter and
+    four-tap sampling on the half-pixel grid; order 1: linear); the others must keep their size.
+    Returns a contiguous ``(C, *target)`` float32 (or float64) tensor.
+    """
+    _require_device(source, "resampling source")
+    if source.dim() != 4 or source.dtype not in (torch.float32, torch.float64):
+        raise ContractError("spline resampling needs (C, X, Y, Z) float32 or float64 values")
+    if order not in (1, 3):
+        raise ContractError(f"spline order {order} is not supported on the device (1 or 3)")
+    target = tuple(int(v) for v in target)
+    if len(target) != 3 or min(target) < 1 or max(*source.shape[1:], *target) >= 2**31:
+        raise ContractError("spline resampling needs three positive sizes within the int32 range")
+    lib = _native.load()
+    dims = _native.dims3(source.shape[1:])
+    workspace = torch.empty((int(lib.nnb_spline_workspace_bytes(int(source.shape[0]), dims, axes, order)) // 8,),
+                            dtype=torch.float64, device=source.device)
+    out = torch.empty((int(source.shape[0]), *target), dtype=torch.float64 if float64_out else torch.float32,
+                      device=source.device)
+    args = _native.SplineResizeArgs()
+    args.source = source.data_ptr()
+    args.source_f64 = 1 if source.dtype == torch.float64 else 0
+    args.channels = int(source.shape[0])
+    args.source_dims = dims
+    args.channel_stride = int(source.stride(0))
+    args.source_strides = _native.I64x3(*(int(s) for s in source.stride()[1:]))
+    args.target_dims = _native.dims3(target)
+    args.axes = int(axes)
+    args.order = int(order)
+    args.coefficients = workspace.data_ptr()
+    args.target = out.data_ptr()
+    args.target_f64 = 1 if float64_out else 0
+    token = PROFILE.start("spline_resize", 0.0, float(workspace.numel() * 8 * 3 + out.numel() * out.element_size()))
+    _native.check(lib.nnb_spline_resize(ctypes.byref(args), _stream()), "spline_resize")
+    PROFILE.stop(token)
+    return out
+
+
+def nearest_axis_resize(source: torch.Tensor, target) -> torch.Tensor:
+    """Order-0 out-of-plane pass: contiguous float64 ``(C, S0, S1, S2)`` -> float32 ``(C, *target)``."""
+    _require_device(source, "resampling source")
+    if source.dim() != 4 or source.dtype != torch.float64 or not source.is_contiguous():
+        raise ContractError("the out-of-plane pass needs a contiguous float64 (C, X, Y, Z) tensor")
+    target = tuple(int(v) for v in target)
+    out = torch.empty((int(source.shape[0]), *target), dtype=torch.float32, device=source.device)
+    _native.check(_native.load().nnb_nearest_axis_resize(source.data_ptr(), int(source.shape[0]),
+                                                         _native.dims3(source.shape[1:]), _native.dims3(target),
+                                                         out.data_ptr(), _stream()), "nearest_axis_resize")
+    return out

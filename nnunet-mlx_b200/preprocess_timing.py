@@ -12,8 +12,10 @@ One JSON line per kernel (mean of ``--iters`` launches after 3 warm-ups, CUDA ev
 launching stream; every input exceeds the 126 MB L2): algorithmic bytes, achieved GB/s and the
 fraction of the measured HBM copy bandwidth.  A last line times the whole ``preprocess_raw_case``
 call from a page-locked host int16 array (upload, bounds read-back, crop + normalise, resample,
-error read-back).  ``--cpu`` adds the reference's host path for the same case (NumPy crop + CT
-normalisation in float32, then upstream's torch-CPU resampler with all host threads).
+error read-back), and the same call under nnU-Net's default spline plan (order 3, separate order-0 z);
+the spline kernels' in-plane pass is timed on its own too.  ``--cpu`` adds the reference's host paths
+for the same case (NumPy crop + CT normalisation in float32, then upstream's torch-CPU resampler with
+all host threads; scipy's order-3 zoom per plane, one thread, on 8 planes scaled to the volume).
 """
 
 from __future__ import annotations
@@ -36,14 +38,18 @@ TARGET_SPACING = (5.0, 1.0, 1.0)
 INTENSITY = {"0": {"mean": 100.0, "std": 50.0, "percentile_00_5": -1000.0, "percentile_99_5": 400.0}}
 
 
-def plans() -> PreprocessingPlans:
-    torch_grid = {"is_seg": False}
+def plans(spline: bool = False) -> PreprocessingPlans:
+    """Torch-grid plan, or nnU-Net's default spline plan (order 3, separate order-0 axis)."""
+    if spline:
+        function, kwargs = "resample_data_or_seg_to_shape", {"order": 3, "order_z": 0, "force_separate_z": None}
+    else:
+        function, kwargs = "resample_torch_fornnunet", {}
     payload = {"transpose_forward": [0, 1, 2], "foreground_intensity_properties_per_channel": INTENSITY,
                "configurations": {"3d_fullres": {
                    "spacing": list(TARGET_SPACING), "normalization_schemes": ["CTNormalization"],
-                   "use_mask_for_norm": [False], "resampling_fn_data": "resample_torch_fornnunet",
-                   "resampling_fn_data_kwargs": torch_grid, "resampling_fn_seg": "resample_torch_fornnunet",
-                   "resampling_fn_seg_kwargs": {"is_seg": True}}}}
+                   "use_mask_for_norm": [False], "resampling_fn_data": function,
+                   "resampling_fn_data_kwargs": {"is_seg": False, **kwargs}, "resampling_fn_seg": function,
+                   "resampling_fn_seg_kwargs": {"is_seg": True, **kwargs}}}}
     return PreprocessingPlans.from_payload(payload, configuration="3d_fullres")
 
 
@@ -104,6 +110,15 @@ def main(argv=None) -> None:
     print(json.dumps(_line("torch_resize (linear, in-plane)", ms, voxels * 4 + int(np.prod(new_shape)) * 4,
                            source=dims, target=list(new_shape))), flush=True)
 
+    spline = lambda: kernels.nearest_axis_resize(  # noqa: E731
+        kernels.spline_resize(x, new_shape, axes=0b110, order=3, float64_out=True), new_shape)
+    ms = _timed(spline, args.iters)
+    print(json.dumps(_line("spline_resize (order 3, in-plane, z kept) + rounding pass", ms,
+                           voxels * 4 + int(np.prod(new_shape)) * 4, source=dims, target=list(new_shape),
+                           note="bytes: float32 in + out only; the padded float64 coefficients "
+                                f"({int(np.prod([101, 792, 792])) * 8} B) are written, prefiltered and read "
+                                "on top")), flush=True)
+
     host = torch.from_numpy(hu).pin_memory()
     the_plans = plans()
     case = lambda: preprocess_raw_case(host, {"spacing": list(SPACING)}, the_plans, device=device)  # noqa: E731
@@ -117,6 +132,16 @@ def main(argv=None) -> None:
             "h2d_bytes": int(hu.nbytes), "raw_voxels_per_s": round(voxels / ms * 1e3)}
     if args.cpu:
         line["cpu"] = cpu_reference(hu, new_shape)
+    print(json.dumps(line), flush=True)
+
+    spline_plans = plans(spline=True)
+    case = lambda: preprocess_raw_case(host, {"spacing": list(SPACING)}, spline_plans, device=device)  # noqa: E731
+    assert tuple(case().data.shape) == (1, *new_shape)
+    ms = _timed(case, max(3, args.iters // 4))
+    line = {"call": "preprocess_raw_case, default spline plan (order 3, separate z)", "ms": round(ms, 3),
+            "raw_voxels_per_s": round(voxels / ms * 1e3)}
+    if args.cpu:
+        line["cpu"] = cpu_spline_reference(hu, new_shape)
     print(json.dumps(line), flush=True)
 
 
@@ -137,6 +162,20 @@ def cpu_reference(hu: np.ndarray, new_shape) -> dict:
     seconds = time.perf_counter() - t0
     return {"s_per_volume": round(seconds, 3), "cores": threads,
             "kind": "reference host path (NumPy normalisation + torch-CPU resampler)"}
+
+
+def cpu_spline_reference(hu: np.ndarray, new_shape, planes: int = 8) -> dict:
+    """The reference's host spline path (scipy zoom order 3 per plane, float64), 8 planes scaled."""
+    from scipy import ndimage
+
+    x = ((np.clip(hu[0, :planes].astype(np.float32), -1000.0, 400.0) - 100.0) / 50.0).astype(np.float32)
+    t0 = time.perf_counter()
+    for k in range(planes):
+        ndimage.zoom(x[k].astype(np.float64), np.divide(new_shape[1:], x.shape[1:]), order=3, mode="nearest",
+                     grid_mode=True)
+    seconds = (time.perf_counter() - t0) * hu.shape[1] / planes
+    return {"s_per_volume": round(seconds, 3), "cores": 1, "sample": f"{planes} of {hu.shape[1]} planes, scaled",
+            "kind": "reference host path (scipy zoom order 3 per plane)"}
 
 
 if __name__ == "__main__":

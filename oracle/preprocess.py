@@ -12,6 +12,11 @@ bounding box, normalise each channel, resample to the target spacing.
 * normalisation (``preprocessing.py:222-319``): CT clip/shift/scale, z-score (over the mask
   when ``use_mask_for_norm``), rescale to [0, 1], RGB / 255, none -- float32 arithmetic with
   the scalars rounded to float32 as NumPy does for Python floats.
+* spline resampling (the reference's host path, ``src/nnunet_mlx/data/resampling.py:87-172,268-306,379-427``):
+  skimage ``resize(order, mode="edge", anti_aliasing=False)`` per channel, which is scipy
+  ``ndimage.zoom(order, mode="nearest", grid_mode=True)`` (skimage is absent here; scipy is the
+  reference's own dependency that does the arithmetic), with the separate-axis planes kept in float64
+  and the out-of-plane axis taken at half-pixel nearest indices;
 * torch-grid resampling (``src/nnunet_mlx/kernels/metal_torch_resample.py:51-131``, its
   separate-axis composition ``:196-216`` and the policy of
   ``src/nnunet_mlx/data/resampling.py:87-172,175-244,587-614``): per axis ``scale =
@@ -146,6 +151,45 @@ def resample_torch(data: np.ndarray, shape, current, new, *, mode="linear", anis
     return torch_resize(first, shape, aniso_axis_mode, is_seg=is_seg, tiebreak=tiebreak)
 
 
+def nearest_axis_indices(old: int, new: int) -> np.ndarray:
+    """Half-pixel nearest indices of one resized axis (reference ``data/resampling.py:401-407``)."""
+    coordinates = float(old) / new * (np.arange(new, dtype=np.float64) + 0.5) - 0.5
+    return np.clip(np.floor(coordinates + 0.5).astype(np.intp), 0, old - 1)
+
+
+def _zoom(values: np.ndarray, shape, order: int) -> np.ndarray:
+    """skimage ``resize(order, mode="edge", anti_aliasing=False)`` as scipy ``zoom`` (grid mode, "nearest")."""
+    from scipy import ndimage
+
+    out = ndimage.zoom(values, np.divide(shape, values.shape), order=order, mode="nearest", grid_mode=True)
+    assert out.shape == tuple(shape)
+    return out
+
+
+def resample_spline(values: np.ndarray, new_shape, current, new, *, order=3, order_z=0, force_separate_z=False,
+                    threshold=3.0) -> np.ndarray:
+    """Spline resampling of float32 ``(C, X, Y, Z)`` data (reference ``data/resampling.py:87-172,268-306``)."""
+    values = np.asarray(values, dtype=np.float32)
+    shape = tuple(int(v) for v in new_shape)
+    if values.shape[1:] == shape:
+        return values.copy()
+    _, axis = separate_z_axis(current, new, force=force_separate_z, threshold=threshold)
+    if axis is None:
+        return np.stack([_zoom(channel, shape, order) for channel in values]).astype(np.float32)
+    plane_shape = tuple(shape[i] for i in range(3) if i != axis)
+    result = []
+    for channel in values:
+        planes = [_zoom(np.take(channel, k, axis=axis).astype(np.float64), plane_shape, order)
+                  for k in range(channel.shape[axis])]
+        intermediate = np.stack(planes, axis=axis)
+        if intermediate.shape != shape:
+            assert order_z == 0
+            intermediate = np.take(intermediate, nearest_axis_indices(intermediate.shape[axis], shape[axis]),
+                                   axis=axis)
+        result.append(intermediate.astype(np.float32))
+    return np.stack(result)
+
+
 def crop_to_nonzero(data: np.ndarray, previous: np.ndarray | None, *, mask_required: bool):
     """(cropped float32 data, int8 mask, cropped previous or None, bounds) as the reference returns."""
     from scipy.ndimage import binary_fill_holes
@@ -221,7 +265,11 @@ def preprocess(data: np.ndarray, spacing, *, transpose_forward, configured_spaci
         configured = (original[0], *configured)
     target = tuple(o if c is None else float(c) for c, o in zip(configured, original, strict=True))
     new_shape = compute_new_shape(normalized.shape[1:], original, target)
-    out = resample_torch(normalized, new_shape, original, target, is_seg=False, **data_resampling)
+    if data_resampling.get("spline"):
+        spline = {k: v for k, v in data_resampling.items() if k != "spline"}
+        out = resample_spline(normalized, new_shape, original, target, **spline)
+    else:
+        out = resample_torch(normalized, new_shape, original, target, is_seg=False, **data_resampling)
     out_prev = None if cropped_prev is None else resample_torch(cropped_prev, new_shape, original, target,
                                                                 is_seg=True, **seg_resampling)
     properties = {"shape_before_cropping": tuple(values.shape[1:]),

@@ -24,7 +24,8 @@ float16 fold-rounding probes) and from ``tests/fixtures/darwin-arm64/torch_resam
 separate-axis policy, and the cascade labels of twelve recorded ``preprocess_raw_case``
 runs with their nonzero mask, previous-stage input, plans and geometry).  Outputs:
 ``geometry.json``, ``gaussian.npz``, ``weights_map.json``, ``upstream_runner_subset.npz``,
-``restore_axes.npz``, ``restore_policy.json``, ``torch_resampling_labels.npz``.  Nothing at
+``restore_axes.npz``, ``restore_policy.json``, ``torch_resampling_labels.npz``,
+``nearest_axis.json`` (``nnunet_mlx.data.resampling.nearest_axis_indices``, reference 401-407).  Nothing at
 test time reads the reference checkout.
 """
 
@@ -183,6 +184,10 @@ class _Tensor:
         return self.array
 
 
+NEAREST_AXIS_CASES = [(1, 1), (1, 4), (3, 7), (7, 3), (5, 5), (10, 4), (4, 10), (101, 81), (81, 101), (2, 3),
+                      (3, 2), (13, 26), (26, 13), (9, 14), (14, 9), (63, 64), (64, 63)]
+
+
 def main(reference: Path) -> None:
     sys.path.insert(0, str(reference / "src"))
     from nnunet_mlx.prediction import inference
@@ -286,6 +291,13 @@ def main(reference: Path) -> None:
     labels["metadata"] = np.array(json.dumps({"cases": cases, "pipeline": pipeline,
                                               "torch": metadata["torch"], "numpy": metadata["numpy"]}))
     np.savez_compressed(HERE / "torch_resampling_labels.npz", **labels)
+
+    # half-pixel nearest indices of the out-of-plane pass (order 0) of spline resampling
+    from nnunet_mlx.data.resampling import nearest_axis_indices
+
+    nearest = [{"old": o, "new": n, "indices": [int(i) for i in nearest_axis_indices(o, n)]}
+               for o, n in NEAREST_AXIS_CASES]
+    (HERE / "nearest_axis.json").write_text(json.dumps(nearest) + "\n")
 
 
 if __name__ == "__main__":

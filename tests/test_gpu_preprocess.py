@@ -6,7 +6,8 @@ boxes and crop shapes exactly; image values bitwise equal to the oracle where th
 has no reduction (crop, CT / rescale / RGB normalisation, torch-grid interpolation), and within
 the reference's own preprocessing tolerance (rtol 1e-5, atol 5e-6,
 ``tests/test_torch_resampling.py:84-86``) where a z-score mean and standard deviation are reduced
-(float64 sums on the device, NumPy's float32 pairwise sums in the oracle).
+(float64 sums on the device, NumPy's float32 pairwise sums in the oracle) and for spline
+resampling against scipy ``zoom`` (float64 on both sides, one rounding to float32).
 """
 
 from __future__ import annotations
@@ -239,15 +240,73 @@ def test_device_preprocessing_errors(cuda_device):
     bright = np.full((1, 4, 5, 6), 300.0, np.float32)
     with pytest.raises(ContractError, match=r"\[0, 255\]"):
         preprocess_raw_case(bright, {"spacing": [1, 1, 1]}, rgb, device=cuda_device)
-    spline = PreprocessingPlans.from_payload(
+    quadratic = PreprocessingPlans.from_payload(
         {"transpose_forward": [0, 1, 2], "configurations": {"c": {
             "spacing": [2.0, 2.0, 2.0], "normalization_schemes": ["NoNormalization"], "use_mask_for_norm": [False],
-            "resampling_fn_data": "resample_data_or_seg_to_shape", "resampling_fn_data_kwargs": {"is_seg": False},
+            "resampling_fn_data": "resample_data_or_seg_to_shape",
+            "resampling_fn_data_kwargs": {"is_seg": False, "order": 2},
             "resampling_fn_seg": "resample_data_or_seg_to_shape", "resampling_fn_seg_kwargs": {"is_seg": True}}}},
         configuration="c")
-    with pytest.raises(ContractError, match="torch grid only"):
-        preprocess_raw_case(np.ones((1, 4, 5, 6), np.float32), {"spacing": [1, 1, 1]}, spline, device=cuda_device)
-    same_grid = preprocess_raw_case(np.ones((1, 4, 5, 6), np.float32), {"spacing": [2, 2, 2]}, spline,
+    with pytest.raises(ContractError, match="orders 1 and 3"):
+        preprocess_raw_case(np.ones((1, 4, 5, 6), np.float32), {"spacing": [1, 1, 1]}, quadratic,
+                            device=cuda_device)
+    with pytest.raises(ContractError, match="cascade labels"):
+        preprocess_raw_case(np.ones((1, 4, 5, 6), np.float32), {"spacing": [1, 1, 1]}, quadratic,
+                            segmentation_previous_stage=np.ones((1, 4, 5, 6), np.int16), device=cuda_device)
+    same_grid = preprocess_raw_case(np.ones((1, 4, 5, 6), np.float32), {"spacing": [2, 2, 2]}, quadratic,
                                     device=cuda_device)
     assert tuple(same_grid.data.shape) == (1, 4, 5, 6)
+    _status_clean()
+
+
+@pytest.mark.parametrize("seed", range(3))
+def test_device_spline_resampling_matches_scipy(cuda_device, seed):
+    """Order 1 and 3, with and without a separate axis (each axis), against scipy zoom (the host path)."""
+    from nnunet_mlx_b200.data.preprocessing import ResamplingContract, resample_spline_device
+
+    rng = np.random.default_rng(200 + seed)
+    for trial in range(10):
+        channels = int(rng.integers(1, 3))
+        source = tuple(int(v) for v in rng.integers(3, 30, 3))
+        target = tuple(int(v) for v in rng.integers(2, 40, 3))
+        values = (rng.standard_normal((channels, *source)) * 20).astype(np.float32)
+        spacing = [float(v) for v in rng.choice([0.7, 1.0, 1.6, 3.0, 5.0], 3)]
+        new = [float(v) for v in rng.choice([0.8, 1.0, 1.4, 2.5], 3)]
+        order = 1 if trial % 4 == 0 else 3
+        force = (None, False, True)[trial % 3]
+        contract = ResamplingContract("resample_data_or_seg_to_shape", order, 0, force)
+        got = resample_spline_device(torch.from_numpy(values).to(cuda_device), target, spacing, new,
+                                     contract).cpu().numpy()
+        expected = op.resample_spline(values, target, spacing, new, order=order, order_z=0, force_separate_z=force)
+        np.testing.assert_allclose(got, expected, rtol=RTOL, atol=ATOL,
+                                   err_msg=f"order {order} {source} -> {target} {spacing} -> {new}")
+    _status_clean()
+
+
+def test_device_preprocessing_default_spline_plan(cuda_device):
+    """nnU-Net's default image resampling (order 3, separate order-0 axis) on an anisotropic CT crop."""
+    from nnunet_mlx_b200.data.preprocessing import PreprocessingPlans, preprocess_raw_case
+
+    rng = np.random.default_rng(8)
+    raw = np.zeros((1, 30, 120, 110), dtype=np.int16)
+    raw[0, 1:29, 4:116, 3:107] = np.round(rng.normal(40, 200, (28, 112, 104)).clip(-1000, 3000)).astype(np.int16)
+    intensity = {"0": {"mean": 100.0, "std": 50.0, "percentile_00_5": -1000.0, "percentile_99_5": 400.0}}
+    plans = PreprocessingPlans.from_payload(
+        {"transpose_forward": [0, 1, 2], "foreground_intensity_properties_per_channel": intensity,
+         "configurations": {"c": {
+             "spacing": [3.0, 1.0, 1.0], "normalization_schemes": ["CTNormalization"], "use_mask_for_norm": [False],
+             "resampling_fn_data": "resample_data_or_seg_to_shape",
+             "resampling_fn_data_kwargs": {"is_seg": False, "order": 3, "order_z": 0, "force_separate_z": None},
+             "resampling_fn_seg": "resample_data_or_seg_to_shape",
+             "resampling_fn_seg_kwargs": {"is_seg": True, "order": 1, "order_z": 0, "force_separate_z": None}}}},
+        configuration="c")
+    result = preprocess_raw_case(raw, {"spacing": [5.0, 0.8, 0.8]}, plans, device=cuda_device)
+    reference, _, properties = op.preprocess(
+        raw, [5.0, 0.8, 0.8], transpose_forward=(0, 1, 2), configured_spacing=(3.0, 1.0, 1.0),
+        schemes=["CTNormalization"], use_mask=[False], intensities=intensity,
+        data_resampling=dict(spline=True, order=3, order_z=0, force_separate_z=None, threshold=3.0),
+        seg_resampling={})
+    assert result.properties["bbox_used_for_cropping"] == properties["bbox_used_for_cropping"]
+    assert tuple(result.data.shape) == reference.shape == (1, 47, 90, 83)
+    np.testing.assert_allclose(result.data.cpu().numpy(), reference, rtol=RTOL, atol=ATOL)
     _status_clean()

@@ -160,3 +160,23 @@ def test_device_path_refuses_before_any_launch():
     with pytest.raises(ContractError, match="previous-stage"):
         preprocess_raw_case(np.zeros((1, 6, 8, 10), np.float32), {"spacing": [1, 1, 1]}, plans,
                             segmentation_previous_stage=np.zeros((1, 6, 8, 9), np.int16), device=cpu)
+
+
+def test_oracle_nearest_axis_indices_match_reference():
+    """The out-of-plane order-0 indices equal the reference's ``nearest_axis_indices`` (recorded)."""
+    for case in json.loads((GOLDEN / "nearest_axis.json").read_text()):
+        np.testing.assert_array_equal(op.nearest_axis_indices(case["old"], case["new"]), case["indices"])
+
+
+def test_oracle_spline_separate_axis_is_planewise_zoom_then_nearest():
+    """Separate-axis spline resampling = float64 per-plane zoom, then the recorded nearest indices."""
+    from scipy import ndimage
+
+    rng = np.random.default_rng(2)
+    values = rng.standard_normal((1, 6, 9, 8)).astype(np.float32)
+    got = op.resample_spline(values, (4, 12, 5), (5.0, 1.0, 1.0), (7.5, 0.75, 1.6), order=3, order_z=0,
+                             force_separate_z=None)
+    planes = [ndimage.zoom(values[0, k].astype(np.float64), (12 / 9, 5 / 8), order=3, mode="nearest",
+                           grid_mode=True) for k in range(6)]
+    expected = np.stack(planes)[op.nearest_axis_indices(6, 4)].astype(np.float32)
+    np.testing.assert_array_equal(got[0], expected)
