@@ -2,10 +2,11 @@
 
 Keeps the constructor and the ``self.predictor`` seam of reference
 ``src/nnunet_mlx/prediction/pipeline.py:171-215`` (an ``ArrayPredictor`` over
-the bundle's fold models).  Raw-image I/O, preprocessing and restoration
-(NIfTI readers, resampling, export) are outside this package's scope; cases
-are passed as preprocessed ``(C, *spatial)`` float32 arrays, in memory or as
-``.npy`` / ``.npz`` files, and written as ``.npz`` (labels, optional
+the bundle's fold models).  Image-file I/O and export are outside this
+package's scope.  Cases are passed either raw, as ``(C, X, Y, Z)`` arrays with
+their spacing (``predict_raw_case``: device preprocessing, inference and
+restoration), or preprocessed, as ``(C, *spatial)`` float32 arrays in memory or
+``.npy`` / ``.npz`` files, written as ``.npz`` (labels, optional
 probabilities/logits).
 """
 
@@ -88,6 +89,51 @@ class ModelFolderPredictor:
                            2 ** len(self.bundle.mirroring_axes), len(self.bundle.models))
         metrics = PredictionMetrics(elapsed, elapsed, work["tiles"], tuple(data.shape[1:]), self.bundle.patch_size)
         return labels, probabilities, metrics
+
+    def predict_raw_case(self, data, properties, *, device=None):
+        """Raw case -> labels in the image's own grid and axis order, every step on the GPU.
+
+        The reference's ``predict_case`` chain (``prediction/pipeline.py:257-387``: preprocess ->
+        infer -> restore) without the file I/O: ``preprocess_raw_case`` (transpose, nonzero crop,
+        normalisation, resampling to the plans' spacing) leaves the case on the device, the fold
+        ensemble's sliding window reads it there, and the class logits are restored (resampled to
+        the crop, first argmax, uncropped, transposed back) on the device; only the uint16 label
+        volume crosses to the host.  ``data`` is ``(C, X, Y, Z)`` in the image's axis order,
+        ``properties["spacing"]`` its voxel size.  Region models raise ``ContractError``.
+        """
+        from nnunet_mlx_b200.data.preprocessing import (
+            PreprocessingPlans,
+            ResamplingContract,
+            preprocess_raw_case,
+        )
+        from nnunet_mlx_b200.prediction.restore import (
+            LabelSemantics,
+            plans_from_payload,
+            restore_segmentation_on_device,
+        )
+        from nnunet_mlx_b200.prediction.sliding_window import volume_work
+
+        if self.bundle.regions_class_order is not None:
+            raise ContractError("region models are restored on the host (sigmoid probabilities)")
+        plans = self.bundle.plans
+        configuration = self.bundle.configuration
+        config = plans.get("configurations", {}).get(configuration, {})
+        start = time.perf_counter()
+        prepared = preprocess_raw_case(data, properties,
+                                       PreprocessingPlans.from_payload(plans, configuration=configuration),
+                                       device=device)
+        logits = self.predictor.predict_device_logits_from_preprocessed_data(prepared.data)
+        restored = restore_segmentation_on_device(
+            logits, prepared.properties, plans_from_payload(plans, configuration=configuration),
+            LabelSemantics(self.bundle.output_channels),
+            probability_resampling=ResamplingContract.from_configuration(
+                config, field="resampling_fn_probabilities", expected_is_seg=False))
+        elapsed = time.perf_counter() - start
+        shape = tuple(int(v) for v in prepared.data.shape[1:])
+        work = volume_work(shape, self.bundle.patch_size, self.step_fraction,
+                           2 ** len(self.bundle.mirroring_axes), len(self.bundle.models))
+        return restored.segmentation, prepared.properties, PredictionMetrics(elapsed, elapsed, work["tiles"], shape,
+                                                                            self.bundle.patch_size)
 
     def predict_case(self, image_files, output_prefix, *, save_probabilities: bool = False):
         """Predict one preprocessed case file and write ``<output_prefix>.npz``."""

@@ -291,3 +291,66 @@ def restore_device_segmentation(logits: torch.Tensor, properties: Mapping[str, o
                                       crop_lo=tuple(start for start, _ in box),
                                       axes=tuple(int(a) for a in plans.transpose_backward))
     return RestoredPrediction(segmentation=kernels.to_host(labels), probabilities=None)
+
+
+def plans_from_payload(payload: Mapping[str, object], *, configuration: str) -> PlansContract:
+    """The restoration view of a plans file: transposes, target spacing, probability resampling."""
+    from nnunet_mlx_b200.data.preprocessing import ResamplingContract as PlanEntry
+
+    forward = payload.get("transpose_forward")
+    if not isinstance(forward, list | tuple) or sorted(forward) != [0, 1, 2]:
+        raise ContractError("transpose_forward must be a permutation of [0, 1, 2]")
+    forward = tuple(int(a) for a in forward)
+    inverse = tuple(forward.index(a) for a in range(3))
+    backward = tuple(int(a) for a in payload.get("transpose_backward", inverse))
+    if backward != inverse:
+        raise ContractError("transpose_backward is not the inverse of transpose_forward")
+    configurations = payload.get("configurations")
+    if not isinstance(configurations, Mapping) or not isinstance(configurations.get(configuration), Mapping):
+        raise ContractError(f"plans have no configuration {configuration!r}")
+    config = configurations[configuration]
+    entry = PlanEntry.from_configuration(config, field="resampling_fn_probabilities", expected_is_seg=False)
+    spacing = tuple(None if v is None else float(v) for v in config.get("spacing", ()))
+    return PlansContract(forward, backward, ConfigurationContract(spacing, ResamplingContract(
+        entry.function_name, entry.order, entry.order_z, entry.force_separate_z,
+        entry.separate_z_anisotropy_threshold)))
+
+
+def restore_segmentation_on_device(logits: torch.Tensor, properties: Mapping[str, object], plans: PlansContract,
+                                   semantics: LabelSemantics, *, probability_resampling=None) -> RestoredPrediction:
+    """Labels in the image's grid from device channels-last logits under every supported policy.
+
+    Where the fused kernel applies this is ``restore_device_segmentation``.  Otherwise (spline plans
+    with a separate axis or order 3, torch-grid plans) the float32 class logits are resampled to the
+    crop grid on the device with the preprocessing kernels -- the arithmetic of the reference's host
+    path (``resample_class_logits_argmax``, reference ``prediction/restore.py:73-103``: the probability
+    contract's resampling of the logits, then the first argmax) -- and reduced, uncropped and
+    transposed by the identity-grid kernel.  ``probability_resampling`` is the plan entry parsed with
+    its torch-grid modes (``data.preprocessing.ResamplingContract``); without it the plans' spline
+    entry is used.  Raises ``ContractError`` where no device path exists (region models, half logits
+    off the fused path, spline orders other than 1 and 3).
+    """
+    fused = restore_device_segmentation(logits, properties, plans, semantics)
+    if fused is not None:
+        return fused
+    from nnunet_mlx_b200.data import preprocessing as pre
+
+    if logits.dtype != torch.float32:
+        raise ContractError("device restoration off the fused kernel needs float32 logits")
+    shape_before = _shape(properties.get("shape_before_cropping"), name="shape_before_cropping")
+    crop_shape = _shape(properties.get("shape_after_cropping_and_before_resampling"),
+                        name="shape_after_cropping_and_before_resampling")
+    box = _bounding_box(properties.get("bbox_used_for_cropping"), shape_before)
+    if tuple(stop - start for start, stop in box) != crop_shape:
+        raise ContractError("restored crop shape does not match bbox_used_for_cropping")
+    current, original = _prediction_resampling_spacings(properties, plans, crop_shape)
+    contract = probability_resampling or plans.configuration.probability_resampling
+    values = logits.permute(3, 0, 1, 2)  # classes first, a view
+    if contract.function_name == "resample_torch_fornnunet":
+        resampled = pre.resample_torch_device(values, crop_shape, current, original, contract, is_seg=False)
+    else:
+        resampled = pre.resample_spline_device(values, crop_shape, current, original, contract)
+    labels = restore_labels_on_device(resampled, crop_shape, class_axis=0, volume_shape=shape_before,
+                                      crop_lo=tuple(start for start, _ in box),
+                                      axes=tuple(int(a) for a in plans.transpose_backward))
+    return RestoredPrediction(segmentation=kernels.to_host(labels), probabilities=None)

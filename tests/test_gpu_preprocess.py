@@ -310,3 +310,60 @@ def test_device_preprocessing_default_spline_plan(cuda_device):
     assert tuple(result.data.shape) == reference.shape == (1, 47, 90, 83)
     np.testing.assert_allclose(result.data.cpu().numpy(), reference, rtol=RTOL, atol=ATOL)
     _status_clean()
+
+
+def test_raw_case_pipeline_on_device(cuda_device, tmp_path):
+    """Raw int16 case -> labels in the image's grid: device preprocessing, inference and restoration."""
+    from nnunet_mlx_b200.data.preprocessing import PreprocessingPlans, preprocess_raw_case
+    from nnunet_mlx_b200.model.folder import load_model_bundle
+    from nnunet_mlx_b200.model.topology import PlainConvUNetSpec
+    from nnunet_mlx_b200.prediction.pipeline import ModelFolderPredictor
+    from nnunet_mlx_b200.synthetic import write_model_folder
+
+    spec = PlainConvUNetSpec(input_channels=1, num_classes=3, features=(32, 64), kernel_sizes=((3, 3, 3),) * 2,
+                             strides=((1, 1, 1), (2, 2, 2)), encoder_convs=(2, 2), decoder_convs=(2,))
+    folder = write_model_folder(tmp_path / "model", spec, seeds=(0,), patch_size=(8, 16, 16))
+    plans = json.loads((folder / "plans.json").read_text())
+    spline = {"order": 3, "order_z": 0, "force_separate_z": None}
+    plans.update({"transpose_forward": [2, 0, 1], "transpose_backward": [1, 2, 0],
+                  "foreground_intensity_properties_per_channel": {"0": {
+                      "mean": 100.0, "std": 50.0, "percentile_00_5": -1000.0, "percentile_99_5": 400.0}}})
+    plans["configurations"]["3d_fullres"].update({
+        "spacing": [2.0, 1.0, 1.0], "normalization_schemes": ["CTNormalization"], "use_mask_for_norm": [False],
+        "resampling_fn_data": "resample_data_or_seg_to_shape",
+        "resampling_fn_data_kwargs": {"is_seg": False, **spline},
+        "resampling_fn_seg": "resample_data_or_seg_to_shape",
+        "resampling_fn_seg_kwargs": {"is_seg": True, "order": 1, "order_z": 0, "force_separate_z": None},
+        "resampling_fn_probabilities": "resample_data_or_seg_to_shape",
+        "resampling_fn_probabilities_kwargs": {"is_seg": False, "order": 1, "order_z": 0, "force_separate_z": None}})
+    (folder / "plans.json").write_text(json.dumps(plans))
+    bundle = load_model_bundle(folder, configuration="3d_fullres", device=cuda_device)
+    predictor = ModelFolderPredictor(bundle)
+
+    rng = np.random.default_rng(4)
+    raw = np.zeros((1, 30, 26, 9), dtype=np.int16)
+    raw[0, 2:28, 3:24, 1:8] = np.round(rng.normal(60, 150, (26, 21, 7)).clip(-1000, 2000)).astype(np.int16)
+    properties = {"spacing": [0.8, 0.8, 4.0]}
+    labels, prepared_properties, metrics = predictor.predict_raw_case(raw, properties, device=cuda_device)
+    assert labels.shape == raw.shape[1:] and labels.dtype == np.uint16
+
+    # the same steps one by one, restored with the host path's arithmetic (scipy zoom per plane)
+    prepared = preprocess_raw_case(raw, properties, PreprocessingPlans.from_payload(plans, configuration="3d_fullres"),
+                                   device=cuda_device)
+    logits = predictor.predictor.predict_logits_from_preprocessed_data(prepared.data.cpu().numpy())
+    crop_shape = tuple(prepared.properties["shape_after_cropping_and_before_resampling"])
+    original = tuple(properties["spacing"][a] for a in (2, 0, 1))
+    resampled = op.resample_spline(logits, crop_shape, (2.0, 1.0, 1.0), original, order=1, order_z=0,
+                                   force_separate_z=None)
+    volume = np.zeros(tuple(prepared.properties["shape_before_cropping"]), dtype=np.uint16)
+    box = tuple(slice(a, b) for a, b in prepared.properties["bbox_used_for_cropping"])
+    volume[box] = np.argmax(resampled, axis=0)
+    expected = volume.transpose(1, 2, 0)
+    ordered = np.sort(resampled, axis=0)
+    clear = np.zeros(volume.shape, dtype=bool)
+    clear[box] = (ordered[-1] - ordered[-2]) > 1e-4
+    clear = clear.transpose(1, 2, 0)
+    np.testing.assert_array_equal(labels[clear], expected[clear])
+    assert (labels == expected).mean() >= 0.999
+    assert prepared_properties["bbox_used_for_cropping"] == prepared.properties["bbox_used_for_cropping"]
+    _status_clean()

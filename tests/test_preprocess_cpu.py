@@ -180,3 +180,21 @@ def test_oracle_spline_separate_axis_is_planewise_zoom_then_nearest():
                            grid_mode=True) for k in range(6)]
     expected = np.stack(planes)[op.nearest_axis_indices(6, 4)].astype(np.float32)
     np.testing.assert_array_equal(got[0], expected)
+
+
+def test_restoration_plans_from_payload():
+    from nnunet_mlx_b200.errors import ContractError
+    from nnunet_mlx_b200.prediction.restore import plans_from_payload
+
+    payload = {"transpose_forward": [2, 0, 1], "configurations": {"c": {
+        "spacing": [None, 0.8, 0.8],
+        "resampling_fn_probabilities": "resample_data_or_seg_to_shape",
+        "resampling_fn_probabilities_kwargs": {"is_seg": False, "order": 1, "order_z": 0, "force_separate_z": None}}}}
+    plans = plans_from_payload(payload, configuration="c")
+    assert plans.transpose_backward == (1, 2, 0)
+    assert plans.configuration.spacing == (None, 0.8, 0.8)
+    entry = plans.configuration.probability_resampling
+    assert (entry.function_name, entry.order, entry.order_z, entry.force_separate_z) == (
+        "resample_data_or_seg_to_shape", 1, 0, None)
+    with pytest.raises(ContractError, match="inverse"):
+        plans_from_payload({**payload, "transpose_backward": [2, 0, 1]}, configuration="c")
