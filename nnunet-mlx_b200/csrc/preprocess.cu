@@ -715,36 +715,127 @@ __device__ __forceinline__ int mirror_index(int j, int n) {
   return j < n ? j : period - 1 - j;
 }
 
-// Cubic B-spline prefilter of every line along `axis` (one thread per line):
-// gain, causal pass with the half-sample-symmetric initial value
-// c+(0) = sum_k z^k x(-k), anticausal pass with c-(n-1) = z / (z - 1) c+(n-1).
-__global__ void __launch_bounds__(kThreads) spline_filter_kernel(double* coef, SplineGeom g, int axis) {
+// Cubic B-spline prefilter of every line along `axis`: gain, causal pass with
+// the half-sample-symmetric initial value c+(0) = sum_k z^k x(-k), anticausal
+// pass with c-(n-1) = z / (z - 1) c+(n-1), each operation rounded separately
+// as the host implementation computes it.  A block of 32 threads filters 32
+// lines that are neighbours in memory; the lines stream through shared memory
+// in chunks of kChunk samples (coalesced loads and stores), and each thread
+// runs its line's serial recursion out of shared memory, carrying the last
+// value between chunks.
+constexpr int kChunk = 64;
+
+// Element offset of (line lane, position j) and the stride between positions.
+__device__ __forceinline__ void filter_line_geometry(const SplineGeom& g, int axis, int64_t group, int lane,
+                                                     int64_t* base, int64_t* step, bool* valid) {
+  const int64_t d0 = g.pdim[0], d1 = g.pdim[1], d2 = g.pdim[2];
+  const int64_t per_channel = d0 * d1 * d2;
+  if (axis == 2) {
+    // 32 consecutive rows (c, p0, p1); positions along p2 (stride 1)
+    const int64_t row = group * 32 + lane;
+    *valid = row < (int64_t)g.channels * d0 * d1;
+    *base = row * d2;
+    *step = 1;
+  } else {
+    // lines (c, q, p2) with p2 = 32 b + lane; q is the other non-filtered axis
+    const int64_t blocks2 = (d2 + 31) / 32;
+    const int64_t q_count = axis == 0 ? d1 : d0;
+    const int64_t cq = group / blocks2;
+    const int64_t p2 = (group - cq * blocks2) * 32 + lane;
+    const int64_t c = cq / q_count, q = cq - c * q_count;
+    *valid = c < g.channels && p2 < d2;
+    *base = c * per_channel + (axis == 0 ? q * d2 : q * d1 * d2) + p2;
+    *step = axis == 0 ? d1 * d2 : d2;
+  }
+}
+
+__global__ void __launch_bounds__(32) spline_filter_kernel(double* coef, SplineGeom g, int axis, int64_t groups) {
+  __shared__ double tile[32][kChunk + 1];
   const double z = sqrt(3.0) - 2.0;
   const double gain = __dmul_rn(1.0 - z, 1.0 - 1.0 / z);
-  const int64_t d0 = g.pdim[0], d1 = g.pdim[1], d2 = g.pdim[2];
+  const double anti = z / (z - 1.0);
+  const int lane = threadIdx.x;
   const int n = g.pdim[axis];
-  const int64_t step = axis == 0 ? d1 * d2 : axis == 1 ? d2 : 1;
-  const int64_t per_channel = d0 * d1 * d2;
-  const int64_t lines = g.channels * (per_channel / n);
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < lines; t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t per = per_channel / n;
-    const int64_t ch = t / per, r = t - ch * per;
-    int64_t base;
-    if (axis == 0) base = r;
-    else if (axis == 1) base = (r / d2) * d1 * d2 + r % d2;
-    else base = r * d2;
-    double* c = coef + ch * per_channel + base;
-    // separate roundings (no fused multiply-add), as the host implementation computes them
-    for (int i = 0; i < n; ++i) c[i * step] = __dmul_rn(c[i * step], gain);
-    double acc = c[0], zk = z;
-    for (int k = 1; k < 64 && fabs(zk) > 1e-30; ++k) {
-      acc = __dadd_rn(acc, __dmul_rn(zk, c[mirror_index(-k, n) * step]));
-      zk = __dmul_rn(zk, z);
+  const int chunks = (n + kChunk - 1) / kChunk;
+  for (int64_t group = blockIdx.x; group < groups; group += gridDim.x) {
+    int64_t my_base, step;
+    bool my_valid;
+    filter_line_geometry(g, axis, group, lane, &my_base, &step, &my_valid);
+    // Load chunk k of all 32 lines into the tile (coalesced along the memory-contiguous direction).
+    auto load = [&](int k) {
+      const int j0 = k * kChunk;
+      const int len = min(kChunk, n - j0);
+      if (axis == 2) {
+        for (int i = 0; i < 32; ++i) {
+          const int64_t b = __shfl_sync(0xffffffffu, my_base, i);
+          const bool v = __shfl_sync(0xffffffffu, my_valid, i);
+          for (int j = lane; j < len; j += 32) tile[i][j] = v ? coef[b + j0 + j] : 0.0;
+        }
+      } else {
+        for (int j = 0; j < len; ++j) tile[lane][j] = my_valid ? coef[my_base + (int64_t)(j0 + j) * step] : 0.0;
+      }
+      __syncwarp();
+    };
+    auto store = [&](int k) {
+      __syncwarp();
+      const int j0 = k * kChunk;
+      const int len = min(kChunk, n - j0);
+      if (axis == 2) {
+        for (int i = 0; i < 32; ++i) {
+          const int64_t b = __shfl_sync(0xffffffffu, my_base, i);
+          const bool v = __shfl_sync(0xffffffffu, my_valid, i);
+          for (int j = lane; j < len; j += 32)
+            if (v) coef[b + j0 + j] = tile[i][j];
+        }
+      } else {
+        for (int j = 0; j < len; ++j)
+          if (my_valid) coef[my_base + (int64_t)(j0 + j) * step] = tile[lane][j];
+      }
+      __syncwarp();
+    };
+    double* t = tile[lane];
+    // causal pass, chunk by chunk
+    double carry = 0.0;
+    for (int k = 0; k < chunks; ++k) {
+      load(k);
+      const int len = min(kChunk, n - k * kChunk);
+      for (int j = 0; j < len; ++j) t[j] = __dmul_rn(t[j], gain);
+      int j = 0;
+      if (k == 0) {
+        // initial value from the first samples (mirror indices of -k lie in the first chunk while
+        // n > kChunk; a line of at most kChunk samples is whole in the tile)
+        double acc = t[0], zk = z;
+        for (int m = 1; m < 64 && fabs(zk) > 1e-30; ++m) {
+          const int src = mirror_index(-m, n);
+          acc = __dadd_rn(acc, __dmul_rn(zk, src < kChunk ? t[src] : 0.0));
+          zk = __dmul_rn(zk, z);
+        }
+        t[0] = acc;
+        carry = acc;
+        j = 1;
+      }
+      for (; j < len; ++j) {
+        carry = __dadd_rn(t[j], __dmul_rn(z, carry));
+        t[j] = carry;
+      }
+      store(k);
     }
-    c[0] = acc;
-    for (int j = 1; j < n; ++j) c[j * step] = __dadd_rn(c[j * step], __dmul_rn(z, c[(j - 1) * step]));
-    c[(n - 1) * step] = __dmul_rn(c[(n - 1) * step], z / (z - 1.0));
-    for (int j = n - 2; j >= 0; --j) c[j * step] = __dmul_rn(z, __dsub_rn(c[(j + 1) * step], c[j * step]));
+    // anticausal pass, last chunk first
+    for (int k = chunks - 1; k >= 0; --k) {
+      load(k);
+      const int len = min(kChunk, n - k * kChunk);
+      int j = len - 1;
+      if (k == chunks - 1) {
+        t[j] = __dmul_rn(t[j], anti);
+        carry = t[j];
+        --j;
+      }
+      for (; j >= 0; --j) {
+        carry = __dmul_rn(z, __dsub_rn(carry, t[j]));
+        t[j] = carry;
+      }
+      store(k);
+    }
   }
 }
 
@@ -1077,8 +1168,11 @@ int32_t nnb_spline_resize(const nnb_spline_resize_args* a, void* stream) {
   if (a->order == 3) {
     for (int axis = 0; axis < 3; ++axis) {
       if (!((a->axes >> axis) & 1)) continue;
-      const int64_t lines = (int64_t)g.channels * g.pdim[0] * g.pdim[1] * g.pdim[2] / g.pdim[axis];
-      spline_filter_kernel<<<grid_for(lines), kThreads, 0, s>>>(a->coefficients, g, axis);
+      const int64_t groups = axis == 2 ? ((int64_t)g.channels * g.pdim[0] * g.pdim[1] + 31) / 32
+                                       : (int64_t)g.channels * (axis == 0 ? g.pdim[1] : g.pdim[0]) *
+                                             ((g.pdim[2] + 31) / 32);
+      const int64_t cap = 148LL * 32;  // 32 resident 32-thread blocks per SM
+      spline_filter_kernel<<<(int)(groups < cap ? groups : cap), 32, 0, s>>>(a->coefficients, g, axis, groups);
     }
   }
   const int64_t rows = (int64_t)g.channels * g.tgt[0] * g.tgt[1];
