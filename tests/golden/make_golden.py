@@ -25,7 +25,9 @@ separate-axis policy, and the cascade labels of twelve recorded ``preprocess_raw
 runs with their nonzero mask, previous-stage input, plans and geometry).  Outputs:
 ``geometry.json``, ``gaussian.npz``, ``weights_map.json``, ``upstream_runner_subset.npz``,
 ``restore_axes.npz``, ``restore_policy.json``, ``torch_resampling_labels.npz``,
-``nearest_axis.json`` (``nnunet_mlx.data.resampling.nearest_axis_indices``, reference 401-407).  Nothing at
+``nearest_axis.json`` (``nnunet_mlx.data.resampling.nearest_axis_indices``, reference 401-407),
+``preprocess_policy.json`` (``nnunet_mlx.plans.ResamplingContract.from_configuration`` on accepted and
+rejected plan entries, ``nnunet_mlx.data.resampling.compute_new_shape``).  Nothing at
 test time reads the reference checkout.
 """
 
@@ -188,6 +190,36 @@ NEAREST_AXIS_CASES = [(1, 1), (1, 4), (3, 7), (7, 3), (5, 5), (10, 4), (4, 10), 
                       (3, 2), (13, 26), (26, 13), (9, 14), (14, 9), (63, 64), (64, 63)]
 
 
+_TORCH = "resample_torch_fornnunet"
+_SPLINE = "resample_data_or_seg_to_shape"
+PLAN_ENTRY_CASES = [
+    (_TORCH, {"is_seg": False}, False), (_TORCH, {"is_seg": False, "mode": "nearest"}, False),
+    (_TORCH, {"is_seg": False, "mode": "cubic"}, False), (_TORCH, {"is_seg": False, "aniso_axis_mode": "linear"}, False),
+    (_TORCH, {"is_seg": False, "force_separate_z": True}, False),
+    (_TORCH, {"is_seg": False, "force_separate_z": "yes"}, False),
+    (_TORCH, {"is_seg": True, "seg_tiebreak": "lowest"}, True), (_TORCH, {"is_seg": True, "seg_tiebreak": "middle"}, True),
+    (_TORCH, {"is_seg": False, "separate_z_anisotropy_threshold": 2}, False),
+    (_TORCH, {"is_seg": False, "separate_z_anisotropy_threshold": 0}, False),
+    (_TORCH, {"is_seg": False, "num_threads": 8}, False), (_TORCH, {"is_seg": False, "device": "cuda"}, False),
+    (_TORCH, {"is_seg": False, "memefficient_seg_resampling": False}, False), (_TORCH, {"is_seg": False, "bogus": 1}, False),
+    (_TORCH, {"is_seg": False, "order": 3}, False), (_TORCH, {"is_seg": True}, False), (_TORCH, {}, False),
+    (_SPLINE, {"is_seg": False}, False), (_SPLINE, {"is_seg": False, "order": 1}, False),
+    (_SPLINE, {"is_seg": False, "order": 6}, False), (_SPLINE, {"is_seg": False, "order": -1}, False),
+    (_SPLINE, {"is_seg": False, "order_z": 3}, False), (_SPLINE, {"is_seg": False, "force_separate_z": None}, False),
+    (_SPLINE, {"is_seg": False, "force_separate_z": True}, False),
+    (_SPLINE, {"is_seg": True, "seg_tiebreak": "highest"}, True), (_SPLINE, {"is_seg": False, "num_threads": 2}, False),
+    (_SPLINE, {"is_seg": False, "order": True}, False),
+    (_SPLINE, {"is_seg": False, "separate_z_anisotropy_threshold": 1.5}, False),
+    (_SPLINE, {"is_seg": False, "order": 3, "order_z": 0, "force_separate_z": None}, False),
+    ("resample_with_magic", {"is_seg": False}, False),
+]
+NEW_SHAPE_CASES = [((5, 5, 5), (1.0, 1.0, 1.0), (2.0, 2.0, 2.0)), ((7, 4, 6), (5.0, 0.7, 1.6), (2.5, 1.4, 0.8)),
+                   ((101, 768, 768), (5.0, 0.8, 0.8), (5.0, 1.0, 1.0)), ((3, 3, 3), (1.5, 1.5, 1.5), (1.0, 1.0, 1.0)),
+                   ((155, 240, 240), (1.0, 1.0, 1.0), (1.0, 1.0, 1.0)), ((284, 400, 400), (3.0, 2.0364, 2.0364),
+                                                                        (3.0, 2.0364, 2.0364)),
+                   ((1, 9, 11), (999.0, 0.5, 0.5), (999.0, 0.75, 0.75)), ((33, 65), (0.6, 0.6), (0.9, 0.9))]
+
+
 def main(reference: Path) -> None:
     sys.path.insert(0, str(reference / "src"))
     from nnunet_mlx.prediction import inference
@@ -298,6 +330,30 @@ def main(reference: Path) -> None:
     nearest = [{"old": o, "new": n, "indices": [int(i) for i in nearest_axis_indices(o, n)]}
                for o, n in NEAREST_AXIS_CASES]
     (HERE / "nearest_axis.json").write_text(json.dumps(nearest) + "\n")
+
+    # the reference's plan-entry parser and new-shape rounding, on accepted and rejected inputs
+    from nnunet_mlx.data.resampling import compute_new_shape
+    from nnunet_mlx.errors import ContractError as ReferenceContractError
+    from nnunet_mlx.plans import ResamplingContract as ReferenceResampling
+
+    entries = []
+    for function, kwargs, expected_is_seg in PLAN_ENTRY_CASES:
+        record = {"function": function, "kwargs": kwargs, "expected_is_seg": expected_is_seg}
+        try:
+            parsed = ReferenceResampling.from_configuration({"f": function, "f_kwargs": kwargs}, field="f",
+                                                           expected_is_seg=expected_is_seg)
+            record["parsed"] = {"function_name": parsed.function_name, "order": parsed.order,
+                                "order_z": parsed.order_z, "force_separate_z": parsed.force_separate_z,
+                                "seg_tiebreak": parsed.seg_tiebreak, "mode": parsed.mode,
+                                "aniso_axis_mode": parsed.aniso_axis_mode,
+                                "separate_z_anisotropy_threshold": parsed.separate_z_anisotropy_threshold}
+        except ReferenceContractError:
+            record["parsed"] = None
+        entries.append(record)
+    shapes = [{"shape": list(a), "old": list(b), "new": list(c), "result": list(compute_new_shape(a, b, c))}
+              for a, b, c in NEW_SHAPE_CASES]
+    (HERE / "preprocess_policy.json").write_text(json.dumps({"entries": entries, "new_shape": shapes}, indent=1)
+                                                 + "\n")
 
 
 if __name__ == "__main__":

@@ -198,3 +198,32 @@ def test_restoration_plans_from_payload():
         "resample_data_or_seg_to_shape", 1, 0, None)
     with pytest.raises(ContractError, match="inverse"):
         plans_from_payload({**payload, "transpose_backward": [2, 0, 1]}, configuration="c")
+
+
+def test_plan_entries_parse_like_the_reference():
+    """Accept/reject decisions and parsed fields equal the reference's parser (recorded)."""
+    from nnunet_mlx_b200.data.preprocessing import ResamplingContract
+    from nnunet_mlx_b200.errors import ContractError
+
+    recorded = json.loads((GOLDEN / "preprocess_policy.json").read_text())
+    for entry in recorded["entries"]:
+        configuration = {"f": entry["function"], "f_kwargs": entry["kwargs"]}
+        expected = entry["parsed"]
+        if expected is None:
+            with pytest.raises(ContractError):
+                ResamplingContract.from_configuration(configuration, field="f", expected_is_seg=entry["expected_is_seg"])
+            continue
+        parsed = ResamplingContract.from_configuration(configuration, field="f",
+                                                       expected_is_seg=entry["expected_is_seg"])
+        for name, value in expected.items():
+            if name == "seg_tiebreak" and value is None:
+                continue  # an omitted spline tie rule: only label resampling, which the device path does not do
+            assert getattr(parsed, name) == value, (entry, name)
+
+
+def test_new_shape_matches_reference():
+    from nnunet_mlx_b200.data.preprocessing import compute_new_shape
+
+    for case in json.loads((GOLDEN / "preprocess_policy.json").read_text())["new_shape"]:
+        assert list(compute_new_shape(case["shape"], case["old"], case["new"])) == case["result"]
+        assert list(op.compute_new_shape(case["shape"], case["old"], case["new"])) == case["result"]
