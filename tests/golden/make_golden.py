@@ -27,7 +27,10 @@ runs with their nonzero mask, previous-stage input, plans and geometry).  Output
 ``restore_axes.npz``, ``restore_policy.json``, ``torch_resampling_labels.npz``,
 ``nearest_axis.json`` (``nnunet_mlx.data.resampling.nearest_axis_indices``, reference 401-407),
 ``preprocess_policy.json`` (``nnunet_mlx.plans.ResamplingContract.from_configuration`` on accepted and
-rejected plan entries, ``nnunet_mlx.data.resampling.compute_new_shape``).  Nothing at
+rejected plan entries, ``nnunet_mlx.data.resampling.compute_new_shape``), and
+``preprocess_reference.npz`` (the reference's own ``preprocess_raw_case``, reference
+``data/preprocessing.py:60-163``, on grid-preserving plans: every normalisation scheme, masks
+with holes, transposes, input dtypes, a cascade input).  Nothing at
 test time reads the reference checkout.
 """
 
@@ -220,6 +223,20 @@ NEW_SHAPE_CASES = [((5, 5, 5), (1.0, 1.0, 1.0), (2.0, 2.0, 2.0)), ((7, 4, 6), (5
                    ((1, 9, 11), (999.0, 0.5, 0.5), (999.0, 0.75, 0.75)), ((33, 65), (0.6, 0.6), (0.9, 0.9))]
 
 
+PREPROCESS_CASES = [
+    ("ct-int16", np.int16, ("CTNormalization",), (False,), (0, 1, 2), False),
+    ("ct-transposed", np.int16, ("CTNormalization",), (False,), (2, 0, 1), False),
+    ("zscore-mask", np.float32, ("ZScoreNormalization",), (True,), (1, 2, 0), False),
+    ("zscore-all", np.float64, ("ZScoreNormalization",), (False,), (0, 2, 1), False),
+    ("rescale", np.int32, ("RescaleTo01Normalization",), (False,), (0, 1, 2), False),
+    ("rgb", np.uint8, ("RGBTo01Normalization",), (False,), (2, 1, 0), False),
+    ("none", np.float32, ("NoNormalization",), (False,), (0, 1, 2), False),
+    ("mixed", np.float32, ("CTNormalization", "ZScoreNormalization", "RescaleTo01Normalization"),
+     (False, True, False), (2, 0, 1), False),
+    ("cascade", np.uint16, ("ZScoreNormalization",), (True,), (2, 0, 1), True),
+]
+
+
 def main(reference: Path) -> None:
     sys.path.insert(0, str(reference / "src"))
     from nnunet_mlx.prediction import inference
@@ -354,6 +371,70 @@ def main(reference: Path) -> None:
               for a, b, c in NEW_SHAPE_CASES]
     (HERE / "preprocess_policy.json").write_text(json.dumps({"entries": entries, "new_shape": shapes}, indent=1)
                                                  + "\n")
+
+    _record_reference_preprocessing(reference, recorded_plans=metadata["pipeline"][6]["plans"])
+
+
+def _load_reference_preprocessing(reference: Path):
+    """The reference's ``data/preprocessing.py`` as a module.
+
+    Its one Python-3.13-only construct (a default on the generic parameter of
+    ``PreprocessedRawCase``) is dropped in memory so that the module runs on 3.12;
+    nothing else changes and nothing is written.
+    """
+    import types
+
+    path = reference / "src" / "nnunet_mlx" / "data" / "preprocessing.py"
+    source = path.read_text().replace("class PreprocessedRawCase[T = FloatArray]:", "class PreprocessedRawCase[T]:")
+    module = types.ModuleType("nnunet_mlx.data.preprocessing")
+    module.__file__ = str(path)
+    sys.modules["nnunet_mlx.data.preprocessing"] = module
+    exec(compile(source, str(path), "exec"), module.__dict__)
+    return module
+
+
+def _record_reference_preprocessing(reference: Path, *, recorded_plans: dict) -> None:
+    """``preprocess_raw_case`` outputs of the reference for grid-preserving plans (no resampler needed)."""
+    from nnunet_mlx.plans import PlansContract
+
+    module = _load_reference_preprocessing(reference)
+    rng = np.random.default_rng(77)
+    ct = {"mean": 60.5, "std": 41.25, "percentile_00_5": -150.0, "percentile_99_5": 230.0}
+    arrays: dict[str, np.ndarray] = {}
+    cases = []
+    for name, dtype, schemes, use_mask, transpose, cascade in PREPROCESS_CASES:
+        channels = len(schemes)
+        shape = (channels, 9, 11, 10)
+        values = np.zeros(shape, dtype=np.float64)
+        values[:, 1:8, 2:10, 1:9] = rng.normal(40, 90, (channels, 7, 8, 8))
+        values[:, 4, 5, 4] = 0  # an enclosed hole of the nonzero mask
+        if "RGBTo01Normalization" in schemes:
+            values = np.clip(np.abs(values), 0, 255)
+        if np.dtype(dtype).kind in "iu":
+            values = np.round(values)
+        raw = values.astype(dtype)
+        plans = json.loads(json.dumps(recorded_plans))
+        plans["transpose_forward"] = list(transpose)
+        plans["transpose_backward"] = [list(transpose).index(a) for a in range(3)]
+        plans["foreground_intensity_properties_per_channel"] = {str(c): dict(ct) for c in range(channels)}
+        config = plans["configurations"]["selected"]
+        config.update({"spacing": [None, None, None], "normalization_schemes": list(schemes),
+                       "use_mask_for_norm": list(use_mask)})
+        previous = rng.integers(0, 3, (1, *shape[1:])).astype(np.int16) if cascade else None
+        spacing = [0.7, 1.6, 5.0]
+        out = module.preprocess_raw_case(raw, {"spacing": spacing},
+                                         PlansContract.from_payload(plans, configuration="selected"),
+                                         segmentation_previous_stage=previous)
+        arrays[f"{name}-raw"] = raw
+        arrays[f"{name}-data"] = np.asarray(out.data)
+        if previous is not None:
+            arrays[f"{name}-previous"] = previous
+            arrays[f"{name}-labels"] = np.asarray(out.previous_stage)
+        cases.append({"name": name, "plans": plans, "spacing": spacing,
+                      "bbox": out.properties["bbox_used_for_cropping"],
+                      "shape_before_cropping": list(out.properties["shape_before_cropping"])})
+    arrays["metadata"] = np.array(json.dumps({"cases": cases}))
+    np.savez_compressed(HERE / "preprocess_reference.npz", **arrays)
 
 
 if __name__ == "__main__":

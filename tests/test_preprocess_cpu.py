@@ -227,3 +227,28 @@ def test_new_shape_matches_reference():
     for case in json.loads((GOLDEN / "preprocess_policy.json").read_text())["new_shape"]:
         assert list(compute_new_shape(case["shape"], case["old"], case["new"])) == case["result"]
         assert list(op.compute_new_shape(case["shape"], case["old"], case["new"])) == case["result"]
+
+
+def test_oracle_preprocessing_matches_reference_outputs():
+    """Normalised data, crop boxes and cascade labels equal the reference's own ``preprocess_raw_case``."""
+    saved = np.load(GOLDEN / "preprocess_reference.npz")
+    cases = json.loads(str(saved["metadata"].item()))["cases"]
+    assert len(cases) == 9
+    for case in cases:
+        plans = case["plans"]
+        config = plans["configurations"]["selected"]
+        name = case["name"]
+        previous = saved[f"{name}-previous"] if f"{name}-previous" in saved.files else None
+        data, labels, properties = op.preprocess(
+            saved[f"{name}-raw"], case["spacing"], transpose_forward=plans["transpose_forward"],
+            configured_spacing=config["spacing"], schemes=config["normalization_schemes"],
+            use_mask=config["use_mask_for_norm"], intensities=plans["foreground_intensity_properties_per_channel"],
+            data_resampling=_oracle_kwargs(config["resampling_fn_data_kwargs"]),
+            seg_resampling={**_oracle_kwargs(config["resampling_fn_seg_kwargs"]), "tiebreak": "nearest"},
+            previous=previous)
+        assert properties["bbox_used_for_cropping"] == case["bbox"], name
+        assert list(properties["shape_before_cropping"]) == case["shape_before_cropping"], name
+        np.testing.assert_array_equal(data, saved[f"{name}-data"], err_msg=name)
+        if previous is not None:
+            np.testing.assert_array_equal(labels.astype(np.int64), saved[f"{name}-labels"].astype(np.int64),
+                                          err_msg=name)
