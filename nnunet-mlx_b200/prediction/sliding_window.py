@@ -168,7 +168,8 @@ class VolumeAccumulator:
         self.shape = tuple(int(s) for s in padded_spatial)
         self.acc = torch.zeros((*self.shape, num_classes), dtype=torch.float32, device=device)
         self.normalizer = torch.zeros(self.shape, dtype=torch.float32, device=device)
-        self.gaussian = torch.from_numpy(np.ascontiguousarray(gaussian_importance(tuple(patch)))).to(device)
+        # the cached map is read-only: hand torch a writable copy of it
+        self.gaussian = torch.from_numpy(np.array(gaussian_importance(tuple(patch)), dtype=np.float32)).to(device)
 
 
 def run_tiles(models, volume: torch.Tensor, acc: VolumeAccumulator, offsets, patch, masks,
