@@ -1,18 +1,22 @@
 // Raw-case preprocessing on the device: nonzero bounding box, hole filling of
-// the nonzero mask, fused transpose + crop + per-channel normalisation, and
-// upstream's torch-grid resampler (image values and labels).  Every kernel is a
-// streaming pass over HBM: the volume kernels give one warp to each row of
-// their output (row coordinates and the outer axes' interpolation taps from
-// one division per row, coalesced loads and stores along the row), the plans'
-// transpose is folded into the source strides, and per-thread partial
-// reductions are combined by warp shuffles with one atomic per warp.  The C entry points (declared in include/nnb.h) validate
-// their arguments here and allocate nothing.
+// the nonzero mask, fused transpose + crop + per-channel normalisation,
+// upstream's torch-grid resampler (image values and labels), and the spline
+// resampler of nnU-Net's default plans (edge padding, cubic B-spline
+// prefilter, order-1/3 sampling on the half-pixel grid, the out-of-plane
+// order-0 pass of separate-axis resampling).  The streaming kernels give one
+// warp to each row of their output (row coordinates and the outer axes'
+// interpolation taps from one division per row, coalesced loads and stores
+// along the row), the plans' transpose is folded into the source strides, and
+// partial reductions are combined by warp shuffles and per-block shared memory
+// before their atomics.  The C entry points (declared in include/nnb.h)
+// validate their arguments here and allocate nothing.
 //
 // Reference: src/nnunet_mlx/data/preprocessing.py:60-163 (step order),
 // :166-217 (crop_to_nonzero), :222-319 (normalisation), :340-343 (hole filling
 // via scipy); src/nnunet_mlx/kernels/metal_torch_resample.py:51-131 (torch-grid
 // kernel), :154-216 (launch and separate-axis composition);
-// src/nnunet_mlx/data/resampling.py:87-172, 175-244 (policy).
+// src/nnunet_mlx/data/resampling.py:87-172, 175-244 (policy), 268-306 and
+// 379-427 (separate-axis spline path), 476-502 (skimage resize = scipy zoom).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
