@@ -30,7 +30,8 @@ runs with their nonzero mask, previous-stage input, plans and geometry).  Output
 rejected plan entries, ``nnunet_mlx.data.resampling.compute_new_shape``), and
 ``preprocess_reference.npz`` (the reference's own ``preprocess_raw_case``, reference
 ``data/preprocessing.py:60-163``, on grid-preserving plans: every normalisation scheme, masks
-with holes, transposes, input dtypes, a cascade input).  Nothing at
+with holes, transposes, input dtypes, a cascade input), and ``plans_reference.json`` (the reference's
+``PlansContract.from_payload`` view of every recorded plans payload plus three spline variants).  Nothing at
 test time reads the reference checkout.
 """
 
@@ -373,6 +374,46 @@ def main(reference: Path) -> None:
                                                  + "\n")
 
     _record_reference_preprocessing(reference, recorded_plans=metadata["pipeline"][6]["plans"])
+    _record_reference_plans(metadata)
+
+
+def _record_reference_plans(metadata: dict) -> None:
+    """The reference's ``PlansContract.from_payload`` view of every plans payload the fixtures hold."""
+    from nnunet_mlx.plans import PlansContract
+
+    payloads = [(f"pipeline:{i}", run["plans"]) for i, run in enumerate(metadata["pipeline"])]
+    with np.load(HERE / "preprocess_reference.npz") as saved:
+        cases = json.loads(str(saved["metadata"].item()))["cases"]
+    payloads += [(f"reference:{i}", case["plans"]) for i, case in enumerate(cases)]
+    spline_variants = []
+    for order, order_z, force in ((3, 0, None), (1, 0, False), (3, 1, True)):
+        plans = json.loads(json.dumps(metadata["pipeline"][8]["plans"]))
+        config = plans["configurations"]["selected"]
+        for field in ("resampling_fn_data", "resampling_fn_seg", "resampling_fn_probabilities"):
+            config[field] = "resample_data_or_seg_to_shape"
+            config[f"{field}_kwargs"] = {"is_seg": field == "resampling_fn_seg", "order": order,
+                                         "order_z": order_z, "force_separate_z": force}
+        spline_variants.append(plans)
+    payloads += [(f"spline:{i}", plans) for i, plans in enumerate(spline_variants)]
+
+    def entry(contract):
+        return {"function_name": contract.function_name, "order": contract.order, "order_z": contract.order_z,
+                "force_separate_z": contract.force_separate_z, "mode": contract.mode,
+                "aniso_axis_mode": contract.aniso_axis_mode,
+                "separate_z_anisotropy_threshold": contract.separate_z_anisotropy_threshold}
+
+    parsed = []
+    for name, plans in payloads:
+        contract = PlansContract.from_payload(plans, configuration="selected")
+        config = contract.configuration
+        parsed.append({"name": name, "transpose_forward": list(contract.transpose_forward),
+                       "transpose_backward": list(contract.transpose_backward), "spacing": list(config.spacing),
+                       "normalization_schemes": list(config.normalization_schemes),
+                       "use_mask_for_norm": list(config.use_mask_for_norm),
+                       "data": entry(config.data_resampling), "seg": entry(config.segmentation_resampling),
+                       "probabilities": entry(config.probability_resampling)})
+    (HERE / "plans_reference.json").write_text(json.dumps({"spline_variants": spline_variants, "parsed": parsed})
+                                               + "\n")
 
 
 def _load_reference_preprocessing(reference: Path):

@@ -252,3 +252,34 @@ def test_oracle_preprocessing_matches_reference_outputs():
         if previous is not None:
             np.testing.assert_array_equal(labels.astype(np.int64), saved[f"{name}-labels"].astype(np.int64),
                                           err_msg=name)
+
+
+def test_plans_views_match_the_reference_parser():
+    """Our preprocessing and restoration views of every recorded plans payload equal the reference's."""
+    from nnunet_mlx_b200.data.preprocessing import PreprocessingPlans
+    from nnunet_mlx_b200.prediction.restore import plans_from_payload
+
+    recorded = json.loads((GOLDEN / "plans_reference.json").read_text())
+    saved, meta = _recorded()
+    with np.load(GOLDEN / "preprocess_reference.npz") as reference:
+        cases = json.loads(str(reference["metadata"].item()))["cases"]
+    sources = {"pipeline": [run["plans"] for run in meta["pipeline"]], "reference": [c["plans"] for c in cases],
+               "spline": recorded["spline_variants"]}
+    assert len(recorded["parsed"]) == 24
+    for expected in recorded["parsed"]:
+        kind, index = expected["name"].split(":")
+        payload = sources[kind][int(index)]
+        ours = PreprocessingPlans.from_payload(payload, configuration="selected")
+        assert list(ours.transpose_forward) == expected["transpose_forward"], expected["name"]
+        assert list(ours.spacing) == expected["spacing"], expected["name"]
+        assert list(ours.normalization_schemes) == expected["normalization_schemes"], expected["name"]
+        assert list(ours.use_mask_for_norm) == expected["use_mask_for_norm"], expected["name"]
+        for view, key in ((ours.data_resampling, "data"), (ours.seg_resampling, "seg")):
+            for field, value in expected[key].items():
+                assert getattr(view, field) == value, (expected["name"], key, field)
+        restore = plans_from_payload(payload, configuration="selected")
+        assert list(restore.transpose_backward) == expected["transpose_backward"], expected["name"]
+        assert list(restore.configuration.spacing) == expected["spacing"], expected["name"]
+        probabilities = restore.configuration.probability_resampling
+        for field in ("function_name", "order", "order_z", "force_separate_z", "separate_z_anisotropy_threshold"):
+            assert getattr(probabilities, field) == expected["probabilities"][field], (expected["name"], field)
