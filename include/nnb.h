@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define NNB_ABI_VERSION 12
+#define NNB_ABI_VERSION 13
 
 enum nnb_status {
   NNB_OK = 0,
@@ -167,6 +167,15 @@ int64_t nnb_operand_range_events(int32_t reset);
  */
 int64_t nnb_conv3d_partial_tiles(const nnb_conv3d_args* args);
 
+/*
+ * Which kernel nnb_conv3d launches for `args` (the fields nnb_conv3d_partial_tiles
+ * reads, plus precision): 0 the CUDA-core kernel (operand_format 0), 1 the
+ * tensor-core box kernel, 2 the halo kernel, 3 the z-streaming kernel.
+ * Negative: an nnb_status error.  For reporting and profiling; no reference
+ * counterpart (MLX chooses its conv3d algorithm internally).
+ */
+int32_t nnb_conv3d_kernel_mode(const nnb_conv3d_args* args);
+
 /* Bytes of the tensor-core weight image for (cout, kvol, cin_total, precision). */
 int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, int32_t precision);
 
@@ -213,7 +222,10 @@ int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t
  *    or threads) race on it; order them.
  *  - The first call on a device looks the scratch address up
  *    (cudaGetSymbolAddress, with that device current); make it before any
- *    stream capture begins.
+ *    stream capture begins.  The address is looked up again when the
+ *    device's current context is not the one it was taken in (after
+ *    cudaDeviceReset, for instance), so that first-call rule applies again
+ *    after a context change.
  */
 #define NNB_STATIC_PARTIALS_FLOATS (4 * 1024 * 1024)
 int32_t nnb_conv3d_norm_static(const nnb_conv3d_args* args, const float* gamma, const float* beta,
@@ -277,6 +289,25 @@ int32_t nnb_gather_views(const float* volume, int32_t cin, const int32_t vol_dim
                          const int32_t* flip_masks, float* out, void* stream);
 
 /*
+ * Gather a batch of `items` (1..8) patches of a channel-first (cin, Z, Y, X)
+ * volume into a channels-last (items, P0, P1, P2, cin) batch: item t is the
+ * patch at offsets[3t .. 3t+2] of the volume zero-padded by pad_lo before each
+ * axis (the reference's _pad_minimum, sliding_window.py:542-562; positions
+ * outside the unpadded volume load 0, nothing is materialised), flipped along
+ * the axes whose bits are set in flip_masks[t].  Items may come from different
+ * tiles (a batch of (tile, view) work units).  Every value read is checked:
+ * each thread that read a non-finite value adds 1 to *nonfinite_count (NULL:
+ * no check), the reference's finite-input check (sliding_window.py:463-486)
+ * folded into the read.  Host arrays: offsets (3 x items), flip_masks (items).
+ * Replaces the padding, the tile slicing and `mx.flip` of
+ * src/nnunet_mlx/prediction/sliding_window.py:408-411,517-518,542-562.
+ */
+int32_t nnb_gather_tiles(const float* volume, int32_t cin, const int32_t vol_dims[3],
+                         const int32_t pad_lo[3], int32_t items, const int32_t* offsets,
+                         const int32_t* flip_masks, const int32_t patch[3], float* out,
+                         int32_t* nonfinite_count, void* stream);
+
+/*
  * Fused segmentation head + mirror flip-back + view average + Gaussian-weighted
  * accumulation of one tile: for each tile voxel, logits_v = W . act(x_v[flip_v(p)]) + b
  * for every view in order, pred = (sum_v logits_v) / views, and
@@ -290,6 +321,21 @@ int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const in
                             const float* seg_bias, int32_t classes, const float* gaussian,
                             float* acc, float* normalizer, const int32_t acc_dims[3],
                             const int32_t offset[3], int32_t add_normalizer, void* stream);
+
+/*
+ * nnb_accumulate_tile for some of a tile's views: the `views` given are summed
+ * in order and divided by view_divisor (the tile's full view count, >= views)
+ * before the Gaussian weighting, so calls over disjoint groups of a tile's
+ * views add up to that tile's mirrored prediction (the groups' float32 sums
+ * round separately).  Used when (tile, view) work units are sharded across
+ * GPUs.  Replaces the same reference lines as nnb_accumulate_tile.
+ */
+int32_t nnb_accumulate_views(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                             int32_t view_divisor, const int32_t patch[3], float slope,
+                             const float* seg_weight, const float* seg_bias, int32_t classes,
+                             const float* gaussian, float* acc, float* normalizer,
+                             const int32_t acc_dims[3], const int32_t offset[3],
+                             int32_t add_normalizer, void* stream);
 
 /*
  * nnunet-fp16 accumulation mode (reference sliding_window.py:96-113,415-433,
@@ -366,12 +412,16 @@ int32_t nnb_normalize_labels(const float* acc, const float* normalizer, int32_t 
  * :462-495 (per-axis metadata), its callers :292-334 and :363-401, and the host
  * uncrop + inverse transpose of src/nnunet_mlx/prediction/export.py:363-373.
  * Unlike the Metal kernel (double-single arithmetic, logits limited to
- * FLT_MAX / 16) any finite float32 or half logits are accepted.
+ * FLT_MAX / 16) any finite float32 or half logits are accepted.  Logits must be
+ * finite: corners of interpolation weight exactly 0 (every corner of an axis
+ * that is not resampled) are not read, so a non-finite value there is not
+ * counted in invalid_count, where the host path's sum would turn it into NaN.
  */
 typedef struct nnb_restore_args {
   const void* logits;           /* class logits on the source grid (device)                  */
   int32_t half;                 /* 0: float32 logits, 1: IEEE half logits                    */
-  int32_t classes;              /* 1 .. 65536 (1 .. 255 for 1-byte labels)                  */
+  int32_t classes;              /* 1 .. 65536 (1 .. 255 for 1-byte labels); with 65536 classes
+                                   the invalid label 65535 is also a class: read invalid_count */
   int32_t source_dims[3];       /* source grid (S0, S1, S2)                                  */
   int32_t target_dims[3];       /* resampled grid = crop box extent (T0, T1, T2)             */
   int64_t class_stride;         /* element strides of the logits: class, then axes 0..2      */

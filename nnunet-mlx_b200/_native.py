@@ -16,13 +16,15 @@ from pathlib import Path
 from nnunet_mlx_b200.errors import ContractError
 
 LIB_PATH = Path(__file__).resolve().parent / "_nnb.so"
-ABI_VERSION = 12
+ABI_VERSION = 13
 
 PREC_FP32 = 0        # split fp16 pairs on the tensor cores, float32-level accuracy (|activation| < 65504)
 PREC_TF32 = 1        # single-pass TF32 tensor cores
 PREC_SIMT = 2        # CUDA-core float32
 PREC_FP32_TF32 = 3   # split-TF32 hi/lo tensor cores, float32-level accuracy at any magnitude
 TENSOR_PRECISIONS = (PREC_FP32, PREC_TF32, PREC_FP32_TF32)
+# nnb_conv3d_kernel_mode -> the kernel a convolution launches
+KERNEL_MODES = {0: "conv3d_simt_kernel", 1: "conv3d_tc_kernel", 2: "conv3d_halo_kernel", 3: "conv3d_zstream_kernel"}
 
 STATUS = {0: "ok", -1: "invalid argument", -2: "unsupported", -3: "CUDA error", -4: "device check failed",
           -5: "non-finite"}
@@ -98,6 +100,7 @@ SYMBOLS = {
     "nnb_conv3d_packed_bytes": (ctypes.c_int64, [ctypes.c_int32] * 4),
     "nnb_operand_range_events": (ctypes.c_int64, [ctypes.c_int32]),
     "nnb_conv3d_raw_operands": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs)]),
+    "nnb_conv3d_kernel_mode": (ctypes.c_int32, [ctypes.POINTER(Conv3dArgs)]),
     "nnb_prepare_operand": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_conv3d_pack": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
@@ -120,6 +123,14 @@ SYMBOLS = {
                                            ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
     "nnb_gather_views": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, I32x3, ctypes.c_int32,
                                           ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_gather_tiles": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, ctypes.c_int32,
+                                          ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), I32x3,
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_accumulate_views": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32,
+                                              ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, I32x3, ctypes.c_float,
+                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p, I32x3, I32x3, ctypes.c_int32,
+                                              ctypes.c_void_p]),
     "nnb_accumulate_tile": (ctypes.c_int32, [ctypes.POINTER(Segment), ctypes.c_int32,
                                              ctypes.POINTER(ctypes.c_int32), I32x3, ctypes.c_float,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,

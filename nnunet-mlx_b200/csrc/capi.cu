@@ -27,6 +27,7 @@ int64_t conv3d_tc_packed_bytes(int cout, int kvol, int cin_total, int precision)
 int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int precision, void* packed,
                        cudaStream_t stream);
 int conv3d_tc_partial_tiles(const nnb_conv3d_args& a);
+int conv3d_tc_mode(const nnb_conv3d_args& a);
 int launch_norm_finalize(const float* partials, int batch, int tiles, int channels, const float* gamma,
                          const float* beta, float eps, float* scale, float* shift, cudaStream_t stream);
 int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t in_dims[3], const int32_t k[3],
@@ -44,10 +45,13 @@ int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch
                          float* out, cudaStream_t stream);
 int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const int32_t off[3],
                         const int32_t patch[3], int views, const int32_t* masks, float* out, cudaStream_t stream);
+int launch_gather_tiles(const float* vol, int cin, const int32_t vd[3], const int32_t pad_lo[3], int items,
+                        const int32_t* offsets, const int32_t* masks, const int32_t patch[3], float* out,
+                        int32_t* nonfinite, cudaStream_t stream);
 int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
                            float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
                            void* acc, void* normalizer, int fp16, const int32_t ad[3], const int32_t off[3],
-                           int add_normalizer, cudaStream_t stream);
+                           int add_normalizer, int view_divisor, cudaStream_t stream);
 int launch_fold_add_fp16(const void* acc, const void* normalizer, int classes, const int32_t ad[3],
                          const int32_t lo[3], const int32_t cd[3], void* total, int first, int32_t* invalid_count,
                          cudaStream_t stream);
@@ -161,6 +165,15 @@ int64_t nnb_conv3d_partial_tiles(const nnb_conv3d_args* a) {
   return tiles_per_sample((int64_t)a->out_dims[0] * a->out_dims[1] * a->out_dims[2]);
 }
 
+int32_t nnb_conv3d_kernel_mode(const nnb_conv3d_args* a) {
+  NNB_REQUIRE(a != nullptr, "conv3d_kernel_mode: null args");
+  NNB_REQUIRE(positive3(a->in_dims) && positive3(a->out_dims) && positive3(a->kernel) && positive3(a->stride),
+              "conv3d_kernel_mode: dims, kernel and stride must be positive");
+  if (a->operand_format != 1 && a->operand_format != 2) return 0;
+  NNB_REQUIRE(a->num_segments == 1 || a->num_segments == 2, "conv3d_kernel_mode: 1 or 2 input segments");
+  return conv3d_tc_mode(*a);
+}
+
 int32_t nnb_instance_norm_finalize(const float* partials, int32_t batch, int32_t tiles, int32_t channels,
                                    const float* gamma, const float* beta, float eps, float* scale, float* shift,
                                    void* stream) {
@@ -238,6 +251,18 @@ int32_t nnb_gather_views(const float* volume, int32_t cin, const int32_t vol_dim
   return launch_gather_views(volume, cin, vol_dims, offset, patch, views, flip_masks, out, (cudaStream_t)stream);
 }
 
+int32_t nnb_gather_tiles(const float* volume, int32_t cin, const int32_t vol_dims[3], const int32_t pad_lo[3],
+                         int32_t items, const int32_t* offsets, const int32_t* flip_masks, const int32_t patch[3],
+                         float* out, int32_t* nonfinite_count, void* stream) {
+  NNB_REQUIRE(volume && out && offsets && flip_masks && cin >= 1, "gather_tiles: bad arguments");
+  NNB_REQUIRE(positive3(vol_dims) && positive3(patch), "gather_tiles: dimensions must be positive");
+  for (int i = 0; i < 3; ++i)
+    NNB_REQUIRE(pad_lo[i] >= 0 && pad_lo[i] < patch[i], "gather_tiles: pad_lo[%d] = %d outside [0, patch)", i,
+                pad_lo[i]);
+  return launch_gather_tiles(volume, cin, vol_dims, pad_lo, items, offsets, flip_masks, patch, out, nonfinite_count,
+                             (cudaStream_t)stream);
+}
+
 static int check_accumulate(const nnb_segment* features, const int32_t* flip_masks, const int32_t patch[3],
                             const float* seg_weight, const float* seg_bias, int32_t classes, const float* gaussian,
                             const void* acc, const void* normalizer, const int32_t acc_dims[3],
@@ -262,7 +287,20 @@ int32_t nnb_accumulate_tile(const nnb_segment* features, int32_t views, const in
                             acc_dims, offset, add_normalizer);
   if (rc) return rc;
   return launch_accumulate_tile(*features, views, flip_masks, patch, slope, seg_weight, seg_bias, classes, gaussian,
-                                acc, normalizer, 0, acc_dims, offset, add_normalizer, (cudaStream_t)stream);
+                                acc, normalizer, 0, acc_dims, offset, add_normalizer, views, (cudaStream_t)stream);
+}
+
+int32_t nnb_accumulate_views(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
+                             int32_t view_divisor, const int32_t patch[3], float slope, const float* seg_weight,
+                             const float* seg_bias, int32_t classes, const float* gaussian, float* acc,
+                             float* normalizer, const int32_t acc_dims[3], const int32_t offset[3],
+                             int32_t add_normalizer, void* stream) {
+  int rc = check_accumulate(features, flip_masks, patch, seg_weight, seg_bias, classes, gaussian, acc, normalizer,
+                            acc_dims, offset, add_normalizer);
+  if (rc) return rc;
+  return launch_accumulate_tile(*features, views, flip_masks, patch, slope, seg_weight, seg_bias, classes, gaussian,
+                                acc, normalizer, 0, acc_dims, offset, add_normalizer, view_divisor,
+                                (cudaStream_t)stream);
 }
 
 int32_t nnb_accumulate_tile_fp16(const nnb_segment* features, int32_t views, const int32_t* flip_masks,
@@ -276,7 +314,8 @@ int32_t nnb_accumulate_tile_fp16(const nnb_segment* features, int32_t views, con
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(acc16) & 1) == 0 && (reinterpret_cast<uintptr_t>(normalizer16) & 1) == 0,
               "accumulate_tile_fp16: half buffers must be 2-byte aligned");
   return launch_accumulate_tile(*features, views, flip_masks, patch, slope, seg_weight, seg_bias, classes, gaussian,
-                                acc16, normalizer16, 1, acc_dims, offset, add_normalizer, (cudaStream_t)stream);
+                                acc16, normalizer16, 1, acc_dims, offset, add_normalizer, views,
+                                (cudaStream_t)stream);
 }
 
 int32_t nnb_fold_add_fp16(const void* acc16, const void* normalizer16, int32_t classes, const int32_t acc_dims[3],
@@ -317,7 +356,9 @@ int32_t nnb_restore_class_labels(const nnb_restore_args* a, void* stream) {
   NNB_REQUIRE(a->logits && a->labels && a->invalid_count, "restore_class_labels: null pointer");
   NNB_REQUIRE(a->half == 0 || a->half == 1, "restore_class_labels: half must be 0 or 1");
   NNB_REQUIRE(a->label_bytes == 1 || a->label_bytes == 2, "restore_class_labels: label_bytes must be 1 or 2");
-  NNB_REQUIRE(a->classes >= 1 && a->classes <= (a->label_bytes == 1 ? 256 : 65536),
+  // 1-byte labels keep 255 free for the invalid label; 2-byte labels accept the reference's 65536 classes, where
+  // the invalid label 65535 is also the top class and only invalid_count tells them apart
+  NNB_REQUIRE(a->classes >= 1 && a->classes <= (a->label_bytes == 1 ? 255 : 65536),
               "restore_class_labels: %d classes do not fit %d-byte labels", a->classes, a->label_bytes);
   NNB_REQUIRE(positive3(a->source_dims) && positive3(a->target_dims) && positive3(a->volume_dims),
               "restore_class_labels: dimensions must be positive");

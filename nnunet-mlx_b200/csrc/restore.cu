@@ -293,7 +293,11 @@ __global__ void __launch_bounds__(256) restore_identity_kernel(const In* __restr
 // Resampling grid.  An axis whose upper weight is exactly 0 (every index of an
 // axis that is not resampled) drops out of a voxel's sum: its lower weight is
 // exactly 1 and the dropped corners contribute +-0, so the sum equals the host
-// path's eight-corner sum.  Each of the 8 patterns of active axes has its own
+// path's eight-corner sum for finite logits.  A dropped corner is never read:
+// a non-finite value there (which the host sum would turn into NaN, 0 * inf,
+// and flag invalid) leaves this voxel's label finite and uncounted.  Finite
+// logits are the contract here as in the reference's fused path (reference
+// kernels/metal_restore.py:298-316 validates them before its launch).  Each of the 8 patterns of active axes has its own
 // unrolled code (Z1, Y1, X1), so only the needed corners are loaded and
 // multiplied; within a warp the pattern is nearly always uniform.
 // ---------------------------------------------------------------------------

@@ -1759,6 +1759,12 @@ bool conv3d_tc_raw_operands(const nnb_conv3d_args& a) {
 // Tiles per sample of the partials a tensor-core convolution writes.
 int conv3d_tc_partial_tiles(const nnb_conv3d_args& a) { return tc::make_geometry(a).tps; }
 
+// Kernel a tensor-core convolution launches: 1 box, 2 halo, 3 z-streaming.
+int conv3d_tc_mode(const nnb_conv3d_args& a) {
+  const tc::Geometry g = tc::make_geometry(a);
+  return g.zs ? 3 : g.halo ? 2 : 1;
+}
+
 int launch_conv3d_tc(const nnb_conv3d_args& a, cudaStream_t stream) {
   tc::Geometry g = tc::make_geometry(a);
   if (g.zs) {

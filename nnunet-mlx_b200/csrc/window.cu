@@ -18,51 +18,91 @@ struct Dims3 {
 };
 
 // ---------------------------------------------------------------------------
-// (cin, Z, Y, X) volume tile at `off` -> (views, P0, P1, P2, cin) channels-last,
-// view v flipped along axis a when bit a of mask[v] is set.
+// Tile gather: item t of the batch is the patch at offset off[t] (coordinates
+// of the zero-padded volume) of a (cin, Z, Y, X) volume, flipped along axis a
+// when bit a of mask[t] is set, written channels-last (items, P0, P1, P2, cin).
+// The volume is read unpadded: padded coordinate c maps to c - pad_lo, and
+// positions outside the volume load 0 (the reference's _pad_minimum zeros).
+// Every loaded value is checked for finiteness (the reference validates the
+// input before inference, sliding_window.py:463-486): each thread that met a
+// non-finite value adds 1 to *nonfinite.
 // Reference: tile slice + mx.flip (sliding_window.py:408-411,517-518).
 // ---------------------------------------------------------------------------
-// Up to 8 views (every subset of 3 mirroring axes); masks carried by value.
+// Up to 8 items (every subset of 3 mirroring axes, or tiles mixed in a batch); carried by value.
 struct ViewMasks {
   int m[8];
 };
 
-__global__ void gather_views8_kernel(const float* __restrict__ vol, int cin, Dims3 vd, Dims3 off, Dims3 patch,
-                                     int views, ViewMasks masks, float* __restrict__ out) {
+struct ItemTable {
+  int off[8][3];
+  int mask[8];
+};
+
+__global__ void gather_tiles_kernel(const float* __restrict__ vol, int cin, Dims3 vd, Dims3 pad_lo, Dims3 patch,
+                                    int items, ItemTable tab, float* __restrict__ out, int* __restrict__ nonfinite) {
   const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
-  const int64_t total = pvox * views;
+  const int64_t total = pvox * items;
   const int64_t vstride = (int64_t)vd.d[0] * vd.d[1] * vd.d[2];
+  bool bad = false;
   for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
        o += (int64_t)gridDim.x * blockDim.x) {
-    const int v = (int)(o / pvox);
-    const int64_t p = o - (int64_t)v * pvox;
+    const int t = (int)(o / pvox);
+    const int64_t p = o - (int64_t)t * pvox;
     const int k = (int)(p % patch.d[2]);
     const int j = (int)((p / patch.d[2]) % patch.d[1]);
     const int i = (int)(p / ((int64_t)patch.d[2] * patch.d[1]));
-    const int mask = masks.m[v];
-    const int si = (mask & 1) ? patch.d[0] - 1 - i : i;
-    const int sj = (mask & 2) ? patch.d[1] - 1 - j : j;
-    const int sk = (mask & 4) ? patch.d[2] - 1 - k : k;
-    const int64_t src = ((int64_t)(off.d[0] + si) * vd.d[1] + (off.d[1] + sj)) * vd.d[2] + (off.d[2] + sk);
+    const int mask = tab.mask[t];
+    const int z = tab.off[t][0] + ((mask & 1) ? patch.d[0] - 1 - i : i) - pad_lo.d[0];
+    const int y = tab.off[t][1] + ((mask & 2) ? patch.d[1] - 1 - j : j) - pad_lo.d[1];
+    const int x = tab.off[t][2] + ((mask & 4) ? patch.d[2] - 1 - k : k) - pad_lo.d[2];
     float* dst = out + o * cin;
-    for (int c = 0; c < cin; ++c) dst[c] = __ldg(vol + (int64_t)c * vstride + src);
+    if ((unsigned)z >= (unsigned)vd.d[0] || (unsigned)y >= (unsigned)vd.d[1] || (unsigned)x >= (unsigned)vd.d[2]) {
+      for (int c = 0; c < cin; ++c) dst[c] = 0.f;
+      continue;
+    }
+    const int64_t src = ((int64_t)z * vd.d[1] + y) * vd.d[2] + x;
+    for (int c = 0; c < cin; ++c) {
+      const float v = __ldg(vol + (int64_t)c * vstride + src);
+      bad |= !isfinite(v);
+      dst[c] = v;
+    }
   }
+  if (bad && nonfinite != nullptr) atomicAdd(nonfinite, 1);
+}
+
+int launch_gather_tiles(const float* vol, int cin, const int32_t vd[3], const int32_t pad_lo[3], int items,
+                        const int32_t* offsets, const int32_t* masks, const int32_t patch[3], float* out,
+                        int32_t* nonfinite, cudaStream_t stream) {
+  NNB_REQUIRE(items >= 1 && items <= 8, "gather_tiles: 1..8 items per batch, got %d", items);
+  ItemTable tab{};
+  for (int t = 0; t < items; ++t) {
+    NNB_REQUIRE(masks[t] >= 0 && masks[t] < 8, "gather_tiles: bad flip mask");
+    tab.mask[t] = masks[t];
+    for (int a = 0; a < 3; ++a) {
+      // the patch must lie inside the padded extent [0, pad_lo + vd + pad_lo + 1)
+      NNB_REQUIRE(offsets[3 * t + a] >= 0 && offsets[3 * t + a] + patch[a] <= vd[a] + 2 * pad_lo[a] + 1,
+                  "gather_tiles: item %d lies outside the padded volume on axis %d", t, a);
+      tab.off[t][a] = offsets[3 * t + a];
+    }
+  }
+  Dims3 dvd{{vd[0], vd[1], vd[2]}}, dpad{{pad_lo[0], pad_lo[1], pad_lo[2]}}, dp{{patch[0], patch[1], patch[2]}};
+  const int64_t total = (int64_t)patch[0] * patch[1] * patch[2] * items;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  gather_tiles_kernel<<<blocks, 256, 0, stream>>>(vol, cin, dvd, dpad, dp, items, tab, out, nonfinite);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
 }
 
 int launch_gather_views(const float* vol, int cin, const int32_t vd[3], const int32_t off[3],
                         const int32_t patch[3], int views, const int32_t* masks, float* out, cudaStream_t stream) {
   NNB_REQUIRE(views >= 1 && views <= 8, "gather_views: 1..8 views supported, got %d", views);
-  ViewMasks vm{};
-  for (int v = 0; v < views; ++v) {
-    NNB_REQUIRE(masks[v] >= 0 && masks[v] < 8, "gather_views: bad flip mask");
-    vm.m[v] = masks[v];
-  }
-  Dims3 dvd{{vd[0], vd[1], vd[2]}}, doff{{off[0], off[1], off[2]}}, dp{{patch[0], patch[1], patch[2]}};
-  const int64_t total = (int64_t)patch[0] * patch[1] * patch[2] * views;
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
-  gather_views8_kernel<<<blocks, 256, 0, stream>>>(vol, cin, dvd, doff, dp, views, vm, out);
-  NNB_LAUNCH_CHECK();
-  return NNB_OK;
+  for (int a = 0; a < 3; ++a)
+    NNB_REQUIRE(off[a] >= 0 && off[a] + patch[a] <= vd[a], "gather_views: tile outside the volume on axis %d", a);
+  int32_t offsets[24];
+  for (int v = 0; v < views; ++v)
+    for (int a = 0; a < 3; ++a) offsets[3 * v + a] = off[a];
+  const int32_t zero[3] = {0, 0, 0};
+  return launch_gather_tiles(vol, cin, vd, zero, views, offsets, masks, patch, out, nullptr, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -87,7 +127,7 @@ template <int FV, typename AccT>  // FV = F / 4 (float4 chunks), compile-time fo
 __global__ void __launch_bounds__(256) accumulate_tile_vec_kernel(
     nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
     const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, AccT* __restrict__ acc,
-    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer, float view_div) {
   constexpr int F = FV * 4;
   __shared__ float s_sc[8][F];
   __shared__ float s_sh[8][F];
@@ -101,7 +141,6 @@ __global__ void __launch_bounds__(256) accumulate_tile_vec_kernel(
     s_sh[v][f] = feat.scale ? feat.shift[v * F + f] : 0.f;
   }
   const bool lazy = feat.scale != nullptr;
-  const float inv_views = 1.0f / (float)views;
   const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
   for (int c0 = 0; c0 < classes; c0 += kAccMaxC) {
     const int nc = min(kAccMaxC, classes - c0);
@@ -153,7 +192,7 @@ __global__ void __launch_bounds__(256) accumulate_tile_vec_kernel(
       AccT* a = acc + dst * classes + c0;
 #pragma unroll
       for (int c = 0; c < kAccMaxC; ++c)
-        if (c < nc) acc_add(a + c, (pred[c] * inv_views) * g);
+        if (c < nc) acc_add(a + c, (pred[c] / view_div) * g);
       if (add_normalizer && c0 == 0) acc_add(normalizer + dst, g);
     }
   }
@@ -163,10 +202,9 @@ template <int CC, typename AccT>
 __global__ void __launch_bounds__(256) accumulate_tile_kernel(
     nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
     const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, AccT* __restrict__ acc,
-    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer, float view_div) {
   const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
   const int F = feat.channels;
-  const float inv_views = 1.0f / (float)views;
   for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pvox;
        p += (int64_t)gridDim.x * blockDim.x) {
     const int k = (int)(p % patch.d[2]);
@@ -200,7 +238,7 @@ __global__ void __launch_bounds__(256) accumulate_tile_kernel(
       }
 #pragma unroll
       for (int c = 0; c < CC; ++c)
-        if (c0 + c < classes) acc_add(acc + dst * classes + c0 + c, (pred[c] * inv_views) * g);
+        if (c0 + c < classes) acc_add(acc + dst * classes + c0 + c, (pred[c] / view_div) * g);
     }
     if (add_normalizer) acc_add(normalizer + dst, g);
   }
@@ -224,7 +262,7 @@ template <typename AccT>
 __global__ void __launch_bounds__(kRowMax) accumulate_tile_rows_kernel(
     nnb_segment feat, int views, ViewMasks masks, Dims3 patch, float slope, const float* __restrict__ seg_w,
     const float* __restrict__ seg_b, int classes, const float* __restrict__ gauss, AccT* __restrict__ acc,
-    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer) {
+    AccT* __restrict__ normalizer, Dims3 ad, Dims3 off, int add_normalizer, float view_div) {
   constexpr int F = 32;
   __shared__ float4 rows[2][kRowMax * 8];
   __shared__ float s_sc[8][F], s_sh[8][F];
@@ -301,12 +339,11 @@ __global__ void __launch_bounds__(kRowMax) accumulate_tile_rows_kernel(
   if (k >= PX) return;
   const int64_t p = ((int64_t)i * patch.d[1] + j) * PX + k;
   const float g = __ldg(gauss + p);
-  const float inv_views = 1.0f / (float)views;
   const int64_t dst = ((int64_t)(off.d[0] + i) * ad.d[1] + (off.d[1] + j)) * ad.d[2] + (off.d[2] + k);
   AccT* a = acc + dst * classes;
 #pragma unroll
   for (int c = 0; c < kAccMaxC; ++c)
-    if (c < classes) acc_add(a + c, (pred[c] * inv_views) * g);
+    if (c < classes) acc_add(a + c, (pred[c] / view_div) * g);
   if (add_normalizer) acc_add(normalizer + dst, g);
 }
 
@@ -314,8 +351,13 @@ template <typename AccT>
 int launch_accumulate_tile_t(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
                              float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
                              AccT* acc, AccT* normalizer, const int32_t ad[3], const int32_t off[3],
-                             int add_normalizer, cudaStream_t stream) {
+                             int add_normalizer, int view_divisor, cudaStream_t stream) {
   NNB_REQUIRE(views >= 1 && views <= 8, "accumulate_tile: 1..8 views supported");
+  NNB_REQUIRE(view_divisor >= views && view_divisor <= 8, "accumulate_tile: view_divisor %d outside [views, 8]",
+              view_divisor);
+  // the view mean divides the view sum by the tile's full view count (reference sliding_window.py:527), also
+  // when this call adds only some of the tile's views (a batch mixing tiles)
+  const float view_div = (float)view_divisor;
   ViewMasks vm{};
   for (int v = 0; v < views; ++v) vm.m[v] = masks[v];
   Dims3 dp{{patch[0], patch[1], patch[2]}}, dad{{ad[0], ad[1], ad[2]}}, doff{{off[0], off[1], off[2]}};
@@ -325,14 +367,16 @@ int launch_accumulate_tile_t(const nnb_segment& feat, int views, const int32_t* 
   if (aligned && feat.channels == 32 && patch[2] <= kRowMax && classes <= kAccMaxC &&
       (int64_t)patch[0] * patch[1] < (1LL << 31)) {
     accumulate_tile_rows_kernel<AccT><<<(unsigned)((int64_t)patch[0] * patch[1]), kRowMax, 0, stream>>>(
-        feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss, acc, normalizer, dad, doff, add_normalizer);
+        feat, views, vm, dp, slope, seg_w, seg_b, classes, gauss, acc, normalizer, dad, doff, add_normalizer,
+        view_div);
   } else if (aligned && feat.channels == 32) {
     accumulate_tile_vec_kernel<8, AccT><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b,
                                                                     classes, gauss, acc, normalizer, dad, doff,
-                                                                    add_normalizer);
+                                                                    add_normalizer, view_div);
   } else {
     accumulate_tile_kernel<4, AccT><<<blocks, 256, 0, stream>>>(feat, views, vm, dp, slope, seg_w, seg_b, classes,
-                                                                gauss, acc, normalizer, dad, doff, add_normalizer);
+                                                                gauss, acc, normalizer, dad, doff, add_normalizer,
+                                                                view_div);
   }
   NNB_LAUNCH_CHECK();
   return NNB_OK;
@@ -341,14 +385,14 @@ int launch_accumulate_tile_t(const nnb_segment& feat, int views, const int32_t* 
 int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* masks, const int32_t patch[3],
                            float slope, const float* seg_w, const float* seg_b, int classes, const float* gauss,
                            void* acc, void* normalizer, int fp16, const int32_t ad[3], const int32_t off[3],
-                           int add_normalizer, cudaStream_t stream) {
+                           int add_normalizer, int view_divisor, cudaStream_t stream) {
   if (fp16)
     return launch_accumulate_tile_t<__half>(feat, views, masks, patch, slope, seg_w, seg_b, classes, gauss,
                                             static_cast<__half*>(acc), static_cast<__half*>(normalizer), ad, off,
-                                            add_normalizer, stream);
+                                            add_normalizer, view_divisor, stream);
   return launch_accumulate_tile_t<float>(feat, views, masks, patch, slope, seg_w, seg_b, classes, gauss,
                                          static_cast<float*>(acc), static_cast<float*>(normalizer), ad, off,
-                                         add_normalizer, stream);
+                                         add_normalizer, view_divisor, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -337,10 +337,19 @@ def conv3d(inputs: list[Lazy], weight: torch.Tensor, *, kernel, stride, pad, cou
                           4.0 * (out.numel() + sum(item.raw.numel() for item in inputs)),
                           detail=lambda: (f"{batch}x{'x'.join(map(str, in_dims))} "
                                           f"{'+'.join(str(i.channels) for i in inputs)}->{cout} "
-                                          f"k{'x'.join(map(str, kernel))} s{'x'.join(map(str, stride))}"))
+                                          f"k{'x'.join(map(str, kernel))} s{'x'.join(map(str, stride))} "
+                                          f"{conv3d_kernel_name(args)}"))
     _native.check(_native.load().nnb_conv3d(ctypes.byref(args), _stream()), "conv3d")
     PROFILE.stop(token)
     return out, partials
+
+
+def conv3d_kernel_name(args) -> str:
+    """Name of the kernel ``nnb_conv3d`` launches for ``args`` (box, halo, z-streaming or CUDA-core)."""
+    mode = int(_native.load().nnb_conv3d_kernel_mode(ctypes.byref(args)))
+    if mode < 0:
+        _native.check(mode, "conv3d_kernel_mode")
+    return _native.KERNEL_MODES[mode]
 
 
 def instance_norm_finalize(partials: torch.Tensor, gamma: torch.Tensor | None, beta: torch.Tensor | None,
@@ -514,14 +523,55 @@ def gather_views(volume: torch.Tensor, offset, patch, masks: list[int], out: tor
     return out
 
 
+def gather_tiles(volume: torch.Tensor, pad_lo, items, patch, out: torch.Tensor | None = None,
+                 nonfinite: torch.Tensor | None = None):
+    """Batch of ``(offset, flip_mask)`` items of a ``(C, Z, Y, X)`` volume -> ``(items, *patch, C)`` channels-last.
+
+    Offsets are coordinates of the volume zero-padded by ``pad_lo`` before each
+    axis; the padding is never materialised (zeros are loaded outside the
+    volume).  ``nonfinite``: a one-element int32 device counter that every
+    thread meeting a non-finite value increments (``None``: no check).
+    """
+    _check_tensor(volume, "volume")
+    cin = int(volume.shape[0])
+    n = len(items)
+    if out is None or int(out.shape[0]) != n:
+        out = torch.empty((n, *patch, cin), dtype=torch.float32, device=volume.device)
+    offsets = (ctypes.c_int32 * (3 * n))(*(int(v) for off, _ in items for v in off))
+    masks = (ctypes.c_int32 * n)(*(int(m) for _, m in items))
+    if nonfinite is not None and (nonfinite.dtype != torch.int32 or not nonfinite.is_cuda):
+        raise ContractError("nonfinite must be an int32 CUDA tensor")
+    token = PROFILE.start("gather_views", 0.0, 8.0 * out.numel())
+    _native.check(_native.load().nnb_gather_tiles(
+        volume.data_ptr(), cin, _native.dims3(volume.shape[1:]), _native.dims3(pad_lo), n, offsets, masks,
+        _native.dims3(patch), out.data_ptr(), _ptr(nonfinite), _stream()), "gather_tiles")
+    PROFILE.stop(token)
+    return out
+
+
+def lazy_items(features: Lazy, lo: int, hi: int) -> Lazy:
+    """Batch items ``[lo, hi)`` of a lazy activation (their raw values and per-sample affine)."""
+    if lo == 0 and hi == int(features.raw.shape[0]):
+        return features
+    if features.scale is None:
+        return Lazy(features.raw[lo:hi])
+    return Lazy(features.raw[lo:hi], features.scale[lo:hi], features.shift[lo:hi], features.leaky)
+
+
 def accumulate_tile(features: Lazy, masks: list[int], seg_weight: torch.Tensor, seg_bias: torch.Tensor,
                     gaussian: torch.Tensor, acc: torch.Tensor, normalizer: torch.Tensor, offset,
-                    add_normalizer: bool, slope: float) -> None:
+                    add_normalizer: bool, slope: float, view_divisor: int | None = None) -> None:
     """Fused seg head + flip-back + view mean + Gaussian-weighted add of one tile.
 
     ``acc`` / ``normalizer`` are float32, or float16 for the nnunet-fp16 mode
-    (half window updates rounded to nearest even).
+    (half window updates rounded to nearest even).  ``view_divisor``: the
+    tile's full view count when ``features`` holds only some of its views
+    (float32 accumulation; default: ``len(masks)``).
     """
+    if view_divisor is not None and view_divisor != len(masks):
+        _accumulate_views(features, masks, view_divisor, seg_weight, seg_bias, gaussian, acc, normalizer, offset,
+                          add_normalizer, slope)
+        return
     seg = features.segment()
     mask_arr = (ctypes.c_int32 * len(masks))(*masks)
     half = acc.dtype == torch.float16
@@ -539,6 +589,25 @@ def accumulate_tile(features: Lazy, masks: list[int], seg_weight: torch.Tensor, 
         seg_weight.data_ptr(), seg_bias.data_ptr(), classes, gaussian.data_ptr(),
         acc.data_ptr(), normalizer.data_ptr(), _native.dims3(acc.shape[:3]), _native.dims3(offset),
         1 if add_normalizer else 0, _stream()), "accumulate_tile")
+    PROFILE.stop(token)
+
+
+def _accumulate_views(features: Lazy, masks: list[int], view_divisor: int, seg_weight, seg_bias, gaussian, acc,
+                      normalizer, offset, add_normalizer: bool, slope: float) -> None:
+    seg = features.segment()
+    mask_arr = (ctypes.c_int32 * len(masks))(*masks)
+    if acc.dtype != torch.float32 or not acc.is_contiguous() or not normalizer.is_contiguous():
+        raise ContractError("a partial-view accumulation needs contiguous float32 accumulators")
+    _check_tensor(gaussian, "gaussian")
+    classes = int(seg_weight.shape[0])
+    pvox = math.prod(features.spatial)
+    token = PROFILE.start("accumulate_tile", 2.0 * features.raw.numel() * classes,
+                          4.0 * features.raw.numel() + pvox * (2 * classes + 2) * 4.0 + 4.0 * pvox)
+    _native.check(_native.load().nnb_accumulate_views(
+        ctypes.byref(seg), len(masks), mask_arr, int(view_divisor), _native.dims3(features.spatial), float(slope),
+        seg_weight.data_ptr(), seg_bias.data_ptr(), classes, gaussian.data_ptr(), acc.data_ptr(),
+        normalizer.data_ptr(), _native.dims3(acc.shape[:3]), _native.dims3(offset), 1 if add_normalizer else 0,
+        _stream()), "accumulate_views")
     PROFILE.stop(token)
 
 

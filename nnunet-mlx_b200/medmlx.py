@@ -6,9 +6,11 @@ Same entry-point names and core arguments as reference
 float32 arrays or ``.npy`` / ``.npz`` files (NIfTI reading, preprocessing and
 grid restoration are outside this package); outputs are written by
 ``ModelFolderPredictor.predict_case``.  ``precision`` selects the convolution
-arithmetic: ``"fp32"`` (default, float32-accurate split-TF32 tensor cores) or
-``"tf32"`` (single-pass, faster, looser).  The reference's ``"native"`` maps
-to ``"fp32"``.
+arithmetic: ``"fp32"`` (default: fp16 hi/lo operand pairs on the tensor cores,
+three products and float32 accumulation, float32-level accuracy; volumes whose
+activations leave the fp16 range are recomputed in split TF32) or ``"tf32"``
+(single-pass, faster, looser).  The reference's ``"native"`` maps to
+``"fp32"``.
 """
 
 from __future__ import annotations

@@ -150,10 +150,8 @@ def _to_device_volume(data, device) -> torch.Tensor:
         volume = torch.from_numpy(np.ascontiguousarray(array))
     if volume.dtype != torch.float32:
         raise ContractError("expected finite float32 (C, *spatial) input")
-    volume = volume.to(device, non_blocking=True).contiguous()
-    if not bool(torch.isfinite(volume).all()):
-        raise ContractError("expected finite float32 (C, *spatial) input")
-    return volume
+    # finiteness is checked by the tile gather as it reads the volume (one count per volume)
+    return volume.to(device, non_blocking=True).contiguous()
 
 
 def tile_offsets(spatial, patch, step_fraction: float) -> list[tuple[int, int, int]]:
@@ -173,10 +171,17 @@ class VolumeAccumulator:
 
 
 def run_tiles(models, volume: torch.Tensor, acc: VolumeAccumulator, offsets, patch, masks,
-              batch_buffer: torch.Tensor | None = None) -> None:
-    """Run every fold on every tile in ``offsets`` and accumulate (the hot loop)."""
+              batch_buffer: torch.Tensor | None = None, pad_lo=(0, 0, 0),
+              nonfinite: torch.Tensor | None = None) -> None:
+    """Run every fold on every tile in ``offsets`` and accumulate (the hot loop).
+
+    ``offsets`` are coordinates of ``volume`` zero-padded by ``pad_lo`` (read
+    unpadded by the gather); ``nonfinite`` counts non-finite input values.
+    """
     for offset in offsets:
-        batch = kernels.gather_views(volume, offset, patch, masks, out=batch_buffer)
+        batch = kernels.gather_tiles(volume, pad_lo, [(offset, m) for m in masks], patch, out=batch_buffer,
+                                     nonfinite=nonfinite)
+        batch_buffer = batch
         for index, model in enumerate(models):
             features = model.forward_features(batch)
             kernels.accumulate_tile(features, masks, model.seg_weight, model.seg_bias, acc.gaussian, acc.acc,
@@ -185,18 +190,21 @@ def run_tiles(models, volume: torch.Tensor, acc: VolumeAccumulator, offsets, pat
             del features
 
 
-def range_guarded(models, run):
+def range_guarded(models, run, nonfinite: torch.Tensor | None = None):
     """``run(models)``, recomputed with the split-TF32 twins when an fp16-pair operand was out of range.
 
     Networks in the default ``fp32`` precision compute with fp16 hi/lo operand
     pairs, exact to float32 level while every activation stays below 65504 in
     magnitude; the operand preparation counts the elements that do not.  The
-    count is read once per volume (one device synchronisation).
+    count is read once per volume (one device synchronisation), after the
+    gather's count of non-finite input values (``nonfinite``), which raises.
     """
     guarded = any(getattr(m, "range_guarded", False) for m in models)
     if guarded:
         kernels.operand_range_events(reset=True)
     result = run(models)
+    if nonfinite is not None and int(nonfinite.item()) != 0:
+        raise ContractError("expected finite float32 (C, *spatial) input")
     if guarded and kernels.operand_range_events(reset=True) > 0:
         result = run([m.range_fallback() for m in models])
     return result
@@ -217,35 +225,34 @@ def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes
     patch, axes = validate_request(shape, None, patch_size, num_classes, mirroring_axes)
     device = torch.device(device) if device is not None else models[0].device
     volume = _to_device_volume(data, device)
+    # axes shorter than the patch are zero-padded virtually: the gather reads the unpadded volume
     pads, crop = pad_minimum(shape[1:], patch)
-    if any(p != (0, 0) for p in pads):
-        padded = torch.zeros((shape[0], *(s + a + b for s, (a, b) in zip(shape[1:], pads))),
-                             dtype=torch.float32, device=device)
-        padded[(slice(None), *crop)] = volume
-        volume = padded
-    spatial = tuple(volume.shape[1:])
+    pad_lo = tuple(a for a, _ in pads)
+    spatial = tuple(s + a + b for s, (a, b) in zip(shape[1:], pads))
     masks = mirror_masks(axes)
     lo = [c.start for c in crop]
     dims = [c.stop - c.start for c in crop]
+    nonfinite = torch.zeros((1,), dtype=torch.int32, device=device)
     if accumulation == "nnunet-fp16":
         return range_guarded(models, lambda ms: _predict_volume_fp16(
             ms, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims, want_logits, label_dtype,
-            half_logits))
+            half_logits, pad_lo, nonfinite), nonfinite)
 
     def run(ms):
         accumulator = VolumeAccumulator(spatial, num_classes, patch, device)
-        run_tiles(ms, volume, accumulator, tile_offsets(spatial, patch, step_fraction), patch, masks)
+        run_tiles(ms, volume, accumulator, tile_offsets(spatial, patch, step_fraction), patch, masks,
+                  pad_lo=pad_lo, nonfinite=nonfinite)
         return kernels.normalize_labels(accumulator.acc, accumulator.normalizer, lo, dims,
                                         fold_divisor=float(len(ms)), want_logits=want_logits, label_dtype=label_dtype)
 
-    logits, labels, invalid = range_guarded(models, run)
+    logits, labels, invalid = range_guarded(models, run, nonfinite)
     if int(invalid.item()) != 0:
         raise ContractError("sliding-window inference produced non-finite logits")
     return logits, labels
 
 
 def _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims, want_logits,
-                         label_dtype, half_logits):
+                         label_dtype, half_logits, pad_lo=(0, 0, 0), nonfinite=None):
     """nnunet-fp16: per fold a float16 window + normaliser, normalised to float16 and summed in fold order."""
     device = volume.device
     gaussian = torch.from_numpy(nnunet_fp16_gaussian(tuple(patch)).astype(np.float32)).to(device)
@@ -259,12 +266,15 @@ def _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, ste
         acc.zero_()
         normalizer.zero_()
         for offset in offsets:
-            batch = kernels.gather_views(volume, offset, patch, masks, out=batch)
+            batch = kernels.gather_tiles(volume, pad_lo, [(offset, m) for m in masks], patch, out=batch,
+                                         nonfinite=nonfinite if index == 0 else None)
             features = model.forward_features(batch)
             kernels.accumulate_tile(features, masks, model.seg_weight, model.seg_bias, gaussian, acc, normalizer,
                                     offset, add_normalizer=True, slope=model.spec.leaky_slope)
             del features
         kernels.fold_add_fp16(acc, normalizer, lo, dims, total, index == 0, invalid)
+    if nonfinite is not None and int(nonfinite.item()) != 0:
+        raise ContractError("expected finite float32 (C, *spatial) input")
     if int(invalid.item()) != 0:
         raise ContractError("sliding-window inference produced non-finite logits")
     logits, labels, invalid = kernels.fold_finalize_fp16(total, len(models), want_logits=want_logits and not half_logits,

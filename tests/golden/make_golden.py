@@ -479,4 +479,6 @@ def _record_reference_preprocessing(reference: Path, *, recorded_plans: dict) ->
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path of the nnunet-mlx checkout>")
+    main(Path(sys.argv[1]))

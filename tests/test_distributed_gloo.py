@@ -11,16 +11,50 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from nnunet_mlx_b200.distributed import exchange_slabs, shard_units, slab_bounds
+from nnunet_mlx_b200.distributed import (
+    exchange_slabs,
+    padded_depth,
+    shard_units,
+    slab_bounds,
+    tile_groups,
+    unit_batches,
+)
 
 
-@pytest.mark.parametrize("tiles,folds,world", [(121, 1, 8), (18, 5, 8), (144, 5, 3), (3, 1, 8), (7, 2, 2)])
-def test_shard_units_cover_every_unit_once_in_order(tiles, folds, world):
-    shards = [shard_units(tiles, folds, r, world) for r in range(world)]
+@pytest.mark.parametrize("tiles,folds,views,world", [(121, 1, 8, 8), (18, 5, 8, 8), (144, 5, 8, 3), (3, 1, 8, 8),
+                                                     (7, 2, 4, 2), (5, 3, 1, 4)])
+def test_shard_units_cover_every_unit_once_in_order(tiles, folds, views, world):
+    shards = [shard_units(tiles, folds, r, world, views) for r in range(world)]
     flat = [u for shard in shards for u in shard]
-    assert flat == [(t, f) for t in range(tiles) for f in range(folds)]
+    assert flat == [(f, t, v) for f in range(folds) for t in range(tiles) for v in range(views)]
     sizes = [len(s) for s in shards]
     assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("tiles,views,world", [(121, 8, 8), (121, 8, 2), (18, 8, 3), (9, 4, 4)])
+def test_unit_batches_fill_the_network_batch(tiles, views, world):
+    """Every rank runs ceil(units / 8) forwards per fold run; each tile's views are accumulated exactly once."""
+    seen = {}
+    for rank in range(world):
+        units = shard_units(tiles, 1, rank, world, views)
+        batches = unit_batches(units)
+        assert len(batches) == -(-len(units) // 8)
+        assert all(1 <= len(items) <= 8 for _, items in batches)
+        for _, items in batches:
+            groups = tile_groups(items)
+            assert [i for t, lo, hi in groups for i in range(lo, hi)] == list(range(len(items)))
+            for tile, lo, hi in groups:
+                assert all(items[i][0] == tile for i in range(lo, hi))
+                for _, v in items[lo:hi]:
+                    seen.setdefault(tile, []).append(v)
+    assert seen == {t: list(range(views)) for t in range(tiles)}
+
+
+def test_unit_batches_never_mix_folds():
+    units = shard_units(3, 2, 0, 1, 3)
+    for fold, items in unit_batches(units):
+        assert all((fold, t, v) in units for t, v in items)
+    assert [f for f, _ in unit_batches(units)] == [0, 0, 1, 1]
 
 
 @pytest.mark.parametrize("depth,world", [(128, 8), (101, 8), (5, 2), (1, 2), (284, 3)])
@@ -42,7 +76,13 @@ def _exchange_worker(rank: int, world: int, port: int, shape, classes: int) -> N
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         acc, norm = _rank_accumulator(rank, shape, classes)
-        z_lo, z_hi, acc_slab, norm_slab = exchange_slabs(acc, norm)
+        # the accumulator's depth is padded to a multiple of the world size; padding planes hold junk here
+        depth = padded_depth(shape[0], world)
+        acc_p = torch.full((depth, *shape[1:], classes), 7.0)
+        norm_p = torch.full((depth, *shape[1:]), 7.0)
+        acc_p[: shape[0]] = acc
+        norm_p[: shape[0]] = norm
+        z_lo, z_hi, acc_slab, norm_slab = exchange_slabs(acc_p, norm_p, shape[0])
         assert (z_lo, z_hi) == slab_bounds(shape[0], rank, world)
         total_acc = sum(_rank_accumulator(r, shape, classes)[0] for r in range(world))
         total_norm = sum(_rank_accumulator(r, shape, classes)[1] for r in range(world))

@@ -167,3 +167,30 @@ def test_larger_grids(cuda_device, dtype):
     slab = _logits(3, (8, 768, 768), dtype, 8)
     labels = restore.restore_labels_on_device(_device(slab, cuda_device), (8, 768, 768), class_axis=0)
     np.testing.assert_array_equal(kernels.to_host(labels), orestore.first_argmax(slab))
+
+
+
+def test_zero_weight_corner_is_not_read(cuda_device):
+    """A corner of interpolation weight exactly 0 is skipped, so a non-finite value there is not seen.
+
+    Only z is resampled (y and x keep their size: every upper weight there is
+    exactly 0).  The inf at x = 5 is the zero-weight upper x corner of the
+    voxels at x = 4, which keep the label of the finite data and are not
+    counted invalid (the host sum would give NaN there); the voxels at x = 5
+    read it with a nonzero weight and are counted.  The contract is finite
+    logits, which the host entry point checks before the launch.
+    """
+    values = _logits(3, (4, 5, 6), np.float32, 21)
+    finite = values.copy()
+    values[1, 2, 3, 5] = np.inf
+    target = (7, 5, 6)
+    labels, invalid = kernels.restore_class_labels(_device(values, cuda_device), target, class_axis=0)
+    got = kernels.to_host(labels).astype(np.uint16)
+    expected = orestore.restore_labels(finite, target)
+    mask = np.ones(target, dtype=bool)
+    mask[:, 3, 5] = False
+    np.testing.assert_array_equal(got[mask], expected[mask])
+    hit = int((got[:, 3, 5] == 65535).sum())
+    assert hit > 0 and int(invalid.item()) == hit
+    with pytest.raises(ContractError):
+        restore.resample_class_logits_argmax_device(values, target)
