@@ -51,14 +51,16 @@ DOMINANT_TRAFFIC = {
 
 
 # tensor products per useful product of each precision, relative to the dense bf16 rate
-MODE_PRODUCTS = {"fp32": 3.0, "fp32-tf32x2": 8.0, "tf32": 2.0}
+MODE_PRODUCTS = {"fp32": 3.0, "fp32-tf32x2": 8.0, "tf32": 2.0, "bf16": 1.0}
 DTYPES = {"fp32": "fp32 (fp16-pair tensor-core products, fp32 accumulation)",
-          "fp32-tf32x2": "fp32 (split-TF32 tensor cores)", "tf32": "tf32"}
+          "fp32-tf32x2": "fp32 (split-TF32 tensor cores)", "tf32": "tf32",
+          "bf16": "bf16 inputs, fp32 accumulation"}
 MODE_NOTES = {
     "fp32": "fp32 mode computes fp16 operand pairs: per 16-channel sub-step A_hi x W0, A_hi x W1 and A_lo x W0 "
             "(3 tensor products per useful product at the bf16/fp16 rate), so its arithmetic ceiling is peak/3",
     "fp32-tf32x2": "split TF32: 4 products at half the bf16 rate, ceiling peak/8",
     "tf32": "single-pass TF32: one product at half the bf16 rate, ceiling peak/2",
+    "bf16": "bf16 operands, float32 accumulation: one product per useful product, ceiling = the dense bf16 peak",
 }
 
 
@@ -69,7 +71,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--config", type=int, default=2, help="benchmark config number (2, 3, 4 or 5)")
-    p.add_argument("--precision", choices=["fp32", "fp32-tf32x2", "tf32"], default="fp32")
+    p.add_argument("--precision", choices=["fp32", "fp32-tf32x2", "tf32", "bf16"], default="fp32")
     p.add_argument("--e2e-steps", type=int, default=None, help="end-to-end steps (default: --steps)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-check", action="store_true", help="skip the sharded-vs-single-device slab check")

@@ -48,8 +48,11 @@ enum nnb_precision {
                              (out-of-range values are counted, see nnb_operand_range_events) */
   NNB_PREC_TF32 = 1,      /* single-pass TF32 tensor cores (fast, looser bound)     */
   NNB_PREC_SIMT = 2,      /* plain float32 FMA on CUDA cores (any shape)            */
-  NNB_PREC_FP32_TF32 = 3  /* split TF32 (hi/lo products): float32-level accuracy at any
+  NNB_PREC_FP32_TF32 = 3, /* split TF32 (hi/lo products): float32-level accuracy at any
                              float32 magnitude; half the speed of NNB_PREC_FP32      */
+  NNB_PREC_BF16 = 4       /* BF16 inputs, float32 accumulation: activations and weights
+                             rounded to bf16, one tensor product per useful product
+                             (fast, looser bound)                                    */
 };
 
 /* One channel segment of a convolution input (two segments = decoder concat). */
@@ -59,8 +62,8 @@ typedef struct nnb_segment {
   const float* shift;  /* (B, channels), required when scale != NULL */
   int32_t channels;
   int32_t leaky;       /* 1: LeakyReLU(slope) after the affine */
-  int32_t prepared;    /* operand_format 2 only: 1 = `data` holds nnb_prepare_operand(NNB_PREC_FP32)
-                          output of the activation (scale must be NULL); 0 = raw */
+  int32_t prepared;    /* operand_format 2 only: 1 = `data` holds nnb_prepare_operand output of the
+                          activation for the call's precision (scale must be NULL); 0 = raw */
   int32_t reserved;    /* 0 */
 } nnb_segment;
 
@@ -119,10 +122,11 @@ int32_t nnb_conv3d(const nnb_conv3d_args* args, void* stream);
 /*
  * 1 when the tensor-core path for `args` (shape fields, precision,
  * num_segments and segment channels read) takes raw lazy segments
- * (operand_format 2): NNB_PREC_FP32 3x3x3 stride-1 padding-1 convolutions
- * with <= 32 output channels and a LeakyReLU slope in [0, 1], whose kernel
- * applies the affine + LeakyReLU and the fp16-pair split to each input plane
- * in shared memory (replacing the nnb_prepare_operand pass); 0 otherwise.  Replaces nothing in the reference
+ * (operand_format 2): NNB_PREC_FP32, NNB_PREC_BF16 or NNB_PREC_TF32 3x3x3
+ * stride-1 padding-1 convolutions with <= 32 output channels and a LeakyReLU
+ * slope in [0, 1], whose kernel applies the affine + LeakyReLU and the
+ * operand conversion (fp16 pair, bf16 or TF32) to each input plane in shared
+ * memory (replacing the nnb_prepare_operand pass); 0 otherwise.  Replaces nothing in the reference
  * (MLX materialises the normalised activation,
  * src/nnunet_mlx/kernels/metal_native_norm.py:62-70).
  */
@@ -138,7 +142,10 @@ int32_t nnb_conv3d_raw_operands(const nnb_conv3d_args* args);
  *                       (C % 32 == 0; out holds batch * voxels * C floats' bytes);
  *   NNB_PREC_FP32_TF32  per voxel [hi(C) | lo(C)], hi = x with the 13 low
  *                       mantissa bits cleared, lo = x - hi (2 C floats);
- *   NNB_PREC_TF32       x rounded to TF32 (C floats).
+ *   NNB_PREC_TF32       x rounded to TF32 (C floats);
+ *   NNB_PREC_BF16       per voxel and 32-channel group, 64 bf16 halves
+ *                       [bf16(x)(32) | 0(32)] (C % 32 == 0; the fp16 pair's
+ *                       layout, of which the convolution reads the first half).
  * Replaces the affine pass of
  * src/nnunet_mlx/kernels/metal_native_norm.py:62-70,155-168 (there the
  * normalised activation is materialised in float32).
@@ -185,7 +192,8 @@ int64_t nnb_conv3d_packed_bytes(int32_t cout, int32_t kvol, int32_t cin_total, i
  * W0 = fp16(s w), W1 = fp16(s w - W0) in 64-byte swizzled K-major
  * rows, s a power of two per output column (max |s w| < 2^14), followed by
  * the float 1/s of every column; NNB_PREC_FP32_TF32: TF32 hi/lo rows;
- * NNB_PREC_TF32: TF32 rows (128-byte swizzled K-major rows).  The image must start on a 1024-byte boundary.  Replaces the
+ * NNB_PREC_TF32: TF32 rows (128-byte swizzled K-major rows); NNB_PREC_BF16:
+ * bf16(w) rows (64-byte swizzled, no column scales).  The image must start on a 1024-byte boundary.  Replaces the
  * weight layout work MLX does inside `mx.conv3d` for
  * src/nnunet_mlx/model/network.py:261-269.
  */
@@ -248,14 +256,16 @@ int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int3
                              float* out, void* stream);
 
 /*
- * nnb_conv_transpose3d on the NNB_PREC_FP32 tensor-core path whose output is
- * written directly as the tensor-core operand of the up-sampled activation
- * (the nnb_prepare_operand(NNB_PREC_FP32) layout: per voxel and 32-channel
- * group [hi(32) | lo(32)] halves, 4 bytes per channel) instead of float32,
- * so the decoder's concat convolution reads it without a preparation pass;
- * out-of-range values count in nnb_operand_range_events.  Requires `packed`,
- * 32-multiple channel counts and precision NNB_PREC_FP32 (else
- * NNB_E_UNSUPPORTED).  Same reference call site as nnb_conv_transpose3d.
+ * nnb_conv_transpose3d on the tensor-core path whose output is written
+ * directly as the tensor-core operand of the up-sampled activation (the
+ * nnb_prepare_operand layout of `precision`, 4 bytes per channel:
+ * NNB_PREC_FP32 [hi(32) | lo(32)] halves per 32-channel group, whose
+ * out-of-range values count in nnb_operand_range_events; NNB_PREC_BF16
+ * [bf16(32) | 0(32)]; NNB_PREC_TF32 TF32 values) instead of float32, so the
+ * decoder's concat convolution reads it without a preparation pass.
+ * Requires `packed`, 32-multiple channel counts and one of those three
+ * precisions (else NNB_E_UNSUPPORTED).  Same reference call site as
+ * nnb_conv_transpose3d.
  */
 int32_t nnb_conv_transpose3d_operand(const nnb_segment* input, int32_t batch, const int32_t in_dims[3],
                                      const int32_t kernel[3], float slope, const float* bias, int32_t cout,

@@ -22,7 +22,10 @@ PREC_FP32 = 0        # split fp16 pairs on the tensor cores, float32-level accur
 PREC_TF32 = 1        # single-pass TF32 tensor cores
 PREC_SIMT = 2        # CUDA-core float32
 PREC_FP32_TF32 = 3   # split-TF32 hi/lo tensor cores, float32-level accuracy at any magnitude
-TENSOR_PRECISIONS = (PREC_FP32, PREC_TF32, PREC_FP32_TF32)
+PREC_BF16 = 4        # bf16 inputs, float32 accumulation (one product per useful product)
+TENSOR_PRECISIONS = (PREC_FP32, PREC_TF32, PREC_FP32_TF32, PREC_BF16)
+# precisions whose transposed convolution can write the next convolution's operand directly
+OPERAND_OUTPUT_PRECISIONS = (PREC_FP32, PREC_TF32, PREC_BF16)
 # nnb_conv3d_kernel_mode -> the kernel a convolution launches
 KERNEL_MODES = {0: "conv3d_simt_kernel", 1: "conv3d_tc_kernel", 2: "conv3d_halo_kernel", 3: "conv3d_zstream_kernel"}
 

@@ -207,9 +207,11 @@ int32_t nnb_conv_transpose3d_operand(const nnb_segment* input, int32_t batch, co
   if (rc) return rc;
   NNB_REQUIRE(batch >= 1 && positive3(in_dims) && positive3(kernel), "conv_transpose3d_operand: bad shape");
   NNB_REQUIRE(out != nullptr && cout >= 1, "conv_transpose3d_operand: missing output");
-  if (packed == nullptr || precision != NNB_PREC_FP32 || input->channels % 32 != 0 || cout % 32 != 0) {
-    set_error("conv_transpose3d_operand: needs the NNB_PREC_FP32 tensor-core path (packed weights, 32-multiple "
-              "channels)");
+  const bool operand_precision = precision == NNB_PREC_FP32 || precision == NNB_PREC_BF16 ||
+                                 precision == NNB_PREC_TF32;
+  if (packed == nullptr || !operand_precision || input->channels % 32 != 0 || cout % 32 != 0) {
+    set_error("conv_transpose3d_operand: needs the NNB_PREC_FP32, NNB_PREC_BF16 or NNB_PREC_TF32 tensor-core path "
+              "(packed weights, 32-multiple channels)");
     return NNB_E_UNSUPPORTED;
   }
   return launch_conv_transpose_tc(*input, batch, in_dims, kernel, slope, bias, cout, packed, precision,

@@ -48,14 +48,22 @@ void set_error(const char* fmt, ...);
 constexpr int kOperandTf32 = 0;    // one TF32 value per element
 constexpr int kOperandTf32x2 = 1;  // TF32 hi/lo pair
 constexpr int kOperandF16x2 = 2;   // fp16 hi + lo pair
+constexpr int kOperandBf16 = 3;    // one bf16 value per element (in the fp16 pair's row layout, lo half unused)
 
 inline bool tensor_precision(int precision) {
-  return precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32 || precision == NNB_PREC_FP32_TF32;
+  return precision == NNB_PREC_FP32 || precision == NNB_PREC_TF32 || precision == NNB_PREC_FP32_TF32 ||
+         precision == NNB_PREC_BF16;
 }
 
 inline int operand_kind(int precision) {
-  return precision == NNB_PREC_FP32 ? kOperandF16x2 : precision == NNB_PREC_FP32_TF32 ? kOperandTf32x2 : kOperandTf32;
+  return precision == NNB_PREC_FP32        ? kOperandF16x2
+         : precision == NNB_PREC_FP32_TF32 ? kOperandTf32x2
+         : precision == NNB_PREC_BF16      ? kOperandBf16
+                                           : kOperandTf32;
 }
+
+// 16-bit operand formats: 128-byte A rows of 64 halves per 32 channels, 64-byte B rows.
+constexpr bool half_rows(int op) { return op == kOperandF16x2 || op == kOperandBf16; }
 
 inline int tiles_per_sample(int64_t voxels) { return (int)((voxels + kTileRows - 1) / kTileRows); }
 

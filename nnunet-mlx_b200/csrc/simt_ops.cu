@@ -2,6 +2,7 @@
 // the few-channel first layer and for shapes outside the tensor-core
 // envelope), the transposed convolution, instance-norm finalisation and the
 // residual join.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -640,6 +641,9 @@ namespace nnb {
 //   kOperandTf32x2  per voxel [hi(C) | lo(C)], hi = x with the 13 low mantissa
 //                   bits cleared, lo = x - hi (both exact).  4 read, 8 written.
 //   kOperandTf32    x rounded to TF32 (nearest).  4 read, 4 written.
+//   kOperandBf16    per voxel and 32-channel group [bf16(x)(32) | 0(32)] as
+//                   bf16 halves (the fp16 pair's row layout; the MMA reads
+//                   only the first half).  4 read, 4 written.
 // ---------------------------------------------------------------------------
 __device__ unsigned long long g_operand_range_events = 0;
 
@@ -674,6 +678,16 @@ __global__ void prepare_operand_kernel(nnb_segment in, int64_t voxels_total, int
       __half* base = reinterpret_cast<__half*>(out) + vox * 2 * C + (c8 / 32) * 64 + (c8 % 32);
       *reinterpret_cast<uint4*>(base) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
       *reinterpret_cast<uint4*>(base + 32) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    } else if (op == kOperandBf16) {
+      uint32_t hb[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(v[e], v[e + 1]);
+        hb[e / 2] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+      __half* base = reinterpret_cast<__half*>(out) + vox * 2 * C + (c8 / 32) * 64 + (c8 % 32);
+      *reinterpret_cast<uint4*>(base) = make_uint4(hb[0], hb[1], hb[2], hb[3]);
+      *reinterpret_cast<uint4*>(base + 32) = make_uint4(0u, 0u, 0u, 0u);
     } else if (op == kOperandTf32x2) {
       float hi[8], lo[8];
 #pragma unroll
@@ -709,8 +723,8 @@ unsigned long long* operand_range_events_ptr() {
 
 int launch_prepare_operand(const nnb_segment& in, int batch, int64_t voxels, float slope, int op, float* out,
                            cudaStream_t stream) {
-  NNB_REQUIRE(in.channels % (op == kOperandF16x2 ? 32 : 8) == 0,
-              "prepare_operand: channels must be a multiple of %d", op == kOperandF16x2 ? 32 : 8);
+  NNB_REQUIRE(in.channels % (half_rows(op) ? 32 : 8) == 0,
+              "prepare_operand: channels must be a multiple of %d", half_rows(op) ? 32 : 8);
   NNB_REQUIRE((reinterpret_cast<uintptr_t>(in.data) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
               "prepare_operand: 16-byte aligned tensors required");
   unsigned long long* events = operand_range_events_ptr();

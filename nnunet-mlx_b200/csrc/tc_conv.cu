@@ -18,6 +18,10 @@
 //    TF32 values, B = [W_hi ; W_lo]; per 8-channel sub-step A_hi x [W_hi;W_lo]
 //    and A_lo x [W_hi;W_lo]; the epilogue adds the halves.
 //  * kOperandTf32 (fast): one TF32 row, B = W_tf32, one MMA per sub-step.
+//  * kOperandBf16 (fast): the fp16 pair's 128-byte A row with bf16(x) in the
+//    hi half (the lo half is never read), B = bf16(w) in 64-byte rows; one
+//    kind::f16 MMA (A and B both bf16, float32 accumulation) per 16-channel
+//    sub-step.
 //
 // A tcgen05.mma costs at least ~46 cycles at M = 128 whatever N is (up to 64),
 // so stacking the split weights along N halves the instruction count of the
@@ -59,6 +63,7 @@
 // copies and MMAs in flight, frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -109,10 +114,10 @@ struct OperandMaps {
 
 template <int BC, int OP>
 struct Cfg {
-  static constexpr bool kSplit = OP != kOperandTf32;
+  static constexpr bool kSplit = OP == kOperandF16x2 || OP == kOperandTf32x2;
   static constexpr int kHalves = OP == kOperandTf32x2 ? 2 : 1;  // A boxes (128-byte rows) per K-step
   static constexpr int N = kSplit ? 2 * BC : BC;                // accumulator columns: stacked [W_hi; W_lo] rows
-  static constexpr int kBRow = OP == kOperandF16x2 ? 64 : 128;  // bytes of one B row (32 channels)
+  static constexpr int kBRow = half_rows(OP) ? 64 : 128;        // bytes of one B row (32 channels)
   static constexpr int kAccBufs = (2 * N <= kTmemCols) ? 2 : 1;
   // epilogue warpgroups: with two accumulators each group drains every other tile (one warp per SM
   // sub-partition alone is latency-bound on the epilogue's dependent chains)
@@ -157,7 +162,7 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
 // B-tile descriptor of the operand format (64-byte rows for the fp16 pair).
 template <int OP>
 __device__ __forceinline__ uint64_t b_desc_at(uint32_t saddr) {
-  if constexpr (OP == kOperandF16x2) return sw64_desc(saddr);
+  if constexpr (half_rows(OP)) return sw64_desc(saddr);
   else return sw128_desc(saddr);
 }
 
@@ -174,6 +179,10 @@ __device__ __forceinline__ void kstep_mmas(uint32_t d, uint64_t ad, uint64_t bd,
       mma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, id2, (acc | kk) ? 1u : 0u);
       mma_f16_ss(d + BC, ad + 4 + 2 * kk, bd + 2 * kk, id1, 1u);
     }
+  } else if constexpr (OP == kOperandBf16) {
+    constexpr uint32_t id = idesc_bf16(BM, BC);
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) mma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, id, (acc | kk) ? 1u : 0u);
   } else {
     constexpr uint32_t id = idesc_tf32(BM, Cfg<BC, OP>::N);
 #pragma unroll
@@ -217,7 +226,7 @@ __device__ __forceinline__ ChunkSource chunk_source(const nnb_conv3d_args& a, co
   const bool second = cg >= g.c0len;
   const int cl = second ? cg - g.c0len : cg;
   const int cs = second ? a.seg[1].channels : g.c0len;
-  if constexpr (OP == kOperandF16x2) return ChunkSource{&maps.seg[second ? 1 : 0], 2 * cl, 0};  // [hi | lo] halves
+  if constexpr (half_rows(OP)) return ChunkSource{&maps.seg[second ? 1 : 0], 2 * cl, 0};  // [hi | lo] halves
   else return ChunkSource{&maps.seg[second ? 1 : 0], cl, cs + cl};
 }
 
@@ -355,20 +364,34 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
         }
       }
       if (g.up_operand) {
-        // the row's [hi(32) | lo(32)] fp16 operand (hi: 13 low mantissa bits cleared, lo = v - hi), 128 bytes
-        // at the same address as its 32 float32 values
+        // the row's operand for the next convolution, 128 bytes at the same address as its 32 float32 values
         float pk[32];
-        bool over = false;
+        if constexpr (OP == kOperandF16x2) {
+          // [hi(32) | lo(32)] fp16 (hi: 13 low mantissa bits cleared, lo = v - hi)
+          bool over = false;
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float h0 = __uint_as_float(__float_as_uint(v[i]) & 0xFFFFE000u);
-          const float h1 = __uint_as_float(__float_as_uint(v[i + 1]) & 0xFFFFE000u);
-          const __half2 hh = __floats2half2_rn(h0, h1), ll = __floats2half2_rn(v[i] - h0, v[i + 1] - h1);
-          pk[i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&hh));
-          pk[16 + i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&ll));
-          over |= fabsf(v[i]) >= 65504.f || fabsf(v[i + 1]) >= 65504.f;
+          for (int i = 0; i < 32; i += 2) {
+            const float h0 = __uint_as_float(__float_as_uint(v[i]) & 0xFFFFE000u);
+            const float h1 = __uint_as_float(__float_as_uint(v[i + 1]) & 0xFFFFE000u);
+            const __half2 hh = __floats2half2_rn(h0, h1), ll = __floats2half2_rn(v[i] - h0, v[i + 1] - h1);
+            pk[i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&hh));
+            pk[16 + i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&ll));
+            over |= fabsf(v[i]) >= 65504.f || fabsf(v[i + 1]) >= 65504.f;
+          }
+          if (over && valid) atomicAdd(g.range_events, 1ull);
+        } else if constexpr (OP == kOperandBf16) {
+          // [bf16(32) | 0(32)]
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const __nv_bfloat162 bb = __floats2bfloat162_rn(v[i], v[i + 1]);
+            pk[i / 2] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&bb));
+            pk[16 + i / 2] = 0.f;
+          }
+        } else {
+          // 32 TF32 values (round to nearest)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(to_tf32(v[i]));
         }
-        if (over && valid) atomicAdd(g.range_events, 1ull);
         store_rows_staged(stg, lane, pk, dst);
       } else {
         store_rows_staged(stg, lane, v, dst);
@@ -814,8 +837,8 @@ __global__ void __launch_bounds__(Cfg<BC, OP>::kThreadsC, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Z-streaming mode (fp16 pairs; 3x3x3, stride 1, padding 1, <= 32 output
-// channels).  The 128^3 stages' layers: a CTA walks a contiguous run of the
+// Z-streaming mode (3x3x3, stride 1, padding 1, <= 32 output channels; fp16
+// pairs, and the single-product bf16 and TF32 formats).  The 128^3 stages' layers: a CTA walks a contiguous run of the
 // output planes of 8 (w) x 16 (h) brick columns (column-major, z fastest; the
 // runs of all CTAs split the volume's planes evenly).  Each input plane u of a
 // column is loaded once (one halo plane box per 32-channel chunk) and, per
@@ -832,17 +855,24 @@ __global__ void __launch_bounds__(Cfg<BC, OP>::kThreadsC, 1)
 // partial column -- are only discarded), zeroes its slot and releases it, so
 // every MMA accumulates.  A column costs 3 MMAs per (tap, sub-step, input
 // plane) instead of 6 per output plane, and each input plane is read once
-// instead of three times.  The input planes are the raw float32 activation
+// instead of three times.  The single-product formats stack only [W(kz0..2)]
+// (96 rows) and issue one MMA per (tap, sub-step): bf16 sub-steps of 16
+// channels, TF32 sub-steps of 8 channels with 128-byte B rows.  The input planes are the raw float32 activation
 // (a lazy segment of the previous layer): two transform warps convert each
 // landed plane in place -- instance-norm affine + LeakyReLU, zero for the
-// padding rows, fp16 hi / lo split into the MMA's [hi | lo] row layout, and
-// the fp16 range count -- so the activation makes no extra trip through HBM.  The 27 taps' weights of a single-chunk layer stay
+// padding rows, fp16 hi / lo split into the MMA's [hi | lo] row layout and
+// the fp16 range count (bf16: the hi half only; TF32: the row rounded to
+// TF32 in place) -- so the activation makes no extra trip through HBM.  The 27 taps' weights of a single-chunk layer stay
 // resident in shared memory for the whole kernel (rearranged from the weight
 // image by bulk copies); wider inputs stream one (chunk, ky) row of stacked
 // weights per stage.
 // ---------------------------------------------------------------------------
 constexpr int kZsSlots = 16;
-constexpr int kZsRows = 6 * 32;  // stacked rows per (ky, kx) tap: [W0 x 3 kz ; W1 x 3 kz]
+
+// Stacked B rows per (ky, kx) tap: fp16 pairs [W0 x 3 kz ; W1 x 3 kz], the single formats [W x 3 kz].
+__host__ __device__ constexpr int zs_rows(int op) { return op == kOperandF16x2 ? 6 * 32 : 3 * 32; }
+__host__ __device__ constexpr int zs_row_bytes(int op) { return half_rows(op) ? 64 : 128; }
+__host__ __device__ constexpr int zs_tap_bytes(int op) { return zs_rows(op) * zs_row_bytes(op); }
 
 struct ZsRun {
   int64_t idx, end;  // [idx, end) of the column-major, z-fastest output-plane sequence
@@ -872,43 +902,71 @@ __device__ __forceinline__ bool zs_next(const Geometry& g, ZsRun& r, ZsSegment& 
 
 __device__ __forceinline__ int zs_slot(int P) { return kZsSlots - 1 - (P & (kZsSlots - 1)); }
 
-// The MMAs of one row of taps (ky fixed; kx = 0..2; two 16-channel sub-steps each) into the slots of the
-// three planes an input feeds (d: TMEM address of slot s0).  N1 = 3: the slots s0..s0+2 are adjacent, three
-// MMAs of N = 96 per (tap, sub-step); N1 = 1 or 2: the ring wraps after N1 blocks, so each MMA splits into
-// N = 32 N1 at s0 and N = 32 (3 - N1) at slot 0.  arow / brow: A (hi) and stacked-B descriptors of the
-// row's kx = 0 tap; the lo half of an A row starts 64 bytes in, the W1 blocks 96 B rows in.
-template <int N1>
+// The MMAs of one row of taps (ky fixed; kx = 0..2; 16-channel sub-steps, or 8-channel ones for TF32) into the
+// slots of the three planes an input feeds (d: TMEM address of slot s0).  N1 = 3: the slots s0..s0+2 are adjacent,
+// one MMA of N = 96 per product; N1 = 1 or 2: the ring wraps after N1 blocks, so each MMA splits into N = 32 N1
+// at s0 and N = 32 (3 - N1) at slot 0.  arow / brow: A (hi) and stacked-B descriptors of the row's kx = 0 tap;
+// the lo half of an fp16-pair A row starts 64 bytes in, the W1 blocks 96 B rows in.
+template <int OP, int N1>
 __device__ __forceinline__ void zs_row(uint32_t tmem, uint32_t d, uint64_t arow, uint64_t brow) {
-  constexpr uint32_t kTap16 = (kZsRows * 64) >> 4;
-  constexpr uint32_t kW116 = (3 * 32 * 64) >> 4;
-  constexpr uint32_t idA = idesc_f16(BM, 32 * N1);
+  constexpr uint32_t kTap16 = (uint32_t)zs_tap_bytes(OP) >> 4;
+  constexpr uint32_t kBlk16 = (uint32_t)(32 * zs_row_bytes(OP)) >> 4;  // one kz block of 32 B rows
+  constexpr uint32_t kSplit16 = N1 * kBlk16;
+  if constexpr (OP == kOperandF16x2) {
+    constexpr uint32_t kW116 = 3 * kBlk16;
+    constexpr uint32_t idA = idesc_f16(BM, 32 * N1);
 #pragma unroll
-  for (int kx = 0; kx < 3; ++kx)
+    for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      const uint64_t ad = arow + (uint64_t)(8 * kx + 2 * kk);
-      const uint64_t bd = brow + (uint64_t)(kx * kTap16 + 2 * kk);
-      mma_f16_ss(d, ad, bd, idA, 1u);
-      mma_f16_ss(d, ad, bd + kW116, idA, 1u);
-      mma_f16_ss(d, ad + 4, bd, idA, 1u);
-      if constexpr (N1 < 3) {
-        constexpr uint32_t idB = idesc_f16(BM, 32 * (3 - N1));
-        constexpr uint32_t kSplit16 = (N1 * 32 * 64) >> 4;
-        mma_f16_ss(tmem, ad, bd + kSplit16, idB, 1u);
-        mma_f16_ss(tmem, ad, bd + kW116 + kSplit16, idB, 1u);
-        mma_f16_ss(tmem, ad + 4, bd + kSplit16, idB, 1u);
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint64_t ad = arow + (uint64_t)(8 * kx + 2 * kk);
+        const uint64_t bd = brow + (uint64_t)(kx * kTap16 + 2 * kk);
+        mma_f16_ss(d, ad, bd, idA, 1u);
+        mma_f16_ss(d, ad, bd + kW116, idA, 1u);
+        mma_f16_ss(d, ad + 4, bd, idA, 1u);
+        if constexpr (N1 < 3) {
+          constexpr uint32_t idB = idesc_f16(BM, 32 * (3 - N1));
+          mma_f16_ss(tmem, ad, bd + kSplit16, idB, 1u);
+          mma_f16_ss(tmem, ad, bd + kW116 + kSplit16, idB, 1u);
+          mma_f16_ss(tmem, ad + 4, bd + kSplit16, idB, 1u);
+        }
       }
-    }
+  } else if constexpr (OP == kOperandBf16) {
+    constexpr uint32_t idA = idesc_bf16(BM, 32 * N1);
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint64_t ad = arow + (uint64_t)(8 * kx + 2 * kk);
+        const uint64_t bd = brow + (uint64_t)(kx * kTap16 + 2 * kk);
+        mma_f16_ss(d, ad, bd, idA, 1u);
+        if constexpr (N1 < 3) mma_f16_ss(tmem, ad, bd + kSplit16, idesc_bf16(BM, 32 * (3 - N1)), 1u);
+      }
+  } else {
+    static_assert(OP == kOperandTf32, "z-streaming formats: fp16 pair, bf16, TF32");
+    constexpr uint32_t idA = idesc_tf32(BM, 32 * N1);
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t ad = arow + (uint64_t)(8 * kx + 2 * kk);
+        const uint64_t bd = brow + (uint64_t)(kx * kTap16 + 2 * kk);
+        mma_tf32_ss(d, ad, bd, idA, 1u);
+        if constexpr (N1 < 3) mma_tf32_ss(tmem, ad, bd + kSplit16, idesc_tf32(BM, 32 * (3 - N1)), 1u);
+      }
+  }
 }
 
 // producer, MMA issuer, two epilogue warpgroups taking alternate planes, two operand-transform warps
 constexpr int kZsThreads = 12 * 32;
 
-// In-place conversion of one landed raw plane box (rows of 32 float32 channels, 128-byte swizzled) into
-// the [hi(32) | lo(32)] fp16 rows the MMA reads, by 64 threads, one whole row per thread at a time (the
-// row's eight 16-byte chunks are all read before any is written, so no other thread touches it).  aff:
-// the chunk's 32 scales then 32 shifts (identity for a raw segment).  Padding rows become zeros.
-// Returns whether any value reached the fp16 range limit.
+// In-place conversion of one landed raw plane box (rows of 32 float32 channels, 128-byte swizzled) into the
+// rows the MMA reads, by 64 threads, one whole row per thread at a time (the row's eight 16-byte chunks are
+// all read before any is written, so no other thread touches it): fp16 pairs [hi(32) | lo(32)], bf16 the hi
+// half only, TF32 the 32 values rounded to TF32 in place.  aff: the chunk's 32 scales then 32 shifts
+// (identity for a raw segment).  Padding rows become zeros.  Returns whether any value reached the fp16
+// range limit (fp16 pairs only).
+template <int OP>
 __device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometry& g, const float* aff,
                                                    bool leaky_act, int w0, int h0, float slope, int t) {
   float amax = 0.f;
@@ -932,30 +990,49 @@ __device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometr
       const float4 sh = *reinterpret_cast<const float4*>(aff + 32 + 4 * k);
       float v[4] = {fmaf(x[k].x, sc.x, sh.x), fmaf(x[k].y, sc.y, sh.y), fmaf(x[k].z, sc.z, sh.z),
                     fmaf(x[k].w, sc.w, sh.w)};
-      float h[4], l[4];
+      if (leaky_act) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if (leaky_act) v[e] = fmaxf(v[e], v[e] * slope);  // LeakyReLU for 0 <= slope <= 1
-        amax = fmaxf(amax, fabsf(v[e]));
-        // hi: v with the 13 low mantissa bits cleared (exactly an fp16 value in fp16's normal range),
-        // lo = v - hi exactly; both are then rounded to fp16
-        h[e] = __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u);
-        l[e] = v[e] - h[e];
+        for (int e = 0; e < 4; ++e) v[e] = fmaxf(v[e], v[e] * slope);  // LeakyReLU for 0 <= slope <= 1
       }
+      if constexpr (OP == kOperandF16x2) {
+        float h[4], l[4];
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const __half2 hh2 = __floats2half2_rn(h[e], h[e + 1]);
-        const __half2 ll2 = __floats2half2_rn(l[e], l[e + 1]);
-        hi[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&hh2);
-        lo[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&ll2);
+        for (int e = 0; e < 4; ++e) {
+          amax = fmaxf(amax, fabsf(v[e]));
+          // hi: v with the 13 low mantissa bits cleared (exactly an fp16 value in fp16's normal range),
+          // lo = v - hi exactly; both are then rounded to fp16
+          h[e] = __uint_as_float(__float_as_uint(v[e]) & 0xFFFFE000u);
+          l[e] = v[e] - h[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const __half2 hh2 = __floats2half2_rn(h[e], h[e + 1]);
+          const __half2 ll2 = __floats2half2_rn(l[e], l[e + 1]);
+          hi[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&hh2);
+          lo[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&ll2);
+        }
+      } else if constexpr (OP == kOperandBf16) {
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const __nv_bfloat162 bb = __floats2bfloat162_rn(v[e], v[e + 1]);
+          hi[2 * k + e / 2] = *reinterpret_cast<const uint32_t*>(&bb);
+        }
+      } else {
+        // TF32: logical chunk k holds channels 4k..4k+3 as 32-bit values (every chunk was read above)
+        *reinterpret_cast<uint4*>(row + ((k ^ sw) << 4)) = make_uint4(to_tf32(v[0]), to_tf32(v[1]), to_tf32(v[2]),
+                                                                      to_tf32(v[3]));
       }
     }
-    // hi halves of channels 8m..8m+7 form logical chunk m, the lo halves chunk 4 + m
+    if constexpr (half_rows(OP)) {
+      // hi halves of channels 8m..8m+7 form logical chunk m, the lo halves (fp16 pairs) chunk 4 + m
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      *reinterpret_cast<uint4*>(row + ((m ^ sw) << 4)) = make_uint4(hi[4 * m], hi[4 * m + 1], hi[4 * m + 2], hi[4 * m + 3]);
-      *reinterpret_cast<uint4*>(row + (((4 + m) ^ sw) << 4)) =
-          make_uint4(lo[4 * m], lo[4 * m + 1], lo[4 * m + 2], lo[4 * m + 3]);
+      for (int m = 0; m < 4; ++m) {
+        *reinterpret_cast<uint4*>(row + ((m ^ sw) << 4)) =
+            make_uint4(hi[4 * m], hi[4 * m + 1], hi[4 * m + 2], hi[4 * m + 3]);
+        if constexpr (OP == kOperandF16x2)
+          *reinterpret_cast<uint4*>(row + (((4 + m) ^ sw) << 4)) =
+              make_uint4(lo[4 * m], lo[4 * m + 1], lo[4 * m + 2], lo[4 * m + 3]);
+      }
     }
   }
   return amax >= 65504.f;
@@ -978,16 +1055,19 @@ __device__ __forceinline__ void zs_load_affine(const nnb_conv3d_args& a, const G
   __syncwarp();
 }
 
+template <int OP>
 __global__ void __launch_bounds__(kZsThreads, 1)
     conv3d_zstream_kernel(const nnb_conv3d_args a, const Geometry g, const __grid_constant__ OperandMaps maps) {
   constexpr int BC = 32;
-  using C = Cfg<BC, kOperandF16x2>;
+  using C = Cfg<BC, OP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int SA = g.sa, SB = g.sb;
   const bool resident = SB == 0;
   const int a_entry = g.nchunk * g.plane_bytes;              // one input plane, all chunks
-  constexpr uint32_t kTapBytes = kZsRows * 64;              // stacked weights of one (ky, kx) tap
+  constexpr uint32_t kTapBytes = zs_tap_bytes(OP);         // stacked weights of one (ky, kx) tap
+  constexpr uint32_t kBlkBytes = 32 * zs_row_bytes(OP);     // one kz block (32 B rows) of a part
+  constexpr int kParts = OP == kOperandF16x2 ? 2 : 1;       // [W0 ; W1] or [W] per image tile
   const uint32_t b_stage = 3u * kTapBytes;                  // one (chunk, ky) row of taps
   const uint32_t b_bytes = resident ? 9u * kTapBytes : (uint32_t)SB * b_stage;
   uint8_t* a_ring = smem;
@@ -1050,15 +1130,15 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     if (lane == 0) {
       bool alive = true;
       if (resident) {
-        // stacked rows of tap (ky, kx): [W0(kz0..2) ; W1(kz0..2)], 32 rows each, from the image's
-        // [W0 ; W1] tile of tap (kz, ky, kx)
+        // stacked rows of tap (ky, kx): [W0(kz0..2) ; W1(kz0..2)] (or [W(kz0..2)]), 32 rows each, from the
+        // image's [W0 ; W1] (or [W]) tile of tap (kz, ky, kx)
         const uint32_t fb = smem_u32(&b_full[0]);
         mbar_arrive_expect_tx(fb, 9u * kTapBytes);
         for (int t = 0; t < 9; ++t)
-          for (int part = 0; part < 2; ++part)
+          for (int part = 0; part < kParts; ++part)
             for (int kz = 0; kz < 3; ++kz)
-              bulk_g2s(smem_u32(b_ring + t * kTapBytes + (part * 3 + kz) * 32 * 64),
-                       wimg + (int64_t)(kz * 9 + t) * C::kBBytes + part * 32 * 64, 32 * 64, fb);
+              bulk_g2s(smem_u32(b_ring + t * kTapBytes + (part * 3 + kz) * kBlkBytes),
+                       wimg + (int64_t)(kz * 9 + t) * C::kBBytes + part * kBlkBytes, kBlkBytes, fb);
       }
       int P = 0, T = 0;
       ZsRun run = zs_run(g);
@@ -1076,9 +1156,9 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           const uint32_t fa = smem_u32(&a_full[sa]);
           mbar_arrive_expect_tx(fa, (uint32_t)(g.nchunk * g.plane_rows * 128));
           for (int c = 0; c < g.nchunk; ++c) {
-            // raw float32 plane of the chunk's 32 channels, or its [hi | lo] fp16 rows when prepared
+            // raw float32 plane of the chunk's 32 channels, or its operand rows when prepared
             const ChunkSource src = a.seg[c * BK >= g.c0len ? 1 : 0].prepared
-                                        ? chunk_source<kOperandF16x2>(a, g, maps, c)
+                                        ? chunk_source<OP>(a, g, maps, c)
                                         : chunk_source<kOperandTf32>(a, g, maps, c);
             tma_load_5d(smem_u32(a_ring + sa * a_entry + c * g.plane_bytes), src.map, src.c_hi, w0, h0, u, b, fa);
           }
@@ -1095,11 +1175,11 @@ __global__ void __launch_bounds__(kZsThreads, 1)
                 mbar_arrive_expect_tx(fb, b_stage);
                 uint8_t* dst = b_ring + sb * b_stage;
                 for (int kx = 0; kx < 3; ++kx)
-                  for (int part = 0; part < 2; ++part)
+                  for (int part = 0; part < kParts; ++part)
                     for (int kz = 0; kz < 3; ++kz)
-                      bulk_g2s(smem_u32(dst + kx * kTapBytes + (part * 3 + kz) * 32 * 64),
-                               wimg + (int64_t)(c * taps + kz * 9 + ky * 3 + kx) * C::kBBytes + part * 32 * 64,
-                               32 * 64, fb);
+                      bulk_g2s(smem_u32(dst + kx * kTapBytes + (part * 3 + kz) * kBlkBytes),
+                               wimg + (int64_t)(c * taps + kz * 9 + ky * 3 + kx) * C::kBBytes + part * kBlkBytes,
+                               kBlkBytes, fb);
                 ++T;
               }
           }
@@ -1118,7 +1198,7 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     // ------------------------------ MMA issuer -------------------------------
     if (lane == 0) {
       const uint64_t adesc0 = sw128_desc(smem_u32(a_ring), (uint32_t)g.pw * 128);
-      const uint64_t bdesc0 = sw64_desc(smem_u32(b_ring));
+      const uint64_t bdesc0 = b_desc_at<OP>(smem_u32(b_ring));
       const uint32_t entry16 = (uint32_t)a_entry >> 4, plane16 = (uint32_t)g.plane_bytes >> 4;
       const uint32_t row16 = (uint32_t)g.pw * 8;  // one ky step of the plane in 16-byte units
       constexpr uint32_t kTap16 = kTapBytes >> 4;
@@ -1154,15 +1234,15 @@ __global__ void __launch_bounds__(kZsThreads, 1)
               if (s0 <= kZsSlots - 3) {
 #pragma unroll 1
                 for (int ky = 0; ky < 3; ++ky)
-                  zs_row<3>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+                  zs_row<OP, 3>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
               } else if (s0 == kZsSlots - 2) {
 #pragma unroll 1
                 for (int ky = 0; ky < 3; ++ky)
-                  zs_row<2>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+                  zs_row<OP, 2>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
               } else {
 #pragma unroll 1
                 for (int ky = 0; ky < 3; ++ky)
-                  zs_row<1>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+                  zs_row<OP, 1>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
               }
             } else {
               for (int ky = 0; ky < 3; ++ky) {
@@ -1175,11 +1255,11 @@ __global__ void __launch_bounds__(kZsThreads, 1)
                 const uint64_t arow = ap + (uint64_t)(ky * row16);
                 const uint64_t brow = bdesc0 + (uint64_t)(sb * stage16);
                 if (s0 <= kZsSlots - 3)
-                  zs_row<3>(tmem, dslot, arow, brow);
+                  zs_row<OP, 3>(tmem, dslot, arow, brow);
                 else if (s0 == kZsSlots - 2)
-                  zs_row<2>(tmem, dslot, arow, brow);
+                  zs_row<OP, 2>(tmem, dslot, arow, brow);
                 else
-                  zs_row<1>(tmem, dslot, arow, brow);
+                  zs_row<OP, 1>(tmem, dslot, arow, brow);
                 mma_commit(smem_u32(&b_empty[sb]));
                 ++T;
               }
@@ -1232,8 +1312,8 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           const nnb_segment& seg = a.seg[c * BK >= g.c0len ? 1 : 0];
           if (seg.prepared) continue;  // already [hi | lo] rows
           const bool lazy_leaky = seg.scale != nullptr && seg.leaky;
-          over |= zs_transform_plane(a_ring + sa * a_entry + c * g.plane_bytes, g, aff + 64 * c, lazy_leaky,
-                                     w0, h0, a.slope, t);
+          over |= zs_transform_plane<OP>(a_ring + sa * a_entry + c * g.plane_bytes, g, aff + 64 * c, lazy_leaky,
+                                         w0, h0, a.slope, t);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
         __syncwarp();
@@ -1279,8 +1359,8 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           o.d0 = z;
           o.h0 = hb * kHaloH;
           o.w0 = wb * kHaloW;
-          epilogue_tile<BC, kOperandF16x2>(a, g, o, rp, acc, 0u, q, lane, red, col_mean, col_inv,
-                                           zs_stg + (warp - 2) * (kStagingBytes / 16), bar);
+          epilogue_tile<BC, OP>(a, g, o, rp, acc, 0u, q, lane, red, col_mean, col_inv,
+                                zs_stg + (warp - 2) * (kStagingBytes / 16), bar);
         }
         tmem_zero32(acc);
         fence_before();
@@ -1408,9 +1488,37 @@ __global__ void pack_f16x2_kernel(const float* __restrict__ w, int cols_total, i
   }
 }
 
+// bf16 image: 64-byte rows of bf16(w) (round to nearest even), SW64 like the fp16-pair image, BC rows per
+// K-step and no column scales (bf16 keeps float32's exponent range).
+__global__ void pack_bf16_kernel(const float* __restrict__ w, int cols_total, int kvol, int cin_total, int bc,
+                                 int nchunk, int row_taps, int up_cout, int64_t total_words,
+                                 uint32_t* __restrict__ out) {
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total_words;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int word = (int)(o % 16);  // 4-byte word (two bf16) within the 64-byte row (physical position)
+    int64_t r = o / 16;
+    const int n = (int)(r % bc);
+    r /= bc;
+    const int ks = (int)(r % ((int64_t)kvol * nchunk));
+    const int nt = (int)(r / ((int64_t)kvol * nchunk));
+    const int k = (((word >> 2) ^ ((n >> 1) & 3)) * 4 + (word & 3)) * 2;  // first of the word's two channels
+    const int col = nt * bc + n;
+    const int chunk = ks / kvol, tap = ks - chunk * kvol;
+    uint32_t res = 0;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int ci = chunk * BK + k + e;
+      float val = 0.f;
+      if (col < cols_total && ci < cin_total) val = weight_at(w, col, tap, ci, kvol, cin_total, row_taps, up_cout);
+      res |= (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(val)) << (16 * e);
+    }
+    out[o] = res;
+  }
+}
+
 // Bytes of one B tile (one K-step of BC columns) in the operand format.
 inline int b_tile_bytes(int op, int bc) {
-  return op == kOperandF16x2 ? 2 * bc * 64 : op == kOperandTf32x2 ? 2 * bc * 128 : bc * 128;
+  return op == kOperandF16x2 ? 2 * bc * 64 : op == kOperandBf16 ? bc * 64 : op == kOperandTf32x2 ? 2 * bc * 128 : bc * 128;
 }
 
 inline int pick_bc(int cols) {
@@ -1479,12 +1587,14 @@ inline bool plan_halo(const nnb_conv3d_args& a, Geometry& g, int halves, int bby
   return true;
 }
 
-// Z-streaming mode (fp16 pairs) when the layer is a 3x3x3, stride-1, padding-1
-// conv with <= 32 output channels over at least one 8-wide brick row, and the
-// A ring plus the weights (resident for one 32-channel chunk, else >= 2
-// streamed (chunk, ky) stages) fit the shared-memory budget.
+// Z-streaming mode (fp16 pairs, bf16 or TF32) when the layer is a 3x3x3,
+// stride-1, padding-1 conv with <= 32 output channels over at least one
+// 8-wide brick row, and the A ring plus the weights (resident for one
+// 32-channel chunk, else >= 2 streamed (chunk, ky) stages) fit the
+// shared-memory budget.
 inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
-  if (a.operand_format != 2 || op != kOperandF16x2 || pick_bc(a.cout) != 32) return false;
+  if (a.operand_format != 2 || pick_bc(a.cout) != 32) return false;
+  if (op != kOperandF16x2 && op != kOperandBf16 && op != kOperandTf32) return false;
   for (int i = 0; i < 3; ++i)
     if (a.kernel[i] != 3 || a.stride[i] != 1 || a.pad[i] != 1) return false;
   if (g.OW < kHaloW || g.OH < kHaloH / 2 || g.nchunk < 1) return false;
@@ -1494,7 +1604,7 @@ inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
   g.plane_bytes = (g.plane_rows * 128 + 1023) & ~1023;
   const int entry = g.nchunk * g.plane_bytes;
   const int budget = kMaxSmem - 1024 - kMiscBytes - 2 * g.nchunk * 64 * 4 - 8 * kStagingBytes;  // tables, staging
-  const int tap_bytes = kZsRows * 64;
+  const int tap_bytes = zs_tap_bytes(op);
   if (g.nchunk == 1 && 2 * entry + 9 * tap_bytes <= budget) {
     g.sb = 0;
     g.sa = std::min(4, (budget - 9 * tap_bytes) / entry);
@@ -1583,7 +1693,7 @@ inline int encode_operand(const nnb_segment& seg, int op, int batch, const Geome
   NNB_REQUIRE(fn != nullptr, "conv3d: cuTensorMapEncodeTiled is not available from the driver");
   // z-streaming mode loads the raw float32 activation, or a segment already prepared as fp16 pairs
   const bool raw = g.zs && !seg.prepared;
-  const bool f16 = op == kOperandF16x2 && !raw;
+  const bool f16 = half_rows(op) && !raw;  // 16-bit rows (fp16 pair or bf16), copied bit for bit
   const cuuint64_t inner = (cuuint64_t)(op == kOperandTf32 || raw ? 1 : 2) * seg.channels;
   const cuuint64_t esize = f16 ? 2 : 4;
   const cuuint64_t dims[5] = {inner, (cuuint64_t)g.IW, (cuuint64_t)g.IH, (cuuint64_t)g.ID, (cuuint64_t)batch};
@@ -1606,13 +1716,14 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   using C = Cfg<BC, OP>;
   int dev = 0;
   NNB_CUDA_CHECK(cudaGetDevice(&dev));
-  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, 1/2 halo TB 1/3, 3 zs)
-  const int bit = g.zs ? 8 : g.halo ? (g.tb == 3 ? 4 : 2) : 1;
+  static int configured[64] = {0};  // dynamic shared memory opt-in done (bit 0 box, 1/2 halo TB 1/3, 3+ zs per OP)
+  const int bit = g.zs ? (8 << OP) : g.halo ? (g.tb == 3 ? 4 : 2) : 1;
   if (dev >= 64 || !(configured[dev] & bit)) {
-    if (g.zs)
-      NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_zstream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kMaxSmem));
-    else if (g.halo && g.tb == 3)
+    if (g.zs) {
+      if constexpr (BC == 32 && (OP == kOperandF16x2 || OP == kOperandBf16 || OP == kOperandTf32))
+        NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_zstream_kernel<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kMaxSmem));
+    } else if (g.halo && g.tb == 3)
       NNB_CUDA_CHECK(cudaFuncSetAttribute(conv3d_halo_kernel<BC, OP, 3>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
     else if (g.halo)
@@ -1627,12 +1738,12 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   NNB_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::min(g.total_tiles, sms);
   if (g.zs) {
-    if constexpr (BC == 32 && OP == kOperandF16x2) {
-      const int b_bytes = g.sb == 0 ? 9 * kZsRows * 64 : g.sb * 3 * kZsRows * 64;
+    if constexpr (BC == 32 && (OP == kOperandF16x2 || OP == kOperandBf16 || OP == kOperandTf32)) {
+      const int b_bytes = g.sb == 0 ? 9 * zs_tap_bytes(OP) : g.sb * 3 * zs_tap_bytes(OP);
       const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes + 2 * g.nchunk * 64 * 4 +
                        8 * kStagingBytes;
       NNB_REQUIRE(smem <= kMaxSmem, "conv3d: z-streaming plan exceeds shared memory (%d bytes)", smem);
-      conv3d_zstream_kernel<<<grid, kZsThreads, smem, stream>>>(a, g, maps);
+      conv3d_zstream_kernel<OP><<<grid, kZsThreads, smem, stream>>>(a, g, maps);
     } else {
       NNB_REQUIRE(false, "conv3d: internal: z-streaming plan for an unsupported tile");
     }
@@ -1673,6 +1784,9 @@ int dispatch(const nnb_conv3d_args& a, Geometry& g, cudaStream_t stream) {
     case kOperandTf32x2 * 4 + 0: return launch_bc<32, kOperandTf32x2>(a, g, maps, stream);
     case kOperandTf32x2 * 4 + 1: return launch_bc<64, kOperandTf32x2>(a, g, maps, stream);
     case kOperandTf32x2 * 4 + 2: return launch_bc<128, kOperandTf32x2>(a, g, maps, stream);
+    case kOperandBf16 * 4 + 0: return launch_bc<32, kOperandBf16>(a, g, maps, stream);
+    case kOperandBf16 * 4 + 1: return launch_bc<64, kOperandBf16>(a, g, maps, stream);
+    case kOperandBf16 * 4 + 2: return launch_bc<128, kOperandBf16>(a, g, maps, stream);
     case kOperandTf32 * 4 + 0: return launch_bc<32, kOperandTf32>(a, g, maps, stream);
     case kOperandTf32 * 4 + 1: return launch_bc<64, kOperandTf32>(a, g, maps, stream);
     default: return launch_bc<128, kOperandTf32>(a, g, maps, stream);
@@ -1721,7 +1835,10 @@ int launch_conv3d_pack_rows(const float* w, int cols, int kvol, int cin_total, i
   const int64_t tile_bytes = (int64_t)n_tiles * kvol * nchunk * tc::b_tile_bytes(op, bc);
   const int64_t words = tile_bytes / 4;
   const int blocks = (int)std::min<int64_t>((words + 255) / 256, 148 * 32);
-  if (op == kOperandF16x2) {
+  if (op == kOperandBf16) {
+    tc::pack_bf16_kernel<<<blocks, 256, 0, stream>>>(w, cols, kvol, cin_total, bc, nchunk, row_taps, up_cout, words,
+                                                     reinterpret_cast<uint32_t*>(packed));
+  } else if (op == kOperandF16x2) {
     float* inv_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(packed) + tile_bytes);
     tc::column_scale_kernel<<<n_tiles * bc, 256, 0, stream>>>(w, cols, kvol, cin_total, row_taps, up_cout,
                                                                inv_scale);
@@ -1744,7 +1861,8 @@ int launch_conv3d_pack(const float* w, int cout, int kvol, int cin_total, int pr
 
 // Whether the tensor-core path reads raw lazy segments for these shapes (z-streaming mode).
 bool conv3d_tc_raw_operands(const nnb_conv3d_args& a) {
-  if (a.precision != NNB_PREC_FP32 || !(a.slope >= 0.f && a.slope <= 1.f)) return false;
+  if (a.precision != NNB_PREC_FP32 && a.precision != NNB_PREC_BF16 && a.precision != NNB_PREC_TF32) return false;
+  if (!(a.slope >= 0.f && a.slope <= 1.f)) return false;
   int cin_total = 0;
   for (int s = 0; s < a.num_segments; ++s) {
     if (a.seg[s].channels % tc::BK != 0) return false;
@@ -1810,7 +1928,8 @@ int launch_conv_transpose_tc(const nnb_segment& in, int batch, const int32_t in_
   g.UKW = k[2];
   g.up_operand = out_operand;
   if (out_operand) {
-    NNB_REQUIRE(precision == NNB_PREC_FP32, "conv_transpose3d: operand output needs NNB_PREC_FP32");
+    NNB_REQUIRE(precision == NNB_PREC_FP32 || precision == NNB_PREC_BF16 || precision == NNB_PREC_TF32,
+                "conv_transpose3d: operand output needs NNB_PREC_FP32, NNB_PREC_BF16 or NNB_PREC_TF32");
     g.range_events = operand_range_events_ptr();
     NNB_REQUIRE(g.range_events != nullptr, "conv_transpose3d: range-event counter unavailable");
   }

@@ -159,7 +159,7 @@ def _ptr(t: torch.Tensor | None) -> int:
 
 
 def _operand_floats(precision: int) -> int:
-    """32-bit words per channel of a prepared operand (fp16 pair: 1, TF32 pair: 2, TF32: 1)."""
+    """32-bit words per channel of a prepared operand (fp16 pair: 1, TF32 pair: 2, TF32: 1, bf16: 1)."""
     return 2 if precision == _native.PREC_FP32_TF32 else 1
 
 
@@ -199,26 +199,28 @@ class _Prepared(Lazy):
 
 
 class OperandOnly(Lazy):
-    """An activation that exists only as its fp32-mode tensor-core operand.
+    """An activation that exists only as its tensor-core operand for one precision.
 
-    ``raw`` is the fp16-pair operand buffer (4 bytes per channel, so it has the
-    activation's shape as float32 words) and is not a float32 activation:
-    ``segment()`` refuses, and only consumers that take the prepared operand
-    (tensor-core convolutions in ``PREC_FP32``) can read it.
+    ``raw`` is the operand buffer of ``precision`` (fp16 pair, bf16 or TF32: 4
+    bytes per channel, so it has the activation's shape as float32 words) and
+    is not a float32 activation: ``segment()`` refuses, and only consumers that
+    take the prepared operand (tensor-core convolutions in that precision) can
+    read it.
     """
 
-    def __init__(self, operand: torch.Tensor) -> None:
+    def __init__(self, operand: torch.Tensor, precision: int = _native.PREC_FP32) -> None:
         super().__init__(operand)
-        self.prepared[_native.PREC_FP32] = _Prepared(operand, int(operand.shape[-1]))
+        object.__setattr__(self, "precision", precision)
+        self.prepared[precision] = _Prepared(operand, int(operand.shape[-1]))
 
     def segment(self) -> _native.Segment:
-        raise ContractError("this activation exists only as a PREC_FP32 tensor-core operand")
+        raise ContractError(f"this activation exists only as a precision-{self.precision} tensor-core operand")
 
 
 def _query_segment(item: Lazy) -> _native.Segment:
     """The segment a shape query sees: an operand-only activation shows its prepared operand."""
     if isinstance(item, OperandOnly):
-        seg = item.prepared[_native.PREC_FP32].segment()
+        seg = item.prepared[item.precision].segment()
         seg.prepared = 1
         return seg
     return item.segment()
@@ -474,10 +476,11 @@ def conv_transpose3d_operand(x: Lazy, weight: torch.Tensor, bias: torch.Tensor |
                              slope: float = 0.01, packed: torch.Tensor | None = None,
                              precision: int = _native.PREC_SIMT) -> Lazy:
     """The up-sampled activation for the next convolution: an ``OperandOnly`` activation on the
-    fp32-mode tensor-core path (the transposed conv writes the fp16-pair operand itself, no
-    preparation pass), otherwise a plain ``Lazy`` of the float32 output."""
+    fp32, bf16 and tf32 tensor-core paths (the transposed conv writes the next convolution's
+    operand itself, no preparation pass), otherwise a plain ``Lazy`` of the float32 output."""
     cout = int(weight.shape[0])
-    if not (packed is not None and precision == _native.PREC_FP32 and x.channels % 32 == 0 and cout % 32 == 0):
+    if not (packed is not None and precision in _native.OPERAND_OUTPUT_PRECISIONS and x.channels % 32 == 0
+            and cout % 32 == 0):
         return Lazy(conv_transpose3d(x, weight, bias, kernel, slope, packed=packed, precision=precision))
     batch = int(x.raw.shape[0])
     out_dims = tuple(s * k for s, k in zip(x.spatial, kernel))
@@ -491,7 +494,7 @@ def conv_transpose3d_operand(x: Lazy, weight: torch.Tensor, bias: torch.Tensor |
         ctypes.byref(seg), batch, _native.dims3(x.spatial), _native.dims3(kernel), float(slope), _ptr(bias), cout,
         packed.data_ptr(), int(precision), out.data_ptr(), _stream()), "conv_transpose3d_operand")
     PROFILE.stop(token)
-    return OperandOnly(out)
+    return OperandOnly(out, precision)
 
 
 def residual_join(branch: Lazy, skip: Lazy, slope: float) -> torch.Tensor:

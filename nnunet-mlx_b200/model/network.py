@@ -45,7 +45,7 @@ from nnunet_mlx_b200.model.topology import NetworkSpec, PlainConvUNetSpec, Resid
 from nnunet_mlx_b200.storage.weights import validate_weights
 
 PRECISIONS = {"fp32": _native.PREC_FP32, "tf32": _native.PREC_TF32, "simt": _native.PREC_SIMT,
-              "fp32-tf32x2": _native.PREC_FP32_TF32}
+              "fp32-tf32x2": _native.PREC_FP32_TF32, "bf16": _native.PREC_BF16}
 # "fp32" runs split fp16 pairs, exact to float32 level while every activation stays below 65504 in
 # magnitude; a forward that met a larger one is recomputed in split TF32 (see range_fallback).
 RANGE_FALLBACK = {"fp32": "fp32-tf32x2"}
@@ -237,7 +237,7 @@ def _match_spatial(up: Lazy, skip: Lazy) -> Lazy:
             padded.narrow(axis + 1, before, raw.shape[axis + 1]).copy_(raw)
             raw = padded
     if isinstance(up, kernels.OperandOnly):
-        return kernels.OperandOnly(raw.contiguous())
+        return kernels.OperandOnly(raw.contiguous(), up.precision)
     return Lazy(raw.contiguous())
 
 

@@ -94,26 +94,26 @@ def validate_spacing(value: Sequence[float], *, name: str) -> tuple[float, float
 
 def separate_z_axis(current_spacing, new_spacing, *, force: bool | None,
                     threshold: float = ANISOTROPY_THRESHOLD) -> tuple[bool, int | None]:
-    """The unique coarsest axis to resample separately, if the policy asks for one.
+    """Whether one coarse axis is resampled on its own, and which (upstream nnU-Net's policy).
 
-    Reference ``data/resampling.py:587-616``: with ``force=None`` a max/min spacing
-    ratio above ``threshold`` (current spacing first, else target spacing) enables
-    it; ``force=True`` uses the current spacing; a tie for the coarsest axis disables it.
+    The spacing that decides is chosen first: with ``force=True`` the current
+    spacing, with ``force=False`` none; with ``force=None`` the first of the
+    current and the target spacing whose largest/smallest ratio exceeds
+    ``threshold``.  The separate axis is that spacing's unique coarsest axis; a
+    tie for the coarsest spacing means no separate axis (reference
+    ``data/resampling.py:587-616``, pinned against the reference's own decisions).
     """
+    def exceeds(spacing) -> bool:
+        return max(spacing) / min(spacing) > threshold
+
     if force is None:
-        current_anisotropic = max(current_spacing) / min(current_spacing) > threshold
-        separate = current_anisotropic or max(new_spacing) / min(new_spacing) > threshold
-        basis = current_spacing if current_anisotropic else new_spacing
+        deciding = next((sp for sp in (current_spacing, new_spacing) if exceeds(sp)), None)
     else:
-        separate = bool(force)
-        basis = current_spacing
-    if not separate:
+        deciding = current_spacing if force else None
+    if deciding is None:
         return False, None
-    largest = max(basis)
-    axes = tuple(i for i, s in enumerate(basis) if largest / s == 1)
-    if len(axes) != 1:
-        return False, None
-    return True, axes[0]
+    coarsest = [axis for axis, value in enumerate(deciding) if value == max(deciding)]
+    return (True, coarsest[0]) if len(coarsest) == 1 else (False, None)
 
 
 def _target_shape(new_shape: Sequence[int]) -> tuple[int, int, int]:

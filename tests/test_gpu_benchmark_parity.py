@@ -32,9 +32,10 @@ pytestmark = pytest.mark.gpu
 LOGIT_TOL = dict(rtol=1e-3, atol=1e-3)
 # Stated bounds of the single-pass modes on the benchmark networks (measured on B200 against the
 # float32 oracle; the figures each test prints are recorded in the design notes).
+# Measured: tf32 max|err| 0.014 (window) / 0.026 (ResEnc-L), argmax 99.85%; bf16 0.096 / 0.21, argmax 98.85%.
 LOOSE_BOUNDS = {
-    "tf32": {"max_abs": 0.5, "argmax": 0.97},
-    "bf16": {"max_abs": 2.0, "argmax": 0.90},
+    "tf32": {"max_abs": 0.1, "argmax": 0.995},
+    "bf16": {"max_abs": 0.5, "argmax": 0.98},
 }
 
 
@@ -136,7 +137,7 @@ def test_config2_window_matches_oracle(cuda_device, window2):
     assert (labels.cpu().numpy() == got.argmax(0)).all()
 
 
-@pytest.mark.parametrize("precision", ["tf32"])
+@pytest.mark.parametrize("precision", ["tf32", "bf16"])
 def test_loose_modes_config2_window(cuda_device, window2, precision):
     from nnunet_mlx_b200.prediction.sliding_window import predict_volume
 
@@ -146,7 +147,7 @@ def test_loose_modes_config2_window(cuda_device, window2, precision):
     assert_loose(logits.cpu().numpy(), ref, 0, precision, "config2 crop 8-view window")
 
 
-@pytest.mark.parametrize("precision", ["tf32"])
+@pytest.mark.parametrize("precision", ["tf32", "bf16"])
 def test_loose_modes_config5_forward(cuda_device, config5, precision):
     spec, weights, x, ref = config5
     got = _net(spec, weights, cuda_device, precision)(torch.from_numpy(x).to(cuda_device)).cpu().numpy()

@@ -188,7 +188,10 @@ def _conv_args(cins, cout, dims, kernel, stride, pad, precision):
     ((32,), 32, (16, 16, 16), (1, 3, 3), (1, 1, 1), (0, 1, 1), 0, 0),     # anisotropic kernel
     ((32,), 32, (16, 4, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 0),      # rows shorter than a brick
     ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 3, 0),     # split-TF32 fallback precision
-    ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 1, 0),     # TF32
+    ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 1, 1),     # TF32 z-streaming
+    ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 1),     # BF16 z-streaming
+    ((32, 32), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 1),  # BF16 concat, streamed weights
+    ((64,), 64, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 0),     # BF16, > 32 output channels
     ((16,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 0),     # channels not a multiple of 32
 ])
 def test_raw_operand_query(cins, cout, dims, kernel, stride, pad, precision, expect):

@@ -123,7 +123,7 @@ def test_rejections(tmp_path):
     torch.save({"network_weights": states[1], "init_args": {"configuration": "3d_fullres"},
                 "trainer_name": "nnUNetTrainer", "inference_allowed_mirroring_axes": (0, 1, 2),
                 "extra": ContractError("not allowed")}, folder / "fold_1" / "checkpoint_final.pth")
-    with pytest.raises(ContractError, match="cannot read"):
+    with pytest.raises(ContractError, match="unreadable"):
         upstream.load_upstream_checkpoint(folder / "fold_1" / "checkpoint_final.pth")
 
 
