@@ -106,6 +106,20 @@ def dominant_launch(trace):
     return detail, count, total_ms / count, flops
 
 
+def launch_table(trace, top: int = 10):
+    """Per convolution launch shape (and kernel): launches, mean CUDA-event ms and useful TFLOP/s, largest total first."""
+    groups = {}
+    for item in trace:
+        if item["name"] not in ("conv3d_tc", "conv_transpose3d_tc", "conv3d_simt"):
+            continue
+        g = groups.setdefault(item["detail"], [0, 0.0, item["flops"]])
+        g[0] += 1
+        g[1] += item["ms"]
+    rows = sorted(groups.items(), key=lambda kv: -kv[1][1])[:top]
+    return [{"launch": detail, "launches": n, "mean_ms": ms / n, "tflops": flops / (ms / n / 1e3) / 1e12}
+            for detail, (n, ms, flops) in rows]
+
+
 def forward_flops(spec, patch) -> float:
     """Algorithmic FLOPs (2 x MAC) of one network forward at ``patch`` (convs, transposed convs, seg head)."""
     from nnunet_mlx_b200.model.topology import ResidualEncoderUNetSpec
@@ -529,6 +543,7 @@ def main():
             "conv_tflops_effective": work["forwards"] * fwd * args.steps / elapsed / 1e12 / world,
             "roofline": roofline,
             "kernels": prof,
+            "conv_launches": launch_table(kernels.PROFILE.trace()),
             "clocks": clocks.summary(),
             "gpu_launches": kernels.PROFILE.launches,
             "e2e": e2e,

@@ -375,6 +375,19 @@ int32_t nnb_fold_add_fp16(const void* acc16, const void* normalizer16, int32_t c
                           void* total16, int32_t first_fold, int32_t* invalid_count, void* stream);
 
 /*
+ * nnunet-fp16 fold sum for folds computed on other devices: total16[i] =
+ * half(f32(total16[i]) + f32(part16[i])) over `elements` halves, where part16
+ * is one fold's normalised half logits (what nnb_fold_add_fp16 stores for a
+ * first fold) -- the same IEEE half add nnb_fold_add_fp16 performs for a later
+ * fold, so folds summed here in fold order give the single-device total bit
+ * for bit.  Non-finite sums add to *invalid_count (not reset).  Replaces the
+ * fold accumulation of src/nnunet_mlx/prediction/inference.py:75-85 when the
+ * folds run on several GPUs (the reference runs them on one device).
+ */
+int32_t nnb_fold_sum_fp16(void* total16, const void* part16, int64_t elements, int32_t* invalid_count,
+                          void* stream);
+
+/*
  * Fold average of the half total in place, half(f32(total) / folds), then
  * optional float32 channel-first logits of the half values and first-argmax
  * labels (1 or 2 bytes; all-ones for a voxel with a non-finite value, counted

@@ -146,6 +146,8 @@ SYMBOLS = {
                                                   ctypes.c_void_p]),
     "nnb_fold_add_fp16": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, I32x3, I32x3, I32x3,
                                            ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
+    "nnb_fold_sum_fp16": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                           ctypes.c_void_p]),
     "nnb_fold_finalize_fp16": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
                                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
                                                 ctypes.c_void_p]),

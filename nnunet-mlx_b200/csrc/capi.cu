@@ -55,6 +55,7 @@ int launch_accumulate_tile(const nnb_segment& feat, int views, const int32_t* ma
 int launch_fold_add_fp16(const void* acc, const void* normalizer, int classes, const int32_t ad[3],
                          const int32_t lo[3], const int32_t cd[3], void* total, int first, int32_t* invalid_count,
                          cudaStream_t stream);
+int launch_fold_sum_fp16(void* total, const void* part, int64_t n, int32_t* invalid_count, cudaStream_t stream);
 int launch_fold_finalize_fp16(void* total, int classes, int64_t vox, int folds, float* logits, void* labels,
                               int label_bytes, int32_t* invalid_count, cudaStream_t stream);
 int launch_normalize_labels(const float* acc, const float* normalizer, int classes, const int32_t ad[3],
@@ -329,6 +330,14 @@ int32_t nnb_fold_add_fp16(const void* acc16, const void* normalizer16, int32_t c
                 "fold_add_fp16: crop outside accumulator on axis %d", i);
   return launch_fold_add_fp16(acc16, normalizer16, classes, acc_dims, crop_lo, crop_dims, total16, first_fold,
                               invalid_count, (cudaStream_t)stream);
+}
+
+int32_t nnb_fold_sum_fp16(void* total16, const void* part16, int64_t elements, int32_t* invalid_count,
+                          void* stream) {
+  NNB_REQUIRE(total16 && part16 && invalid_count && elements >= 1, "fold_sum_fp16: bad arguments");
+  NNB_REQUIRE((reinterpret_cast<uintptr_t>(total16) & 1) == 0 && (reinterpret_cast<uintptr_t>(part16) & 1) == 0,
+              "fold_sum_fp16: half buffers must be 2-byte aligned");
+  return launch_fold_sum_fp16(total16, part16, elements, invalid_count, (cudaStream_t)stream);
 }
 
 int32_t nnb_fold_finalize_fp16(void* total16, int32_t classes, int64_t voxels, int32_t folds, float* logits,

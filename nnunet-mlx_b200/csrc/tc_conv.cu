@@ -1069,7 +1069,7 @@ __global__ void __launch_bounds__(kZsThreads, 1)
   constexpr uint32_t kBlkBytes = 32 * zs_row_bytes(OP);     // one kz block (32 B rows) of a part
   constexpr int kParts = OP == kOperandF16x2 ? 2 : 1;       // [W0 ; W1] or [W] per image tile
   const uint32_t b_stage = 3u * kTapBytes;                  // one (chunk, ky) row of taps
-  const uint32_t b_bytes = resident ? 9u * kTapBytes : (uint32_t)SB * b_stage;
+  const uint32_t b_bytes = resident ? (uint32_t)g.nchunk * 9u * kTapBytes : (uint32_t)SB * b_stage;
   uint8_t* a_ring = smem;
   uint8_t* b_ring = smem + SA * a_entry;
   const SharedMisc sm = shared_misc(b_ring + b_bytes);
@@ -1130,15 +1130,16 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     if (lane == 0) {
       bool alive = true;
       if (resident) {
-        // stacked rows of tap (ky, kx): [W0(kz0..2) ; W1(kz0..2)] (or [W(kz0..2)]), 32 rows each, from the
-        // image's [W0 ; W1] (or [W]) tile of tap (kz, ky, kx)
+        // per chunk, the stacked rows of tap (ky, kx): [W0(kz0..2) ; W1(kz0..2)] (or [W(kz0..2)]), 32 rows each,
+        // from the image's [W0 ; W1] (or [W]) tile of K-step (chunk, tap (kz, ky, kx))
         const uint32_t fb = smem_u32(&b_full[0]);
-        mbar_arrive_expect_tx(fb, 9u * kTapBytes);
-        for (int t = 0; t < 9; ++t)
-          for (int part = 0; part < kParts; ++part)
-            for (int kz = 0; kz < 3; ++kz)
-              bulk_g2s(smem_u32(b_ring + t * kTapBytes + (part * 3 + kz) * kBlkBytes),
-                       wimg + (int64_t)(kz * 9 + t) * C::kBBytes + part * kBlkBytes, kBlkBytes, fb);
+        mbar_arrive_expect_tx(fb, (uint32_t)g.nchunk * 9u * kTapBytes);
+        for (int c = 0; c < g.nchunk; ++c)
+          for (int t = 0; t < 9; ++t)
+            for (int part = 0; part < kParts; ++part)
+              for (int kz = 0; kz < 3; ++kz)
+                bulk_g2s(smem_u32(b_ring + (c * 9 + t) * kTapBytes + (part * 3 + kz) * kBlkBytes),
+                         wimg + (int64_t)(c * taps + kz * 9 + t) * C::kBBytes + part * kBlkBytes, kBlkBytes, fb);
       }
       int P = 0, T = 0;
       ZsRun run = zs_run(g);
@@ -1230,19 +1231,20 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           for (int c = 0; c < g.nchunk && alive; ++c) {
             const uint64_t ap = adesc0 + (uint64_t)(sa * entry16 + c * plane16);
             if (resident) {
+              const uint64_t bchunk = bdesc0 + (uint64_t)(c * 9) * kTap16;  // this chunk's resident taps
               // the wrap case is uniform per input plane: one straight-line row variant per case
               if (s0 <= kZsSlots - 3) {
 #pragma unroll 1
                 for (int ky = 0; ky < 3; ++ky)
-                  zs_row<OP, 3>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+                  zs_row<OP, 3>(tmem, dslot, ap + (uint64_t)(ky * row16), bchunk + (uint64_t)(ky * 3 * kTap16));
               } else if (s0 == kZsSlots - 2) {
 #pragma unroll 1
                 for (int ky = 0; ky < 3; ++ky)
-                  zs_row<OP, 2>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+                  zs_row<OP, 2>(tmem, dslot, ap + (uint64_t)(ky * row16), bchunk + (uint64_t)(ky * 3 * kTap16));
               } else {
 #pragma unroll 1
                 for (int ky = 0; ky < 3; ++ky)
-                  zs_row<OP, 1>(tmem, dslot, ap + (uint64_t)(ky * row16), bdesc0 + (uint64_t)(ky * 3 * kTap16));
+                  zs_row<OP, 1>(tmem, dslot, ap + (uint64_t)(ky * row16), bchunk + (uint64_t)(ky * 3 * kTap16));
               }
             } else {
               for (int ky = 0; ky < 3; ++ky) {
@@ -1605,9 +1607,10 @@ inline bool plan_zstream(const nnb_conv3d_args& a, Geometry& g, int op) {
   const int entry = g.nchunk * g.plane_bytes;
   const int budget = kMaxSmem - 1024 - kMiscBytes - 2 * g.nchunk * 64 * 4 - 8 * kStagingBytes;  // tables, staging
   const int tap_bytes = zs_tap_bytes(op);
-  if (g.nchunk == 1 && 2 * entry + 9 * tap_bytes <= budget) {
+  if (2 * entry + g.nchunk * 9 * tap_bytes <= budget) {
+    // every chunk's weights resident (one chunk of any format; two chunks of the bf16 format)
     g.sb = 0;
-    g.sa = std::min(4, (budget - 9 * tap_bytes) / entry);
+    g.sa = std::min(4, (budget - g.nchunk * 9 * tap_bytes) / entry);
   } else {
     g.sa = 2;
     g.sb = std::min(4, (budget - 2 * entry) / (3 * tap_bytes));
@@ -1739,7 +1742,7 @@ int launch_bc(const nnb_conv3d_args& a, const Geometry& g, const OperandMaps& ma
   const int grid = std::min(g.total_tiles, sms);
   if (g.zs) {
     if constexpr (BC == 32 && (OP == kOperandF16x2 || OP == kOperandBf16 || OP == kOperandTf32)) {
-      const int b_bytes = g.sb == 0 ? 9 * zs_tap_bytes(OP) : g.sb * 3 * zs_tap_bytes(OP);
+      const int b_bytes = g.sb == 0 ? g.nchunk * 9 * zs_tap_bytes(OP) : g.sb * 3 * zs_tap_bytes(OP);
       const int smem = 1024 + g.sa * g.nchunk * g.plane_bytes + b_bytes + kMiscBytes + 2 * g.nchunk * 64 * 4 +
                        8 * kStagingBytes;
       NNB_REQUIRE(smem <= kMaxSmem, "conv3d: z-streaming plan exceeds shared memory (%d bytes)", smem);

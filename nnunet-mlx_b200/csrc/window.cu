@@ -40,31 +40,37 @@ struct ItemTable {
 
 __global__ void gather_tiles_kernel(const float* __restrict__ vol, int cin, Dims3 vd, Dims3 pad_lo, Dims3 patch,
                                     int items, ItemTable tab, float* __restrict__ out, int* __restrict__ nonfinite) {
-  const int64_t pvox = (int64_t)patch.d[0] * patch.d[1] * patch.d[2];
-  const int64_t total = pvox * items;
+  // one warp per output row (item t, i, j): the row's source row and flips are resolved once, lanes walk k
+  const int64_t rows = (int64_t)items * patch.d[0] * patch.d[1];
   const int64_t vstride = (int64_t)vd.d[0] * vd.d[1] * vd.d[2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   bool bad = false;
-  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(o / pvox);
-    const int64_t p = o - (int64_t)t * pvox;
-    const int k = (int)(p % patch.d[2]);
-    const int j = (int)((p / patch.d[2]) % patch.d[1]);
-    const int i = (int)(p / ((int64_t)patch.d[2] * patch.d[1]));
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const int j = (int)(r % patch.d[1]);
+    const int64_t ti = r / patch.d[1];
+    const int i = (int)(ti % patch.d[0]);
+    const int t = (int)(ti / patch.d[0]);
     const int mask = tab.mask[t];
     const int z = tab.off[t][0] + ((mask & 1) ? patch.d[0] - 1 - i : i) - pad_lo.d[0];
     const int y = tab.off[t][1] + ((mask & 2) ? patch.d[1] - 1 - j : j) - pad_lo.d[1];
-    const int x = tab.off[t][2] + ((mask & 4) ? patch.d[2] - 1 - k : k) - pad_lo.d[2];
-    float* dst = out + o * cin;
-    if ((unsigned)z >= (unsigned)vd.d[0] || (unsigned)y >= (unsigned)vd.d[1] || (unsigned)x >= (unsigned)vd.d[2]) {
-      for (int c = 0; c < cin; ++c) dst[c] = 0.f;
-      continue;
-    }
-    const int64_t src = ((int64_t)z * vd.d[1] + y) * vd.d[2] + x;
-    for (int c = 0; c < cin; ++c) {
-      const float v = __ldg(vol + (int64_t)c * vstride + src);
-      bad |= !isfinite(v);
-      dst[c] = v;
+    const bool row_in = (unsigned)z < (unsigned)vd.d[0] && (unsigned)y < (unsigned)vd.d[1];
+    const int64_t src_row = row_in ? ((int64_t)z * vd.d[1] + y) * vd.d[2] : 0;
+    const int x0 = tab.off[t][2] - pad_lo.d[2];
+    const bool flip_x = (mask & 4) != 0;
+    float* dst_row = out + r * patch.d[2] * cin;
+    for (int k = lane; k < patch.d[2]; k += 32) {
+      const int x = x0 + (flip_x ? patch.d[2] - 1 - k : k);
+      float* dst = dst_row + (int64_t)k * cin;
+      if (!row_in || (unsigned)x >= (unsigned)vd.d[2]) {
+        for (int c = 0; c < cin; ++c) dst[c] = 0.f;
+        continue;
+      }
+      for (int c = 0; c < cin; ++c) {
+        const float v = __ldg(vol + (int64_t)c * vstride + src_row + x);
+        bad |= !isfinite(v);
+        dst[c] = v;
+      }
     }
   }
   if (bad && nonfinite != nullptr) atomicAdd(nonfinite, 1);
@@ -86,8 +92,8 @@ int launch_gather_tiles(const float* vol, int cin, const int32_t vd[3], const in
     }
   }
   Dims3 dvd{{vd[0], vd[1], vd[2]}}, dpad{{pad_lo[0], pad_lo[1], pad_lo[2]}}, dp{{patch[0], patch[1], patch[2]}};
-  const int64_t total = (int64_t)patch[0] * patch[1] * patch[2] * items;
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  const int64_t rows = (int64_t)patch[0] * patch[1] * items;
+  const int blocks = (int)std::min<int64_t>((rows + 7) / 8, 148 * 32);  // 8 warps (rows) per block
   gather_tiles_kernel<<<blocks, 256, 0, stream>>>(vol, cin, dvd, dpad, dp, items, tab, out, nonfinite);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
@@ -404,32 +410,38 @@ __global__ void normalize_labels_kernel(const float* __restrict__ acc, const flo
                                         int classes, Dims3 ad, Dims3 lo, Dims3 cd, float fold_divisor,
                                         float* __restrict__ logits, LabelT* __restrict__ labels,
                                         int* __restrict__ invalid_count, LabelT invalid_label) {
+  // one warp per output row (z, y) of the crop: the row's source offset is computed once, lanes walk x
   const int64_t total = (int64_t)cd.d[0] * cd.d[1] * cd.d[2];
+  const int64_t rows = (int64_t)cd.d[0] * cd.d[1];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   int local_invalid = 0;
-  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
-       o += (int64_t)gridDim.x * blockDim.x) {
-    const int x = (int)(o % cd.d[2]);
-    const int y = (int)((o / cd.d[2]) % cd.d[1]);
-    const int z = (int)(o / ((int64_t)cd.d[2] * cd.d[1]));
-    const int64_t src = ((int64_t)(lo.d[0] + z) * ad.d[1] + (lo.d[1] + y)) * ad.d[2] + (lo.d[2] + x);
-    const float den = __ldg(normalizer + src);
-    bool invalid = !isfinite(den) || den <= 0.f;
-    float best = -INFINITY;
-    int winner = 0;
-    bool have = false;
-    for (int c = 0; c < classes; ++c) {
-      float q = __ldg(acc + src * classes + c) / den;
-      if (fold_divisor != 1.0f) q = q / fold_divisor;
-      invalid |= !isfinite(q);
-      if (logits != nullptr) logits[(int64_t)c * total + o] = q;
-      if (!have || q > best) {
-        best = q;
-        winner = c;
-        have = true;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const int z = (int)(r / cd.d[1]), y = (int)(r - (int64_t)z * cd.d[1]);
+    const int64_t src_row = ((int64_t)(lo.d[0] + z) * ad.d[1] + (lo.d[1] + y)) * ad.d[2] + lo.d[2];
+    const int64_t out_row = r * cd.d[2];
+    for (int x = lane; x < cd.d[2]; x += 32) {
+      const int64_t src = src_row + x, o = out_row + x;
+      const float den = __ldg(normalizer + src);
+      bool invalid = !isfinite(den) || den <= 0.f;
+      float best = -INFINITY;
+      int winner = 0;
+      bool have = false;
+      const float* a = acc + src * classes;
+      for (int c = 0; c < classes; ++c) {
+        float q = __ldg(a + c) / den;
+        if (fold_divisor != 1.0f) q = q / fold_divisor;
+        invalid |= !isfinite(q);
+        if (logits != nullptr) logits[(int64_t)c * total + o] = q;
+        if (!have || q > best) {
+          best = q;
+          winner = c;
+          have = true;
+        }
       }
+      if (labels != nullptr) labels[o] = invalid ? invalid_label : (LabelT)winner;
+      local_invalid += invalid ? 1 : 0;
     }
-    if (labels != nullptr) labels[o] = invalid ? invalid_label : (LabelT)winner;
-    local_invalid += invalid ? 1 : 0;
   }
   if (local_invalid) atomicAdd(invalid_count, local_invalid);
 }
@@ -438,8 +450,8 @@ int launch_normalize_labels(const float* acc, const float* normalizer, int class
                             const int32_t lo[3], const int32_t cd[3], float fold_divisor, float* logits,
                             void* labels, int label_bytes, int32_t* invalid_count, cudaStream_t stream) {
   Dims3 dad{{ad[0], ad[1], ad[2]}}, dlo{{lo[0], lo[1], lo[2]}}, dcd{{cd[0], cd[1], cd[2]}};
-  const int64_t total = (int64_t)cd[0] * cd[1] * cd[2];
-  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  const int64_t rows = (int64_t)cd[0] * cd[1];
+  const int blocks = (int)std::min<int64_t>((rows + 7) / 8, 148 * 16);  // 8 warps (rows) per block
   NNB_CUDA_CHECK(cudaMemsetAsync(invalid_count, 0, sizeof(int32_t), stream));
   if (label_bytes == 1) {
     NNB_REQUIRE(classes <= 255, "normalize_labels: uint8 labels need <= 255 classes");
@@ -519,6 +531,29 @@ __global__ void fold_finalize_fp16_kernel(__half* __restrict__ total, int classe
     local_invalid += invalid ? 1 : 0;
   }
   if (local_invalid) atomicAdd(invalid_count, local_invalid);
+}
+
+// One fold's normalised half logits (channel-first, as fold_add_fp16 stored them for a first fold) added into
+// the half total in fold order: total = half(f32(total) + f32(part)) -- the same IEEE half add fold_add_fp16
+// performs for a later fold, for folds computed on other devices.  Non-finite sums are counted.
+__global__ void fold_sum_fp16_kernel(__half* __restrict__ total, const __half* __restrict__ part, int64_t n,
+                                     int* __restrict__ invalid_count) {
+  int local_invalid = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = __half2float(total[i]) + __half2float(part[i]);
+    const __half h = __float2half_rn(v);
+    local_invalid += isfinite(__half2float(h)) ? 0 : 1;
+    total[i] = h;
+  }
+  if (local_invalid) atomicAdd(invalid_count, local_invalid);
+}
+
+int launch_fold_sum_fp16(void* total, const void* part, int64_t n, int32_t* invalid_count, cudaStream_t stream) {
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  fold_sum_fp16_kernel<<<blocks, 256, 0, stream>>>(static_cast<__half*>(total), static_cast<const __half*>(part), n,
+                                                   invalid_count);
+  NNB_LAUNCH_CHECK();
+  return NNB_OK;
 }
 
 int launch_fold_add_fp16(const void* acc, const void* normalizer, int classes, const int32_t ad[3],

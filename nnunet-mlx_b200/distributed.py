@@ -24,6 +24,13 @@ independent (reference ``prediction/inference.py:65-85``).  So:
 A tile whose views are split across ranks sums its view groups separately,
 so its float32 rounding differs from the single-device order (the check in
 ``bench.py`` and the 2-GPU test bound the difference).
+
+The nnunet-fp16 accumulation mode (``predict_volume_fp16_sharded``) depends on
+the order of its float16 roundings, so it shards whole folds instead: each
+rank runs its folds' float16 windows and normalises each to its float16 crop
+exactly as one device does; the folds' halves are broadcast and summed in
+fold order on every rank (the same half adds), which gives the single-device
+result bit for bit.
 """
 
 from __future__ import annotations
@@ -35,6 +42,8 @@ from nnunet_mlx_b200 import kernels
 from nnunet_mlx_b200.errors import ContractError
 from nnunet_mlx_b200.prediction.sliding_window import (
     VolumeAccumulator,
+    fold_window_fp16,
+    fp16_gaussian,
     mirror_masks,
     pad_minimum,
     tile_offsets,
@@ -210,3 +219,115 @@ def predict_volume_sharded(models, volume: torch.Tensor, *, patch_size, num_clas
                                                        fold_divisor=float(len(models)), want_logits=want_logits,
                                                        label_dtype=label_dtype)
     return lo - c0, hi - c0, logits, labels, invalid
+
+
+# ---------------------------------------------------------------------------- nnunet-fp16 across GPUs
+def shard_folds(n_folds: int, rank: int, world: int) -> range:
+    """Contiguous folds of one rank (``[r*F/N, (r+1)*F/N)``; a rank may get none)."""
+    if world < 1 or not 0 <= rank < world or n_folds < 1:
+        raise ContractError(f"invalid fold sharding: {n_folds} folds, rank {rank} of {world}")
+    return range(rank * n_folds // world, (rank + 1) * n_folds // world)
+
+
+def fold_owner(fold: int, n_folds: int, world: int) -> int:
+    """The rank whose ``shard_folds`` holds ``fold``."""
+    for rank in range(world):
+        if fold in shard_folds(n_folds, rank, world):
+            return rank
+    raise ContractError(f"fold {fold} is outside 0..{n_folds - 1}")
+
+
+def ordered_fold_sum(n_folds: int, mine: dict, fetch, add):
+    """Sum fold parts in fold order: ``total = part_0``, then ``add(total, part_f)`` for f = 1..F-1.
+
+    ``mine``: this rank's parts by fold; ``fetch(fold, part_or_None)`` returns
+    the fold's part on every rank (a broadcast from its owner); ``add`` adds a
+    part into the total in place.
+    """
+    total = None
+    for fold in range(n_folds):
+        part = fetch(fold, mine.get(fold))
+        if total is None:
+            total = part
+        else:
+            add(total, part)
+    return total
+
+
+def predict_volume_fp16_sharded(models, volume: torch.Tensor, *, patch_size, num_classes: int, mirroring_axes=(),
+                                step_fraction: float = 0.5, group=None, want_logits: bool = True,
+                                label_dtype=torch.uint8, half_logits: bool = False):
+    """nnunet-fp16 fold ensemble of a device volume ``(C, *spatial)`` present on every rank, folds sharded.
+
+    Bit for bit the single-device ``predict_volume(..., accumulation="nnunet-fp16")`` result.  Returns
+    ``(logits, labels)`` on rank 0 (logits as float32 values of the halves, or the float16 total with
+    ``half_logits``) and ``(None, None)`` on the other ranks.
+    """
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    patch, axes = validate_request(tuple(volume.shape), None, patch_size, num_classes, mirroring_axes)
+    if volume.dtype != torch.float32 or not volume.is_cuda:
+        raise ContractError("expected a float32 CUDA (C, *spatial) volume")
+    if not models:
+        raise ContractError("fold inference requires at least one model")
+    volume = volume.contiguous()
+    device = volume.device
+    pads, crop = pad_minimum(tuple(volume.shape[1:]), patch)
+    pad_lo = tuple(a for a, _ in pads)
+    spatial = tuple(int(s) + a + b for s, (a, b) in zip(volume.shape[1:], pads))
+    lo = [c.start for c in crop]
+    dims = [c.stop - c.start for c in crop]
+    offsets = tile_offsets(spatial, patch, step_fraction)
+    masks = mirror_masks(axes)
+    n_folds = len(models)
+    mine_folds = shard_folds(n_folds, rank, world)
+    gaussian = fp16_gaussian(patch, device)
+    invalid = torch.zeros((1,), dtype=torch.int32, device=device)
+    nonfinite = torch.zeros((1,), dtype=torch.int32, device=device)
+
+    def run(ms):
+        parts = {}
+        if len(mine_folds):
+            acc = torch.empty((*spatial, num_classes), dtype=torch.float16, device=device)
+            normalizer = torch.empty(spatial, dtype=torch.float16, device=device)
+            batch = None
+            for fold in mine_folds:
+                batch = fold_window_fp16(ms[fold], volume, offsets, patch, masks, gaussian, acc, normalizer, pad_lo,
+                                         nonfinite, batch)
+                part = torch.empty((num_classes, *dims), dtype=torch.float16, device=device)
+                kernels.fold_add_fp16(acc, normalizer, lo, dims, part, True, invalid)
+                parts[fold] = part
+        return parts
+
+    guarded = any(getattr(m, "range_guarded", False) for m in models)
+    if guarded:
+        kernels.operand_range_events(reset=True)
+    parts = run(models)
+    out_of_range = guarded and kernels.operand_range_events(reset=True) > 0
+    bad_input, out_of_range = _any_rank([int(nonfinite.item()) != 0, out_of_range], device, world, group)
+    if bad_input:
+        raise ContractError("expected finite float32 (C, *spatial) input")
+    if out_of_range:
+        parts = run([m.range_fallback() for m in models])
+
+    def fetch(fold, part):
+        if world == 1:
+            return part
+        owner = fold_owner(fold, n_folds, world)
+        buf = part if owner == rank else torch.empty((num_classes, *dims), dtype=torch.float16, device=device)
+        src = owner if group is None else dist.get_global_rank(group, owner)
+        dist.broadcast(buf, src=src, group=group)
+        return buf
+
+    total = ordered_fold_sum(n_folds, parts, fetch, lambda t, p: kernels.fold_sum_fp16(t, p, invalid))
+    if _any_rank(int(invalid.item()) != 0, device, world, group):
+        raise ContractError("sliding-window inference produced non-finite logits")
+    if rank != 0:
+        return None, None
+    logits, labels, bad = kernels.fold_finalize_fp16(total, n_folds, want_logits=want_logits and not half_logits,
+                                                     label_dtype=label_dtype)
+    if int(bad.item()) != 0:
+        raise ContractError("fold averaging produced non-finite logits")
+    if half_logits and want_logits:
+        logits = total
+    return logits, labels

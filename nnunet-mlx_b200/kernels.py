@@ -629,6 +629,17 @@ def fold_add_fp16(acc16: torch.Tensor, normalizer16: torch.Tensor, crop_lo, crop
     PROFILE.stop(token)
 
 
+def fold_sum_fp16(total16: torch.Tensor, part16: torch.Tensor, invalid: torch.Tensor) -> None:
+    """nnunet-fp16: ``total16 = half(total16 + part16)`` element-wise (a fold computed on another device)."""
+    if (total16.dtype != torch.float16 or part16.dtype != torch.float16 or total16.shape != part16.shape
+            or not total16.is_contiguous() or not part16.is_contiguous()):
+        raise ContractError("fold sum needs contiguous float16 tensors of one shape")
+    token = PROFILE.start("fold_sum_fp16", 0.0, 6.0 * total16.numel())
+    _native.check(_native.load().nnb_fold_sum_fp16(total16.data_ptr(), part16.data_ptr(), total16.numel(),
+                                                   invalid.data_ptr(), _stream()), "fold_sum_fp16")
+    PROFILE.stop(token)
+
+
 def fold_finalize_fp16(total16: torch.Tensor, folds: int, *, want_logits: bool = True,
                        label_dtype: torch.dtype | None = torch.uint8):
     """Fold average of the half total (in place); float32 logits of the half values, labels, invalid count."""

@@ -48,7 +48,7 @@ def time_forward(config: int, precision: str, batch: int, patch: int, warmup: in
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("--config", type=int, default=2)
-    p.add_argument("--precision", choices=["fp32", "fp32-tf32x2", "tf32"], default="fp32")
+    p.add_argument("--precision", choices=["fp32", "fp32-tf32x2", "tf32", "bf16"], default="fp32")
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--patch", type=int, default=128)
     p.add_argument("--warmup", type=int, default=2)

@@ -251,11 +251,31 @@ def predict_volume(models, data, *, patch_size, num_classes: int, mirroring_axes
     return logits, labels
 
 
+def fold_window_fp16(model, volume, offsets, patch, masks, gaussian, acc, normalizer, pad_lo=(0, 0, 0),
+                     nonfinite=None, batch=None):
+    """One fold's float16 window + normaliser over every tile (nnunet-fp16; ``acc`` / ``normalizer`` are zeroed
+    first).  Returns the reusable gather buffer."""
+    acc.zero_()
+    normalizer.zero_()
+    for offset in offsets:
+        batch = kernels.gather_tiles(volume, pad_lo, [(offset, m) for m in masks], patch, out=batch,
+                                     nonfinite=nonfinite)
+        features = model.forward_features(batch)
+        kernels.accumulate_tile(features, masks, model.seg_weight, model.seg_bias, gaussian, acc, normalizer, offset,
+                                add_normalizer=True, slope=model.spec.leaky_slope)
+        del features
+    return batch
+
+
+def fp16_gaussian(patch, device) -> torch.Tensor:
+    return torch.from_numpy(nnunet_fp16_gaussian(tuple(patch)).astype(np.float32)).to(device)
+
+
 def _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, step_fraction, lo, dims, want_logits,
                          label_dtype, half_logits, pad_lo=(0, 0, 0), nonfinite=None):
     """nnunet-fp16: per fold a float16 window + normaliser, normalised to float16 and summed in fold order."""
     device = volume.device
-    gaussian = torch.from_numpy(nnunet_fp16_gaussian(tuple(patch)).astype(np.float32)).to(device)
+    gaussian = fp16_gaussian(patch, device)
     offsets = tile_offsets(spatial, patch, step_fraction)
     total = torch.empty((num_classes, *dims), dtype=torch.float16, device=device)
     invalid = torch.zeros((1,), dtype=torch.int32, device=device)
@@ -263,15 +283,8 @@ def _predict_volume_fp16(models, volume, spatial, num_classes, patch, masks, ste
     normalizer = torch.empty(spatial, dtype=torch.float16, device=device)
     batch = None
     for index, model in enumerate(models):
-        acc.zero_()
-        normalizer.zero_()
-        for offset in offsets:
-            batch = kernels.gather_tiles(volume, pad_lo, [(offset, m) for m in masks], patch, out=batch,
-                                         nonfinite=nonfinite if index == 0 else None)
-            features = model.forward_features(batch)
-            kernels.accumulate_tile(features, masks, model.seg_weight, model.seg_bias, gaussian, acc, normalizer,
-                                    offset, add_normalizer=True, slope=model.spec.leaky_slope)
-            del features
+        batch = fold_window_fp16(model, volume, offsets, patch, masks, gaussian, acc, normalizer, pad_lo,
+                                 nonfinite if index == 0 else None, batch)
         kernels.fold_add_fp16(acc, normalizer, lo, dims, total, index == 0, invalid)
     if nonfinite is not None and int(nonfinite.item()) != 0:
         raise ContractError("expected finite float32 (C, *spatial) input")

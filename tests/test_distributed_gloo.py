@@ -119,3 +119,45 @@ def _any_rank_worker(rank: int, world: int, port: int, flagged: tuple) -> None:
 def test_range_flag_is_or_reduced_over_ranks(world, flagged):
     """Every rank recomputes in split TF32 when any rank met an out-of-range operand."""
     mp.spawn(_any_rank_worker, args=(world, _free_port(), flagged), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("folds,world", [(5, 8), (5, 2), (5, 3), (1, 2), (3, 3)])
+def test_shard_folds_partition_in_order(folds, world):
+    from nnunet_mlx_b200.distributed import fold_owner, shard_folds
+
+    shards = [list(shard_folds(folds, r, world)) for r in range(world)]
+    assert [f for s in shards for f in s] == list(range(folds))
+    assert all(fold_owner(f, folds, world) == r for r, s in enumerate(shards) for f in s)
+
+
+def _fold_sum_worker(rank: int, world: int, port: int, folds: int) -> None:
+    from nnunet_mlx_b200.distributed import fold_owner, ordered_fold_sum, shard_folds
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        def part(fold):
+            rng = np.random.default_rng(40 + fold)
+            return torch.from_numpy(rng.normal(scale=30.0, size=(2, 5, 7)).astype(np.float16))
+
+        def half_add(total, p):
+            total.copy_((total.float() + p.float()).half())
+
+        def fetch(fold, mine):
+            buf = mine if mine is not None else torch.empty((2, 5, 7), dtype=torch.float16)
+            dist.broadcast(buf, src=fold_owner(fold, folds, world))
+            return buf
+
+        mine = {f: part(f) for f in shard_folds(folds, rank, world)}
+        got = ordered_fold_sum(folds, mine, fetch, half_add)
+        expect = part(0).clone()
+        for f in range(1, folds):
+            half_add(expect, part(f))
+        assert torch.equal(got, expect)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,folds", [(2, 5), (3, 5), (2, 1)])
+def test_fold_parts_are_summed_in_fold_order_across_ranks(world, folds):
+    """The fold-sharded nnunet-fp16 sum equals the single-device half sum bit for bit (CPU half adds here)."""
+    mp.spawn(_fold_sum_worker, args=(world, _free_port(), folds), nprocs=world, join=True)

@@ -1,9 +1,10 @@
 """Sharded sliding window on 2 GPUs (NCCL): every rank's z-slab equals the single-device result.
 
 Runs only when at least two CUDA devices are visible; each rank is a spawned
-process bound to its own GPU.  Units (tile, fold) are split across the ranks and
-one reduce-scatter sums the accumulators, so the float32 sums differ from the
-single-device order by rounding only.
+process bound to its own GPU.  (fold, tile, view) units are split across the
+ranks and reduce-scatters sum the accumulators, so the float32 sums differ
+from the single-device order by rounding only.  The nnunet-fp16 mode shards
+whole folds and must equal the single-device result bit for bit.
 """
 
 from __future__ import annotations
@@ -66,6 +67,18 @@ def _worker(rank: int, world: int, port: int) -> None:
                                        atol=1e-5)
             agree = (labels.cpu().numpy() == ref_labels[lo:hi].cpu().numpy()).mean()
             assert agree >= 0.9995, agree
+        # nnunet-fp16: whole folds per rank, bitwise the single-device fold ensemble
+        from nnunet_mlx_b200.distributed import predict_volume_fp16_sharded
+
+        half, half_labels = predict_volume_fp16_sharded(models, volume, patch_size=(16, 16, 16), num_classes=3,
+                                                        mirroring_axes=(0, 1, 2))
+        ref_half, ref_half_labels = predict_volume(models, data, patch_size=(16, 16, 16), num_classes=3,
+                                                   mirroring_axes=(0, 1, 2), device=device,
+                                                   accumulation="nnunet-fp16")
+        if rank == 0:
+            assert torch.equal(half, ref_half) and torch.equal(half_labels, ref_half_labels)
+        else:
+            assert half is None and half_labels is None
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -190,7 +190,7 @@ def _conv_args(cins, cout, dims, kernel, stride, pad, precision):
     ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 3, 0),     # split-TF32 fallback precision
     ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 1, 1),     # TF32 z-streaming
     ((32,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 1),     # BF16 z-streaming
-    ((32, 32), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 1),  # BF16 concat, streamed weights
+    ((32, 32), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 1),  # BF16 concat, resident weights
     ((64,), 64, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 4, 0),     # BF16, > 32 output channels
     ((16,), 32, (16, 16, 16), (3, 3, 3), (1, 1, 1), (1, 1, 1), 0, 0),     # channels not a multiple of 32
 ])
