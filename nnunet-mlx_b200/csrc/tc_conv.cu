@@ -83,7 +83,7 @@ __device__ int g_device_status_where = 0;
 namespace nnb {
 namespace tc {
 
-constexpr int kMiscBytes = 2048;  // mbarriers, TMEM slot, flags, epilogue reduction scratch
+constexpr int kMiscBytes = 2048;  // mbarriers, TMEM slot, flags, stop votes
 constexpr int kMaxBars = 48;
 constexpr int kStagingBytes = 2048;  // per epilogue warp: 16 output rows of 32 floats (coalesced stores)
 constexpr int kStageBudget = kMaxSmem - 1024 /*alignment slack*/ - kMiscBytes - 4 * kMaxKsteps - 8 * kStagingBytes;
@@ -234,12 +234,8 @@ struct SharedMisc {
   uint64_t* bars;
   uint32_t* tmem_slot;
   volatile int* abort_flag;
-  volatile int* votes;  // [4]
-  float* red;           // [4][32]
-  float* col_mean;      // [32]
-  volatile int* votes2;  // second epilogue group (z-streaming mode): [4], [4][32], [32]
-  float* red2;
-  float* col_mean2;
+  volatile int* votes;   // [4] stop votes of the first epilogue group
+  volatile int* votes2;  // [4] of the second epilogue group
 };
 
 __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
@@ -248,10 +244,6 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
   m.tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * kMaxBars);
   m.abort_flag = reinterpret_cast<volatile int*>(m.tmem_slot + 1);
   m.votes = reinterpret_cast<volatile int*>(m.tmem_slot + 2);
-  m.red = reinterpret_cast<float*>(misc + 512);
-  m.col_mean = reinterpret_cast<float*>(misc + 1024);
-  m.red2 = reinterpret_cast<float*>(misc + 1152);
-  m.col_mean2 = reinterpret_cast<float*>(misc + 1664);
   m.votes2 = reinterpret_cast<volatile int*>(misc + 1792);
   return m;
 }
@@ -260,8 +252,14 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
 // shared staging buffer 16 at a time (16-byte chunks XOR-swizzled by row % 8) and every store
 // instruction then writes four whole 128-byte rows, instead of one 16-byte piece of 32 rows.  dst: this
 // lane's row destination (16-byte aligned), or nullptr to skip the row.  All 32 lanes must call it.
-__device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const float (&v)[32], float* dst) {
+// kStats: while the rows are staged, lane c also reads column c of each staged row and accumulates, over
+// the rows whose bit is set in vmask, the deviations from `shift` (the value of row 0): s += d, s2 += d^2.
+template <bool kStats = false>
+__device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const float (&v)[32], float* dst,
+                                                  unsigned vmask = 0u, float* shift = nullptr, float* s = nullptr,
+                                                  float* s2 = nullptr) {
   const unsigned long long d = reinterpret_cast<unsigned long long>(dst);
+  const float* f = reinterpret_cast<const float*>(stg);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     if ((lane >> 4) == half) {
@@ -278,6 +276,20 @@ __device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const f
       const unsigned long long rd = __shfl_sync(0xffffffffu, d, half * 16 + r);
       const float4 val = stg[r * 8 + (c ^ (r & 7))];
       if (rd != 0ull) reinterpret_cast<float4*>(rd)[c] = val;
+    }
+    if constexpr (kStats) {
+      // column `lane` of staged row r: word 4 ((lane / 4) ^ (r % 8)) + lane % 4 of the row (conflict-free)
+      float acc = 0.f, acc2 = 0.f;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const float x = f[r * 32 + ((((lane >> 2) ^ (r & 7))) << 2) + (lane & 3)];
+        if (half == 0 && r == 0) *shift = x;
+        const float dv = (vmask >> (half * 16 + r)) & 1u ? x - *shift : 0.f;
+        acc += dv;
+        acc2 = fmaf(dv, dv, acc2);
+      }
+      *s += acc;
+      *s2 += acc2;
     }
     __syncwarp();
   }
@@ -301,16 +313,19 @@ __device__ __forceinline__ RowPos row_pos(const Geometry& g, int q, int lane) {
 // acc: TMEM address of the tile's (hi) accumulator columns for this warp's lanes; acc_lo: of the second
 // accumulator of the split formats, or 0 when one accumulator holds every product (z-streaming mode).
 // bar: named barrier of the four epilogue warps working on this tile; stg: this warp's staging buffer.
+// stg_group: the staging buffers of the four warps of this epilogue group (2 KB each, in group order);
+// widx: this warp's index in the group (the buffer it stages rows in).
 template <int BC, int OP>
 __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Geometry& g, const TileOrigin& o,
-                                              const RowPos& rp, uint32_t acc, uint32_t acc_lo, int q, int lane,
-                                              float* red, float* col_mean, const float* __restrict__ col_inv,
-                                              float4* stg, int bar = 1) {
+                                              const RowPos& rp, uint32_t acc, uint32_t acc_lo, int lane,
+                                              const float* __restrict__ col_inv, float4* stg_group, int widx,
+                                              int bar = 1) {
+  float4* stg = stg_group + widx * (kStagingBytes / 16);
   const int z = o.d0 + rp.dz, y = o.h0 + rp.dy, x = o.w0 + rp.dx;
   const bool valid = rp.row < g.rows && z < g.OD && y < g.OH && x < g.OW;
   const int64_t ovox = (int64_t)g.OD * g.OH * g.OW;
   const int64_t m = ((int64_t)z * g.OH + y) * g.OW + x;
-  const int nvalid = min(g.td, g.OD - o.d0) * min(g.th, g.OH - o.h0) * min(g.tw, g.OW - o.w0);
+  const unsigned vmask = __ballot_sync(0xffffffffu, valid);  // this warp's rows inside the output
 #pragma unroll 1
   for (int cc = 0; cc < BC / 32; ++cc) {
     const int nbase = o.nt * BC + cc * 32;
@@ -403,39 +418,57 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
       if (a.bias != nullptr && nbase + i < a.cout) v[i] += __ldg(a.bias + nbase + i);
       if (!valid) v[i] = 0.f;
     }
+    const bool stats = a.partials != nullptr;  // uniform
+    float shift = 0.f, cs = 0.f, cs2 = 0.f;
     if (nbase + 32 <= a.cout && (a.cout & 3) == 0) {  // uniform across the warp
-      store_rows_staged(stg, lane, v, valid ? a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase : nullptr);
-    } else if (valid) {
-      float* dst = a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase;
+      float* dst = valid ? a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase : nullptr;
+      if (stats) store_rows_staged<true>(stg, lane, v, dst, vmask, &shift, &cs, &cs2);
+      else store_rows_staged(stg, lane, v, dst);
+    } else {
+      if (valid) {
+        float* dst = a.out + ((int64_t)o.b * ovox + m) * a.cout + nbase;
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (nbase + i < a.cout) dst[i] = v[i];
+        for (int i = 0; i < 32; ++i)
+          if (nbase + i < a.cout) dst[i] = v[i];
+      }
+      if (stats) store_rows_staged<true>(stg, lane, v, nullptr, vmask, &shift, &cs, &cs2);  // statistics only
     }
-    if (a.partials != nullptr) {
-      // per-tile (sum, M2, n) of each column over the brick's valid rows
-      float xs[32];
+    if (stats) {
+      // per-tile (sum, M2, n) of each column over the brick's valid rows: each warp's shifted sums give its
+      // (sum, M2 around its mean, n); the group's first warp combines the four exactly (Chan et al.)
+      const float nw = (float)__popc(vmask);
+      const float sw = fmaf(nw, shift, cs);
+      const float mw = nw > 0.f ? fmaf(-cs, cs / nw, cs2) : 0.f;
+      float* mine = reinterpret_cast<float*>(stg);  // free: the warp's stores have read it
+      mine[lane] = sw;
+      mine[32 + lane] = fmaxf(mw, 0.f);
+      if (lane == 0) mine[64] = nw;
+      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+      if (widx == 0 && nbase + lane < a.cout) {
+        float sum = 0.f, n = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) xs[i] = v[i];
-      red[q * 32 + lane] = warp_column_sums(xs);
-      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
-      const float total = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-      if (q == 0) col_mean[lane] = total / (float)nvalid;
-      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+        for (int w = 0; w < 4; ++w) {
+          const float* b = reinterpret_cast<const float*>(stg_group + w * (kStagingBytes / 16));
+          sum += b[lane];
+          n += b[64];
+        }
+        const float mean = n > 0.f ? sum / n : 0.f;
+        float m2 = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float dv = valid ? v[i] - col_mean[i] : 0.f;
-        xs[i] = dv * dv;
-      }
-      const float colm2 = warp_column_sums(xs);
-      red[q * 32 + lane] = colm2;  // every warp read red before the barrier above
-      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
-      if (q == 0 && nbase + lane < a.cout) {
+        for (int w = 0; w < 4; ++w) {
+          const float* b = reinterpret_cast<const float*>(stg_group + w * (kStagingBytes / 16));
+          const float nb = b[64];
+          if (nb > 0.f) {
+            const float dm = b[lane] / nb - mean;
+            m2 += fmaf(nb * dm, dm, b[32 + lane]);
+          }
+        }
         float* p = a.partials + (((int64_t)o.b * a.cout + nbase + lane) * g.tps + o.t) * 3;
-        p[0] = total;
-        p[1] = red[lane] + red[32 + lane] + red[64 + lane] + red[96 + lane];
-        p[2] = (float)nvalid;
+        p[0] = sum;
+        p[1] = m2;
+        p[2] = n;
       }
-      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");  // the staging buffers are free again
     }
   }
 }
@@ -454,8 +487,6 @@ __device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Ge
   const int grp = C::kEpiGroups == 2 ? (warp - 2) >> 2 : 0;  // group grp drains accumulator grp
   const int bar = 1 + grp;
   volatile int* votes = grp ? sm.votes2 : sm.votes;
-  float* red = grp ? sm.red2 : sm.red;
-  float* col_mean = grp ? sm.col_mean2 : sm.col_mean;
   const uint32_t lane_base = (uint32_t)(q * 32) << 16;
   const RowPos rp = row_pos(g, q, lane);
   for (int it = grp; it < my_tiles; it += C::kEpiGroups) {
@@ -470,8 +501,8 @@ __device__ __forceinline__ void epilogue_role(const nnb_conv3d_args& a, const Ge
     fence_after();
     const TileOrigin o = tile_origin(g, blockIdx.x + it * gridDim.x);
     const uint32_t acc = tmem + ab * C::N + lane_base;
-    epilogue_tile<BC, OP>(a, g, o, rp, acc, acc + BC, q, lane, red, col_mean, col_inv,
-                          stg_base + (warp - 2) * (kStagingBytes / 16), bar);
+    epilogue_tile<BC, OP>(a, g, o, rp, acc, acc + BC, lane, col_inv, stg_base + 4 * grp * (kStagingBytes / 16),
+                          (warp - 2) & 3, bar);
     fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&acce[ab]));
@@ -970,6 +1001,13 @@ template <int OP>
 __device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometry& g, const float* aff,
                                                    bool leaky_act, int w0, int h0, float slope, int t) {
   float amax = 0.f;
+  // the chunk's affine in registers for the whole plane (not re-read from shared memory per row)
+  float4 sc[8], sh[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    sc[k] = *reinterpret_cast<const float4*>(aff + 4 * k);
+    sh[k] = *reinterpret_cast<const float4*>(aff + 32 + 4 * k);
+  }
   for (int r = t; r < g.plane_rows; r += 64) {
     uint8_t* row = plane + r * 128;
     const int sw = r & 7;
@@ -986,10 +1024,8 @@ __device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometr
     uint32_t hi[16], lo[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float4 sc = *reinterpret_cast<const float4*>(aff + 4 * k);
-      const float4 sh = *reinterpret_cast<const float4*>(aff + 32 + 4 * k);
-      float v[4] = {fmaf(x[k].x, sc.x, sh.x), fmaf(x[k].y, sc.y, sh.y), fmaf(x[k].z, sc.z, sh.z),
-                    fmaf(x[k].w, sc.w, sh.w)};
+      float v[4] = {fmaf(x[k].x, sc[k].x, sh[k].x), fmaf(x[k].y, sc[k].y, sh[k].y), fmaf(x[k].z, sc[k].z, sh[k].z),
+                    fmaf(x[k].w, sc[k].w, sh[k].w)};
       if (leaky_act) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) v[e] = fmaxf(v[e], v[e] * slope);  // LeakyReLU for 0 <= slope <= 1
@@ -1330,8 +1366,6 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     const int grp = warp >= 6 ? 1 : 0;
     const int bar = 1 + grp;
     volatile int* votes = grp ? sm.votes2 : sm.votes;
-    float* red = grp ? sm.red2 : sm.red;
-    float* col_mean = grp ? sm.col_mean2 : sm.col_mean;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const float* col_inv = reinterpret_cast<const float*>(wimg + (int64_t)g.ksteps * C::kBBytes);
     const RowPos rp = row_pos(g, q, lane);
@@ -1361,8 +1395,8 @@ __global__ void __launch_bounds__(kZsThreads, 1)
           o.d0 = z;
           o.h0 = hb * kHaloH;
           o.w0 = wb * kHaloW;
-          epilogue_tile<BC, OP>(a, g, o, rp, acc, 0u, q, lane, red, col_mean, col_inv,
-                                zs_stg + (warp - 2) * (kStagingBytes / 16), bar);
+          epilogue_tile<BC, OP>(a, g, o, rp, acc, 0u, lane, col_inv, zs_stg + 4 * grp * (kStagingBytes / 16),
+                                (warp - 2) & 3, bar);
         }
         tmem_zero32(acc);
         fence_before();

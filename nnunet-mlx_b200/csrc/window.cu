@@ -410,38 +410,32 @@ __global__ void normalize_labels_kernel(const float* __restrict__ acc, const flo
                                         int classes, Dims3 ad, Dims3 lo, Dims3 cd, float fold_divisor,
                                         float* __restrict__ logits, LabelT* __restrict__ labels,
                                         int* __restrict__ invalid_count, LabelT invalid_label) {
-  // one warp per output row (z, y) of the crop: the row's source offset is computed once, lanes walk x
   const int64_t total = (int64_t)cd.d[0] * cd.d[1] * cd.d[2];
-  const int64_t rows = (int64_t)cd.d[0] * cd.d[1];
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   int local_invalid = 0;
-  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const int z = (int)(r / cd.d[1]), y = (int)(r - (int64_t)z * cd.d[1]);
-    const int64_t src_row = ((int64_t)(lo.d[0] + z) * ad.d[1] + (lo.d[1] + y)) * ad.d[2] + lo.d[2];
-    const int64_t out_row = r * cd.d[2];
-    for (int x = lane; x < cd.d[2]; x += 32) {
-      const int64_t src = src_row + x, o = out_row + x;
-      const float den = __ldg(normalizer + src);
-      bool invalid = !isfinite(den) || den <= 0.f;
-      float best = -INFINITY;
-      int winner = 0;
-      bool have = false;
-      const float* a = acc + src * classes;
-      for (int c = 0; c < classes; ++c) {
-        float q = __ldg(a + c) / den;
-        if (fold_divisor != 1.0f) q = q / fold_divisor;
-        invalid |= !isfinite(q);
-        if (logits != nullptr) logits[(int64_t)c * total + o] = q;
-        if (!have || q > best) {
-          best = q;
-          winner = c;
-          have = true;
-        }
+  for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+       o += (int64_t)gridDim.x * blockDim.x) {
+    const int x = (int)(o % cd.d[2]);
+    const int y = (int)((o / cd.d[2]) % cd.d[1]);
+    const int z = (int)(o / ((int64_t)cd.d[2] * cd.d[1]));
+    const int64_t src = ((int64_t)(lo.d[0] + z) * ad.d[1] + (lo.d[1] + y)) * ad.d[2] + (lo.d[2] + x);
+    const float den = __ldg(normalizer + src);
+    bool invalid = !isfinite(den) || den <= 0.f;
+    float best = -INFINITY;
+    int winner = 0;
+    bool have = false;
+    for (int c = 0; c < classes; ++c) {
+      float q = __ldg(acc + src * classes + c) / den;
+      if (fold_divisor != 1.0f) q = q / fold_divisor;
+      invalid |= !isfinite(q);
+      if (logits != nullptr) logits[(int64_t)c * total + o] = q;
+      if (!have || q > best) {
+        best = q;
+        winner = c;
+        have = true;
       }
-      if (labels != nullptr) labels[o] = invalid ? invalid_label : (LabelT)winner;
-      local_invalid += invalid ? 1 : 0;
     }
+    if (labels != nullptr) labels[o] = invalid ? invalid_label : (LabelT)winner;
+    local_invalid += invalid ? 1 : 0;
   }
   if (local_invalid) atomicAdd(invalid_count, local_invalid);
 }
@@ -450,8 +444,8 @@ int launch_normalize_labels(const float* acc, const float* normalizer, int class
                             const int32_t lo[3], const int32_t cd[3], float fold_divisor, float* logits,
                             void* labels, int label_bytes, int32_t* invalid_count, cudaStream_t stream) {
   Dims3 dad{{ad[0], ad[1], ad[2]}}, dlo{{lo[0], lo[1], lo[2]}}, dcd{{cd[0], cd[1], cd[2]}};
-  const int64_t rows = (int64_t)cd[0] * cd[1];
-  const int blocks = (int)std::min<int64_t>((rows + 7) / 8, 148 * 16);  // 8 warps (rows) per block
+  const int64_t total = (int64_t)cd[0] * cd[1] * cd[2];
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
   NNB_CUDA_CHECK(cudaMemsetAsync(invalid_count, 0, sizeof(int32_t), stream));
   if (label_bytes == 1) {
     NNB_REQUIRE(classes <= 255, "normalize_labels: uint8 labels need <= 255 classes");
