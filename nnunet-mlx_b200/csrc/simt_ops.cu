@@ -226,6 +226,9 @@ __global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int
     const int t = (int)(tile % tps);
     const int b = (int)(tile / tps);
     const float* x = a.seg[0].data + (int64_t)b * ovox * CIN;
+    // accumulators as float pairs (channels 2j, 2j+1) for packed f32x2 FMAs: each pair is two fmaf's with
+    // the same operands and rounding, so the result equals the scalar FMA chain's bit for bit
+    unsigned long long acc2[2][16];
     float acc[2][32];
     int base[2];
     uint32_t mask[2];  // bits 0-8: kx, ky, kz validity (3 bits each)
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int
       mask[v] = mk;
       base[v] = valid[v] ? (int)((((int64_t)(oz - 1) * H + (oy - 1)) * W + (ox - 1)) * CIN) : 0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[v][j] = 0.f;
+      for (int j = 0; j < 16; ++j) acc2[v][j] = 0ull;
     }
 #pragma unroll
     for (int kz = 0; kz < 3; ++kz) {
@@ -255,30 +258,35 @@ __global__ void __launch_bounds__(64) conv3d_first_kernel(nnb_conv3d_args a, int
         for (int kx = 0; kx < 3; ++kx) {
           const int tap = (kz * 3 + ky) * 3 + kx;
           const int off = ((kz * H + ky) * W + kx) * CIN;
-          float xv[2][CIN];
+          unsigned long long xv[2][CIN];
 #pragma unroll
           for (int v = 0; v < 2; ++v) {
             const bool in = (mask[v] >> kx & 1) & (mask[v] >> (3 + ky) & 1) & (mask[v] >> (6 + kz) & 1);
 #pragma unroll
-            for (int ci = 0; ci < CIN; ++ci) xv[v][ci] = in ? __ldg(x + base[v] + off + ci) : 0.f;
+            for (int ci = 0; ci < CIN; ++ci) {
+              const float xs = in ? __ldg(x + base[v] + off + ci) : 0.f;
+              asm("mov.b64 %0, {%1, %1};" : "=l"(xv[v][ci]) : "f"(xs));
+            }
           }
 #pragma unroll
           for (int ci = 0; ci < CIN; ++ci) {
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-              const float4 w = w_s[(tap * CIN + ci) * 8 + q];
+              const ulonglong2 w = reinterpret_cast<const ulonglong2*>(w_s)[(tap * CIN + ci) * 8 + q];
 #pragma unroll
               for (int v = 0; v < 2; ++v) {
-                acc[v][4 * q + 0] = fmaf(xv[v][ci], w.x, acc[v][4 * q + 0]);
-                acc[v][4 * q + 1] = fmaf(xv[v][ci], w.y, acc[v][4 * q + 1]);
-                acc[v][4 * q + 2] = fmaf(xv[v][ci], w.z, acc[v][4 * q + 2]);
-                acc[v][4 * q + 3] = fmaf(xv[v][ci], w.w, acc[v][4 * q + 3]);
+                asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc2[v][2 * q]) : "l"(xv[v][ci]), "l"(w.x));
+                asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc2[v][2 * q + 1]) : "l"(xv[v][ci]), "l"(w.y));
               }
             }
           }
         }
       }
     }
+#pragma unroll
+    for (int v = 0; v < 2; ++v)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[v][2 * j]), "=f"(acc[v][2 * j + 1]) : "l"(acc2[v][j]));
     if (a.bias != nullptr) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
