@@ -597,38 +597,68 @@ int launch_conv_transpose_simt(const nnb_segment& in, int batch, const int32_t i
 
 // ---------------------------------------------------------------------------
 // Residual join: out = LeakyReLU(act(branch) + act(skip)), float4 vectorised.
+// One float4 per thread step covers 4 channels of one voxel (channels % 4 == 0), so the sample and channel
+// indices come from one division of the float4 index and the per-(sample, channel) affine is read as float4s;
+// 32-bit index arithmetic when the element count allows it.
 // ---------------------------------------------------------------------------
-__global__ void residual_join_kernel(nnb_segment br, nnb_segment sk, int64_t per_sample, int channels,
-                                     int64_t total4, float slope, float* __restrict__ out) {
-  for (int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4;
-       i4 += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = i4 * 4;
-    const float4 x = __ldg(reinterpret_cast<const float4*>(br.data) + i4);
-    const float4 y = __ldg(reinterpret_cast<const float4*>(sk.data) + i4);
-    const float xs[4] = {x.x, x.y, x.z, x.w};
-    const float ys[4] = {y.x, y.y, y.z, y.w};
-    float r[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int64_t idx = i + e;
-      const int c = (int)(idx % channels);
-      const int b = (int)(idx / per_sample);
-      const float u = activate(xs[e], br.scale, br.shift, br.leaky, slope, b * channels + c);
-      const float w = activate(ys[e], sk.scale, sk.shift, sk.leaky, slope, b * channels + c);
-      r[e] = leaky(u + w, slope);
-    }
-    reinterpret_cast<float4*>(out)[i4] = make_float4(r[0], r[1], r[2], r[3]);
+__device__ __forceinline__ float4 affine4(const nnb_segment& s, int idx, float4 x, float slope) {
+  if (s.scale == nullptr) return x;
+  const float4 sc = __ldg(reinterpret_cast<const float4*>(s.scale + idx));
+  const float4 sh = __ldg(reinterpret_cast<const float4*>(s.shift + idx));
+  float4 y = make_float4(fmaf(x.x, sc.x, sh.x), fmaf(x.y, sc.y, sh.y), fmaf(x.z, sc.z, sh.z), fmaf(x.w, sc.w, sh.w));
+  if (s.leaky) y = make_float4(leaky(y.x, slope), leaky(y.y, slope), leaky(y.z, slope), leaky(y.w, slope));
+  return y;
+}
+
+template <typename Index>
+__global__ void residual_join_kernel(nnb_segment br, nnb_segment sk, Index voxels, int channels, Index total4,
+                                     float slope, float* __restrict__ out) {
+  const Index c4n = (Index)(channels / 4);
+  for (Index i4 = (Index)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4; i4 += (Index)gridDim.x * blockDim.x) {
+    const Index vox = i4 / c4n;                   // voxel over all samples
+    const int c = (int)(i4 - vox * c4n) * 4;      // first of the float4's channels
+    const int b = (int)(vox / voxels);            // sample
+    const int idx = b * channels + c;
+    const float4 u = affine4(br, idx, __ldg(reinterpret_cast<const float4*>(br.data) + i4), slope);
+    const float4 w = affine4(sk, idx, __ldg(reinterpret_cast<const float4*>(sk.data) + i4), slope);
+    reinterpret_cast<float4*>(out)[i4] = make_float4(leaky(u.x + w.x, slope), leaky(u.y + w.y, slope),
+                                                     leaky(u.z + w.z, slope), leaky(u.w + w.w, slope));
+  }
+}
+
+// Channel counts that are not a multiple of 4 (or unaligned tensors): one element per thread step.
+__global__ void residual_join_scalar_kernel(nnb_segment br, nnb_segment sk, int64_t per_sample, int channels,
+                                            int64_t total, float slope, float* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int idx = (int)(i / per_sample) * channels + (int)(i % channels);
+    const float u = activate(__ldg(br.data + i), br.scale, br.shift, br.leaky, slope, idx);
+    const float w = activate(__ldg(sk.data + i), sk.scale, sk.shift, sk.leaky, slope, idx);
+    out[i] = leaky(u + w, slope);
   }
 }
 
 int launch_residual_join(const nnb_segment& br, const nnb_segment& sk, int batch, int64_t voxels, float slope,
                          float* out, cudaStream_t stream) {
-  const int64_t per_sample = voxels * br.channels;
-  const int64_t total = per_sample * batch;
-  NNB_REQUIRE(total % 4 == 0, "residual_join: element count must be a multiple of 4");
-  const int64_t total4 = total / 4;
+  NNB_REQUIRE(br.channels == sk.channels, "residual_join: channel mismatch");
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  bool vec = br.channels % 4 == 0 && aligned(br.data) && aligned(sk.data) && aligned(out);
+  for (const nnb_segment* s : {&br, &sk})
+    vec = vec && (s->scale == nullptr || (aligned(s->scale) && aligned(s->shift)));
+  if (!vec) {
+    const int64_t total = voxels * batch * br.channels;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    residual_join_scalar_kernel<<<blocks, 256, 0, stream>>>(br, sk, voxels * br.channels, br.channels, total, slope,
+                                                            out);
+    NNB_LAUNCH_CHECK();
+    return NNB_OK;
+  }
+  const int64_t total4 = voxels * batch * (br.channels / 4);
   const int blocks = (int)std::min<int64_t>((total4 + 255) / 256, 148 * 16);
-  residual_join_kernel<<<blocks, 256, 0, stream>>>(br, sk, per_sample, br.channels, total4, slope, out);
+  if (total4 + (int64_t)blocks * 256 < (1LL << 31))
+    residual_join_kernel<int32_t><<<blocks, 256, 0, stream>>>(br, sk, (int32_t)voxels, br.channels, (int32_t)total4,
+                                                              slope, out);
+  else
+    residual_join_kernel<int64_t><<<blocks, 256, 0, stream>>>(br, sk, voxels, br.channels, total4, slope, out);
   NNB_LAUNCH_CHECK();
   return NNB_OK;
 }

@@ -905,8 +905,15 @@ __host__ __device__ constexpr int zs_rows(int op) { return op == kOperandF16x2 ?
 __host__ __device__ constexpr int zs_row_bytes(int op) { return half_rows(op) ? 64 : 128; }
 __host__ __device__ constexpr int zs_tap_bytes(int op) { return zs_rows(op) * zs_row_bytes(op); }
 
+// A CTA's share of the output planes.  Whole columns first, in rounds: in round k CTA i takes column
+// k * ncta + i from plane 0 to the last, so at any time the CTAs work on neighbouring columns at about the same
+// depth, and the halo rows one CTA loads of its neighbours' columns are the rows those neighbours are loading
+// (L2 hits instead of a second trip to DRAM).  The columns left after the last full round are split evenly as
+// contiguous runs of their column-major, z-fastest plane sequence, so every CTA gets the same number of planes
+// to within one.
 struct ZsRun {
-  int64_t idx, end;  // [idx, end) of the column-major, z-fastest output-plane sequence
+  int round, rounds;  // whole-column rounds taken / to take
+  int64_t idx, end;   // then [idx, end) of the column-major, z-fastest output-plane sequence
 };
 
 struct ZsSegment {
@@ -914,20 +921,30 @@ struct ZsSegment {
   int ua, ub;       // input planes loaded: [ua, ub]
 };
 
-__device__ __forceinline__ ZsRun zs_run(const Geometry& g) {
+__host__ __device__ __forceinline__ ZsRun zs_run(const Geometry& g, int cta, int ncta) {
   const int64_t total = (int64_t)g.total_tiles;  // columns x OD
-  return ZsRun{total * blockIdx.x / gridDim.x, total * (blockIdx.x + 1) / gridDim.x};
+  const int64_t ncols = total / g.OD;
+  const int rounds = (int)(ncols / ncta);
+  const int64_t base = (int64_t)rounds * ncta * g.OD, tail = total - base;
+  return ZsRun{0, rounds, base + tail * cta / ncta, base + tail * (cta + 1) / ncta};
 }
 
-__device__ __forceinline__ bool zs_next(const Geometry& g, ZsRun& r, ZsSegment& s) {
-  if (r.idx >= r.end) return false;
-  s.col = (int)(r.idx / g.OD);
-  s.z0 = (int)(r.idx - (int64_t)s.col * g.OD);
-  const int64_t stop = min(r.end, (int64_t)(s.col + 1) * g.OD);
-  s.z1 = s.z0 + (int)(stop - r.idx);
-  r.idx = stop;
-  s.ua = max(s.z0 - 1, 0);
-  s.ub = min(s.z1, g.ID - 1);
+__host__ __device__ __forceinline__ bool zs_next(const Geometry& g, ZsRun& r, ZsSegment& s, int cta, int ncta) {
+  if (r.round < r.rounds) {
+    s.col = r.round * ncta + cta;
+    s.z0 = 0;
+    s.z1 = g.OD;
+    ++r.round;
+  } else {
+    if (r.idx >= r.end) return false;
+    s.col = (int)(r.idx / g.OD);
+    s.z0 = (int)(r.idx - (int64_t)s.col * g.OD);
+    const int64_t stop = r.end < (int64_t)(s.col + 1) * g.OD ? r.end : (int64_t)(s.col + 1) * g.OD;
+    s.z1 = s.z0 + (int)(stop - r.idx);
+    r.idx = stop;
+  }
+  s.ua = s.z0 - 1 > 0 ? s.z0 - 1 : 0;
+  s.ub = s.z1 < g.ID - 1 ? s.z1 : g.ID - 1;
   return true;
 }
 
@@ -1178,9 +1195,9 @@ __global__ void __launch_bounds__(kZsThreads, 1)
                          wimg + (int64_t)(c * taps + kz * 9 + t) * C::kBBytes + part * kBlkBytes, kBlkBytes, fb);
       }
       int P = 0, T = 0;
-      ZsRun run = zs_run(g);
+      ZsRun run = zs_run(g, (int)blockIdx.x, (int)gridDim.x);
       ZsSegment sg;
-      while (alive && zs_next(g, run, sg)) {
+      while (alive && zs_next(g, run, sg, (int)blockIdx.x, (int)gridDim.x)) {
         const int b = sg.col / bricks, rem = sg.col - b * bricks;
         const int hb = rem / g.nw, wb = rem - hb * g.nw;
         const int w0 = wb * kHaloW - 1, h0 = hb * kHaloH - 1;
@@ -1245,9 +1262,9 @@ __global__ void __launch_bounds__(kZsThreads, 1)
       if (alive) fence_after();
       int P = 0, PA = 0, T = 0;
       int acquired = -1;  // planes [0, acquired] have had their slot released by its previous plane
-      ZsRun run = zs_run(g);
+      ZsRun run = zs_run(g, (int)blockIdx.x, (int)gridDim.x);
       ZsSegment sg;
-      while (alive && zs_next(g, run, sg)) {
+      while (alive && zs_next(g, run, sg, (int)blockIdx.x, (int)gridDim.x)) {
         // planes ua - 1 .. ub + 1 of this segment are P .. P + (ub - ua) + 2
         for (int u = sg.ua; u <= sg.ub && alive; ++u) {
           const int Pn = P + (u - sg.ua) + 2;  // plane u + 1: this input's first contribution
@@ -1325,9 +1342,9 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     const int t = threadIdx.x - 10 * 32;
     int PA = 0, cur_b = -1;
     bool alive = true, over = false;
-    ZsRun run = zs_run(g);
+    ZsRun run = zs_run(g, (int)blockIdx.x, (int)gridDim.x);
     ZsSegment sg;
-    while (alive && zs_next(g, run, sg)) {
+    while (alive && zs_next(g, run, sg, (int)blockIdx.x, (int)gridDim.x)) {
       const int b = sg.col / bricks, rem = sg.col - b * bricks;
       const int hb = rem / g.nw, wb = rem - hb * g.nw;
       const int w0 = wb * kHaloW - 1, h0 = hb * kHaloH - 1;
@@ -1370,10 +1387,10 @@ __global__ void __launch_bounds__(kZsThreads, 1)
     const float* col_inv = reinterpret_cast<const float*>(wimg + (int64_t)g.ksteps * C::kBBytes);
     const RowPos rp = row_pos(g, q, lane);
     int P = 0;
-    ZsRun run = zs_run(g);
+    ZsRun run = zs_run(g, (int)blockIdx.x, (int)gridDim.x);
     ZsSegment sg;
     bool stop = false;
-    while (!stop && zs_next(g, run, sg)) {
+    while (!stop && zs_next(g, run, sg, (int)blockIdx.x, (int)gridDim.x)) {
       const int b = sg.col / bricks, rem = sg.col - b * bricks;
       const int hb = rem / g.nw, wb = rem - hb * g.nw;
       for (int z = sg.ua - 1; z <= sg.ub + 1; ++z, ++P) {

@@ -172,12 +172,13 @@ def test_conv_transpose_matches_torch(cuda_device, kernel, cin, cout, precision)
     np.testing.assert_allclose(out.cpu().numpy(), ref.numpy(), **tol)
 
 
-def test_residual_join_matches_reference(cuda_device):
+@pytest.mark.parametrize("channels", [8, 6])  # float4 path; element path for a count that is not a multiple of 4
+def test_residual_join_matches_reference(cuda_device, channels):
     from nnunet_mlx_b200 import kernels
 
     rng = np.random.default_rng(6)
-    a, ra, sa, ha = _make_segment(rng, 2, (3, 4, 5), 8, True, cuda_device)
-    b, rb, sb, hb = _make_segment(rng, 2, (3, 4, 5), 8, False, cuda_device)
+    a, ra, sa, ha = _make_segment(rng, 2, (3, 4, 5), channels, True, cuda_device)
+    b, rb, sb, hb = _make_segment(rng, 2, (3, 4, 5), channels, False, cuda_device)
     # branch without LeakyReLU (conv2 + norm), skip identity
     a = kernels.Lazy(a.raw, a.scale, a.shift, leaky=False)
     out = kernels.residual_join(a, b, 0.01)
