@@ -49,6 +49,7 @@ BF16_CASES = [
     # (batch, in_dims, segments [(channels, lazy)], cout, kernel, stride, pad, expected kernel)
     (2, (5, 9, 17), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "conv3d_zstream_kernel"),
     (1, (40, 24, 24), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "conv3d_zstream_kernel"),
+    (2, (9, 32, 600), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "conv3d_zstream_kernel"),
     (1, (1, 8, 8), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "conv3d_zstream_kernel"),
     (3, (4, 16, 8), [(96, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "conv3d_zstream_kernel"),
     (1, (3, 8, 8), [(32, True), (32, False)], 16, (3, 3, 3), (1, 1, 1), (1, 1, 1), "conv3d_zstream_kernel"),

@@ -78,6 +78,10 @@ CONV_CASES = [
     (1, (3, 8, 8), [(32, True), (32, False)], 16, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
     (3, (4, 16, 8), [(96, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
     (1, (40, 24, 24), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    # z-streaming schedule on 148 SMs: exactly one round of whole columns (4 x 37 columns), and two rounds
+    # followed by 4 columns split into runs (2 x 150 columns)
+    (4, (4, 16, 296), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
+    (2, (9, 32, 600), [(32, True)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32"),
     # split TF32 (the range fallback of the default fp16-pair mode): halo, box, 128-column and concat shapes
     (2, (10, 12, 16), [(32, True), (32, False)], 32, (3, 3, 3), (1, 1, 1), (1, 1, 1), "fp32-tf32x2"),
     (2, (9, 10, 11), [(32, True)], 64, (3, 3, 3), (2, 2, 2), (1, 1, 1), "fp32-tf32x2"),
