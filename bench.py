@@ -541,6 +541,8 @@ def main():
             "data": "synthetic",
             "config": bench_config(args, shape, patch, views, len(models), work, fwd / 1e9, world),
             "conv_tflops_effective": work["forwards"] * fwd * args.steps / elapsed / 1e12 / world,
+            # the whole step against the tensor-core roof: algorithmic conv FLOPs per GPU / wall / sustained peak
+            "step_roofline_frac": work["forwards"] * fwd * args.steps / elapsed / 1e12 / world / peak,
             "roofline": roofline,
             "kernels": prof,
             "conv_launches": launch_table(kernels.PROFILE.trace()),
