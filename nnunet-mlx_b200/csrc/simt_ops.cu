@@ -478,53 +478,55 @@ int launch_conv3d_simt(const nnb_conv3d_args& a, cudaStream_t stream) {
 
 // ---------------------------------------------------------------------------
 // Instance-norm finalisation: one block per (channel, sample) over its
-// contiguous run of per-tile (sum, M2, n) records, in float64 and two passes:
-// the mean from the summed sums and counts, then
-//   M2 = sum_t [ M2_t + (sum_t - n_t * mean)^2 / n_t ]
-// (the parallel-variance identity; every term is independent, so no chain of
-// merges and divisions serialises a thread).
+// contiguous run of per-tile (sum, M2, n) records, in float64 and one pass.
+// With K the first record's mean and d_t = sum_t - n_t K, the parallel-variance
+// identity M2 = sum_t [ M2_t + (sum_t - n_t mean)^2 / n_t ] expands to
+//   M2 = sum_t M2_t + sum_t d_t^2 / n_t - D^2 / N,   D = sum_t d_t, N = sum_t n_t,
+// so every record is read once and contributes four independent terms.  The
+// shift keeps the cancellation harmless: (mean - K)^2 <= (N / n_0) var, so the
+// relative error of the difference is at most (tiles) x 2^-52.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ double block_sum(double v, double* red) {
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();  // red is free (a previous call's readers are done)
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  double t = 0.0;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-  return t;
-}
-
 __global__ void __launch_bounds__(1024) norm_finalize_kernel(const float* __restrict__ partials,
                                                             int channels, int tps,
                                                             const float* __restrict__ gamma,
                                                             const float* __restrict__ beta, float eps,
                                                             float* __restrict__ scale,
                                                             float* __restrict__ shift) {
-  __shared__ double red[32];
+  __shared__ double red[4][32];
   const int c = blockIdx.x;
   const int b = blockIdx.y;
   const float* run = partials + ((int64_t)b * channels + c) * tps * 3;
-  double s = 0.0, n = 0.0;
+  const double n0 = (double)run[2];
+  const double K = n0 > 0.0 ? (double)run[0] / n0 : 0.0;
+  double v[4] = {0.0, 0.0, 0.0, 0.0};  // sum_t sum_t, sum_t n_t, sum_t M2_t, sum_t d_t^2 / n_t
 #pragma unroll 4
   for (int t = threadIdx.x; t < tps; t += blockDim.x) {
-    s += (double)run[3 * t];
-    n += (double)run[3 * t + 2];
-  }
-  const double total = block_sum(s, red), count = block_sum(n, red);
-  const double mean = count > 0.0 ? total / count : 0.0;
-  double m2 = 0.0;
-#pragma unroll 4
-  for (int t = threadIdx.x; t < tps; t += blockDim.x) {
-    const double nt = (double)run[3 * t + 2];
+    const double st = (double)run[3 * t], mt = (double)run[3 * t + 1], nt = (double)run[3 * t + 2];
     if (nt <= 0.0) continue;
-    const double d = (double)run[3 * t] - nt * mean;
-    m2 += (double)run[3 * t + 1] + d * d / nt;
+    const double d = st - nt * K;
+    v[0] += st;
+    v[1] += nt;
+    v[2] += mt;
+    v[3] += d * d / nt;
   }
-  const double m2_total = block_sum(m2, red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+    if (lane == 0) red[k][warp] = v[k];
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    double var = count > 0.0 ? m2_total / count : 0.0;
+    double tot[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tot[k] += red[k][w];
+    const double count = tot[1];
+    const double mean = count > 0.0 ? tot[0] / count : 0.0;
+    const double D = tot[0] - count * K;
+    const double m2 = count > 0.0 ? tot[2] + tot[3] - D * D / count : 0.0;
+    double var = count > 0.0 ? m2 / count : 0.0;
     if (var < 0) var = 0;
     const double inv = 1.0 / sqrt(var + (double)eps);
     const double sc = gamma != nullptr ? (double)gamma[c] * inv : inv;
