@@ -41,12 +41,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "voxels/sec full-volume 3D U-Net inference (8x mirror TTA)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the dominant convolution launch, by precision, from the ncu
-# captures summarised in profiles/ (one view per capture; views are independent samples of the batch,
-# so an 8-view launch moves 8x that): the z-streaming kernel (fp32) read 394.5 MB (the raw input plus
-# halo rows) and wrote 240.1 MB; split TF32 (halo kernel) read 537.2 MB (the hi/lo operand) and wrote
-# 252.1 MB.
+# captures summarised in profiles/: the z-streaming kernel (fp32) on the bench's own 8-view launch read
+# 2274.9 MB (the raw input, 2147.5 MB, plus halo rows that missed L2) and wrote 2163.7 MB; split TF32 (halo
+# kernel), captured on one view (views are independent samples of the batch, so an 8-view launch moves 8x
+# that), read 537.2 MB (the hi/lo operand) and wrote 252.1 MB.
 DOMINANT_TRAFFIC = {
-    ("fp32", "8x128x128x128 32->32 k3x3x3 s1x1x1 conv3d_zstream_kernel"): 8 * (394.499584e6 + 240.076032e6),
+    ("fp32", "8x128x128x128 32->32 k3x3x3 s1x1x1 conv3d_zstream_kernel"): 2274.894336e6 + 2163.651328e6,
     ("fp32-tf32x2", "8x128x128x128 32->32 k3x3x3 s1x1x1 conv3d_halo_kernel"): 8 * (537.210624e6 + 252.089088e6)}
 
 
