@@ -1018,13 +1018,15 @@ template <int OP>
 __device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometry& g, const float* aff,
                                                    bool leaky_act, int w0, int h0, float slope, int t) {
   float amax = 0.f;
-  // the chunk's affine in registers for the whole plane (not re-read from shared memory per row)
-  float4 sc[8], sh[8];
+  // the chunk's affine in registers for the whole plane (not re-read from shared memory per row), as channel
+  // pairs for packed f32x2 arithmetic (each half is the scalar operation with the same rounding)
+  unsigned long long sc2[16], sh2[16], slope2;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    sc[k] = *reinterpret_cast<const float4*>(aff + 4 * k);
-    sh[k] = *reinterpret_cast<const float4*>(aff + 32 + 4 * k);
+  for (int k = 0; k < 16; ++k) {
+    sc2[k] = *reinterpret_cast<const unsigned long long*>(aff + 2 * k);
+    sh2[k] = *reinterpret_cast<const unsigned long long*>(aff + 32 + 2 * k);
   }
+  asm("mov.b64 %0, {%1, %1};" : "=l"(slope2) : "f"(slope));
   for (int r = t; r < g.plane_rows; r += 64) {
     uint8_t* row = plane + r * 128;
     const int sw = r & 7;
@@ -1041,11 +1043,26 @@ __device__ __forceinline__ bool zs_transform_plane(uint8_t* plane, const Geometr
     uint32_t hi[16], lo[16];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      float v[4] = {fmaf(x[k].x, sc[k].x, sh[k].x), fmaf(x[k].y, sc[k].y, sh[k].y), fmaf(x[k].z, sc[k].z, sh[k].z),
-                    fmaf(x[k].w, sc[k].w, sh[k].w)};
-      if (leaky_act) {
+      float v[4];
+      {
+        unsigned long long x01, x23, y01, y23;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(x01) : "f"(x[k].x), "f"(x[k].y));
+        asm("mov.b64 %0, {%1, %2};" : "=l"(x23) : "f"(x[k].z), "f"(x[k].w));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(y01) : "l"(x01), "l"(sc2[2 * k]), "l"(sh2[2 * k]));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(y23) : "l"(x23), "l"(sc2[2 * k + 1]), "l"(sh2[2 * k + 1]));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(v[0]), "=f"(v[1]) : "l"(y01));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(v[2]), "=f"(v[3]) : "l"(y23));
+        if (leaky_act) {
+          // LeakyReLU for 0 <= slope <= 1: max(v, v * slope)
+          unsigned long long m01, m23;
+          float m[4];
+          asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(m01) : "l"(y01), "l"(slope2));
+          asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(m23) : "l"(y23), "l"(slope2));
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(m[0]), "=f"(m[1]) : "l"(m01));
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(m[2]), "=f"(m[3]) : "l"(m23));
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = fmaxf(v[e], v[e] * slope);  // LeakyReLU for 0 <= slope <= 1
+          for (int e = 0; e < 4; ++e) v[e] = fmaxf(v[e], m[e]);
+        }
       }
       if constexpr (OP == kOperandF16x2) {
         float h[4], l[4];
