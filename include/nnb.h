@@ -144,8 +144,9 @@ int32_t nnb_conv3d_raw_operands(const nnb_conv3d_args* args);
  *                       mantissa bits cleared, lo = x - hi (2 C floats);
  *   NNB_PREC_TF32       x rounded to TF32 (C floats);
  *   NNB_PREC_BF16       per voxel and 32-channel group, 64 bf16 halves
- *                       [bf16(x)(32) | 0(32)] (C % 32 == 0; the fp16 pair's
- *                       layout, of which the convolution reads the first half).
+ *                       [bf16(x)(32) | (32)] (C % 32 == 0; the fp16 pair's
+ *                       layout, of which the convolution reads the first half;
+ *                       the second half is left unwritten).
  * Replaces the affine pass of
  * src/nnunet_mlx/kernels/metal_native_norm.py:62-70,155-168 (there the
  * normalised activation is materialised in float32).

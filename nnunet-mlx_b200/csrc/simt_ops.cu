@@ -681,9 +681,10 @@ namespace nnb {
 //   kOperandTf32x2  per voxel [hi(C) | lo(C)], hi = x with the 13 low mantissa
 //                   bits cleared, lo = x - hi (both exact).  4 read, 8 written.
 //   kOperandTf32    x rounded to TF32 (nearest).  4 read, 4 written.
-//   kOperandBf16    per voxel and 32-channel group [bf16(x)(32) | 0(32)] as
-//                   bf16 halves (the fp16 pair's row layout; the MMA reads
-//                   only the first half).  4 read, 4 written.
+//   kOperandBf16    per voxel and 32-channel group [bf16(x)(32) | (32)] as
+//                   bf16 halves (the fp16 pair's row layout); the MMA reads
+//                   only the first half, so the second is not written.
+//                   4 read, 2 written.
 // ---------------------------------------------------------------------------
 __device__ unsigned long long g_operand_range_events = 0;
 
@@ -727,7 +728,6 @@ __global__ void prepare_operand_kernel(nnb_segment in, int64_t voxels_total, int
       }
       __half* base = reinterpret_cast<__half*>(out) + vox * 2 * C + (c8 / 32) * 64 + (c8 % 32);
       *reinterpret_cast<uint4*>(base) = make_uint4(hb[0], hb[1], hb[2], hb[3]);
-      *reinterpret_cast<uint4*>(base + 32) = make_uint4(0u, 0u, 0u, 0u);
     } else if (op == kOperandTf32x2) {
       float hi[8], lo[8];
 #pragma unroll
