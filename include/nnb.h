@@ -262,7 +262,8 @@ int32_t nnb_conv_transpose3d(const nnb_segment* input, int32_t batch, const int3
  * nnb_prepare_operand layout of `precision`, 4 bytes per channel:
  * NNB_PREC_FP32 [hi(32) | lo(32)] halves per 32-channel group, whose
  * out-of-range values count in nnb_operand_range_events; NNB_PREC_BF16
- * [bf16(32) | 0(32)]; NNB_PREC_TF32 TF32 values) instead of float32, so the
+ * [bf16(32) | (32)], the second half left unwritten; NNB_PREC_TF32 TF32
+ * values) instead of float32, so the
  * decoder's concat convolution reads it without a preparation pass.
  * Requires `packed`, 32-multiple channel counts and one of those three
  * precisions (else NNB_E_UNSUPPORTED).  Same reference call site as

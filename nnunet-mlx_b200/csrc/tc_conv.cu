@@ -254,7 +254,9 @@ __device__ __forceinline__ SharedMisc shared_misc(uint8_t* misc) {
 // lane's row destination (16-byte aligned), or nullptr to skip the row.  All 32 lanes must call it.
 // kStats: while the rows are staged, lane c also reads column c of each staged row and accumulates, over
 // the rows whose bit is set in vmask, the deviations from `shift` (the value of row 0): s += d, s2 += d^2.
-template <bool kStats = false>
+// kChunks: only the first kChunks 16-byte chunks of each row are staged and written (4: a bf16 operand row,
+// whose second half no MMA reads).
+template <bool kStats = false, int kChunks = 8>
 __device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const float (&v)[32], float* dst,
                                                   unsigned vmask = 0u, float* shift = nullptr, float* s = nullptr,
                                                   float* s2 = nullptr) {
@@ -265,7 +267,7 @@ __device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const f
     if ((lane >> 4) == half) {
       const int r = lane & 15;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < kChunks; ++j)
         stg[r * 8 + (j ^ (r & 7))] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
     __syncwarp();
@@ -275,7 +277,7 @@ __device__ __forceinline__ void store_rows_staged(float4* stg, int lane, const f
       const int c = lane & 7;
       const unsigned long long rd = __shfl_sync(0xffffffffu, d, half * 16 + r);
       const float4 val = stg[r * 8 + (c ^ (r & 7))];
-      if (rd != 0ull) reinterpret_cast<float4*>(rd)[c] = val;
+      if (rd != 0ull && c < kChunks) reinterpret_cast<float4*>(rd)[c] = val;
     }
     if constexpr (kStats) {
       // column `lane` of staged row r: word 4 ((lane / 4) ^ (r % 8)) + lane % 4 of the row (conflict-free)
@@ -395,7 +397,7 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
           }
           if (over && valid) atomicAdd(g.range_events, 1ull);
         } else if constexpr (OP == kOperandBf16) {
-          // [bf16(32) | 0(32)]
+          // [bf16(32) | (32)]: only the first half, which the MMAs read, is written
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const __nv_bfloat162 bb = __floats2bfloat162_rn(v[i], v[i + 1]);
@@ -407,7 +409,8 @@ __device__ __forceinline__ void epilogue_tile(const nnb_conv3d_args& a, const Ge
 #pragma unroll
           for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(to_tf32(v[i]));
         }
-        store_rows_staged(stg, lane, pk, dst);
+        if constexpr (OP == kOperandBf16) store_rows_staged<false, 4>(stg, lane, pk, dst);
+        else store_rows_staged(stg, lane, pk, dst);
       } else {
         store_rows_staged(stg, lane, v, dst);
       }
