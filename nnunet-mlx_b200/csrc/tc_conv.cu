@@ -79,6 +79,7 @@ __device__ int g_device_status_where = 0;
 }  // namespace nnb
 
 #include "tc_common.cuh"
+#include "zs_schedule.cuh"
 
 namespace nnb {
 namespace tc {
@@ -908,47 +909,13 @@ __host__ __device__ constexpr int zs_rows(int op) { return op == kOperandF16x2 ?
 __host__ __device__ constexpr int zs_row_bytes(int op) { return half_rows(op) ? 64 : 128; }
 __host__ __device__ constexpr int zs_tap_bytes(int op) { return zs_rows(op) * zs_row_bytes(op); }
 
-// A CTA's share of the output planes.  Whole columns first, in rounds: in round k CTA i takes column
-// k * ncta + i from plane 0 to the last, so at any time the CTAs work on neighbouring columns at about the same
-// depth, and the halo rows one CTA loads of its neighbours' columns are the rows those neighbours are loading
-// (L2 hits instead of a second trip to DRAM).  The columns left after the last full round are split evenly as
-// contiguous runs of their column-major, z-fastest plane sequence, so every CTA gets the same number of planes
-// to within one.
-struct ZsRun {
-  int round, rounds;  // whole-column rounds taken / to take
-  int64_t idx, end;   // then [idx, end) of the column-major, z-fastest output-plane sequence
-};
-
-struct ZsSegment {
-  int col, z0, z1;  // output planes [z0, z1) of brick column col
-  int ua, ub;       // input planes loaded: [ua, ub]
-};
-
+// The work split (zs_schedule.cuh) over this launch's geometry.
 __host__ __device__ __forceinline__ ZsRun zs_run(const Geometry& g, int cta, int ncta) {
-  const int64_t total = (int64_t)g.total_tiles;  // columns x OD
-  const int64_t ncols = total / g.OD;
-  const int rounds = (int)(ncols / ncta);
-  const int64_t base = (int64_t)rounds * ncta * g.OD, tail = total - base;
-  return ZsRun{0, rounds, base + tail * cta / ncta, base + tail * (cta + 1) / ncta};
+  return zs_run((int64_t)g.total_tiles, g.OD, cta, ncta);  // total_tiles = brick columns x OD
 }
 
 __host__ __device__ __forceinline__ bool zs_next(const Geometry& g, ZsRun& r, ZsSegment& s, int cta, int ncta) {
-  if (r.round < r.rounds) {
-    s.col = r.round * ncta + cta;
-    s.z0 = 0;
-    s.z1 = g.OD;
-    ++r.round;
-  } else {
-    if (r.idx >= r.end) return false;
-    s.col = (int)(r.idx / g.OD);
-    s.z0 = (int)(r.idx - (int64_t)s.col * g.OD);
-    const int64_t stop = r.end < (int64_t)(s.col + 1) * g.OD ? r.end : (int64_t)(s.col + 1) * g.OD;
-    s.z1 = s.z0 + (int)(stop - r.idx);
-    r.idx = stop;
-  }
-  s.ua = s.z0 - 1 > 0 ? s.z0 - 1 : 0;
-  s.ub = s.z1 < g.ID - 1 ? s.z1 : g.ID - 1;
-  return true;
+  return zs_next(r, s, g.OD, g.ID, cta, ncta);
 }
 
 __device__ __forceinline__ int zs_slot(int P) { return kZsSlots - 1 - (P & (kZsSlots - 1)); }
